@@ -1,0 +1,105 @@
+// Shared device helpers and specialization structs of the sm_100a kernel library.
+//
+// Every specialization struct is a sequence of int64 fields so that the host compiler (Python)
+// packs it as "<Nq" with no padding questions.  Field meaning is documented per struct.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include "../library.hpp"
+
+namespace ckl::kernels {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float warpSum(float v) {
+#pragma unroll
+  for (int o = kWarp / 2; o > 0; o >>= 1)
+    v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warpMax(float v) {
+#pragma unroll
+  for (int o = kWarp / 2; o > 0; o >>= 1)
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Argmax pair reduction with first-index tie-breaking: `b` replaces `a` when it is strictly
+// larger, or equal with a smaller index (the greedy kernel's strict ">" scan keeps the first
+// maximum).
+__device__ __forceinline__ void argmaxMerge(float &value, int &index, float otherValue,
+                                            int otherIndex) {
+  if (otherValue > value || (otherValue == value && otherIndex < index)) {
+    value = otherValue;
+    index = otherIndex;
+  }
+}
+
+__device__ __forceinline__ bool aligned16(const void *p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+inline unsigned ceilDiv(int64_t a, int64_t b) { return unsigned((a + b - 1) / b); }
+
+template <typename Spec> const Spec &specOf(const void *spec) {
+  return *static_cast<const Spec *>(spec);
+}
+
+// ---- specializations ------------------------------------------------------------------
+// Elementwise pointwise kernels over a 1-D vector: n elements, `count` = elements the
+// original launch covers (min(n, grid.x * block.x)).
+struct PointwiseSpec {
+  int64_t n, count;
+};
+// Fused chain of scalar pointwise ops: op codes 0 = add scalar, 1 = multiply scalar.
+struct ChainSpec {
+  int64_t n, count, steps, op[4];
+};
+struct EmbeddingSpec {
+  int64_t B, C, V;
+};
+struct RowsSpec {
+  int64_t B, C;
+};
+struct RmsApplySpec {
+  int64_t B, C, L, layer;
+};
+// dst[B, O] = x[B, I] @ W[layer, I, O] with W holding `W` layers.
+struct LinearSpec {
+  int64_t B, I, O, W, layer;
+};
+struct RopeSpec {
+  int64_t B, C, A, R, T;
+};
+// Cache shape [L, B, A, T, D]; hidden C = A * D.
+struct CacheSpec {
+  int64_t B, C, L, A, T, D, layer;
+};
+struct SoftmaxSpec {
+  int64_t B, A, T;
+};
+struct GreedySpec {
+  int64_t B, V, T;
+};
+
+// Fused projection: out = epilogue(prologue(x) @ W[layer]).
+//   M rows (requests), K inner, N outputs; W holds `layers` matrices [K, N].
+//   Cache-writing epilogues address cache[L=layers, M, A, T, D] at position[0].
+//   `tiles` is the number of column tiles of the argmax epilogue (partials per row).
+struct GemmSpec {
+  int64_t M, K, N, layers, layer, A, D, T, tiles, config;
+};
+// Flash-decoding attention over cache[L, B, A, T, D] at positions 0..position[0].
+struct AttentionSpec {
+  int64_t B, A, T, D, L, layer, splits, chunk;
+};
+// Greedy combine of per-tile argmax partials [B, tiles] of (value, index).
+struct CombineSpec {
+  int64_t B, tiles, T, V;
+};
+
+} // namespace ckl::kernels

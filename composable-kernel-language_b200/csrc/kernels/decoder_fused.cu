@@ -1,0 +1,356 @@
+// Fused decode-step kernels for the decoder program (benchmarks/decoder/workloads.py:191-254).
+//
+// One layer of the reference runs 21 dependent launches.  Here it is six graph nodes in five
+// dependency levels:
+//   q: RMSNorm -> x @ wq -> RoPE                       (norm_linear_rope)
+//   k: RMSNorm -> x @ wk -> RoPE -> append to kc at p  (norm_linear_rope_append)
+//   v: RMSNorm -> x @ wv -> append to vc at p          (norm_linear_append)
+//   attention over kc/vc[0..p] (flash decoding; scores and probabilities never stored)
+//   residual = x + context @ wo                        (linear_residual)
+//   gate, up: RMSNorm -> x @ wg / wu                   (norm_linear, two concurrent nodes)
+//   next_x = residual + (silu(gate) * up) @ wd         (swiglu_linear_residual)
+// and the head is RMSNorm -> x @ lm with per-tile argmax partials, followed by a combine
+// that writes tokens and history and advances the position.
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace ckl::kernels {
+namespace {
+
+using gemm::Large;
+using gemm::Medium;
+using gemm::Params;
+using gemm::Small;
+
+// ---- projection wrappers ---------------------------------------------------------------
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    linearKernel(const float *x, const float *w, float *dst, GemmSpec s) {
+  Params p;
+  p.a = x, p.w = w, p.out = dst, p.s = s;
+  gemm::body<Cfg, gemm::kPlain, gemm::kStore>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    normLinearKernel(const float *x, const float *gain, const float *w, float *dst, float eps,
+                     GemmSpec s) {
+  Params p;
+  p.a = x, p.gain = gain, p.w = w, p.out = dst, p.eps = eps, p.s = s;
+  gemm::body<Cfg, gemm::kRms, gemm::kStore>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    normLinearRopeKernel(const float *x, const float *gain, const float *w, const float *table,
+                         const int *position, float *dst, float eps, GemmSpec s) {
+  Params p;
+  p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = dst;
+  p.eps = eps, p.s = s;
+  gemm::body<Cfg, gemm::kRms, gemm::kRope>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    normLinearRopeAppendKernel(const float *x, const float *gain, const float *w,
+                               const float *table, const int *position, float *cache, float eps,
+                               GemmSpec s) {
+  Params p;
+  p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = cache;
+  p.eps = eps, p.s = s;
+  gemm::body<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    normLinearAppendKernel(const float *x, const float *gain, const float *w, const int *position,
+                           float *cache, float eps, GemmSpec s) {
+  Params p;
+  p.a = x, p.gain = gain, p.w = w, p.position = position, p.out = cache, p.eps = eps, p.s = s;
+  gemm::body<Cfg, gemm::kRms, gemm::kAppend>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    linearResidualKernel(const float *x, const float *w, const float *residual, float *dst,
+                         GemmSpec s) {
+  Params p;
+  p.a = x, p.w = w, p.residual = residual, p.out = dst, p.s = s;
+  gemm::body<Cfg, gemm::kPlain, gemm::kResidual>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    swigluLinearResidualKernel(const float *gate, const float *up, const float *w,
+                               const float *residual, float *dst, GemmSpec s) {
+  Params p;
+  p.a = gate, p.a2 = up, p.w = w, p.residual = residual, p.out = dst, p.s = s;
+  gemm::body<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads)
+    normLinearArgmaxKernel(const float *x, const float *gain, const float *w, float *logits,
+                           float2 *partials, float eps, GemmSpec s) {
+  Params p;
+  p.a = x, p.gain = gain, p.w = w, p.out = logits, p.partials = partials, p.eps = eps, p.s = s;
+  gemm::body<Cfg, gemm::kRms, gemm::kArgmax>(p);
+}
+
+bool gemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  return gemm::geometry(specOf<GemmSpec>(spec), g);
+}
+
+bool ropeGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  if (s.D <= 0 || s.D % 2 || s.N % s.D || s.T <= 0)
+    return false;
+  return gemm::geometry(s, g);
+}
+
+bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  if (s.D <= 0 || s.D % 2 || s.N != s.A * s.D || s.T <= 0)
+    return false;
+  return gemm::geometry(s, g);
+}
+
+#define CKL_GEMM_SELECT(fn)                                                                    \
+  [](const void *spec) -> const void * {                                                       \
+    switch (gemm::chooseConfig(specOf<GemmSpec>(spec))) {                                      \
+    case 0: return reinterpret_cast<const void *>(&fn<Small>);                                 \
+    case 1: return reinterpret_cast<const void *>(&fn<Medium>);                                \
+    case 2: return reinterpret_cast<const void *>(&fn<Large>);                                 \
+    default: return nullptr;                                                                   \
+    }                                                                                          \
+  }
+
+// ---- attention (flash decoding) ---------------------------------------------------------
+// One CTA per (request, head): WARPS warps stream the K and V rows 0..p of the cache with
+// 16-byte loads, D/4 lanes per row; each lane group keeps an online softmax state
+// (running max, normaliser, weighted V) and the states merge across groups and warps.
+struct SoftmaxState {
+  float m, l;
+  float4 acc;
+};
+
+__device__ __forceinline__ void mergeState(SoftmaxState &a, const SoftmaxState &b) {
+  const float M = fmaxf(a.m, b.m);
+  if (M == -CUDART_INF_F)
+    return; // both empty
+  const float ca = a.m == -CUDART_INF_F ? 0.f : expf(a.m - M);
+  const float cb = b.m == -CUDART_INF_F ? 0.f : expf(b.m - M);
+  a.l = a.l * ca + b.l * cb;
+  a.acc.x = a.acc.x * ca + b.acc.x * cb;
+  a.acc.y = a.acc.y * ca + b.acc.y * cb;
+  a.acc.z = a.acc.z * ca + b.acc.z * cb;
+  a.acc.w = a.acc.w * ca + b.acc.w * cb;
+  a.m = M;
+}
+
+__device__ __forceinline__ SoftmaxState shuffleState(const SoftmaxState &s, int offset) {
+  SoftmaxState o;
+  o.m = __shfl_xor_sync(0xffffffffu, s.m, offset);
+  o.l = __shfl_xor_sync(0xffffffffu, s.l, offset);
+  o.acc.x = __shfl_xor_sync(0xffffffffu, s.acc.x, offset);
+  o.acc.y = __shfl_xor_sync(0xffffffffu, s.acc.y, offset);
+  o.acc.z = __shfl_xor_sync(0xffffffffu, s.acc.z, offset);
+  o.acc.w = __shfl_xor_sync(0xffffffffu, s.acc.w, offset);
+  return o;
+}
+
+constexpr int kAttentionWarps = 4;
+constexpr int kAttentionUnroll = 4;
+
+template <int D>
+__global__ void __launch_bounds__(kAttentionWarps *kWarp)
+    attentionKernel(const float *q, const float *kc, const float *vc, const int *position,
+                    float *ctx, float scale, AttentionSpec s) {
+  constexpr int LPR = D / 4;             // lanes per cache row
+  constexpr int RPW = kWarp / LPR;       // rows per warp per iteration
+  constexpr int STEP = kAttentionWarps * RPW;
+  __shared__ SoftmaxState warpState[kAttentionWarps][LPR];
+
+  const int64_t bh = blockIdx.x;
+  const int64_t h = bh % s.A, b = bh / s.A;
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  const int group = lane / LPR, sub = lane % LPR;
+  const int64_t C = s.A * D;
+  const int p = position[0];
+  const int64_t end = int64_t(p) + 1;
+  const int64_t n = end < 0 ? 0 : (end < s.T ? end : s.T);
+
+  const float4 qv = *reinterpret_cast<const float4 *>(q + b * C + h * D + 4 * sub);
+  const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D + 4 * sub;
+  const float4 *kRows = reinterpret_cast<const float4 *>(kc + base);
+  const float4 *vRows = reinterpret_cast<const float4 *>(vc + base);
+  constexpr int ROW4 = D / 4; // float4 per row
+
+  SoftmaxState st{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
+  for (int64_t t0 = int64_t(warp) * RPW; t0 < n; t0 += int64_t(STEP) * kAttentionUnroll) {
+    float4 kv[kAttentionUnroll], vv[kAttentionUnroll];
+    bool valid[kAttentionUnroll];
+#pragma unroll
+    for (int u = 0; u < kAttentionUnroll; ++u) {
+      const int64_t t = t0 + int64_t(u) * STEP + group;
+      valid[u] = t < n;
+      if (valid[u]) {
+        kv[u] = __ldcs(kRows + t * ROW4);
+        vv[u] = __ldcs(vRows + t * ROW4);
+      } else {
+        kv[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kAttentionUnroll; ++u) {
+      float dot = qv.x * kv[u].x + qv.y * kv[u].y + qv.z * kv[u].z + qv.w * kv[u].w;
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1)
+        dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (valid[u]) {
+        const float score = dot * scale;
+        const float M = fmaxf(st.m, score);
+        const float c = st.m == -CUDART_INF_F ? 0.f : expf(st.m - M);
+        const float e = expf(score - M);
+        st.l = st.l * c + e;
+        st.acc.x = st.acc.x * c + e * vv[u].x;
+        st.acc.y = st.acc.y * c + e * vv[u].y;
+        st.acc.z = st.acc.z * c + e * vv[u].z;
+        st.acc.w = st.acc.w * c + e * vv[u].w;
+        st.m = M;
+      }
+    }
+  }
+  // Merge the lane groups of the warp (same `sub`, different rows).
+#pragma unroll
+  for (int o = LPR; o < kWarp; o <<= 1) {
+    const SoftmaxState other = shuffleState(st, o);
+    mergeState(st, other);
+  }
+  if (group == 0)
+    warpState[warp][sub] = st;
+  __syncthreads();
+  if (warp == 0 && group == 0) {
+    SoftmaxState total = warpState[0][sub];
+#pragma unroll
+    for (int w = 1; w < kAttentionWarps; ++w)
+      mergeState(total, warpState[w][sub]);
+    float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (total.l > 0.f) {
+      out.x = total.acc.x / total.l;
+      out.y = total.acc.y / total.l;
+      out.z = total.acc.z / total.l;
+      out.w = total.acc.w / total.l;
+    }
+    *reinterpret_cast<float4 *>(ctx + b * C + h * D + 4 * sub) = out;
+  }
+}
+
+bool attentionGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<AttentionSpec>(spec);
+  if (s.B <= 0 || s.A <= 0 || s.T <= 0 || s.layer < 0 || s.layer >= s.L || s.splits != 1)
+    return false;
+  if (s.D != 16 && s.D != 32 && s.D != 64 && s.D != 128)
+    return false;
+  if (s.B * s.A >= (int64_t(1) << 31))
+    return false;
+  g->grid[0] = unsigned(s.B * s.A);
+  g->block[0] = kAttentionWarps * kWarp;
+  return true;
+}
+
+const void *attentionSelect(const void *spec) {
+  switch (specOf<AttentionSpec>(spec).D) {
+  case 16: return reinterpret_cast<const void *>(&attentionKernel<16>);
+  case 32: return reinterpret_cast<const void *>(&attentionKernel<32>);
+  case 64: return reinterpret_cast<const void *>(&attentionKernel<64>);
+  case 128: return reinterpret_cast<const void *>(&attentionKernel<128>);
+  default: return nullptr;
+  }
+}
+
+// ---- greedy combine -----------------------------------------------------------------
+// One warp per request merges its [tiles] argmax partials (first index wins ties), writes
+// tokens[b] and history[p, b]; the last CTA to finish advances position.  `counter` is a
+// zero-initialised word that the last CTA returns to zero, so replays need no reset.
+constexpr int kCombineWarps = 8;
+
+__global__ void __launch_bounds__(kCombineWarps *kWarp)
+    greedyCombineKernel(const float2 *partials, const float *logits, int *tokens, int *history,
+                        int *position, unsigned *counter, CombineSpec s) {
+  const int p = position[0];
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  const int64_t row = int64_t(blockIdx.x) * kCombineWarps + warp;
+  if (row < s.B) {
+    float best = -CUDART_INF_F;
+    int index = 0x7fffffff;
+    for (int64_t t = lane; t < s.tiles; t += kWarp) {
+      const float2 v = partials[row * s.tiles + t];
+      argmaxMerge(best, index, v.x, __float_as_int(v.y));
+    }
+#pragma unroll
+    for (int o = kWarp / 2; o > 0; o >>= 1)
+      argmaxMerge(best, index, __shfl_xor_sync(0xffffffffu, best, o),
+                  __shfl_xor_sync(0xffffffffu, index, o));
+    if (lane == 0) {
+      const float first = logits[row * s.V];
+      if (first != first || index == 0x7fffffff)
+        index = 0; // a NaN first score wins the reference's strict scan outright
+      tokens[row] = index;
+      if (p >= 0 && p < s.T)
+        history[int64_t(p) * s.B + row] = index;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(counter, 1u);
+    if (done == gridDim.x - 1) {
+      position[0] = p + 1;
+      atomicExch(counter, 0u);
+      __threadfence();
+    }
+  }
+}
+
+bool combineGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<CombineSpec>(spec);
+  if (s.B <= 0 || s.tiles <= 0 || s.V <= 0)
+    return false;
+  g->grid[0] = ceilDiv(s.B, kCombineWarps);
+  g->block[0] = kCombineWarps * kWarp;
+  return true;
+}
+
+} // namespace
+
+CKL_REGISTER_KERNEL("ckl.decoder.linear", reinterpret_cast<const void *>(&linearKernel<Medium>),
+                    "PPPS", sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(linearKernel));
+CKL_REGISTER_KERNEL("ckl.fused.norm_linear", reinterpret_cast<const void *>(&normLinearKernel<Medium>),
+                    "PPPPFS", sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(normLinearKernel));
+CKL_REGISTER_KERNEL("ckl.fused.norm_linear_rope",
+                    reinterpret_cast<const void *>(&normLinearRopeKernel<Medium>), "PPPPPPFS",
+                    sizeof(GemmSpec), ropeGemmGeometry, CKL_GEMM_SELECT(normLinearRopeKernel));
+CKL_REGISTER_KERNEL("ckl.fused.norm_linear_rope_append",
+                    reinterpret_cast<const void *>(&normLinearRopeAppendKernel<Medium>), "PPPPPPFS",
+                    sizeof(GemmSpec), appendGemmGeometry,
+                    CKL_GEMM_SELECT(normLinearRopeAppendKernel));
+CKL_REGISTER_KERNEL("ckl.fused.norm_linear_append",
+                    reinterpret_cast<const void *>(&normLinearAppendKernel<Medium>), "PPPPPFS",
+                    sizeof(GemmSpec), appendGemmGeometry, CKL_GEMM_SELECT(normLinearAppendKernel));
+CKL_REGISTER_KERNEL("ckl.fused.linear_residual",
+                    reinterpret_cast<const void *>(&linearResidualKernel<Medium>), "PPPPS",
+                    sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(linearResidualKernel));
+CKL_REGISTER_KERNEL("ckl.fused.swiglu_linear_residual",
+                    reinterpret_cast<const void *>(&swigluLinearResidualKernel<Medium>), "PPPPPS",
+                    sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(swigluLinearResidualKernel));
+CKL_REGISTER_KERNEL("ckl.fused.norm_linear_argmax",
+                    reinterpret_cast<const void *>(&normLinearArgmaxKernel<Medium>), "PPPPPFS",
+                    sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(normLinearArgmaxKernel));
+CKL_REGISTER_KERNEL("ckl.fused.attention", reinterpret_cast<const void *>(&attentionKernel<64>),
+                    "PPPPPFS", sizeof(AttentionSpec), attentionGeometry, attentionSelect);
+CKL_REGISTER_KERNEL("ckl.fused.greedy_combine",
+                    reinterpret_cast<const void *>(&greedyCombineKernel), "PPPPPPS",
+                    sizeof(CombineSpec), combineGeometry, nullptr);
+
+} // namespace ckl::kernels

@@ -1,0 +1,325 @@
+// FP32 SIMT projection kernel with fused prologues and epilogues.
+//
+// out = epilogue(prologue(A) @ W[layer]), A row-major [M, K], W row-major [K, N] per layer.
+// The decoder's projections must agree with an FP32 reference within 1e-4 relative, so they
+// run on FFMA (no TF32).  A CTA computes a BM x BN tile with a TM x TN register tile per
+// thread; K advances in BK-wide slices staged in double-buffered shared memory, loaded with
+// 16-byte vectors when shapes and pointers allow (register prefetch of the next slice
+// overlaps the FMAs of the current one).
+//
+// Prologues: plain; RMSNorm (row scale rsqrt(mean(x^2)+eps) times the layer gain, computed
+// by the CTA for its rows before the K loop); SwiGLU (silu(gate) * up from two inputs).
+// Epilogues: store; residual add; RoPE at position[0]; RoPE + KV-cache append; KV-cache
+// append; store + per-row argmax partials for the greedy head.
+#pragma once
+
+#include "common.cuh"
+
+namespace ckl::kernels::gemm {
+
+enum Prologue : int { kPlain = 0, kRms = 1, kSwiGlu = 2 };
+enum Epilogue : int { kStore = 0, kResidual = 1, kRope = 2, kRopeAppend = 3, kAppend = 4, kArgmax = 5 };
+
+struct Params {
+  const float *a = nullptr;        // [M, K]
+  const float *a2 = nullptr;       // [M, K] up projection (SwiGLU)
+  const float *gain = nullptr;     // [layers, K] (RMSNorm)
+  const float *w = nullptr;        // [layers, K, N]
+  const float *residual = nullptr; // [M, N]
+  const float *table = nullptr;    // [T, D/2, 2]
+  const int *position = nullptr;   // [1]
+  float *out = nullptr;            // [M, N] or cache [layers, M, A, T, D]
+  float2 *partials = nullptr;      // [M, tiles] (value, index bits)
+  float eps = 0.f;
+  GemmSpec s{};
+};
+
+template <int BM_, int BN_, int BK_, int TM_, int TN_> struct Config {
+  static constexpr int BM = BM_, BN = BN_, BK = BK_, TM = TM_, TN = TN_;
+  static constexpr int kColThreads = BN / TN;
+  static constexpr int kThreads = (BM / TM) * kColThreads;
+  static constexpr int kALoads = (BM * BK / 4 + kThreads - 1) / kThreads; // float4 per thread
+  static constexpr int kBLoads = (BK * BN / 4 + kThreads - 1) / kThreads;
+  static_assert(BK % 4 == 0 && BN % 4 == 0 && TN % 2 == 0, "tile shape");
+};
+
+using Small = Config<16, 64, 16, 2, 4>;    // 128 threads, M <= 16
+using Medium = Config<64, 64, 16, 4, 4>;   // 256 threads
+using Large = Config<128, 128, 8, 8, 8>;   // 256 threads, M >= 256 and wide N
+
+// Tile configuration for a specialization: 0 small, 1 medium, 2 large.
+inline int chooseConfig(const GemmSpec &s) {
+  if (s.config > 0)
+    return int(s.config - 1);
+  if (s.M <= 16)
+    return 0;
+  if (s.M >= 256 && s.N >= 2048)
+    return 2;
+  return 1;
+}
+
+template <class Cfg> inline void tileGrid(const GemmSpec &s, library::Geometry *g) {
+  g->grid[0] = ceilDiv(s.N, Cfg::BN);
+  g->grid[1] = ceilDiv(s.M, Cfg::BM);
+  g->block[0] = Cfg::kThreads;
+}
+
+inline bool geometry(const GemmSpec &s, library::Geometry *g) {
+  if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
+    return false;
+  switch (chooseConfig(s)) {
+  case 0: tileGrid<Small>(s, g); break;
+  case 1: tileGrid<Medium>(s, g); break;
+  case 2: tileGrid<Large>(s, g); break;
+  default: return false;
+  }
+  return g->grid[1] <= 65535;
+}
+
+template <int PRO>
+__device__ __forceinline__ float prologue(const Params &p, float v, int64_t m, int64_t k,
+                                          const float *rowInv, int localRow) {
+  if constexpr (PRO == kRms) {
+    return __fmul_rn(__fmul_rn(v, rowInv[localRow]), p.gain[p.s.layer * p.s.K + k]);
+  } else if constexpr (PRO == kSwiGlu) {
+    const float up = p.a2[m * p.s.K + k];
+    return __fmul_rn(v / (1.0f + expf(-v)), up);
+  } else {
+    return v;
+  }
+}
+
+template <class Cfg, int PRO, int EPI> __device__ void body(const Params &p) {
+  constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, TM = Cfg::TM, TN = Cfg::TN;
+  constexpr int T = Cfg::kThreads;
+  __shared__ __align__(16) float As[2][BK][BM + 4];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  __shared__ float rowInv[BM];
+
+  const GemmSpec &s = p.s;
+  const int tid = threadIdx.x;
+  const int tx = tid % Cfg::kColThreads, ty = tid / Cfg::kColThreads;
+  const int64_t m0 = int64_t(blockIdx.y) * BM, n0 = int64_t(blockIdx.x) * BN;
+  const int64_t M = s.M, K = s.K, N = s.N;
+  const float *A = p.a;
+  const float *W = p.w + s.layer * K * N;
+
+  int position = 0;
+  if constexpr (EPI == kRope || EPI == kRopeAppend || EPI == kAppend) {
+    position = p.position[0];
+    if (position < 0 || position >= s.T)
+      return; // outside cache capacity: the step writes nothing
+  }
+
+  if constexpr (PRO == kRms) {
+    const int warp = tid / kWarp, lane = tid % kWarp;
+    for (int r = warp; r < BM; r += T / kWarp) {
+      const int64_t m = m0 + r;
+      float total = 0.f;
+      if (m < M)
+        for (int64_t k = lane; k < K; k += kWarp) {
+          const float v = A[m * K + k];
+          total += v * v;
+        }
+      total = warpSum(total);
+      if (lane == 0)
+        rowInv[r] = rsqrtf(total / float(K) + p.eps);
+    }
+    __syncthreads();
+  }
+
+  const bool vec = (K % 4 == 0) && (N % 4 == 0) && aligned16(A) && aligned16(W) &&
+                   (PRO != kSwiGlu || aligned16(p.a2));
+  float4 aReg[Cfg::kALoads], bReg[Cfg::kBLoads];
+
+  auto loadA = [&](int64_t k0) {
+#pragma unroll
+    for (int l = 0; l < Cfg::kALoads; ++l) {
+      const int e = tid + l * T; // float4 index within the BM x BK/4 tile
+      const int r = e / (BK / 4), c = (e % (BK / 4)) * 4;
+      const int64_t m = m0 + r, k = k0 + c;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < BM * BK / 4 && m < M) {
+        if (vec && k + 3 < K) {
+          v = *reinterpret_cast<const float4 *>(A + m * K + k);
+        } else {
+          v.x = k < K ? A[m * K + k] : 0.f;
+          v.y = k + 1 < K ? A[m * K + k + 1] : 0.f;
+          v.z = k + 2 < K ? A[m * K + k + 2] : 0.f;
+          v.w = k + 3 < K ? A[m * K + k + 3] : 0.f;
+        }
+        if constexpr (PRO != kPlain) {
+          if (k < K) v.x = prologue<PRO>(p, v.x, m, k, rowInv, r);
+          if (k + 1 < K) v.y = prologue<PRO>(p, v.y, m, k + 1, rowInv, r);
+          if (k + 2 < K) v.z = prologue<PRO>(p, v.z, m, k + 2, rowInv, r);
+          if (k + 3 < K) v.w = prologue<PRO>(p, v.w, m, k + 3, rowInv, r);
+        }
+      }
+      aReg[l] = v;
+    }
+  };
+  auto storeA = [&](int stage) {
+#pragma unroll
+    for (int l = 0; l < Cfg::kALoads; ++l) {
+      const int e = tid + l * T;
+      if (e < BM * BK / 4) {
+        const int r = e / (BK / 4), c = (e % (BK / 4)) * 4;
+        As[stage][c][r] = aReg[l].x;
+        As[stage][c + 1][r] = aReg[l].y;
+        As[stage][c + 2][r] = aReg[l].z;
+        As[stage][c + 3][r] = aReg[l].w;
+      }
+    }
+  };
+  auto loadB = [&](int64_t k0) {
+#pragma unroll
+    for (int l = 0; l < Cfg::kBLoads; ++l) {
+      const int e = tid + l * T;
+      const int r = e / (BN / 4), c = (e % (BN / 4)) * 4;
+      const int64_t k = k0 + r, n = n0 + c;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < BK * BN / 4 && k < K) {
+        const float *row = W + k * N;
+        if (vec && n + 3 < N) {
+          v = __ldg(reinterpret_cast<const float4 *>(row + n));
+        } else {
+          v.x = n < N ? row[n] : 0.f;
+          v.y = n + 1 < N ? row[n + 1] : 0.f;
+          v.z = n + 2 < N ? row[n + 2] : 0.f;
+          v.w = n + 3 < N ? row[n + 3] : 0.f;
+        }
+      }
+      bReg[l] = v;
+    }
+  };
+  auto storeB = [&](int stage) {
+#pragma unroll
+    for (int l = 0; l < Cfg::kBLoads; ++l) {
+      const int e = tid + l * T;
+      if (e < BK * BN / 4) {
+        const int r = e / (BN / 4), c = (e % (BN / 4)) * 4;
+        *reinterpret_cast<float4 *>(&Bs[stage][r][c]) = bReg[l];
+      }
+    }
+  };
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j)
+      acc[i][j] = 0.f;
+
+  loadA(0);
+  loadB(0);
+  storeA(0);
+  storeB(0);
+  __syncthreads();
+  int stage = 0;
+  for (int64_t k0 = 0; k0 < K; k0 += BK) {
+    const bool more = k0 + BK < K;
+    if (more) {
+      loadA(k0 + BK);
+      loadB(k0 + BK);
+    }
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+        a[i] = As[stage][kk][ty * TM + i];
+#pragma unroll
+      for (int j = 0; j < TN; j += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(&Bs[stage][kk][tx * TN + j]);
+        b[j] = v.x;
+        if (j + 1 < TN) b[j + 1] = v.y;
+        if (j + 2 < TN) b[j + 2] = v.z;
+        if (j + 3 < TN) b[j + 3] = v.w;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j)
+          acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (more) {
+      storeA(stage ^ 1);
+      storeB(stage ^ 1);
+    }
+    __syncthreads();
+    stage ^= 1;
+  }
+
+  // ---- epilogue ----------------------------------------------------------------------
+  const int64_t nBase = n0 + tx * TN;
+  if constexpr (EPI == kArgmax) {
+    // Store logits and reduce each row's maximum over this CTA's columns.
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const int64_t m = m0 + ty * TM + i;
+      float best = -CUDART_INF_F;
+      int bestIndex = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        const int64_t n = nBase + j;
+        if (m < M && n < N) {
+          p.out[m * N + n] = acc[i][j];
+          argmaxMerge(best, bestIndex, acc[i][j], int(n));
+        }
+      }
+#pragma unroll
+      for (int o = Cfg::kColThreads / 2; o > 0; o >>= 1)
+        argmaxMerge(best, bestIndex, __shfl_xor_sync(0xffffffffu, best, o),
+                    __shfl_xor_sync(0xffffffffu, bestIndex, o));
+      if (tx == 0 && m < M)
+        p.partials[m * s.tiles + blockIdx.x] = make_float2(best, __int_as_float(bestIndex));
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int64_t m = m0 + ty * TM + i;
+    if (m >= M)
+      continue;
+    if constexpr (EPI == kStore || EPI == kResidual) {
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        const int64_t n = nBase + j;
+        if (n < N) {
+          float v = acc[i][j];
+          if constexpr (EPI == kResidual)
+            v = __fadd_rn(p.residual[m * N + n], v);
+          p.out[m * N + n] = v;
+        }
+      }
+    } else {
+      const int64_t D = s.D, R = s.D / 2;
+#pragma unroll
+      for (int j = 0; j < TN; j += 2) {
+        const int64_t n = nBase + j;
+        if (n >= N)
+          continue;
+        float first = acc[i][j], second = acc[i][j + 1];
+        const int64_t h = n / D, d = n % D;
+        if constexpr (EPI == kRope || EPI == kRopeAppend) {
+          const float *cs = p.table + (int64_t(position) * R + d / 2) * 2;
+          const float cosine = cs[0], sine = cs[1];
+          const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
+          const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
+          first = x;
+          second = y;
+        }
+        if constexpr (EPI == kRope) {
+          p.out[m * N + n] = first;
+          p.out[m * N + n + 1] = second;
+        } else {
+          float *slot = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
+          slot[0] = first;
+          slot[1] = second;
+        }
+      }
+    }
+  }
+}
+
+} // namespace ckl::kernels::gemm

@@ -1,0 +1,17 @@
+"""CKL on B200: the reference's kernel/program authoring API over an sm_100a runtime."""
+from .compiler import (CompilationError, CompiledModule, CompilerOptions, GPUObject,
+                       NVIDIATarget, extract_gpu_objects)
+from .frontend import FrontendError, LoweredProgram, kernel, program
+from .cuda import CompiledProgram, Device, DeviceBuffer, Invocation
+from .frontend.source import INTRINSICS as _intrinsics
+from .types import Buffer, BufferSpec, constexpr, dim, f32, f64, i32, i64, index
+from .types import bool_ as bool
+
+globals().update(_intrinsics)
+
+__all__ = [
+    "CompilationError", "CompiledModule", "CompilerOptions", "GPUObject", "NVIDIATarget",
+    "CompiledProgram", "Device", "DeviceBuffer", "Invocation", "extract_gpu_objects",
+    "Buffer", "BufferSpec", "constexpr", "dim", "f32", "f64", "i32", "i64", "index", "bool",
+    "FrontendError", "LoweredProgram", "kernel", "program", *_intrinsics,
+]

@@ -1,0 +1,675 @@
+"""Lower a traced CKL program onto the sm_100a kernel library.
+
+Stages (the reference's ``ckl-fuse-pointwise``, ``ckl-prepare-cuda``, ``ckl-build-graph`` and
+``ckl-lower-graph-to-exec`` passes, ``python/ckl/_jit.py:74-154``, restated without MLIR):
+
+1. every dispatch is resolved to a library kernel (:mod:`ckl.library`);
+2. optional fusions rewrite the dispatch list:
+   * pointwise fusion chains adjacent scalar pointwise launches through a single-use
+     temporary (``lib/Transforms/PointwiseFusion.cpp``);
+   * decoder fusion maps the decode step onto the fused decoder kernels (six graph nodes per
+     layer instead of 21);
+   a fused plan assumes distinct caller buffers and keeps the unfused plan as the fallback
+   that binding selects when buffers overlap (``lib/Runtime/NvidiaProgram.cpp:194-205``);
+3. the native planner infers dependency edges from per-operand effects, reduces them onto
+   dispatches and plans temporary storage (``include/ckl_b200.h``, planning section);
+4. the result is emitted as the native executable plan and as ``ckl_exec`` text.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+from dataclasses import dataclass, field
+
+from . import _native
+from .compiler import CompilationError
+from .frontend import analysis
+from .frontend.tracer import LoweredProgram, Resource
+from .library import Selection, pack, select
+from .types import BufferSpec, f32, f64, i32, i64
+
+READ, WRITE, ALLOCATE, FREE = analysis.READ, analysis.WRITE, analysis.ALLOCATE, analysis.FREE
+ALIGNMENT = 256  # temporary allocation alignment (lib/Analysis/GraphAnalysis.cpp:147)
+LIBRARY_BINARY = "ckl-b200:library"
+POSITION = (0, 4)  # position[0] of an i32 buffer
+
+
+@dataclass
+class Slot:
+    kind: str                 # "resource" | "scalar" | "value"
+    resource: int = -1        # program resource id
+    argument: int = -1        # runtime parameter position
+    data: bytes = b""
+
+
+@dataclass
+class Node:
+    """A dispatch on a library kernel, with its argument slots and memory effects."""
+
+    name: str
+    slots: list
+    spec: bytes
+    accesses: list            # [(resource id, bits, region)], region "whole" or (offset, length)
+    label: str
+    grid: tuple = (1, 1, 1)
+    block: tuple = (1, 1, 1)
+    shared: int = 0
+    # Pointwise chain description (ops, scalar slots, n, count) when the node is one.
+    chain: tuple = None
+    source: object = None     # the traced dispatch (1:1 nodes)
+    selection: Selection = None
+
+
+@dataclass
+class Event:
+    kind: str                 # "alloc" | "dispatch" | "free"
+    resource: int = -1
+    node: Node = None
+
+
+@dataclass
+class Plan:
+    """One executable plan: native text, ``ckl_exec`` text and statistics."""
+
+    text: str
+    executable_ir: str
+    node_names: list
+    nodes: int
+    edges: int
+    temporaries: int
+    heap_bytes: int
+    baseline_bytes: int
+    topology: dict
+    fused: bool = False
+
+
+@dataclass
+class CompiledPlans:
+    primary: Plan
+    fallback: Plan = None
+    prepared_ir: str = ""
+    device_ir: str = ""
+    host_ir: str = ""
+
+
+# ---------------------------------------------------------------------------------------
+def _scalar_slot(operand) -> Slot:
+    if operand.kind == "scalar":
+        return Slot("scalar", argument=operand.argument)
+    code = {f32: "<f", f64: "<d", i32: "<i", i64: "<q"}[operand.dtype]
+    return Slot("value", data=struct.pack(code, operand.value))
+
+
+def _one_to_one(dispatch) -> Node:
+    selection = select(dispatch)
+    spec = dispatch.specialization
+    summary = analysis.summarize(spec.definition, spec.signature)
+    slots, accesses = [], []
+    for position, operand in enumerate(dispatch.operands):
+        if operand.kind == "resource":
+            slots.append(Slot("resource", resource=operand.resource))
+            bits, region = summary.bits[position], summary.regions[position]
+            if bits:
+                accesses.append((operand.resource, bits, region))
+        else:
+            slots.append(_scalar_slot(operand))
+    node = Node(selection.entry.native, slots, selection.spec, accesses,
+                f"{spec.definition.name} @ {dispatch.location}", source=dispatch,
+                selection=selection)
+    node.grid, node.block = dispatch.grid, dispatch.block
+    if selection.entry.pointwise_op >= 0 and dispatch.shared_memory == 0:
+        n, count = struct.unpack("<2q", selection.spec)
+        node.chain = ((selection.entry.pointwise_op,), (slots[2],), n, count)
+    return node
+
+
+def _resource_users(events) -> dict:
+    users: dict[int, list] = {}
+    for index, event in enumerate(events):
+        if event.kind == "dispatch":
+            for slot in event.node.slots:
+                if slot.kind == "resource":
+                    seen = users.setdefault(slot.resource, [])
+                    if not seen or seen[-1] != index:
+                        seen.append(index)
+    return users
+
+
+# ---- pointwise fusion ------------------------------------------------------------------
+def _fuse_pointwise(events, resources) -> bool:
+    """Fuse adjacent scalar pointwise chains through a single-use temporary (in place)."""
+    changed = False
+    while True:
+        fused = False
+        previous = None
+        for index, event in enumerate(events):
+            if event.kind == "alloc":
+                continue
+            if event.kind != "dispatch":
+                previous = None
+                continue
+            node = event.node
+            if previous is not None and _try_fuse_pair(events, resources, previous, index):
+                fused = changed = True
+                break
+            previous = index
+        if not fused:
+            return changed
+
+
+def _try_fuse_pair(events, resources, first_index, second_index) -> bool:
+    first, second = events[first_index].node, events[second_index].node
+    if first.chain is None or second.chain is None:
+        return False
+    ops1, scalars1, n1, count1 = first.chain
+    ops2, scalars2, n2, count2 = second.chain
+    if len(ops1) + len(ops2) > 4 or (n1, count1) != (n2, count2):
+        return False
+    if first.grid != second.grid or first.block != second.block or first.grid[1:] != (1, 1) \
+            or first.block[1:] != (1, 1):
+        return False
+    src, temp = first.slots[0].resource, first.slots[1].resource
+    consumed, dst = second.slots[0].resource, second.slots[1].resource
+    if consumed != temp or resources[temp].kind != "temporary" or src == dst:
+        return False
+    users = _resource_users(events)
+    if users.get(temp) != [first_index, second_index]:
+        return False
+    ops, scalars = ops1 + ops2, scalars1 + scalars2
+    steps = len(ops)
+    spec = pack(n1, count1, steps, *(list(ops) + [0] * (4 - steps)))
+    regions = {}
+    for rid, bits, region in first.accesses + second.accesses:
+        if rid != temp:
+            regions[rid] = (regions.get(rid, (0, None))[0] | bits,
+                            analysis._merge(regions.get(rid, (0, None))[1], region))
+    node = Node(f"ckl.pointwise.chain{steps}",
+                [Slot("resource", resource=src), Slot("resource", resource=dst), *scalars],
+                spec, [(rid, b, r) for rid, (b, r) in regions.items()],
+                f"fused({first.label}; {second.label})",
+                grid=first.grid, block=first.block, chain=(ops, scalars, n1, count1))
+    events[second_index] = Event("dispatch", node=node)
+    del events[first_index]
+    events[:] = [e for e in events if not (e.kind in ("alloc", "free") and e.resource == temp)]
+    return True
+
+
+# ---- decoder fusion --------------------------------------------------------------------
+_LAYER = ("rms_stats", "rms_apply", "linear", "linear", "linear", "rope", "rope", "append_kv",
+          "attention_scores", "softmax", "attention_values", "linear", "add", "rms_stats",
+          "rms_apply", "linear", "linear", "silu", "multiply", "linear", "add")
+_HEAD = ("rms_stats", "rms_apply", "linear", "greedy", "advance")
+_ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
+
+
+class _NoMatch(Exception):
+    pass
+
+
+def _short(node: Node) -> str:
+    return node.name.rsplit(".", 1)[-1] if node.name.startswith("ckl.decoder.") else node.name
+
+
+def _fuse_decoder(events, resources: list) -> bool:
+    dispatches = [e.node for e in events if e.kind == "dispatch"]
+    names = [_short(n) for n in dispatches]
+    if len(names) < 1 + len(_LAYER) + len(_HEAD) or (len(names) - 1 - len(_HEAD)) % len(_LAYER):
+        return False
+    layers = (len(names) - 1 - len(_HEAD)) // len(_LAYER)
+    expected = ("embedding",) + _LAYER * layers + _HEAD
+    if tuple(names) != expected:
+        return False
+    try:
+        new_nodes, eliminated, added = _decoder_nodes(dispatches, layers, resources)
+    except _NoMatch:
+        return False
+    users = _resource_users(events)
+    dispatch_index = {id(e.node): i for i, e in enumerate(events) if e.kind == "dispatch"}
+    for rid, allowed in eliminated.items():
+        if resources[rid].kind != "temporary":
+            return False
+        if sorted(users.get(rid, [])) != sorted(dispatch_index[id(n)] for n in allowed):
+            return False
+    # Rebuild events: kept temporaries are allocated before first use; frees at the end.
+    kept_allocs = [e.resource for e in events if e.kind == "alloc" and e.resource not in eliminated]
+    new_events, allocated = [], set()
+    for node in new_nodes:
+        for slot in node.slots:
+            rid = slot.resource
+            if slot.kind == "resource" and rid not in allocated and \
+                    resources[rid].kind == "temporary" and (rid in kept_allocs or rid in added):
+                new_events.append(Event("alloc", resource=rid))
+                allocated.add(rid)
+        new_events.append(Event("dispatch", node=node))
+    order = [rid for rid in kept_allocs + added if rid in allocated]
+    for rid in reversed(order):
+        new_events.append(Event("free", resource=rid))
+    events[:] = new_events
+    return True
+
+
+def _decoder_nodes(dispatches, layers, resources):
+    def op(node, i):
+        return node.source.operands[i]
+
+    def res(node, i):
+        operand = op(node, i)
+        if operand.kind != "resource" or resources[operand.resource].kind == "view":
+            raise _NoMatch
+        return operand.resource
+
+    def const(node, i=0):
+        return [p.value for p in node.source.specialization.signature.parameters if p.is_constant][i]
+
+    def shape(rid):
+        return resources[rid].spec.shape
+
+    def same(*values):
+        if any(v != values[0] for v in values):
+            raise _NoMatch
+
+    def gemm_spec(M, K, N, layers_, layer, A=0, D=0, T=0, tiles=0):
+        return pack(M, K, N, layers_, layer, A, D, T, tiles, 0)
+
+    embedding = dispatches[0]
+    x = res(embedding, 2)
+    new_nodes = [embedding]
+    eliminated: dict[int, list] = {}
+    position = sincos = kc = vc = None
+    for layer_index in range(layers):
+        d = dispatches[1 + layer_index * len(_LAYER):1 + (layer_index + 1) * len(_LAYER)]
+        same(res(d[0], 0), res(d[1], 0), x)
+        inv, normed = res(d[0], 1), res(d[1], 3)
+        same(res(d[1], 1), inv)
+        same(res(d[2], 0), res(d[3], 0), res(d[4], 0), normed)
+        q, k, v = res(d[2], 2), res(d[3], 2), res(d[4], 2)
+        wq, wk, wv = res(d[2], 1), res(d[3], 1), res(d[4], 1)
+        g1 = res(d[1], 2)
+        same(res(d[5], 0), q)
+        same(res(d[6], 0), k)
+        same(res(d[5], 1), res(d[6], 1))
+        same(res(d[5], 2), res(d[6], 2), res(d[7], 4), res(d[8], 2), res(d[9], 1), res(d[10], 2))
+        if position is None:
+            position, sincos = res(d[5], 2), res(d[5], 1)
+        same(res(d[5], 2), position)
+        same(res(d[5], 1), sincos)
+        qr, kr = res(d[5], 3), res(d[6], 3)
+        same(res(d[7], 0), kr)
+        same(res(d[7], 1), v)
+        if kc is None:
+            kc, vc = res(d[7], 2), res(d[7], 3)
+        same(res(d[7], 2), res(d[8], 1), kc)
+        same(res(d[7], 3), res(d[10], 1), vc)
+        same(res(d[8], 0), qr)
+        scores = res(d[8], 3)
+        same(res(d[9], 0), scores)
+        probs = res(d[9], 2)
+        same(res(d[10], 0), probs)
+        context = res(d[10], 3)
+        same(res(d[11], 0), context)
+        wo, projected = res(d[11], 1), res(d[11], 2)
+        same(res(d[12], 0), x)
+        same(res(d[12], 1), projected)
+        residual = res(d[12], 2)
+        same(res(d[13], 0), res(d[14], 0), residual)
+        inv2, normed2 = res(d[13], 1), res(d[14], 3)
+        same(res(d[14], 1), inv2)
+        g2 = res(d[14], 2)
+        same(res(d[15], 0), res(d[16], 0), normed2)
+        wg, gate, wu, up = res(d[15], 1), res(d[15], 2), res(d[16], 1), res(d[16], 2)
+        same(res(d[17], 0), gate)
+        activated = res(d[17], 1)
+        same(res(d[18], 0), activated)
+        same(res(d[18], 1), up)
+        product = res(d[18], 2)
+        same(res(d[19], 0), product)
+        wd, down = res(d[19], 1), res(d[19], 2)
+        same(res(d[20], 0), residual)
+        same(res(d[20], 1), down)
+        next_x = res(d[20], 2)
+        layer = const(d[1])
+        same(layer, const(d[2]), const(d[3]), const(d[4]), const(d[7]), const(d[8]), const(d[10]),
+             const(d[11]), const(d[14]), const(d[15]), const(d[16]), const(d[19]))
+        B, Cdim = shape(x)
+        L_, Bc, A, T, D = shape(kc)
+        F = shape(wg)[2]
+        Lw = shape(wq)[0]
+        same(Bc, B)
+        if D not in _ATTENTION_HEAD_DIMS or A * D != Cdim:
+            raise _NoMatch
+        eps1, eps2 = _scalar_slot(op(d[0], 2)), _scalar_slot(op(d[13], 2))
+        scale = _scalar_slot(op(d[8], 4))
+
+        def node(name, slots, spec, reads, writes, label):
+            accesses = [(r, READ, "whole") for r in reads]
+            accesses += [(r, bits, region) for r, bits, region in writes]
+            return Node(name, slots, spec, accesses, f"{label} (layer {layer})")
+
+        R = lambda r: Slot("resource", resource=r)
+        pos_read = (position, READ, POSITION)
+        new_nodes.append(node("ckl.fused.norm_linear_rope",
+                              [R(x), R(g1), R(wq), R(sincos), R(position), R(qr), eps1],
+                              gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                              [x, g1, wq, sincos], [pos_read, (qr, WRITE, "whole")], "q projection"))
+        new_nodes.append(node("ckl.fused.norm_linear_rope_append",
+                              [R(x), R(g1), R(wk), R(sincos), R(position), R(kc), eps1],
+                              gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                              [x, g1, wk, sincos], [pos_read, (kc, WRITE, "whole")], "k projection"))
+        new_nodes.append(node("ckl.fused.norm_linear_append",
+                              [R(x), R(g1), R(wv), R(position), R(vc), eps1],
+                              gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                              [x, g1, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
+        new_nodes.append(node("ckl.fused.attention",
+                              [R(qr), R(kc), R(vc), R(position), R(context), scale],
+                              pack(B, A, T, D, L_, layer, 1, 0),
+                              [qr, kc, vc], [pos_read, (context, WRITE, "whole")], "attention"))
+        new_nodes.append(node("ckl.fused.linear_residual",
+                              [R(context), R(wo), R(x), R(residual)],
+                              gemm_spec(B, Cdim, Cdim, Lw, layer),
+                              [context, wo, x], [(residual, WRITE, "whole")], "o projection"))
+        new_nodes.append(node("ckl.fused.norm_linear", [R(residual), R(g2), R(wg), R(gate), eps2],
+                              gemm_spec(B, Cdim, F, shape(wg)[0], layer),
+                              [residual, g2, wg], [(gate, WRITE, "whole")], "gate projection"))
+        new_nodes.append(node("ckl.fused.norm_linear", [R(residual), R(g2), R(wu), R(up), eps2],
+                              gemm_spec(B, Cdim, F, shape(wu)[0], layer),
+                              [residual, g2, wu], [(up, WRITE, "whole")], "up projection"))
+        new_nodes.append(node("ckl.fused.swiglu_linear_residual",
+                              [R(gate), R(up), R(wd), R(residual), R(next_x)],
+                              gemm_spec(B, F, Cdim, shape(wd)[0], layer),
+                              [gate, up, wd, residual], [(next_x, WRITE, "whole")],
+                              "down projection"))
+        for rid, users in ((inv, (d[0], d[1])), (normed, (d[1], d[2], d[3], d[4])),
+                           (q, (d[2], d[5])), (k, (d[3], d[6])), (v, (d[4], d[7])),
+                           (kr, (d[6], d[7])), (scores, (d[8], d[9])), (probs, (d[9], d[10])),
+                           (projected, (d[11], d[12])), (inv2, (d[13], d[14])),
+                           (normed2, (d[14], d[15], d[16])), (activated, (d[17], d[18])),
+                           (product, (d[18], d[19])), (down, (d[19], d[20]))):
+            eliminated[rid] = list(users)
+        x = next_x
+    h = dispatches[1 + layers * len(_LAYER):]
+    same(res(h[0], 0), res(h[1], 0), x)
+    finv, final_x = res(h[0], 1), res(h[1], 3)
+    same(res(h[1], 1), finv)
+    same(res(h[2], 0), final_x)
+    fgain, lm, logits = res(h[1], 2), res(h[2], 1), res(h[2], 2)
+    same(res(h[3], 0), logits)
+    tokens, history = res(h[3], 1), res(h[3], 2)
+    if position is None:
+        raise _NoMatch
+    same(res(h[3], 3), res(h[4], 0), position)
+    same(const(h[1]), const(h[2]))
+    B, Cdim = shape(x)
+    V = shape(lm)[2]
+    T = shape(history)[0]
+    head_spec = gemm_spec(B, Cdim, V, shape(lm)[0], const(h[2]))
+    geometry = library_geometry("ckl.fused.norm_linear_argmax", head_spec)
+    tiles = geometry[0][0]
+    head_spec = gemm_spec(B, Cdim, V, shape(lm)[0], const(h[2]), tiles=tiles)
+    partials = _add_resource(resources, "temporary", BufferSpec((B, tiles, 2), f32), "partials")
+    counter = _add_resource(resources, "persistent", BufferSpec((1,), i32), "counter")
+    R = lambda r: Slot("resource", resource=r)
+    eps = _scalar_slot(op(h[0], 2))
+    new_nodes.append(Node("ckl.fused.norm_linear_argmax",
+                          [R(x), R(fgain), R(lm), R(logits), R(partials), eps], head_spec,
+                          [(x, READ, "whole"), (fgain, READ, "whole"), (lm, READ, "whole"),
+                           (logits, WRITE, "whole"), (partials, WRITE, "whole")],
+                          "lm head"))
+    new_nodes.append(Node("ckl.fused.greedy_combine",
+                          [R(partials), R(logits), R(tokens), R(history), R(position), R(counter)],
+                          pack(B, tiles, T, V),
+                          [(partials, READ, "whole"), (logits, READ, "whole"),
+                           (tokens, WRITE, "whole"), (history, WRITE, "whole"),
+                           (position, READ | WRITE, POSITION), (counter, READ | WRITE, "whole")],
+                          "greedy + advance"))
+    eliminated[finv] = [h[0], h[1]]
+    eliminated[final_x] = [h[1], h[2]]
+    return new_nodes, eliminated, [partials]
+
+
+def _add_resource(resources, kind, spec, name) -> int:
+    rid = len(resources)
+    resources.append(Resource(rid, kind, spec, name=f"{name}{rid}"))
+    return rid
+
+
+# ---- native planning -------------------------------------------------------------------
+def library_geometry(name: str, spec: bytes):
+    lib = _native.load()
+    grid, block, shared = (C.c_uint32 * 3)(), (C.c_uint32 * 3)(), C.c_uint32()
+    buffer = C.create_string_buffer(spec, len(spec)) if spec else None
+    status = lib.ckl_library_geometry(name.encode(), buffer, len(spec), grid, block, C.byref(shared))
+    if status:
+        raise CompilationError(("ckl-b200", "geometry"), f"{name}: {_native.message()}")
+    return tuple(grid), tuple(block), shared.value
+
+
+def _root(resources, rid):
+    r = resources[rid]
+    return (r.base, r.byte_offset, r.spec.nbytes) if r.kind == "view" else (rid, 0, r.spec.nbytes)
+
+
+def _region(resources, rid, region):
+    root, offset, size = _root(resources, rid)
+    if region == "whole":
+        if resources[rid].kind == "view":
+            return root, offset, size
+        return root, -1, 0
+    return root, offset + region[0], region[1]
+
+
+def _plan(lowered: LoweredProgram, events, resources, *, reuse_storage: bool,
+          externals_disjoint: bool, fused: bool) -> Plan:
+    lib = _native.load()
+    nodes, accesses = [], []
+    labels = []
+    for event in events:
+        first = len(accesses)
+        if event.kind == "dispatch":
+            for rid, bits, region in event.node.accesses:
+                root, offset, length = _region(resources, rid, region)
+                accesses.append(_native.GraphAccess(root, bits, offset, length))
+            kind = 0
+        else:
+            root = _root(resources, event.resource)[0]
+            accesses.append(_native.GraphAccess(root, ALLOCATE if event.kind == "alloc" else FREE,
+                                                -1, 0))
+            kind = 1 if event.kind == "alloc" else 2
+        nodes.append(_native.GraphNode(kind, 0, first, len(accesses) - first))
+        labels.append(event)
+    graph_resources = []
+    for r in resources:
+        temporary = {"temporary": 1, "persistent": 2}.get(r.kind, 0)
+        graph_resources.append(_native.GraphResource(temporary, 0, max(r.spec.nbytes, 1), ALIGNMENT))
+    flags = (1 if reuse_storage else 0) | (2 if externals_disjoint else 0)
+    handle = C.c_void_p()
+    status = lib.ckl_graph_plan_create(
+        len(nodes), (_native.GraphNode * len(nodes))(*nodes), len(accesses),
+        (_native.GraphAccess * max(len(accesses), 1))(*accesses), len(graph_resources),
+        (_native.GraphResource * max(len(graph_resources), 1))(*graph_resources), flags,
+        C.byref(handle))
+    if status:
+        raise CompilationError(("ckl-b200", "plan"), _native.message())
+    try:
+        return _emit(lowered, lib, handle, events, resources, fused)
+    finally:
+        lib.ckl_graph_plan_release(handle)
+
+
+def _emit(lowered, lib, handle, events, resources, fused) -> Plan:
+    count = lib.ckl_graph_plan_resource_count(handle)
+    order = (C.c_uint32 * max(count, 1))()
+    lib.ckl_graph_plan_resources(handle, order)
+    order = list(order)[:count]
+    baseline, planned, heap_count = C.c_uint64(), C.c_uint64(), C.c_uint32()
+    lib.ckl_graph_plan_memory(handle, C.byref(baseline), C.byref(planned), C.byref(heap_count))
+    heaps = (C.c_uint64 * max(heap_count.value, 1))()
+    alignments = (C.c_uint64 * max(heap_count.value, 1))()
+    lib.ckl_graph_plan_heaps(handle, heaps, alignments)
+    plan_index = {rid: i for i, rid in enumerate(order)}
+    runtime = [p for p in lowered.signature.parameters if not p.is_constant]
+
+    text = ["ckl-b200-plan 1"]
+    ir = ['"ckl_exec.plan"() ({']
+    for position, parameter in enumerate(runtime):
+        if isinstance(parameter.dtype, BufferSpec):
+            text.append(f"arg {position} buffer {parameter.dtype.nbytes}")
+        else:
+            text.append(f"arg {position} scalar {parameter.dtype.name}")
+    text.append("binary library")
+    for h in range(heap_count.value):
+        text.append(f"heap {h} {heaps[h]}")
+        ir.append(f'  "ckl_exec.heap"() {{id = {h} : i64, bytes = {heaps[h]} : i64, alignment = '
+                  f'{alignments[h]} : i64, device = 0 : i64, address_space = "global"}} : () -> ()')
+    temporaries = 0
+    for i, rid in enumerate(order):
+        r = resources[rid]
+        if r.kind == "argument":
+            text.append(f"resource {i} external {r.argument}")
+            ir.append(f'  "ckl_exec.resource"() {{name = "arg{r.argument}", kind = "external", '
+                      f'device = "cuda:0", address_space = "global", alignment = {ALIGNMENT} : i64}}'
+                      ' : () -> ()')
+            continue
+        heap, offset, slot = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        if lib.ckl_graph_plan_assignment(handle, rid, C.byref(heap), C.byref(offset), C.byref(slot)):
+            raise CompilationError(("ckl-b200", "plan"), _native.message())
+        text.append(f"resource {i} temporary {heap.value} {offset.value}")
+        kind = "temporary" if r.kind == "temporary" else "persistent"
+        temporaries += r.kind == "temporary"
+        ir.append(f'  "ckl_exec.resource"() {{name = "{r.name}", kind = "{kind}", device = '
+                  f'"cuda:0", address_space = "global", alignment = {ALIGNMENT} : i64, bytes = '
+                  f'{r.spec.nbytes} : i64, heap = {heap.value} : i64, offset = {offset.value} : i64}}'
+                  ' : () -> ()')
+    topology, names, edges = {}, [], 0
+    for node_id, event in enumerate(events):
+        if event.kind != "dispatch":
+            continue
+        node = event.node
+        grid, block, shared = library_geometry(node.name, node.spec)
+        deps_count = lib.ckl_graph_plan_dependency_count(handle, node_id)
+        deps = (C.c_uint32 * max(deps_count, 1))()
+        lib.ckl_graph_plan_dependencies(handle, node_id, deps)
+        deps = list(deps)[:deps_count]
+        topology[node_id] = deps
+        edges += len(deps)
+        names.append(node.name)
+        text.append(f"kernel {node_id} {node.name} {grid[0]} {grid[1]} {grid[2]} {block[0]} "
+                    f"{block[1]} {block[2]} {shared}")
+        for slot in node.slots:
+            if slot.kind == "resource":
+                root, offset, _ = _root(resources, slot.resource)
+                text.append(f"argres {plan_index[root]} {offset}")
+            elif slot.kind == "scalar":
+                text.append(f"argscalar {slot.argument}")
+            else:
+                text.append(f"argvalue {slot.data.hex()}")
+        if node.spec:
+            text.append(f"argvalue {node.spec.hex()}")
+        for d in deps:
+            text.append(f"dep {d}")
+        dep_text = "array<i64>" if not deps else "array<i64: " + ", ".join(map(str, deps)) + ">"
+        ir.append(f'  "ckl_exec.kernel"() {{id = {node_id} : i64, kernel = @{node.name}, grid = '
+                  f'array<i64: {grid[0]}, {grid[1]}, {grid[2]}>, block = array<i64: {block[0]}, '
+                  f'{block[1]}, {block[2]}>, shared_memory = {shared} : i64, abi = "cuda.direct", '
+                  f'dependencies = {dep_text}}} : () -> ()  // {node.label}')
+    text.append("end")
+    ir.append(f'}}) {{backend = "cuda", name = "{lowered.trace.name}.exec"}} : () -> ()')
+    return Plan("\n".join(text) + "\n", "\n".join(ir) + "\n", names, len(names), edges,
+                temporaries, int(planned.value), int(baseline.value), topology, fused)
+
+
+def _initial_events(lowered: LoweredProgram):
+    trace = lowered.trace
+    resources = [Resource(r.id, r.kind, r.spec, r.argument, r.base, r.byte_offset, r.name)
+                 for r in trace.resources]
+    events = []
+    for e in trace.events:
+        if e.kind == "dispatch":
+            events.append(Event("dispatch", node=_one_to_one(e.dispatch)))
+        else:
+            events.append(Event(e.kind, resource=e.resource))
+    return events, resources
+
+
+def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library: bool,
+                 reuse_storage: bool) -> CompiledPlans:
+    events, resources = _initial_events(lowered)
+    if not any(e.kind == "dispatch" for e in events):
+        raise CompilationError(("ckl-b200", "plan"), "program launches no kernels")
+    baseline = _plan(lowered, [Event(e.kind, e.resource, e.node) for e in events],
+                     list(resources), reuse_storage=reuse_storage, externals_disjoint=False,
+                     fused=False)
+    fused = False
+    if fuse_pointwise:
+        fused |= _fuse_pointwise(events, resources)
+    if fuse_library:
+        fused |= _fuse_decoder(events, resources)
+    plans = CompiledPlans(baseline)
+    if fused:
+        primary = _plan(lowered, events, resources, reuse_storage=reuse_storage,
+                        externals_disjoint=True, fused=True)
+        plans = CompiledPlans(primary, baseline)
+    plans.prepared_ir = lowered.mlir
+    plans.device_ir = _device_text(plans)
+    plans.host_ir = _host_text(plans.primary)
+    return plans
+
+
+def _device_text(plans: CompiledPlans) -> str:
+    lib = _native.load()
+    used = sorted(set(plans.primary.node_names) |
+                  set(plans.fallback.node_names if plans.fallback else []))
+    lines = ["// sm_100a kernel library entries used by this program (signature codes: "
+             "P pointer, F f32, S specialization)"]
+    for name in used:
+        signature = C.create_string_buffer(64)
+        lib.ckl_library_signature(name.encode(), signature, 64)
+        lines.append(f"ckl.library.kernel @{name} signature \"{signature.value.decode()}\" "
+                     "target \"sm_100a\"")
+    return "\n".join(lines) + "\n"
+
+
+def _host_text(plan: Plan) -> str:
+    """The callback sequence the native entry replays, in LLVM-like text."""
+    lines = [f'@ckl.binary = internal constant [{len(LIBRARY_BINARY) + 1} x i8] '
+             f'c"{LIBRARY_BINARY}\\00"',
+             "define void @ckl_entry(ptr %frame, ptr %arguments) {",
+             f"  call void @ckl_begin(ptr %frame, ptr @ckl.binary, i64 {len(LIBRARY_BINARY)})"]
+    current = None
+    for line in plan.text.splitlines():
+        parts = line.split()
+        if not parts:
+            continue
+        if parts[0] in ("kernel", "end") and current is not None:
+            lines.append(f"  call void @ckl_commit(ptr %frame, i64 {current})")
+            current = None
+        if parts[0] == "kernel":
+            current = parts[1]
+        if parts[0] == "heap":
+            lines.append(f"  call void @ckl_heap(ptr %frame, i64 {parts[1]}, i64 {parts[2]})")
+        elif parts[0] == "resource":
+            if parts[2] == "external":
+                lines.append(f"  call void @ckl_resource(ptr %frame, i64 {parts[1]}, i64 0, i64 0, "
+                             f"ptr %arg{parts[3]})")
+            else:
+                lines.append(f"  call void @ckl_resource(ptr %frame, i64 {parts[1]}, i64 {parts[3]}, "
+                             f"i64 {parts[4]}, ptr null)")
+        elif parts[0] == "kernel":
+            lines.append(f'  call void @ckl_kernel(ptr %frame, ptr @"{parts[2]}", '
+                         + ", ".join(f"i64 {p}" for p in parts[3:]) + ")")
+        elif parts[0] == "argres":
+            lines.append(f"  call void @ckl_argument_resource(ptr %frame, i64 {parts[1]}, i64 {parts[2]})")
+        elif parts[0] == "argscalar":
+            lines.append(f"  call void @ckl_argument_value(ptr %frame, ptr %arg{parts[1]}, i64 ?)")
+        elif parts[0] == "argvalue":
+            lines.append(f"  call void @ckl_argument_value(ptr %frame, ptr x\"{parts[1]}\", "
+                         f"i64 {len(parts[1]) // 2})")
+        elif parts[0] == "dep":
+            lines.append(f"  call void @ckl_dependency(ptr %frame, i64 {parts[1]})")
+    lines += ["  ret void", "}"]
+    return "\n".join(lines) + "\n"
+
+
+def reference_plan_text(lowered: LoweredProgram) -> str:
+    """Executable plan of the unfused program with the reference's may-alias rules."""
+    return plan_program(lowered, fuse_pointwise=False, fuse_library=False,
+                        reuse_storage=True).primary.executable_ir

@@ -1,0 +1,395 @@
+"""Devices, buffers, compiled programs and bound invocations on the B200 runtime.
+
+Same public surface and argument validation as the reference (``python/ckl/cuda.py:65-300``):
+``Device``, ``DeviceBuffer``, ``CompiledProgram.bind/run`` and ``Invocation.run/benchmark/
+node_count``, context-manager scopes with idempotent ``close()``, ``TypeError``/``ValueError``
+for bad arguments before native code runs, ``RuntimeError`` for runtime failures.  Additions
+for the B200 build: ``Device(ordinal)`` for multi-GPU jobs, asynchronous submission and
+host copies on the invocation's stream, and node inspection.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import struct
+import weakref
+from contextlib import AbstractContextManager
+from pathlib import Path
+
+from . import _native
+from .compiler import NVIDIATarget, SUPPORTED_CHIPS
+from .types import BufferSpec, f32, f64, i32, i64
+
+_SCALARS = {f32: ("f", 4), f64: ("d", 8), i32: ("i", 4), i64: ("q", 8)}
+_ARG_KIND = {f32: _native.ARG_F32, f64: _native.ARG_F64, i32: _native.ARG_I32, i64: _native.ARG_I64}
+_MODES = {"ordinary": 0, "graph": 1, "capture": 2}
+
+
+def _byte_count(spec) -> int:
+    if not isinstance(spec, BufferSpec) or spec.dtype not in _SCALARS:
+        raise TypeError("device storage requires a numeric BufferSpec")
+    size = math.prod(spec.shape) * _SCALARS[spec.dtype][1]
+    if not 0 < size < (1 << 64):
+        raise ValueError("device storage byte count must fit a positive 64-bit size")
+    return size
+
+
+class _Handle:
+    """Owns one native handle; released when the last Python reference goes away."""
+
+    __slots__ = ("value", "__weakref__")
+
+    def __init__(self, value: int, release):
+        self.value = value
+        weakref.finalize(self, release, value)
+
+
+def _host_pointer(obj, writable: bool):
+    """(pointer, nbytes, keepalive) of a contiguous Python buffer."""
+    view = memoryview(obj)
+    if not view.contiguous:
+        raise ValueError("host buffers must be contiguous")
+    view = view.cast("B")
+    if writable and view.readonly:
+        raise ValueError("destination must be writable and match device storage byte count")
+    if view.nbytes == 0:
+        return 0, 0, view
+    import numpy as np  # pointer extraction only
+
+    array = np.frombuffer(view, dtype=np.uint8)
+    return array.ctypes.data, view.nbytes, (view, array)
+
+
+class _ContextManager(AbstractContextManager):
+    _resource = None
+
+    @property
+    def _native_resource(self):
+        if self._resource is None:
+            raise RuntimeError(f"{type(self).__name__} is closed")
+        return self._resource
+
+    @property
+    def closed(self):
+        return self._resource is None
+
+    def close(self):
+        self._resource = None
+
+    def __enter__(self):
+        _ = self._native_resource
+        return self
+
+    def __exit__(self, exc_type, exc_value, traceback):
+        self.close()
+        return False
+
+
+class Device(_ContextManager):
+    """One CUDA device (default ordinal 0).  Construction initializes CUDA on it."""
+
+    def __init__(self, ordinal: int = 0):
+        if type(ordinal) is not int or ordinal < 0:
+            raise ValueError("device ordinal must be a nonnegative int")
+        self._lib = _native.load()
+        if not self._lib.ckl_cuda_available():
+            raise RuntimeError("no CUDA device is available to the CKL runtime")
+        handle = C.c_void_p()
+        _native.check(self._lib.ckl_device_create(ordinal, C.byref(handle)), "device")
+        self._resource = _Handle(handle.value, self._lib.ckl_device_release)
+        self.ordinal = ordinal
+
+    @property
+    def native_library(self) -> Path:
+        return _native.library_path().resolve()
+
+    @property
+    def name(self) -> str:
+        buffer = C.create_string_buffer(256)
+        _native.check(self._lib.ckl_device_name(self._native_resource.value, buffer, 256))
+        return buffer.value.decode()
+
+    def empty(self, spec: BufferSpec) -> "DeviceBuffer":
+        size = _byte_count(spec)
+        handle = C.c_void_p()
+        _native.check(self._lib.ckl_buffer_allocate(self._native_resource.value, size,
+                                                    C.byref(handle)), "allocate")
+        return DeviceBuffer(self, _Handle(handle.value, self._lib.ckl_buffer_release), spec)
+
+    def import_buffer(self, address: int, spec: BufferSpec, *, owner) -> "DeviceBuffer":
+        """Borrow device storage, retaining its Python owner for the buffer's lifetime."""
+        size = _byte_count(spec)
+        if type(address) is not int or not 0 < address < (1 << 64) or owner is None:
+            raise ValueError("imported storage requires a valid address and a live owner")
+        handle = C.c_void_p()
+        _native.check(self._lib.ckl_buffer_import(self._native_resource.value, address, size,
+                                                  C.byref(handle)), "import")
+        return DeviceBuffer(self, _Handle(handle.value, self._lib.ckl_buffer_release), spec, owner)
+
+
+class DeviceBuffer(_ContextManager):
+    def __init__(self, device, resource, spec, owner=None):
+        self.device, self.spec, self._owner = device, spec, owner
+        self._lib = device._lib
+        self._resource = resource
+        # Borrowed storage keeps its owner's native allocation alive as well.
+        self._owner_resource = owner._resource if isinstance(owner, DeviceBuffer) else None
+
+    def close(self):
+        super().close()
+        self.device = self._owner = None
+
+    @property
+    def address(self) -> int:
+        return int(self._lib.ckl_buffer_address(self._native_resource.value))
+
+    @property
+    def nbytes(self) -> int:
+        return int(self._lib.ckl_buffer_size(self._native_resource.value))
+
+    def subview(self, *, offset: int, shape: tuple) -> "DeviceBuffer":
+        """A bounded contiguous view; ``offset`` is in elements of this buffer."""
+        spec = BufferSpec(shape, self.spec.dtype)
+        size = _byte_count(spec)
+        if type(offset) is not int or offset < 0:
+            raise ValueError("subview requires a nonnegative element offset")
+        byte_offset = offset * _SCALARS[self.spec.dtype][1]
+        if byte_offset > self.nbytes or size > self.nbytes - byte_offset:
+            raise ValueError("subview exceeds its source buffer")
+        handle = C.c_void_p()
+        _native.check(self._lib.ckl_buffer_slice(self._native_resource.value, byte_offset, size,
+                                                 C.byref(handle)), "subview")
+        return DeviceBuffer(self.device, _Handle(handle.value, self._lib.ckl_buffer_release),
+                            spec, self)
+
+    def copy_from_host(self, source):
+        pointer, nbytes, keep = _host_pointer(source, writable=False)
+        if nbytes != self.nbytes:
+            raise ValueError("host buffer byte count does not match device storage")
+        _native.check(self._lib.ckl_buffer_copy_from_host(self._native_resource.value, pointer,
+                                                          nbytes), "copy_from_host")
+
+    def copy_to_host(self, destination):
+        pointer, nbytes, keep = _host_pointer(destination, writable=True)
+        if nbytes != self.nbytes:
+            raise ValueError("destination must be writable and match device storage byte count")
+        _native.check(self._lib.ckl_buffer_copy_to_host(self._native_resource.value, pointer,
+                                                        nbytes), "copy_to_host")
+
+
+class _NativeProgram:
+    """A native program built from an executable plan (optionally with a fallback)."""
+
+    def __init__(self, lib, plans):
+        self._lib = lib
+        fallback = None
+        if plans.fallback is not None:
+            handle = C.c_void_p()
+            _native.check(lib.ckl_program_create_from_plan(plans.fallback.text.encode(), None,
+                                                           C.byref(handle)), "program")
+            fallback = _Handle(handle.value, lib.ckl_program_release)
+        handle = C.c_void_p()
+        _native.check(lib.ckl_program_create_from_plan(
+            plans.primary.text.encode(), fallback.value if fallback else None, C.byref(handle)),
+            "program")
+        self.fallback = fallback
+        self.handle = _Handle(handle.value, lib.ckl_program_release)
+
+
+class CompiledProgram(_ContextManager):
+    """A program resolved onto the sm_100a kernel library with its planned graph and storage."""
+
+    def __init__(self, program, target: NVIDIATarget, *, fuse_pointwise=True, reuse_storage=True,
+                 fuse_library=True):
+        if type(fuse_pointwise) is not bool:
+            raise TypeError("fuse_pointwise must be bool")
+        if type(reuse_storage) is not bool:
+            raise TypeError("reuse_storage must be bool")
+        if type(fuse_library) is not bool:
+            raise TypeError("fuse_library must be bool")
+        if not isinstance(target, NVIDIATarget) or target.binary_format != "bin":
+            raise ValueError("CKL CUDA compilation requires a binary target")
+        if target.chip not in SUPPORTED_CHIPS:
+            raise ValueError(f"this build generates sm_100a code only; got chip {target.chip!r}")
+        from .compile import plan_program
+
+        self.signature, self.target = program.signature, target
+        self.lowered = program
+        self._lib = _native.load()
+        self.plans = plan_program(program, fuse_pointwise=fuse_pointwise,
+                                  fuse_library=fuse_library, reuse_storage=reuse_storage)
+        self._resource = _NativeProgram(self._lib, self.plans)
+
+    @property
+    def prepared_ir(self) -> str:
+        return self.plans.prepared_ir
+
+    @property
+    def executable_ir(self) -> str:
+        return self.plans.primary.executable_ir
+
+    @property
+    def fallback_ir(self) -> str:
+        return self.plans.fallback.executable_ir if self.plans.fallback else ""
+
+    @property
+    def device_ir(self) -> str:
+        return self.plans.device_ir
+
+    @property
+    def host_ir(self) -> str:
+        return self.plans.host_ir
+
+    @property
+    def host_mlir(self) -> str:
+        return self.plans.host_ir
+
+    def bind(self, *arguments, device: Device | None = None) -> "Invocation":
+        parameters = self.signature.runtime
+        if len(arguments) != len(parameters):
+            raise TypeError(f"expected {len(parameters)} runtime arguments, got {len(arguments)}")
+        buffers = [a for a in arguments if isinstance(a, DeviceBuffer)]
+        device = device or (buffers[0].device if buffers else None)
+        if device is None:
+            raise ValueError("pass a Device for programs without buffer arguments")
+        packed = (_native.Argument * max(len(arguments), 1))()
+        for index, (parameter, value) in enumerate(zip(parameters, arguments)):
+            if isinstance(parameter.dtype, BufferSpec):
+                if not isinstance(value, DeviceBuffer) or value.spec != parameter.dtype:
+                    raise TypeError(f"{parameter.name} requires {parameter.dtype}")
+                if value.device is not device:
+                    raise ValueError("all buffers must belong to the selected Device")
+                packed[index].kind = _native.ARG_BUFFER
+                packed[index].buffer = value._native_resource.value
+                continue
+            code, width = _SCALARS[parameter.dtype]
+            if parameter.dtype in (i32, i64):
+                bits = width * 8
+                if type(value) is not int or not -(1 << (bits - 1)) <= value < (1 << (bits - 1)):
+                    raise TypeError(f"{parameter.name} requires a {bits}-bit integer")
+            elif type(value) not in (int, float) or not math.isfinite(float(value)):
+                raise TypeError(f"{parameter.name} requires a finite numeric value")
+            if parameter.dtype in (f32, f64):
+                try:
+                    rounded = struct.unpack(code, struct.pack(code, value))[0]
+                except (OverflowError, struct.error):
+                    raise ValueError(f"{parameter.name} overflows {parameter.dtype.name}") from None
+                if not math.isfinite(rounded):
+                    raise ValueError(f"{parameter.name} overflows {parameter.dtype.name}")
+            raw = struct.pack("<" + code, value)
+            packed[index].kind = _ARG_KIND[parameter.dtype]
+            packed[index].bits = int.from_bytes(raw.ljust(8, b"\0"), "little")
+        handle = C.c_void_p()
+        _native.check(self._lib.ckl_bind(self._native_resource.handle.value,
+                                         device._native_resource.value, len(arguments), packed,
+                                         C.byref(handle)), "bind")
+        return Invocation(self, device, arguments, _Handle(handle.value,
+                                                           self._lib.ckl_invocation_release))
+
+    def run(self, *arguments, graph=False, device=None) -> "Invocation":
+        return self.bind(*arguments, device=device).run(graph=graph)
+
+
+class Invocation(_ContextManager):
+    """A bound program owning its temporaries, stream and lazily built CUDA graphs."""
+
+    def __init__(self, program, device, arguments, resource):
+        self.program, self.device, self.arguments = program, device, arguments
+        self._lib = program._lib
+        # The native invocation retains its program, device and buffers; keep the Python
+        # owners of imported storage alive as well.
+        self._keep = (program._resource, [getattr(a, "_owner", None) for a in arguments],
+                      [getattr(a, "_owner_resource", None) for a in arguments],
+                      [getattr(a, "_resource", None) for a in arguments])
+        self._resource = resource
+
+    def close(self):
+        super().close()
+        self.program = self.device = self.arguments = None
+
+    @staticmethod
+    def _execution(graph, mode, batch_size) -> int:
+        if type(batch_size) is not int or not 0 < batch_size < (1 << 64):
+            raise ValueError("batch_size must be a positive 64-bit count")
+        if mode is not None and graph:
+            raise ValueError("specify either graph or mode")
+        if mode is not None and mode not in _MODES:
+            raise ValueError("mode must be ordinary, graph, or capture")
+        return _MODES[mode] if mode is not None else int(bool(graph))
+
+    def run(self, *, graph=False, mode=None, batch_size=1) -> "Invocation":
+        execution = self._execution(graph, mode, batch_size)
+        _native.check(self._lib.ckl_run(self._native_resource.value, execution, batch_size), "run")
+        return self
+
+    @property
+    def node_count(self) -> int:
+        """Kernel nodes of one program execution (after fusion or the overlap fallback)."""
+        out = C.c_uint64()
+        _native.check(self._lib.ckl_node_count(self._native_resource.value, C.byref(out)))
+        return int(out.value)
+
+    @property
+    def node_names(self) -> list:
+        names = []
+        for i in range(self.node_count):
+            buffer = C.create_string_buffer(128)
+            _native.check(self._lib.ckl_node_name(self._native_resource.value, i, buffer, 128))
+            names.append(buffer.value.decode())
+        return names
+
+    def benchmark(self, *, iterations=200, graph=False, mode=None, batch_size=1) -> dict:
+        """Time ``iterations`` submissions of ``batch_size`` programs; report per program."""
+        if type(iterations) is not int or not 0 < iterations < (1 << 64):
+            raise ValueError("iterations must be a positive 64-bit count")
+        execution = self._execution(graph, mode, batch_size)
+        out = (C.c_double * 3)()
+        _native.check(self._lib.ckl_benchmark(self._native_resource.value, execution, iterations,
+                                              batch_size, out), "benchmark")
+        return {"stream_us": out[0], "wall_us": out[1], "graph_setup_ms": out[2]}
+
+    # ---- asynchronous interface (B200 build) ------------------------------------------
+    def launch(self, *, graph=False, mode=None, batch_size=1) -> None:
+        """Submit without waiting; pair with :meth:`synchronize`."""
+        execution = self._execution(graph, mode, batch_size)
+        _native.check(self._lib.ckl_launch(self._native_resource.value, execution, batch_size),
+                      "launch")
+
+    def synchronize(self) -> None:
+        _native.check(self._lib.ckl_synchronize(self._native_resource.value), "synchronize")
+
+    def copy_in_async(self, buffer: DeviceBuffer, source_pointer: int, nbytes: int) -> None:
+        """Enqueue a host-to-device copy from page-locked memory on the invocation stream."""
+        _native.check(self._lib.ckl_copy_in_async(self._native_resource.value,
+                                                  buffer._native_resource.value, source_pointer,
+                                                  nbytes), "copy_in_async")
+
+    def copy_out_async(self, buffer: DeviceBuffer, destination_pointer: int, nbytes: int) -> None:
+        _native.check(self._lib.ckl_copy_out_async(self._native_resource.value,
+                                                   buffer._native_resource.value,
+                                                   destination_pointer, nbytes), "copy_out_async")
+
+    def time_launches(self, steps: int, *, mode="graph", batch_size=1) -> float:
+        """Device milliseconds of ``steps`` back-to-back submissions (CUDA events)."""
+        out = C.c_double()
+        _native.check(self._lib.ckl_time_launches(self._native_resource.value, _MODES[mode],
+                                                  batch_size, steps, C.byref(out)), "timing")
+        return out.value
+
+
+class PinnedHostBuffer:
+    """Page-locked host memory for asynchronous copies."""
+
+    def __init__(self, nbytes: int):
+        self._lib = _native.load()
+        pointer = C.c_void_p()
+        _native.check(self._lib.ckl_host_alloc(nbytes, C.byref(pointer)), "pinned allocation")
+        self.pointer, self.nbytes = pointer.value, nbytes
+        self._handle = _Handle(pointer.value, self._lib.ckl_host_free)
+
+    def view(self):
+        return (C.c_char * self.nbytes).from_address(self.pointer)
+
+
+def cuda_available() -> bool:
+    return bool(_native.load().ckl_cuda_available())
