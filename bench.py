@@ -1,0 +1,348 @@
+"""Decode-step throughput of the CKL decoder on B200: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload cfg5|cfg1|cfg3|cfg4|vector] [--requests-per-gpu R]
+
+Default workload: BASELINE config 5 (scale-out decoder: 4 layers, hidden 1024, 16 heads x 64,
+SwiGLU 4096, vocab 32000, 2048-token prompts in the KV cache, greedy decode).  Requests are
+sharded across GPUs with no collective in the step; each GPU holds 512 requests, so 8 GPUs
+run the full 4096-request configuration (weak scaling; the full configuration's 279 GB KV
+cache does not fit one GPU).  Weights are seeded random (reference draw order, seed 4),
+prompts uniform over the vocabulary; the prompt is prefilled on the GPU by teacher forcing
+through the same decode graph.  Every timed step is one complete decode step (all layers, LM
+head, greedy argmax, KV append) for every request on the GPU.
+
+Timing: W warm-up steps, then K graph launches bracketed by a barrier and a synchronize on
+both sides, CUDA events on the invocation stream, max over ranks.  The KV cache (34.9 GB per
+GPU) is far larger than L2, so no flush is needed between steps.  ``e2e`` repeats K steps
+through the public API with the step's tokens copied host->device from pinned memory and the
+generated tokens copied back every step.  ``roofline`` reports the attention kernel (the
+dominant, HBM-bound kernel) from per-node CUDA events over one extra profiled step.
+``--impl reference`` times the reference's own CPU decoder (its NumPy algorithm, restated in
+oracle/) on a bounded sample of requests on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "composable-kernel-language_b200" / "python"))
+
+WORKLOADS = {
+    # name: (batch per GPU, hidden, heads, layers, ffn, vocab, context, steps, seed, eps)
+    "cfg5": (512, 1024, 16, 4, 4096, 32000, 2048, 32, 4, 1e-6),
+    "cfg1": (1, 64, 4, 2, 256, 512, 16, 16, 0, 1e-6),
+    "cfg3": (64, 256, 8, 2, 1024, 512, 16, 16, 2, 1e-6),
+    "cfg4": (256, 64, 4, 8, 256, 512, 16, 16, 3, 1e-6),
+}
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+
+
+def peaks():
+    if PEAKS.exists():
+        data = json.loads(PEAKS.read_text())
+        return data["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples for this rank's GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, ordinal: int):
+        self.ordinal, self.samples, self.process = ordinal, [], None
+
+    def __enter__(self):
+        try:
+            self.process = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.ordinal}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.process = None
+        return self
+
+    def _read(self):
+        for line in self.process.stdout:
+            self.samples.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.process:
+            self.process.terminate()
+            try:
+                self.process.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.process.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        rows = [r for r in self.samples if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, value in zip(names, r[5:9]):
+                if value.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def distributed():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        group = dist
+    return world, rank, local, group
+
+
+def reduce_max(group, value: float) -> float:
+    if group is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    group.all_reduce(t, op=group.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(group):
+    if group is not None:
+        group.barrier()
+
+
+# ---- CPU leg: the reference algorithm on the host --------------------------------------
+def cpu_decode_rate(workload, budget_s: float, min_steps: int, max_steps: int, sample: int):
+    """Tokens/s of the NumPy decoder (oracle restatement) on `sample` requests."""
+    from oracle import decoder as ref
+
+    b, h, a, l, f, v, ctx, steps, seed, eps = workload
+    config = ref.Config(batch=sample, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
+                        steps=max(steps, max_steps + 1))
+    arrays, rng = ref.make_weights(config, seed)
+    arrays.update(ref.empty_state(config))
+    prompts = ref.make_prompts(config, rng)
+    # The KV prefix the prompt would leave: random values (the step's cost does not depend
+    # on them), position at the last prompt token, as after a prefill.
+    fill = np.random.default_rng(seed + 1)
+    p0 = ctx - 1
+    for name in ("kc", "vc"):
+        arrays[name][:, :, :, :p0] = fill.standard_normal(arrays[name][:, :, :, :p0].shape,
+                                                          dtype=np.float32)
+    arrays["position"][0] = p0
+    arrays["tokens"] = prompts[-1].copy()
+    times = []
+    begin = time.perf_counter()
+    while len(times) < max_steps and (len(times) < min_steps or time.perf_counter() - begin < budget_s):
+        t0 = time.perf_counter()
+        ref.decode_step(arrays, config, eps)
+        times.append(time.perf_counter() - t0)
+    return sample / statistics.mean(times), len(times), sample
+
+
+def reference_arm(args, workload, world, rank):
+    if rank != 0:
+        return 0
+    sample = 8 if workload[0] >= 8 else workload[0]
+    steps = max(args.steps, 1)
+    # Warm-up steps, then `steps` timed steps of the bounded sample.
+    cpu_decode_rate(workload, 0.0, args.warmup, args.warmup, sample) if args.warmup else None
+    rate, done, sample = cpu_decode_rate(workload, 1e9, steps, steps, sample)
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": metric_name(args.workload), "value": rate,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": done, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * sample / rate, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, workload, world),
+        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} requests at position {workload[6] - 1}, "
+                                   f"{done} decode steps, NumPy with {cores} host threads"},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def metric_name(workload: str) -> str:
+    return "decode tokens/s" if workload != "vector" else "vector pipeline elements/s"
+
+
+def workload_config(args, workload, world):
+    b, h, a, l, f, v, ctx, steps, seed, eps = workload
+    return {"workload": f"{args.workload} decoder (BASELINE config "
+                        f"{ {'cfg5': 5, 'cfg1': 1, 'cfg3': 3, 'cfg4': 4}[args.workload]}), "
+                        f"{b} requests per GPU, request-sharded",
+            "requests_per_gpu": b, "total_requests": b * world, "layers": l, "hidden": h,
+            "heads": a, "head_dim": h // a, "ffn": f, "vocab": v, "context": ctx,
+            "seed": seed, "epsilon": eps, "parallelism": f"requests x{world}, no collective",
+            "l2": "no flush: per-GPU KV cache and weights exceed the 126 MB L2"
+            if args.workload == "cfg5" else "small working set, L2-resident (latency-bound)"}
+
+
+# ---- GPU leg ----------------------------------------------------------------------------
+def gpu_arm(args, workload, world, rank, local, group):
+    import ckl
+    from ckl.workloads import session as S
+
+    b, h, a, l, f, v, ctx, steps, seed, eps = workload
+    total_steps = args.warmup + args.steps
+    capacity_steps = max(steps, 2 * total_steps + 4)
+    shape = S.DecoderShape(batch=b, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
+                           steps=capacity_steps)
+    arrays, rng = S.make_weights(shape, seed)
+    all_prompts = rng.integers(0, v, (ctx, b * world), dtype=np.int32)
+    prompts = np.ascontiguousarray(all_prompts[:, rank * b:(rank + 1) * b])
+    cache = (l, b, a, shape.capacity, h // a)
+    arrays.update(tokens=prompts[0].copy(), position=np.zeros(1, np.int32),
+                  history=np.full((shape.capacity, b), -1, np.int32),
+                  kc=(cache, np.float32), vc=(cache, np.float32),
+                  logits=np.zeros((b, v), np.float32))
+    device = ckl.Device(local)
+    t_setup = time.perf_counter()
+    sess = S.DecoderSession(device, arrays, epsilon=eps, attention_scale=(h // a) ** -0.5,
+                            tails=False)
+    sess.prefill(prompts)
+    setup_s = time.perf_counter() - t_setup
+    inv = sess.invocation
+    nodes = inv.node_count
+    for _ in range(args.warmup):
+        inv.run(mode="graph")
+    with ClockSampler(local) as clocks:
+        barrier(group)
+        inv.synchronize()
+        elapsed_ms = inv.time_launches(args.steps, mode="graph")
+        inv.synchronize()
+        barrier(group)
+    elapsed_ms = reduce_max(group, elapsed_ms)
+    value = b * world * args.steps / (elapsed_ms / 1000.0)
+
+    # End to end through the public API: per step, tokens host->device from pinned memory,
+    # the step, generated tokens device->host, wait for them.
+    pinned_in = ckl.cuda.PinnedHostBuffer(4 * b)
+    pinned_out = ckl.cuda.PinnedHostBuffer(4 * b)
+    tokens_buf = sess.buffers["tokens"]
+    host_tokens = np.frombuffer(pinned_in.view(), dtype=np.int32)
+    host_tokens[:] = sess.read("tokens")
+    out_tokens = np.frombuffer(pinned_out.view(), dtype=np.int32)
+    barrier(group)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        inv.copy_in_async(tokens_buf, pinned_in.pointer, 4 * b)
+        inv.launch(mode="graph")
+        inv.copy_out_async(tokens_buf, pinned_out.pointer, 4 * b)
+        inv.synchronize()
+        host_tokens[:] = out_tokens
+    e2e_s = reduce_max(group, time.perf_counter() - t0)
+    e2e = b * world * args.steps / e2e_s
+
+    # Per-kernel device time of one more (profiled, ordinary-mode) step.
+    position = int(sess.read("position")[0])
+    per_node = inv.profile_nodes(1)
+    names = inv.node_names
+    attention = [t for n, t in zip(names, per_node) if n == "ckl.fused.attention"]
+    hbm, peak_kind = peaks()
+    roofline = None
+    if attention:
+        n_rows = position + 1
+        algorithmic = 2 * b * a * n_rows * (h // a) * 4 + 2 * b * h * 4
+        launch_ms = statistics.mean(attention)
+        achieved = algorithmic / (launch_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "kernel": "ckl.fused.attention", "achieved": achieved,
+                    "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": None, "algorithmic_bytes_per_launch": algorithmic,
+                    "launch_ms": launch_ms, "launches_profiled": len(attention),
+                    "kv_rows_per_head": n_rows}
+    share = {}
+    for n, t in zip(names, per_node):
+        share[n] = share.get(n, 0.0) + t
+    total = sum(per_node)
+    line = None
+    if rank == 0:
+        line = {
+            "metric": metric_name(args.workload), "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seeded random weights (reference draw order), uniform prompts",
+            "config": workload_config(args, workload, world),
+            "roofline": roofline,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4 * b * world,
+                    "d2h_bytes_per_step": 4 * b * world},
+            "gpu_launches": nodes * args.steps,
+            "graph_nodes_per_step": nodes,
+            "kernel_share": {k: round(t / total, 4) for k, t in sorted(share.items(),
+                                                                       key=lambda kv: -kv[1])},
+            "prefill_setup_s": round(setup_s, 2),
+            "clocks": clocks.summary(),
+        }
+    return line
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg5")
+    parser.add_argument("--requests-per-gpu", type=int)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 0 or args.steps < 1:
+        parser.error("steps must be positive and warmup nonnegative")
+    workload = list(WORKLOADS[args.workload])
+    if args.requests_per_gpu:
+        workload[0] = args.requests_per_gpu
+    workload = tuple(workload)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        return reference_arm(args, workload, world, int(os.environ.get("RANK", "0")))
+    world, rank, local, group = distributed()
+    line = gpu_arm(args, workload, world, rank, local, group)
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            rate, done, sample = cpu_decode_rate(workload, 15.0, 3, 40, min(8, workload[0]))
+            cores = os.cpu_count()
+            line["cpu_baseline"] = {
+                "value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                "sample": f"{sample} requests at position {workload[6] - 1}, {done} decode steps "
+                          f"of the NumPy decoder (reference algorithm) with {cores} host threads"}
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        group.barrier()
+        group.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

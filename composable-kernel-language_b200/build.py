@@ -23,6 +23,8 @@ CSRC = HERE / "csrc"
 INCLUDE = ROOT / "include"
 BUILD = HERE / "_build"
 OUTPUT = HERE / "python" / "ckl" / "libckl_b200.so"
+TEST_KERNELS = ROOT / "tests" / "native" / "kernels.cu"
+TEST_CUBIN = ROOT / "tests" / "native" / "runtime_kernels.cubin"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I", str(INCLUDE), "-I", str(CSRC)]
@@ -74,6 +76,11 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
         result = subprocess.run(command, capture_output=True, text=True)
         if result.returncode:
             raise RuntimeError(f"link failed:\n{result.stderr}")
+    if TEST_KERNELS.exists() and (force or stale(TEST_CUBIN, [TEST_KERNELS])):
+        command = [nvcc(), "-cubin", *ARCH, "-O3", str(TEST_KERNELS), "-o", str(TEST_CUBIN)]
+        result = subprocess.run(command, capture_output=True, text=True)
+        if result.returncode:
+            raise RuntimeError(f"test CUBIN build failed:\n{result.stderr}")
     return OUTPUT
 
 

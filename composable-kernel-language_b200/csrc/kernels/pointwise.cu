@@ -65,6 +65,20 @@ __global__ void __launch_bounds__(kPointwiseThreads)
 }
 
 __global__ void __launch_bounds__(kPointwiseThreads)
+    fillKernel(float *dst, float value, PointwiseSpec spec) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < spec.count; e += stride)
+    dst[e] = value;
+}
+
+__global__ void __launch_bounds__(kPointwiseThreads)
+    copyKernel(const float *src, float *dst, PointwiseSpec spec) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < spec.count; e += stride)
+    dst[e] = src[e];
+}
+
+__global__ void __launch_bounds__(kPointwiseThreads)
     chain2Kernel(const float *src, float *dst, float s0, float s1, ChainSpec spec) {
   const float scalars[2] = {s0, s1};
   chainBody<2>(src, dst, scalars, spec);
@@ -119,6 +133,10 @@ CKL_REGISTER_KERNEL("ckl.pointwise.add_scalar", reinterpret_cast<const void *>(&
                     "PPFS", sizeof(PointwiseSpec), pointwiseGeometry, nullptr);
 CKL_REGISTER_KERNEL("ckl.pointwise.mul_scalar", reinterpret_cast<const void *>(&scaleKernel),
                     "PPFS", sizeof(PointwiseSpec), pointwiseGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.pointwise.fill", reinterpret_cast<const void *>(&fillKernel), "PFS",
+                    sizeof(PointwiseSpec), pointwiseGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.pointwise.copy", reinterpret_cast<const void *>(&copyKernel), "PPS",
+                    sizeof(PointwiseSpec), pointwiseGeometry, nullptr);
 CKL_REGISTER_KERNEL("ckl.pointwise.chain2", reinterpret_cast<const void *>(&chain2Kernel),
                     "PPFFS", sizeof(ChainSpec), chainGeometry, nullptr);
 CKL_REGISTER_KERNEL("ckl.pointwise.chain3", reinterpret_cast<const void *>(&chain3Kernel),

@@ -884,6 +884,49 @@ int ckl_time_launches(ckl_invocation *invocation, int mode, uint64_t batch, uint
   });
 }
 
+int ckl_profile_nodes(ckl_invocation *invocation, uint64_t iterations, double *out_ms,
+                      uint64_t capacity) {
+  return guarded([&] {
+    if (!invocation || !out_ms || !iterations)
+      throw std::invalid_argument("invalid profiling request");
+    auto &f = *invocation->state;
+    std::lock_guard<std::mutex> lock(f.runMutex);
+    const std::size_t n = f.plan.nodes.size();
+    if (capacity < n)
+      throw std::out_of_range("profile output holds fewer entries than the plan has nodes");
+    f.device->current();
+    std::vector<cudaEvent_t> events(n + 1, nullptr);
+    auto destroy = [&] {
+      for (cudaEvent_t e : events)
+        if (e)
+          cudaEventDestroy(e);
+    };
+    try {
+      for (auto &e : events)
+        check(cudaEventCreate(&e), "cudaEventCreate");
+      for (std::size_t i = 0; i < n; ++i)
+        out_ms[i] = 0;
+      for (uint64_t it = 0; it < iterations; ++it) {
+        for (std::size_t i = 0; i < n; ++i) {
+          check(cudaEventRecord(events[i], f.stream), "cudaEventRecord");
+          launchOne(f.plan.nodes[i], f.stream);
+        }
+        check(cudaEventRecord(events[n], f.stream), "cudaEventRecord");
+        check(cudaEventSynchronize(events[n]), "cudaEventSynchronize");
+        for (std::size_t i = 0; i < n; ++i) {
+          float ms = 0;
+          check(cudaEventElapsedTime(&ms, events[i], events[i + 1]), "cudaEventElapsedTime");
+          out_ms[i] += ms;
+        }
+      }
+    } catch (...) {
+      destroy();
+      throw;
+    }
+    destroy();
+  });
+}
+
 int ckl_node_count(const ckl_invocation *invocation, uint64_t *out) {
   return guarded([&] {
     if (!invocation || !out)

@@ -169,6 +169,9 @@ class DeviceBuffer(_ContextManager):
         _native.check(self._lib.ckl_buffer_copy_from_host(self._native_resource.value, pointer,
                                                           nbytes), "copy_from_host")
 
+    def fill_zero(self):
+        _native.check(self._lib.ckl_buffer_fill_zero(self._native_resource.value), "fill_zero")
+
     def copy_to_host(self, destination):
         pointer, nbytes, keep = _host_pointer(destination, writable=True)
         if nbytes != self.nbytes:
@@ -368,6 +371,14 @@ class Invocation(_ContextManager):
         _native.check(self._lib.ckl_copy_out_async(self._native_resource.value,
                                                    buffer._native_resource.value,
                                                    destination_pointer, nbytes), "copy_out_async")
+
+    def profile_nodes(self, iterations: int = 1) -> list:
+        """Per-node device milliseconds over ``iterations`` ordinary executions (state advances)."""
+        count = self.node_count
+        out = (C.c_double * count)()
+        _native.check(self._lib.ckl_profile_nodes(self._native_resource.value, iterations, out,
+                                                  count), "profile")
+        return list(out)
 
     def time_launches(self, steps: int, *, mode="graph", batch_size=1) -> float:
         """Device milliseconds of ``steps`` back-to-back submissions (CUDA events)."""

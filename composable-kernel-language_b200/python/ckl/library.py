@@ -101,7 +101,9 @@ def _pointwise_entries():
         n = s[0][0]
         return pack(n, min(n, e[0]))
     return [Entry("ckl.pointwise.add_scalar", "update", spec, lambda s, e: True, pointwise_op=0),
-            Entry("ckl.pointwise.mul_scalar", "scale", spec, lambda s, e: True, pointwise_op=1)]
+            Entry("ckl.pointwise.mul_scalar", "scale", spec, lambda s, e: True, pointwise_op=1),
+            Entry("ckl.pointwise.fill", "fill", spec, lambda s, e: True),
+            Entry("ckl.pointwise.copy", "copy", spec, lambda s, e: True)]
 
 
 @lru_cache(maxsize=1)
@@ -113,7 +115,8 @@ def catalogue() -> dict:
         "embedding", "rms_stats", "rms_apply", "linear", "rope", "append_kv",
         "attention_scores", "softmax", "attention_values", "add", "silu", "multiply",
         "greedy", "advance")},
-        "update": vector_pipeline.update, "scale": vector_pipeline.scale}
+        "update": vector_pipeline.update, "scale": vector_pipeline.scale,
+        "fill": vector_pipeline.fill, "copy": vector_pipeline.copy}
     table = {}
     for entry in _decoder_entries() + _pointwise_entries():
         table[canonical_key(sources[entry.source])] = entry

@@ -25,6 +25,20 @@ def scale(src: Vector, dst: Vector, factor: ckl.f32) -> None:
         dst[i] = src[i] * factor
 
 
+@ckl.kernel
+def fill(dst: Vector, value: ckl.f32) -> None:
+    i = ckl.global_id(0)
+    if i < N:
+        dst[i] = value
+
+
+@ckl.kernel
+def copy(src: Vector, dst: Vector) -> None:
+    i = ckl.global_id(0)
+    if i < N:
+        dst[i] = src[i]
+
+
 @ckl.program
 def step(src: Vector, dst: Vector, bias: ckl.f32) -> None:
     temporary = ckl.empty_like(src)

@@ -130,6 +130,13 @@ int ckl_copy_out_async(ckl_invocation *invocation, const ckl_buffer *buffer, voi
 int ckl_time_launches(ckl_invocation *invocation, int mode, uint64_t batch, uint64_t steps,
                       double *out_ms);
 
+/* Per-kernel device time: `iterations` ordinary executions of the bound plan with an event
+ * pair around every node; out_ms[i] accumulates node i (capacity >= node count).  Each
+ * iteration is a real execution of the program (state advances).  No reference counterpart
+ * (the reference profiles with nsys, benchmarks/decoder/collect.py:14-96). */
+int ckl_profile_nodes(ckl_invocation *invocation, uint64_t iterations, double *out_ms,
+                      uint64_t capacity);
+
 /* CUDA profiler range.  Replaces: nvidiaProfilerStart/Stop, NvidiaProgram.cpp:287-294. */
 int ckl_profiler_start(void);
 int ckl_profiler_stop(void);

@@ -1,0 +1,120 @@
+"""Decode-step parity on the GPU against the CPU oracle and the published known answers.
+
+Tolerances: greedy tokens, history and position bit-exact; logits and
+KV-cache rows within 1e-4 relative / 1e-5 absolute in float32.  Like the reference harness
+(benchmarks/decoder/run.py:107-132) every check also verifies the 256-element sentinel tails,
+unchanged weights and the untouched KV-cache prefix and suffix.
+"""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+import ckl
+from ckl.workloads import decoder, session as S
+from oracle import decoder as ref
+
+pytestmark = pytest.mark.gpu
+RTOL, ATOL = 1e-4, 1e-5
+PUBLISHED = json.loads((GOLDEN / "published_cases.json").read_text())["cases"]
+CFG1 = ref.Config(batch=1, hidden=64, heads=4, layers=2, ffn=256, vocab=512, context=16, steps=16)
+
+
+@pytest.fixture(scope="module")
+def device():
+    return ckl.Device()
+
+
+def open_session(device, config, arrays, eps, **kw):
+    return S.DecoderSession(device, arrays, epsilon=eps, attention_scale=config.head_dim ** -0.5, **kw)
+
+
+def verify(session, initial, expected, config):
+    start, end = int(initial["position"][0]), int(expected["position"][0])
+    for name in S.MUTABLE + S.WEIGHTS + ("sincos",):
+        assert session.tail_intact(name), f"{name}: tail overwritten"
+        actual = session.read(name)
+        if name not in S.MUTABLE:
+            assert np.array_equal(actual, initial[name]), f"{name}: weights changed"
+        elif actual.dtype == np.int32:
+            assert np.array_equal(actual, expected[name]), f"{name}: mismatch"
+        else:
+            assert np.all(np.isfinite(actual[..., :end, :] if name in ("kc", "vc") else actual))
+            if name in ("kc", "vc"):
+                assert np.array_equal(actual[:, :, :, :start], initial[name][:, :, :, :start])
+                assert np.array_equal(actual[:, :, :, end:], initial[name][:, :, :, end:])
+                assert np.allclose(actual[:, :, :, start:end], expected[name][:, :, :, start:end],
+                                   rtol=RTOL, atol=ATOL), name
+            else:
+                assert np.allclose(actual, expected[name], rtol=RTOL, atol=ATOL), name
+
+
+@pytest.mark.parametrize("fuse", [True, False], ids=["fused", "unfused"])
+@pytest.mark.parametrize("eps", [1e-6, 1e-5])
+def test_cfg1_sixteen_steps_match_oracle(device, fuse, eps):
+    initial, _ = ref.make_inputs(CFG1, 0, eps=eps)
+    expected = ref.expected(initial, CFG1, CFG1.steps, eps=eps)
+    session = open_session(device, CFG1, initial, eps, fuse_library=fuse)
+    assert session.invocation.node_count == (19 if fuse else 48)
+    session.step(CFG1.steps)
+    verify(session, initial, expected, CFG1)
+
+
+@pytest.mark.parametrize("mode,group", [("ordinary", 1), ("capture", 1), ("graph", 4),
+                                        ("capture", 16), ("graph", 16)])
+def test_modes_and_step_groups(device, mode, group):
+    config = ref.Config(batch=3, hidden=48, heads=3, layers=1, ffn=80, vocab=129, context=3, steps=16)
+    initial, _ = ref.make_inputs(config, 123)
+    expected = ref.expected(initial, config, config.steps)
+    session = open_session(device, config, initial, 1e-5)
+    session.step(config.steps, mode=mode, batch_size=group)
+    verify(session, initial, expected, config)
+
+
+@pytest.mark.parametrize("case", [c for c in PUBLISHED if "deep-dive" in c["source"]],
+                         ids=lambda c: c["name"])
+def test_published_tokens_with_gpu_prefill(device, case):
+    """Prompts prefilled on the GPU by teacher forcing reproduce the published tokens."""
+    config = ref.Config(**case["config"])
+    shape = S.DecoderShape(**case["config"])
+    arrays, rng = S.make_weights(shape, case["seed"])
+    prompts = S.make_prompts(shape, rng)
+    assert prompts.tolist() == case["prompts"]
+    arrays.update(S.initial_state(shape))
+    session = open_session(device, config, arrays, 1e-5)
+    session.prefill(prompts)
+    session.step(config.steps)
+    history = session.read("history")
+    start = config.context - 1
+    assert history[start:start + config.steps].tolist() == case["generated_tokens"]
+    assert int(session.read("position")[0]) == config.context - 1 + config.steps
+
+
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,seed,steps", [
+    (64, 256, 8, 2, 1024, 2, 4),     # cfg3 shape
+    (256, 64, 4, 8, 256, 3, 3),      # cfg4 shape
+    (33, 128, 2, 1, 96, 5, 3),       # ragged batch, head dim 64
+])
+def test_batched_shapes_match_oracle(device, batch, hidden, heads, layers, ffn, seed, steps):
+    config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn, vocab=512,
+                        context=16, steps=steps)
+    initial, _ = ref.make_inputs(config, seed, eps=1e-6)
+    expected = ref.expected(initial, config, steps, eps=1e-6)
+    session = open_session(device, config, initial, 1e-6)
+    session.step(steps)
+    verify(session, initial, expected, config)
+
+
+def test_overlapping_bindings_take_the_reference_graph(device):
+    """Fused plans require distinct buffers; an aliased binding falls back to 21L+6 nodes."""
+    initial, _ = ref.make_inputs(CFG1, 0)
+    session = open_session(device, CFG1, initial, 1e-5)
+    buffers = [session.buffers[n] for n in decoder.ARGUMENTS[:-2]]
+    aliased = list(buffers)
+    aliased[18] = device.import_buffer(session.buffers["vc"].address, session.buffers["logits"].spec,
+                                       owner=session.owners["vc"])
+    invocation = session.program.bind(*aliased, 1e-5, CFG1.head_dim ** -0.5)
+    assert invocation.node_count == 21 * CFG1.layers + 6
