@@ -69,7 +69,7 @@ class ClockSampler:
         try:
             self.process = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.ordinal}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -231,18 +231,22 @@ def gpu_arm(args, workload, world, rank, local, group):
     t_setup = time.perf_counter()
     sess = S.DecoderSession(device, arrays, epsilon=eps, attention_scale=(h // a) ** -0.5,
                             tails=False)
-    sess.prefill(prompts)
+    if args.prefill == "graph":
+        sess.prefill(prompts)
+    else:
+        sess.write("tokens", prompts[-1])
+        sess.write("position", np.array([ctx - 1], np.int32))
     setup_s = time.perf_counter() - t_setup
     inv = sess.invocation
     nodes = inv.node_count
+    clocks = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
         inv.run(mode="graph")
-    with ClockSampler(local) as clocks:
-        barrier(group)
-        inv.synchronize()
-        elapsed_ms = inv.time_launches(args.steps, mode="graph")
-        inv.synchronize()
-        barrier(group)
+    barrier(group)
+    inv.synchronize()
+    elapsed_ms = inv.time_launches(args.steps, mode="graph")
+    inv.synchronize()
+    barrier(group)
     elapsed_ms = reduce_max(group, elapsed_ms)
     value = b * world * args.steps / (elapsed_ms / 1000.0)
 
@@ -264,6 +268,7 @@ def gpu_arm(args, workload, world, rank, local, group):
         host_tokens[:] = out_tokens
     e2e_s = reduce_max(group, time.perf_counter() - t0)
     e2e = b * world * args.steps / e2e_s
+    clocks.__exit__(None, None, None)
 
     # Per-kernel device time of one more (profiled, ordinary-mode) step.
     position = int(sess.read("position")[0])
@@ -302,6 +307,7 @@ def gpu_arm(args, workload, world, rank, local, group):
             "graph_nodes_per_step": nodes,
             "kernel_share": {k: round(t / total, 4) for k, t in sorted(share.items(),
                                                                        key=lambda kv: -kv[1])},
+            "prefill": args.prefill,
             "prefill_setup_s": round(setup_s, 2),
             "clocks": clocks.summary(),
         }
@@ -316,13 +322,19 @@ def main():
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg5")
     parser.add_argument("--requests-per-gpu", type=int)
+    parser.add_argument("--context", type=int, help="override the prompt length (profiling)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--prefill", choices=("graph", "synthetic"), default="graph",
+                        help="graph: teacher-forced prefill through the decode graph; synthetic: "
+                             "zero KV prefix and position at the last prompt token (profiling)")
     args = parser.parse_args()
     if args.warmup < 0 or args.steps < 1:
         parser.error("steps must be positive and warmup nonnegative")
     workload = list(WORKLOADS[args.workload])
     if args.requests_per_gpu:
         workload[0] = args.requests_per_gpu
+    if args.context:
+        workload[6] = args.context
     workload = tuple(workload)
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
