@@ -8,6 +8,7 @@
 // machines without a driver), resolves kernel names against the linked sm_100a library or a
 // loaded CUBIN, and adds asynchronous submission and host-copy entry points.
 #include "ckl_b200.h"
+#include "errors.hpp"
 #include "library.hpp"
 #include "planner.hpp"
 
@@ -59,6 +60,12 @@ template <typename F> int guarded(F &&body) {
     return CKL_RUNTIME_ERROR;
   }
 }
+
+} // namespace
+
+void ckl::setLastError(const std::string &message) { lastError = message; }
+
+namespace {
 
 std::atomic<uint64_t> nextDeviceId{0};
 constexpr const char kLibraryMarker[] = "ckl-b200:library";

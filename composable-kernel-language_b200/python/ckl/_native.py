@@ -79,6 +79,9 @@ _PROTOTYPES = {
     "ckl_time_launches": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_uint64,
                                     C.POINTER(C.c_double)]),
     "ckl_profile_nodes": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_double), C.c_uint64]),
+    "ckl_greedy_head_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                          C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "ckl_profiler_start": (C.c_int, []),
     "ckl_profiler_stop": (C.c_int, []),
     "ckl_runtime_symbols": (C.c_int, [C.POINTER(RuntimeSymbol)]),

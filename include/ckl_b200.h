@@ -176,6 +176,22 @@ int ckl_library_signature(const char *name, char *signature, size_t capacity);
 uint32_t ckl_library_count(void);
 const char *ckl_library_name(uint32_t index);
 
+/* Greedy LM head that allocates nothing (no counterpart in the reference).  For callers
+ * that cannot allocate device memory where they run the head: logits = RMSNorm(x; gain,
+ * eps) @ lm, tokens[b] = first-index argmax of logits[b], history[position * batch + b] =
+ * tokens[b], position += 1, enqueued on `stream` (NULL: the default stream).  x: [batch,
+ * hidden], gain: [hidden], lm: [hidden, vocab], logits: [batch, vocab], tokens: [batch],
+ * history: [capacity, batch], position: [1], all device pointers.  Its scratch (argmax
+ * partials and a completion counter) is a fixed 4 MiB array in the library's device memory:
+ * batch * ceil(vocab / tile width) may not exceed 524288 partials (rejected with
+ * CKL_INVALID_ARGUMENT).  All calls on a device share that array: calls that overlap on the
+ * GPU race.  The first call on a device resolves the array's address (cudaGetSymbolAddress);
+ * make it before any stream capture on that device. */
+int ckl_greedy_head_noalloc(const float *x, const float *gain, const float *lm, float eps,
+                            int64_t batch, int64_t hidden, int64_t vocab, int64_t capacity,
+                            float *logits, int32_t *tokens, int32_t *history, int32_t *position,
+                            void *stream);
+
 /* ---- planning (no GPU needed) ------------------------------------------------------------ */
 /* Inference of the dependency graph, its transitive reduction onto dispatch nodes and the
  * temporary-storage plan of one traced program.  Replaces: buildGraph + attachMemoryPlan
