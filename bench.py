@@ -220,8 +220,11 @@ def gpu_arm(args, workload, world, rank, local, group):
     shape = S.DecoderShape(batch=b, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
                            steps=capacity_steps)
     arrays, rng = S.make_weights(shape, seed)
+    from ckl.workloads.sharding import shard_prompts
+
+    # Prompts for the whole job, sliced: a request's prompt does not depend on the GPU count.
     all_prompts = rng.integers(0, v, (ctx, b * world), dtype=np.int32)
-    prompts = np.ascontiguousarray(all_prompts[:, rank * b:(rank + 1) * b])
+    prompts = shard_prompts(all_prompts, world, rank)
     cache = (l, b, a, shape.capacity, h // a)
     arrays.update(tokens=prompts[0].copy(), position=np.zeros(1, np.int32),
                   history=np.full((shape.capacity, b), -1, np.int32),

@@ -16,12 +16,12 @@ import weakref
 from contextlib import AbstractContextManager
 from pathlib import Path
 
-from . import _native
+from . import _native as _abi
 from .compiler import NVIDIATarget, SUPPORTED_CHIPS
 from .types import BufferSpec, f32, f64, i32, i64
 
 _SCALARS = {f32: ("f", 4), f64: ("d", 8), i32: ("i", 4), i64: ("q", 8)}
-_ARG_KIND = {f32: _native.ARG_F32, f64: _native.ARG_F64, i32: _native.ARG_I32, i64: _native.ARG_I64}
+_ARG_KIND = {f32: _abi.ARG_F32, f64: _abi.ARG_F64, i32: _abi.ARG_I32, i64: _abi.ARG_I64}
 _MODES = {"ordinary": 0, "graph": 1, "capture": 2}
 
 
@@ -91,28 +91,28 @@ class Device(_ContextManager):
     def __init__(self, ordinal: int = 0):
         if type(ordinal) is not int or ordinal < 0:
             raise ValueError("device ordinal must be a nonnegative int")
-        self._lib = _native.load()
+        self._lib = _abi.load()
         if not self._lib.ckl_cuda_available():
             raise RuntimeError("no CUDA device is available to the CKL runtime")
         handle = C.c_void_p()
-        _native.check(self._lib.ckl_device_create(ordinal, C.byref(handle)), "device")
+        _abi.check(self._lib.ckl_device_create(ordinal, C.byref(handle)), "device")
         self._resource = _Handle(handle.value, self._lib.ckl_device_release)
         self.ordinal = ordinal
 
     @property
     def native_library(self) -> Path:
-        return _native.library_path().resolve()
+        return _abi.library_path().resolve()
 
     @property
     def name(self) -> str:
         buffer = C.create_string_buffer(256)
-        _native.check(self._lib.ckl_device_name(self._native_resource.value, buffer, 256))
+        _abi.check(self._lib.ckl_device_name(self._native_resource.value, buffer, 256))
         return buffer.value.decode()
 
     def empty(self, spec: BufferSpec) -> "DeviceBuffer":
         size = _byte_count(spec)
         handle = C.c_void_p()
-        _native.check(self._lib.ckl_buffer_allocate(self._native_resource.value, size,
+        _abi.check(self._lib.ckl_buffer_allocate(self._native_resource.value, size,
                                                     C.byref(handle)), "allocate")
         return DeviceBuffer(self, _Handle(handle.value, self._lib.ckl_buffer_release), spec)
 
@@ -122,7 +122,7 @@ class Device(_ContextManager):
         if type(address) is not int or not 0 < address < (1 << 64) or owner is None:
             raise ValueError("imported storage requires a valid address and a live owner")
         handle = C.c_void_p()
-        _native.check(self._lib.ckl_buffer_import(self._native_resource.value, address, size,
+        _abi.check(self._lib.ckl_buffer_import(self._native_resource.value, address, size,
                                                   C.byref(handle)), "import")
         return DeviceBuffer(self, _Handle(handle.value, self._lib.ckl_buffer_release), spec, owner)
 
@@ -157,7 +157,7 @@ class DeviceBuffer(_ContextManager):
         if byte_offset > self.nbytes or size > self.nbytes - byte_offset:
             raise ValueError("subview exceeds its source buffer")
         handle = C.c_void_p()
-        _native.check(self._lib.ckl_buffer_slice(self._native_resource.value, byte_offset, size,
+        _abi.check(self._lib.ckl_buffer_slice(self._native_resource.value, byte_offset, size,
                                                  C.byref(handle)), "subview")
         return DeviceBuffer(self.device, _Handle(handle.value, self._lib.ckl_buffer_release),
                             spec, self)
@@ -166,17 +166,17 @@ class DeviceBuffer(_ContextManager):
         pointer, nbytes, keep = _host_pointer(source, writable=False)
         if nbytes != self.nbytes:
             raise ValueError("host buffer byte count does not match device storage")
-        _native.check(self._lib.ckl_buffer_copy_from_host(self._native_resource.value, pointer,
+        _abi.check(self._lib.ckl_buffer_copy_from_host(self._native_resource.value, pointer,
                                                           nbytes), "copy_from_host")
 
     def fill_zero(self):
-        _native.check(self._lib.ckl_buffer_fill_zero(self._native_resource.value), "fill_zero")
+        _abi.check(self._lib.ckl_buffer_fill_zero(self._native_resource.value), "fill_zero")
 
     def copy_to_host(self, destination):
         pointer, nbytes, keep = _host_pointer(destination, writable=True)
         if nbytes != self.nbytes:
             raise ValueError("destination must be writable and match device storage byte count")
-        _native.check(self._lib.ckl_buffer_copy_to_host(self._native_resource.value, pointer,
+        _abi.check(self._lib.ckl_buffer_copy_to_host(self._native_resource.value, pointer,
                                                         nbytes), "copy_to_host")
 
 
@@ -188,11 +188,11 @@ class _NativeProgram:
         fallback = None
         if plans.fallback is not None:
             handle = C.c_void_p()
-            _native.check(lib.ckl_program_create_from_plan(plans.fallback.text.encode(), None,
+            _abi.check(lib.ckl_program_create_from_plan(plans.fallback.text.encode(), None,
                                                            C.byref(handle)), "program")
             fallback = _Handle(handle.value, lib.ckl_program_release)
         handle = C.c_void_p()
-        _native.check(lib.ckl_program_create_from_plan(
+        _abi.check(lib.ckl_program_create_from_plan(
             plans.primary.text.encode(), fallback.value if fallback else None, C.byref(handle)),
             "program")
         self.fallback = fallback
@@ -218,7 +218,7 @@ class CompiledProgram(_ContextManager):
 
         self.signature, self.target = program.signature, target
         self.lowered = program
-        self._lib = _native.load()
+        self._lib = _abi.load()
         self.plans = plan_program(program, fuse_pointwise=fuse_pointwise,
                                   fuse_library=fuse_library, reuse_storage=reuse_storage)
         self._resource = _NativeProgram(self._lib, self.plans)
@@ -255,14 +255,14 @@ class CompiledProgram(_ContextManager):
         device = device or (buffers[0].device if buffers else None)
         if device is None:
             raise ValueError("pass a Device for programs without buffer arguments")
-        packed = (_native.Argument * max(len(arguments), 1))()
+        packed = (_abi.Argument * max(len(arguments), 1))()
         for index, (parameter, value) in enumerate(zip(parameters, arguments)):
             if isinstance(parameter.dtype, BufferSpec):
                 if not isinstance(value, DeviceBuffer) or value.spec != parameter.dtype:
                     raise TypeError(f"{parameter.name} requires {parameter.dtype}")
                 if value.device is not device:
                     raise ValueError("all buffers must belong to the selected Device")
-                packed[index].kind = _native.ARG_BUFFER
+                packed[index].kind = _abi.ARG_BUFFER
                 packed[index].buffer = value._native_resource.value
                 continue
             code, width = _SCALARS[parameter.dtype]
@@ -283,7 +283,7 @@ class CompiledProgram(_ContextManager):
             packed[index].kind = _ARG_KIND[parameter.dtype]
             packed[index].bits = int.from_bytes(raw.ljust(8, b"\0"), "little")
         handle = C.c_void_p()
-        _native.check(self._lib.ckl_bind(self._native_resource.handle.value,
+        _abi.check(self._lib.ckl_bind(self._native_resource.handle.value,
                                          device._native_resource.value, len(arguments), packed,
                                          C.byref(handle)), "bind")
         return Invocation(self, device, arguments, _Handle(handle.value,
@@ -322,14 +322,14 @@ class Invocation(_ContextManager):
 
     def run(self, *, graph=False, mode=None, batch_size=1) -> "Invocation":
         execution = self._execution(graph, mode, batch_size)
-        _native.check(self._lib.ckl_run(self._native_resource.value, execution, batch_size), "run")
+        _abi.check(self._lib.ckl_run(self._native_resource.value, execution, batch_size), "run")
         return self
 
     @property
     def node_count(self) -> int:
         """Kernel nodes of one program execution (after fusion or the overlap fallback)."""
         out = C.c_uint64()
-        _native.check(self._lib.ckl_node_count(self._native_resource.value, C.byref(out)))
+        _abi.check(self._lib.ckl_node_count(self._native_resource.value, C.byref(out)))
         return int(out.value)
 
     @property
@@ -337,7 +337,7 @@ class Invocation(_ContextManager):
         names = []
         for i in range(self.node_count):
             buffer = C.create_string_buffer(128)
-            _native.check(self._lib.ckl_node_name(self._native_resource.value, i, buffer, 128))
+            _abi.check(self._lib.ckl_node_name(self._native_resource.value, i, buffer, 128))
             names.append(buffer.value.decode())
         return names
 
@@ -347,7 +347,7 @@ class Invocation(_ContextManager):
             raise ValueError("iterations must be a positive 64-bit count")
         execution = self._execution(graph, mode, batch_size)
         out = (C.c_double * 3)()
-        _native.check(self._lib.ckl_benchmark(self._native_resource.value, execution, iterations,
+        _abi.check(self._lib.ckl_benchmark(self._native_resource.value, execution, iterations,
                                               batch_size, out), "benchmark")
         return {"stream_us": out[0], "wall_us": out[1], "graph_setup_ms": out[2]}
 
@@ -355,20 +355,20 @@ class Invocation(_ContextManager):
     def launch(self, *, graph=False, mode=None, batch_size=1) -> None:
         """Submit without waiting; pair with :meth:`synchronize`."""
         execution = self._execution(graph, mode, batch_size)
-        _native.check(self._lib.ckl_launch(self._native_resource.value, execution, batch_size),
+        _abi.check(self._lib.ckl_launch(self._native_resource.value, execution, batch_size),
                       "launch")
 
     def synchronize(self) -> None:
-        _native.check(self._lib.ckl_synchronize(self._native_resource.value), "synchronize")
+        _abi.check(self._lib.ckl_synchronize(self._native_resource.value), "synchronize")
 
     def copy_in_async(self, buffer: DeviceBuffer, source_pointer: int, nbytes: int) -> None:
         """Enqueue a host-to-device copy from page-locked memory on the invocation stream."""
-        _native.check(self._lib.ckl_copy_in_async(self._native_resource.value,
+        _abi.check(self._lib.ckl_copy_in_async(self._native_resource.value,
                                                   buffer._native_resource.value, source_pointer,
                                                   nbytes), "copy_in_async")
 
     def copy_out_async(self, buffer: DeviceBuffer, destination_pointer: int, nbytes: int) -> None:
-        _native.check(self._lib.ckl_copy_out_async(self._native_resource.value,
+        _abi.check(self._lib.ckl_copy_out_async(self._native_resource.value,
                                                    buffer._native_resource.value,
                                                    destination_pointer, nbytes), "copy_out_async")
 
@@ -376,14 +376,14 @@ class Invocation(_ContextManager):
         """Per-node device milliseconds over ``iterations`` ordinary executions (state advances)."""
         count = self.node_count
         out = (C.c_double * count)()
-        _native.check(self._lib.ckl_profile_nodes(self._native_resource.value, iterations, out,
+        _abi.check(self._lib.ckl_profile_nodes(self._native_resource.value, iterations, out,
                                                   count), "profile")
         return list(out)
 
     def time_launches(self, steps: int, *, mode="graph", batch_size=1) -> float:
         """Device milliseconds of ``steps`` back-to-back submissions (CUDA events)."""
         out = C.c_double()
-        _native.check(self._lib.ckl_time_launches(self._native_resource.value, _MODES[mode],
+        _abi.check(self._lib.ckl_time_launches(self._native_resource.value, _MODES[mode],
                                                   batch_size, steps, C.byref(out)), "timing")
         return out.value
 
@@ -392,9 +392,9 @@ class PinnedHostBuffer:
     """Page-locked host memory for asynchronous copies."""
 
     def __init__(self, nbytes: int):
-        self._lib = _native.load()
+        self._lib = _abi.load()
         pointer = C.c_void_p()
-        _native.check(self._lib.ckl_host_alloc(nbytes, C.byref(pointer)), "pinned allocation")
+        _abi.check(self._lib.ckl_host_alloc(nbytes, C.byref(pointer)), "pinned allocation")
         self.pointer, self.nbytes = pointer.value, nbytes
         self._handle = _Handle(pointer.value, self._lib.ckl_host_free)
 
@@ -403,4 +403,37 @@ class PinnedHostBuffer:
 
 
 def cuda_available() -> bool:
-    return bool(_native.load().ckl_cuda_available())
+    return bool(_abi.load().ckl_cuda_available())
+
+
+class _NativeModule:
+    """The subset of the reference's ``_ckl_native`` module that harness code calls."""
+
+    def __init__(self):
+        self._lib = _abi.load()
+        self.__file__ = str(_abi.library_path())
+        self.has_cuda_runtime = True
+
+    def cuda_available(self) -> bool:
+        return bool(self._lib.ckl_cuda_available())
+
+    def profiler_start(self) -> None:
+        _abi.check(self._lib.ckl_profiler_start(), "profiler_start")
+
+    def profiler_stop(self) -> None:
+        _abi.check(self._lib.ckl_profiler_stop(), "profiler_stop")
+
+
+_MODULE = None
+
+
+def _native_module():
+    global _MODULE
+    if _MODULE is None:
+        _MODULE = _NativeModule()
+    return _MODULE
+
+
+def _native():
+    """The reference exposes its native module as ``ckl.cuda._native()`` (cuda.py:31-62)."""
+    return _native_module()
