@@ -233,7 +233,7 @@ def gpu_arm(args, workload, world, rank, local, group):
     device = ckl.Device(local)
     t_setup = time.perf_counter()
     sess = S.DecoderSession(device, arrays, epsilon=eps, attention_scale=(h // a) ** -0.5,
-                            tails=False)
+                            tails=False, tensor_cores=args.projections == "tensor")
     if args.prefill == "graph":
         sess.prefill(prompts)
     else:
@@ -311,6 +311,7 @@ def gpu_arm(args, workload, world, rank, local, group):
             "kernel_share": {k: round(t / total, 4) for k, t in sorted(share.items(),
                                                                        key=lambda kv: -kv[1])},
             "prefill": args.prefill,
+            "projections": args.projections,
             "prefill_setup_s": round(setup_s, 2),
             "clocks": clocks.summary(),
         }
@@ -327,6 +328,8 @@ def main():
     parser.add_argument("--requests-per-gpu", type=int)
     parser.add_argument("--context", type=int, help="override the prompt length (profiling)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--projections", choices=("tensor", "ffma"), default="tensor",
+                        help="batched projections on tcgen05 tensor cores (3xTF32) or FFMA")
     parser.add_argument("--prefill", choices=("graph", "synthetic"), default="graph",
                         help="graph: teacher-forced prefill through the decode graph; synthetic: "
                              "zero KV prefix and position at the last prompt token (profiling)")

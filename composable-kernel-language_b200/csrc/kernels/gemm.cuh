@@ -47,9 +47,10 @@ using Small = Config<16, 64, 16, 2, 4>;    // 128 threads, M <= 16
 using Medium = Config<64, 64, 16, 4, 4>;   // 256 threads
 using Large = Config<128, 128, 8, 8, 8>;   // 256 threads, M >= 256 and wide N
 
-// Tile configuration for a specialization: 0 small, 1 medium, 2 large.
+// Tile configuration for a specialization: 0 small, 1 medium, 2 large.  `config` 1-3 forces
+// one of them; 0 (automatic) and 5 (FFMA only) choose by shape.
 inline int chooseConfig(const GemmSpec &s) {
-  if (s.config > 0)
+  if (s.config > 0 && s.config <= 3)
     return int(s.config - 1);
   if (s.M <= 16)
     return 0;

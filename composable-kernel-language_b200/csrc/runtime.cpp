@@ -1043,7 +1043,8 @@ void ckl_kernel(void *frame, const char *name, uint64_t gx, uint64_t gy, uint64_
       if (!fn.entry)
         throw std::invalid_argument(std::string("unknown library kernel: ") + name);
       fn.address = fn.entry->function;
-      if (shared > 48 * 1024) {
+      // Entries that pick a configuration at commit raise the limit for the one they pick.
+      if (shared > 48 * 1024 && !fn.entry->select) {
         f.device->current();
         check(cudaFuncSetAttribute(fn.address, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(shared)),

@@ -89,6 +89,7 @@ _PROTOTYPES = {
                                        C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
                                        C.POINTER(C.c_uint32)]),
     "ckl_library_signature": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t]),
+    "ckl_library_faults": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
     "ckl_library_count": (C.c_uint32, []),
     "ckl_library_name": (C.c_char_p, [C.c_uint32]),
     "ckl_graph_plan_create": (C.c_int, [C.c_uint32, C.POINTER(GraphNode), C.c_uint32,

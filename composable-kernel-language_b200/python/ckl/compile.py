@@ -200,6 +200,9 @@ _LAYER = ("rms_stats", "rms_apply", "linear", "linear", "linear", "rope", "rope"
           "rms_apply", "linear", "linear", "silu", "multiply", "linear", "add")
 _HEAD = ("rms_stats", "rms_apply", "linear", "greedy", "advance")
 _ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
+# Projections with at least one 128-row tile of requests run on tcgen05 tensor cores (GemmSpec
+# config 0); config 5 keeps every projection on FFMA.
+_TENSOR_CORE_ROWS = 128
 
 
 class _NoMatch(Exception):
@@ -210,7 +213,7 @@ def _short(node: Node) -> str:
     return node.name.rsplit(".", 1)[-1] if node.name.startswith("ckl.decoder.") else node.name
 
 
-def _fuse_decoder(events, resources: list) -> bool:
+def _fuse_decoder(events, resources: list, tensor_cores: bool = True) -> bool:
     dispatches = [e.node for e in events if e.kind == "dispatch"]
     names = [_short(n) for n in dispatches]
     if len(names) < 1 + len(_LAYER) + len(_HEAD) or (len(names) - 1 - len(_HEAD)) % len(_LAYER):
@@ -220,7 +223,8 @@ def _fuse_decoder(events, resources: list) -> bool:
     if tuple(names) != expected:
         return False
     try:
-        new_nodes, eliminated, added = _decoder_nodes(dispatches, layers, resources)
+        new_nodes, eliminated, added = _decoder_nodes(dispatches, layers, resources,
+                                                      0 if tensor_cores else 5)
     except _NoMatch:
         return False
     users = _resource_users(events)
@@ -248,7 +252,7 @@ def _fuse_decoder(events, resources: list) -> bool:
     return True
 
 
-def _decoder_nodes(dispatches, layers, resources):
+def _decoder_nodes(dispatches, layers, resources, config=0):
     def op(node, i):
         return node.source.operands[i]
 
@@ -269,7 +273,7 @@ def _decoder_nodes(dispatches, layers, resources):
             raise _NoMatch
 
     def gemm_spec(M, K, N, layers_, layer, A=0, D=0, T=0, tiles=0):
-        return pack(M, K, N, layers_, layer, A, D, T, tiles, 0)
+        return pack(M, K, N, layers_, layer, A, D, T, tiles, config)
 
     embedding = dispatches[0]
     x = res(embedding, 2)
@@ -373,17 +377,32 @@ def _decoder_nodes(dispatches, layers, resources):
         new_nodes.append(node("ckl.fused.norm_linear", [R(residual), R(g2), R(wu), R(up), eps2],
                               gemm_spec(B, Cdim, F, shape(wu)[0], layer),
                               [residual, g2, wu], [(up, WRITE, "whole")], "up projection"))
-        new_nodes.append(node("ckl.fused.swiglu_linear_residual",
-                              [R(gate), R(up), R(wd), R(residual), R(next_x)],
-                              gemm_spec(B, F, Cdim, shape(wd)[0], layer),
-                              [gate, up, wd, residual], [(next_x, WRITE, "whole")],
-                              "down projection"))
-        for rid, users in ((inv, (d[0], d[1])), (normed, (d[1], d[2], d[3], d[4])),
+        eliminated_here = [(inv, (d[0], d[1])), (normed, (d[1], d[2], d[3], d[4])),
                            (q, (d[2], d[5])), (k, (d[3], d[6])), (v, (d[4], d[7])),
                            (kr, (d[6], d[7])), (scores, (d[8], d[9])), (probs, (d[9], d[10])),
                            (projected, (d[11], d[12])), (inv2, (d[13], d[14])),
                            (normed2, (d[14], d[15], d[16])), (activated, (d[17], d[18])),
-                           (product, (d[18], d[19])), (down, (d[19], d[20]))):
+                           (down, (d[19], d[20]))]
+        if config == 0 and B >= _TENSOR_CORE_ROWS:
+            # Tensor-core down projection: the activation is materialised once (in the
+            # program's own `product` temporary) and the GEMM takes it as a plain operand.
+            if shape(product) != (B, F):
+                raise _NoMatch
+            new_nodes.append(node("ckl.fused.swiglu", [R(gate), R(up), R(product)], pack(B, F),
+                                  [gate, up], [(product, WRITE, "whole")], "swiglu"))
+            new_nodes.append(node("ckl.fused.linear_residual",
+                                  [R(product), R(wd), R(residual), R(next_x)],
+                                  gemm_spec(B, F, Cdim, shape(wd)[0], layer),
+                                  [product, wd, residual], [(next_x, WRITE, "whole")],
+                                  "down projection"))
+        else:
+            new_nodes.append(node("ckl.fused.swiglu_linear_residual",
+                                  [R(gate), R(up), R(wd), R(residual), R(next_x)],
+                                  gemm_spec(B, F, Cdim, shape(wd)[0], layer),
+                                  [gate, up, wd, residual], [(next_x, WRITE, "whole")],
+                                  "down projection"))
+            eliminated_here.append((product, (d[18], d[19])))
+        for rid, users in eliminated_here:
             eliminated[rid] = list(users)
         x = next_x
     h = dispatches[1 + layers * len(_LAYER):]
@@ -591,7 +610,7 @@ def _initial_events(lowered: LoweredProgram):
 
 
 def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library: bool,
-                 reuse_storage: bool) -> CompiledPlans:
+                 reuse_storage: bool, tensor_cores: bool = True) -> CompiledPlans:
     events, resources = _initial_events(lowered)
     if not any(e.kind == "dispatch" for e in events):
         raise CompilationError(("ckl-b200", "plan"), "program launches no kernels")
@@ -602,7 +621,7 @@ def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library:
     if fuse_pointwise:
         fused |= _fuse_pointwise(events, resources)
     if fuse_library:
-        fused |= _fuse_decoder(events, resources)
+        fused |= _fuse_decoder(events, resources, tensor_cores)
     plans = CompiledPlans(baseline)
     if fused:
         primary = _plan(lowered, events, resources, reuse_storage=reuse_storage,

@@ -128,12 +128,17 @@ class LoweredProgram:
         plan_program(self, fuse_pointwise=False, fuse_library=False, reuse_storage=True)
         return self
 
-    def compile(self, *, target, fuse_pointwise=True, reuse_storage=True, fuse_library=True):
-        """Select sm_100a kernels, infer the dependency graph and plan temporary storage."""
+    def compile(self, *, target, fuse_pointwise=True, reuse_storage=True, fuse_library=True,
+                tensor_cores=True):
+        """Select sm_100a kernels, infer the dependency graph and plan temporary storage.
+
+        ``tensor_cores=False`` keeps batched fused projections on FFMA instead of tcgen05.
+        """
         from ..cuda import CompiledProgram
 
         return CompiledProgram(self, target, fuse_pointwise=fuse_pointwise,
-                               reuse_storage=reuse_storage, fuse_library=fuse_library)
+                               reuse_storage=reuse_storage, fuse_library=fuse_library,
+                               tensor_cores=tensor_cores)
 
 
 @dataclass(frozen=True)

@@ -90,6 +90,7 @@ class DecoderSession:
 
     def __init__(self, device: ckl.Device, arrays: dict, *, epsilon: float, attention_scale: float,
                  fuse_library: bool = True, reuse_storage: bool = True, tails: bool = True,
+                 tensor_cores: bool = True,
                  shared_weights: "DecoderSession | None" = None):
         self.device = device
         self.owners, self.buffers, self.shapes = {}, {}, {}
@@ -121,7 +122,8 @@ class DecoderSession:
         signature.update(epsilon=ckl.f32, attention_scale=ckl.f32)
         self.lowered = decoder.decode.lower(signature=signature)
         self.program = self.lowered.compile(target=ckl.NVIDIATarget("sm_100a"),
-                                            fuse_library=fuse_library, reuse_storage=reuse_storage)
+                                            fuse_library=fuse_library, reuse_storage=reuse_storage,
+                                            tensor_cores=tensor_cores)
         arguments = [self.buffers[name] for name in decoder.ARGUMENTS[:-2]]
         self.invocation = self.program.bind(*arguments, float(epsilon), float(attention_scale))
 

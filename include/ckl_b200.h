@@ -173,6 +173,10 @@ int ckl_runtime_symbols(ckl_runtime_symbol out[8]);
 int ckl_library_geometry(const char *name, const void *spec, uint64_t spec_bytes,
                          uint32_t grid[3], uint32_t block[3], uint32_t *shared_bytes);
 int ckl_library_signature(const char *name, char *signature, size_t capacity);
+/* Fault word of the kernel library on the current device: bit 0 is set when a tensor-core
+ * kernel gave up a bounded wait (it then skipped its work instead of hanging).  `reset`
+ * clears the word after reading it.  No reference counterpart. */
+int ckl_library_faults(uint32_t *out, int reset);
 uint32_t ckl_library_count(void);
 const char *ckl_library_name(uint32_t index);
 

@@ -1,0 +1,51 @@
+"""Batched projections on tcgen05 tensor cores (3xTF32) match the FP32 oracle.
+
+Fused decoder kernels switch to the tensor-core path at 128 or more requests.  These cases
+cover full and ragged row tiles, K not a multiple of the 32-wide slice, N not a multiple of
+the column tile, every epilogue (RoPE, KV append, residual, SwiGLU prologue, argmax head), and
+check that no kernel reported an expired wait.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import ckl
+from ckl import _native
+from ckl.workloads import session as S
+from oracle import decoder as ref
+from test_gpu_decoder import verify
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def device():
+    return ckl.Device()
+
+
+def faults():
+    value = C.c_uint32()
+    assert _native.load().ckl_library_faults(C.byref(value), 1) == 0
+    return value.value
+
+
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", [
+    (128, 256, 4, 2, 512, 1024, 3),    # one full row tile, head dim 64
+    (300, 128, 2, 1, 96, 1000, 3),     # ragged rows, K = 96, N tails
+    (512, 1024, 16, 1, 4096, 4000, 2), # cfg5 layer shapes, 4 row tiles (smaller vocab)
+    (128, 1024, 16, 4, 4096, 32000, 2),  # cfg5 depth and vocabulary
+])
+def test_tensor_core_decoder_matches_oracle(device, batch, hidden, heads, layers, ffn, vocab, steps):
+    faults()
+    config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
+                        vocab=vocab, context=8, steps=steps)
+    initial, _ = ref.make_inputs(config, 21, eps=1e-6)
+    expected = ref.expected(initial, config, steps, eps=1e-6)
+    session = S.DecoderSession(device, initial, epsilon=1e-6,
+                               attention_scale=config.head_dim ** -0.5)
+    session.step(steps)
+    verify(session, initial, expected, config)
+    assert faults() == 0
