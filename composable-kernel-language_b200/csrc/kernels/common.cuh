@@ -94,8 +94,9 @@ struct GemmSpec {
   int64_t M, K, N, layers, layer, A, D, T, tiles, config;
 };
 // Flash-decoding attention over cache[L, B, A, T, D] at positions 0..position[0].
+// `panel` 1 writes the context as a split tensor-core operand (panel.cuh) instead of [B, A*D].
 struct AttentionSpec {
-  int64_t B, A, T, D, L, layer, splits, chunk;
+  int64_t B, A, T, D, L, layer, splits, chunk, panel;
 };
 // Greedy combine of per-tile argmax partials [B, tiles] of (value, index).
 struct CombineSpec {

@@ -1,21 +1,22 @@
 // Fused decode-step kernels for the decoder program (benchmarks/decoder/workloads.py:191-254).
 //
-// One layer of the reference runs 21 dependent launches.  Here it is six graph nodes in five
-// dependency levels:
+// One layer of the reference runs 21 dependent launches.  With FFMA projections (fewer than
+// 128 requests) it is eight graph nodes in five dependency levels:
 //   q: RMSNorm -> x @ wq -> RoPE                       (norm_linear_rope)
 //   k: RMSNorm -> x @ wk -> RoPE -> append to kc at p  (norm_linear_rope_append)
 //   v: RMSNorm -> x @ wv -> append to vc at p          (norm_linear_append)
 //   attention over kc/vc[0..p] (flash decoding; scores and probabilities never stored)
 //   residual = x + context @ wo                        (linear_residual)
 //   gate, up: RMSNorm -> x @ wg / wu                   (norm_linear, two concurrent nodes)
-//   next_x = residual + (silu(gate) * up) @ wd         (swiglu_linear_residual; on the
-//            tensor-core path: swiglu, then linear_residual)
+//   next_x = residual + (silu(gate) * up) @ wd         (swiglu_linear_residual)
 // and the head is RMSNorm -> x @ lm with per-tile argmax partials, followed by a combine
-// that writes tokens and history and advances the position.
+// that writes tokens and history and advances the position.  Batches of 128 or more requests
+// run the projections on the tensor cores instead (decoder_tc.cu); attention then writes its
+// context as a split operand panel (AttentionSpec::panel).
 #include "ckl_b200.h"
 #include "common.cuh"
 #include "gemm.cuh"
-#include "tcgemm.cuh"
+#include "panel.cuh"
 
 namespace ckl::kernels {
 namespace {
@@ -100,161 +101,23 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   gemm::body<Cfg, gemm::kRms, gemm::kArgmax>(p);
 }
 
-// ---- tensor-core (tcgen05, 3xTF32) variants for batched projections ------------------
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    normLinearTc(const float *x, const float *gain, const float *w, float *dst, float eps,
-                 GemmSpec s) {
-  Params p;
-  p.a = x, p.gain = gain, p.w = w, p.out = dst, p.eps = eps, p.s = s;
-  tc::run<BN, gemm::kRms, gemm::kStore>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    normLinearRopeTc(const float *x, const float *gain, const float *w, const float *table,
-                     const int *position, float *dst, float eps, GemmSpec s) {
-  Params p;
-  p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = dst;
-  p.eps = eps, p.s = s;
-  tc::run<BN, gemm::kRms, gemm::kRope>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    normLinearRopeAppendTc(const float *x, const float *gain, const float *w, const float *table,
-                           const int *position, float *cache, float eps, GemmSpec s) {
-  Params p;
-  p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = cache;
-  p.eps = eps, p.s = s;
-  tc::run<BN, gemm::kRms, gemm::kRopeAppend>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    normLinearAppendTc(const float *x, const float *gain, const float *w, const int *position,
-                       float *cache, float eps, GemmSpec s) {
-  Params p;
-  p.a = x, p.gain = gain, p.w = w, p.position = position, p.out = cache, p.eps = eps, p.s = s;
-  tc::run<BN, gemm::kRms, gemm::kAppend>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    linearResidualTc(const float *x, const float *w, const float *residual, float *dst,
-                     GemmSpec s) {
-  Params p;
-  p.a = x, p.w = w, p.residual = residual, p.out = dst, p.s = s;
-  tc::run<BN, gemm::kPlain, gemm::kResidual>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    normLinearArgmaxTc(const float *x, const float *gain, const float *w, float *logits,
-                       float2 *partials, float eps, GemmSpec s) {
-  Params p;
-  p.a = x, p.gain = gain, p.w = w, p.out = logits, p.partials = partials, p.eps = eps, p.s = s;
-  tc::run<BN, gemm::kRms, gemm::kArgmax>(p);
-}
-
-// ---- SwiGLU activation (workloads.py:157-167), computed once per element -----------------
-// The tensor-core path materialises silu(gate) * up and runs the down projection as a plain
-// GEMM: recomputing the activation in every column tile's prologue would repeat each
-// exponential N / BN times.  Same formula and rounding as the unfused silu + multiply pair.
-constexpr int kSwiGluThreads = 256;
-
-__device__ __forceinline__ float swiglu(float g, float u) {
-  return __fmul_rn(g / (1.0f + expf(-g)), u);
-}
-
-__global__ void __launch_bounds__(kSwiGluThreads)
-    swigluKernel(const float *gate, const float *up, float *dst, RowsSpec s) {
-  const int64_t count = s.B * s.C;
-  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (aligned16(gate) && aligned16(up) && aligned16(dst)) {
-    const int64_t vectors = count / 4;
-    for (int64_t v = i; v < vectors; v += stride) {
-      const float4 g = __ldcs(reinterpret_cast<const float4 *>(gate) + v);
-      const float4 u = __ldcs(reinterpret_cast<const float4 *>(up) + v);
-      reinterpret_cast<float4 *>(dst)[v] =
-          make_float4(swiglu(g.x, u.x), swiglu(g.y, u.y), swiglu(g.z, u.z), swiglu(g.w, u.w));
-    }
-    for (int64_t e = vectors * 4 + i; e < count; e += stride)
-      dst[e] = swiglu(gate[e], up[e]);
-  } else {
-    for (int64_t e = i; e < count; e += stride)
-      dst[e] = swiglu(gate[e], up[e]);
-  }
-}
-
-bool swigluGeometry(const void *spec, std::size_t, library::Geometry *g) {
-  const auto &s = specOf<RowsSpec>(spec);
-  if (s.B <= 0 || s.C <= 0)
-    return false;
-  const int64_t wanted = ceilDiv(s.B * s.C, int64_t(kSwiGluThreads) * 4 * 4);
-  const int64_t cap = 148 * 8 * 4;
-  g->grid[0] = unsigned(wanted > cap ? cap : wanted);
-  g->block[0] = kSwiGluThreads;
-  return true;
-}
-
-// Tensor cores serve batched projections (at least one full 128-row tile of requests);
-// smaller batches stay on FFMA.  `config` 4 forces tensor cores, 1-3 force an FFMA tile.
-bool useTensorCores(const GemmSpec &s) { return s.config == 0 ? s.M >= tc::BM : s.config == 4; }
-
-bool fusedGeometry(const GemmSpec &s, library::Geometry *g) {
-  if (!useTensorCores(s))
-    return gemm::geometry(s, g);
-  if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
-    return false;
-  const int width = tc::chooseWidth(s);
-  g->grid[0] = ceilDiv(s.N, width);
-  g->grid[1] = ceilDiv(s.M, tc::BM);
-  g->block[0] = tc::kThreads;
-  g->sharedBytes = unsigned(tc::sharedBytes(width));
-  return g->grid[1] <= 65535;
-}
-
 bool gemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
   return gemm::geometry(specOf<GemmSpec>(spec), g);
-}
-
-bool fusedGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
-  return fusedGeometry(specOf<GemmSpec>(spec), g);
 }
 
 bool ropeGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<GemmSpec>(spec);
   if (s.D <= 0 || s.D % 2 || s.N % s.D || s.T <= 0)
     return false;
-  return fusedGeometry(s, g);
+  return gemm::geometry(s, g);
 }
 
 bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<GemmSpec>(spec);
   if (s.D <= 0 || s.D % 2 || s.N != s.A * s.D || s.T <= 0)
     return false;
-  return fusedGeometry(s, g);
+  return gemm::geometry(s, g);
 }
-
-#define CKL_FUSED_SELECT(fn, tcfn)                                                             \
-  [](const void *spec) -> const void * {                                                       \
-    const GemmSpec &s = specOf<GemmSpec>(spec);                                                \
-    if (useTensorCores(s)) {                                                                   \
-      switch (tc::chooseWidth(s)) {                                                            \
-      case 128: return reinterpret_cast<const void *>(&tcfn<128>);                             \
-      case 64: return reinterpret_cast<const void *>(&tcfn<64>);                               \
-      default: return reinterpret_cast<const void *>(&tcfn<32>);                               \
-      }                                                                                        \
-    }                                                                                          \
-    switch (gemm::chooseConfig(s)) {                                                           \
-    case 0: return reinterpret_cast<const void *>(&fn<Small>);                                 \
-    case 1: return reinterpret_cast<const void *>(&fn<Medium>);                                \
-    case 2: return reinterpret_cast<const void *>(&fn<Large>);                                 \
-    default: return nullptr;                                                                   \
-    }                                                                                          \
-  }
 
 #define CKL_GEMM_SELECT(fn)                                                                    \
   [](const void *spec) -> const void * {                                                       \
@@ -383,7 +246,10 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
       out.z = total.acc.z / total.l;
       out.w = total.acc.w / total.l;
     }
-    *reinterpret_cast<float4 *>(ctx + b * C + h * D + 4 * sub) = out;
+    if (s.panel)
+      panel::store4(ctx, b, h * D + 4 * sub, C, out); // split operand of the o projection
+    else
+      *reinterpret_cast<float4 *>(ctx + b * C + h * D + 4 * sub) = out;
   }
 }
 
@@ -468,33 +334,31 @@ bool combineGeometry(const void *spec, std::size_t, library::Geometry *g) {
 CKL_REGISTER_KERNEL("ckl.decoder.linear", reinterpret_cast<const void *>(&linearKernel<Medium>),
                     "PPPS", sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(linearKernel));
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear", reinterpret_cast<const void *>(&normLinearKernel<Medium>),
-                    "PPPPFS", sizeof(GemmSpec), fusedGemmGeometry,
-                    CKL_FUSED_SELECT(normLinearKernel, normLinearTc));
+                    "PPPPFS", sizeof(GemmSpec), gemmGeometry,
+                    CKL_GEMM_SELECT(normLinearKernel));
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_rope",
                     reinterpret_cast<const void *>(&normLinearRopeKernel<Medium>), "PPPPPPFS",
                     sizeof(GemmSpec), ropeGemmGeometry,
-                    CKL_FUSED_SELECT(normLinearRopeKernel, normLinearRopeTc));
+                    CKL_GEMM_SELECT(normLinearRopeKernel));
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_rope_append",
                     reinterpret_cast<const void *>(&normLinearRopeAppendKernel<Medium>), "PPPPPPFS",
                     sizeof(GemmSpec), appendGemmGeometry,
-                    CKL_FUSED_SELECT(normLinearRopeAppendKernel, normLinearRopeAppendTc));
+                    CKL_GEMM_SELECT(normLinearRopeAppendKernel));
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_append",
                     reinterpret_cast<const void *>(&normLinearAppendKernel<Medium>), "PPPPPFS",
                     sizeof(GemmSpec), appendGemmGeometry,
-                    CKL_FUSED_SELECT(normLinearAppendKernel, normLinearAppendTc));
+                    CKL_GEMM_SELECT(normLinearAppendKernel));
 CKL_REGISTER_KERNEL("ckl.fused.linear_residual",
                     reinterpret_cast<const void *>(&linearResidualKernel<Medium>), "PPPPS",
-                    sizeof(GemmSpec), fusedGemmGeometry,
-                    CKL_FUSED_SELECT(linearResidualKernel, linearResidualTc));
+                    sizeof(GemmSpec), gemmGeometry,
+                    CKL_GEMM_SELECT(linearResidualKernel));
 CKL_REGISTER_KERNEL("ckl.fused.swiglu_linear_residual",
                     reinterpret_cast<const void *>(&swigluLinearResidualKernel<Medium>), "PPPPPS",
                     sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(swigluLinearResidualKernel));
-CKL_REGISTER_KERNEL("ckl.fused.swiglu", reinterpret_cast<const void *>(&swigluKernel), "PPPS",
-                    sizeof(RowsSpec), swigluGeometry, nullptr);
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_argmax",
                     reinterpret_cast<const void *>(&normLinearArgmaxKernel<Medium>), "PPPPPFS",
-                    sizeof(GemmSpec), fusedGemmGeometry,
-                    CKL_FUSED_SELECT(normLinearArgmaxKernel, normLinearArgmaxTc));
+                    sizeof(GemmSpec), gemmGeometry,
+                    CKL_GEMM_SELECT(normLinearArgmaxKernel));
 CKL_REGISTER_KERNEL("ckl.fused.attention", reinterpret_cast<const void *>(&attentionKernel<64>),
                     "PPPPPFS", sizeof(AttentionSpec), attentionGeometry, attentionSelect);
 CKL_REGISTER_KERNEL("ckl.fused.greedy_combine",
@@ -502,19 +366,3 @@ CKL_REGISTER_KERNEL("ckl.fused.greedy_combine",
                     sizeof(CombineSpec), combineGeometry, nullptr);
 
 } // namespace ckl::kernels
-
-extern "C" int ckl_library_faults(uint32_t *out, int reset) {
-  unsigned value = 0;
-  cudaError_t status = cudaMemcpyFromSymbol(&value, ckl::kernels::tc::g_libraryFaults, sizeof(value));
-  if (status == cudaSuccess && reset) {
-    const unsigned zero = 0;
-    status = cudaMemcpyToSymbol(ckl::kernels::tc::g_libraryFaults, &zero, sizeof(zero));
-  }
-  if (status != cudaSuccess) {
-    cudaGetLastError();
-    return CKL_RUNTIME_ERROR;
-  }
-  if (out)
-    *out = value;
-  return CKL_OK;
-}

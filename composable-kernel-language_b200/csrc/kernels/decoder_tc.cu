@@ -1,0 +1,254 @@
+// Tensor-core path of the decoder's batched projections (benchmarks/decoder/workloads.py:191-254
+// with 128 or more requests).
+//
+// Each projection's activation operand is split into a TF32 hi/lo panel once, by the kernel
+// that produces it, and every projection then runs the tcgen05 3xTF32 kernel (tcgemm.cuh) on
+// that panel with the layer's FP32 weights:
+//   rms_panel:    panel = split(RMSNorm(x) * gain)        (feeds q/k/v, gate/up, lm head)
+//   swiglu_panel: panel = split(silu(gate) * up)          (feeds the down projection)
+//   attention writes its context rows as a panel           (feeds the o projection)
+//   panel_linear{,_rope,_rope_append,_append,_residual,_argmax}: the projections with the same
+//   fused epilogues as the FFMA kernels.
+// The normalised and activated values are rounded exactly as in the FFMA kernels
+// (x * rsqrt(mean(x^2) + eps) * gain, silu(g) * u) before the split.
+#include "ckl_b200.h"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "panel.cuh"
+#include "tcgemm.cuh"
+
+namespace ckl::kernels {
+namespace {
+
+using gemm::Params;
+
+// ---- panel producers -----------------------------------------------------------------------
+constexpr int kPanelWarps = 8;
+
+// One warp per row: sum of squares, then the normalised row split into the panel.  Columns
+// between K and the next multiple of 32 are written as zeros.
+__global__ void __launch_bounds__(kPanelWarps *kWarp)
+    rmsPanelKernel(const float *x, const float *gain, float *out, float eps, RmsApplySpec s) {
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int64_t m = int64_t(blockIdx.x) * kPanelWarps + warp;
+  if (m >= s.B)
+    return;
+  const int64_t K = s.C;
+  const float *row = x + m * K;
+  const float *g = gain + s.layer * K;
+  const bool vec = K % 4 == 0 && aligned16(row) && aligned16(g);
+  float total = 0.f;
+  if (vec) {
+    for (int64_t q = lane; q < K / 4; q += kWarp) {
+      const float4 v = reinterpret_cast<const float4 *>(row)[q];
+      total += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  } else {
+    for (int64_t k = lane; k < K; k += kWarp)
+      total += row[k] * row[k];
+  }
+  total = warpSum(total);
+  const float inv = rsqrtf(total / float(K) + eps);
+  const int64_t padded = panel::slices(K) * panel::kSlice;
+  for (int64_t k = 4 * int64_t(lane); k < padded; k += 4 * kWarp) {
+    float4 v;
+    if (vec && k < K) {
+      const float4 a = reinterpret_cast<const float4 *>(row)[k / 4];
+      const float4 b = reinterpret_cast<const float4 *>(g)[k / 4];
+      v = make_float4(__fmul_rn(__fmul_rn(a.x, inv), b.x), __fmul_rn(__fmul_rn(a.y, inv), b.y),
+                      __fmul_rn(__fmul_rn(a.z, inv), b.z), __fmul_rn(__fmul_rn(a.w, inv), b.w));
+    } else {
+      float *lanes = &v.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        lanes[j] = k + j < K ? __fmul_rn(__fmul_rn(row[k + j], inv), g[k + j]) : 0.f;
+    }
+    panel::store4(out, m, k, K, v);
+  }
+}
+
+bool rmsPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<RmsApplySpec>(spec);
+  if (s.B <= 0 || s.C <= 0 || s.layer < 0 || s.layer >= s.L)
+    return false;
+  g->grid[0] = ceilDiv(s.B, kPanelWarps);
+  g->block[0] = kPanelWarps * kWarp;
+  return true;
+}
+
+__device__ __forceinline__ float swiglu(float g, float u) {
+  return __fmul_rn(g / (1.0f + expf(-g)), u);
+}
+
+// One thread per four consecutive columns of a row (rows [B], columns padded to 32).
+__global__ void __launch_bounds__(256)
+    swigluPanelKernel(const float *gate, const float *up, float *out, RowsSpec s) {
+  const int64_t K = s.C;
+  const int64_t quads = panel::slices(K) * (panel::kSlice / 4);
+  const int64_t total = s.B * quads;
+  const bool vec = K % 4 == 0 && aligned16(gate) && aligned16(up);
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / quads, k = 4 * (i % quads);
+    float4 v;
+    if (vec && k < K) {
+      const float4 a = reinterpret_cast<const float4 *>(gate + m * K)[k / 4];
+      const float4 b = reinterpret_cast<const float4 *>(up + m * K)[k / 4];
+      v = make_float4(swiglu(a.x, b.x), swiglu(a.y, b.y), swiglu(a.z, b.z), swiglu(a.w, b.w));
+    } else {
+      float *lanes = &v.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        lanes[j] = k + j < K ? swiglu(gate[m * K + k + j], up[m * K + k + j]) : 0.f;
+    }
+    panel::store4(out, m, k, K, v);
+  }
+}
+
+bool swigluPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<RowsSpec>(spec);
+  if (s.B <= 0 || s.C <= 0)
+    return false;
+  const int64_t wanted = ceilDiv(s.B * panel::slices(s.C) * (panel::kSlice / 4), 256 * 4);
+  const int64_t cap = 148 * 8 * 4;
+  g->grid[0] = unsigned(wanted > cap ? cap : wanted);
+  g->block[0] = 256;
+  return true;
+}
+
+// ---- projections on a panel ------------------------------------------------------------------
+template <int BN>
+__global__ void __launch_bounds__(tc::kThreads)
+    panelLinearTc(const float *a, const float *w, float *dst, GemmSpec s) {
+  Params p;
+  p.a = a, p.w = w, p.out = dst, p.s = s;
+  tc::body<BN, gemm::kStore>(p);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(tc::kThreads)
+    panelLinearRopeTc(const float *a, const float *w, const float *table, const int *position,
+                      float *dst, GemmSpec s) {
+  Params p;
+  p.a = a, p.w = w, p.table = table, p.position = position, p.out = dst, p.s = s;
+  tc::body<BN, gemm::kRope>(p);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(tc::kThreads)
+    panelLinearRopeAppendTc(const float *a, const float *w, const float *table,
+                            const int *position, float *cache, GemmSpec s) {
+  Params p;
+  p.a = a, p.w = w, p.table = table, p.position = position, p.out = cache, p.s = s;
+  tc::body<BN, gemm::kRopeAppend>(p);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(tc::kThreads)
+    panelLinearAppendTc(const float *a, const float *w, const int *position, float *cache,
+                        GemmSpec s) {
+  Params p;
+  p.a = a, p.w = w, p.position = position, p.out = cache, p.s = s;
+  tc::body<BN, gemm::kAppend>(p);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(tc::kThreads)
+    panelLinearResidualTc(const float *a, const float *w, const float *residual, float *dst,
+                          GemmSpec s) {
+  Params p;
+  p.a = a, p.w = w, p.residual = residual, p.out = dst, p.s = s;
+  tc::body<BN, gemm::kResidual>(p);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(tc::kThreads)
+    panelLinearArgmaxTc(const float *a, const float *w, float *logits, float2 *partials,
+                        GemmSpec s) {
+  Params p;
+  p.a = a, p.w = w, p.out = logits, p.partials = partials, p.s = s;
+  tc::body<BN, gemm::kArgmax>(p);
+}
+
+bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
+  if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
+    return false;
+  const int width = tc::chooseWidth(s);
+  g->grid[0] = ceilDiv(s.N, width);
+  g->grid[1] = ceilDiv(s.M, tc::BM);
+  g->block[0] = tc::kThreads;
+  g->sharedBytes = unsigned(tc::sharedBytes(width));
+  return g->grid[1] <= 65535;
+}
+
+bool panelGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  return panelGeometry(specOf<GemmSpec>(spec), g);
+}
+
+bool panelRopeGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  if (s.D <= 0 || s.D % 2 || s.N % s.D || s.T <= 0)
+    return false;
+  return panelGeometry(s, g);
+}
+
+bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  if (s.D <= 0 || s.D % 2 || s.N != s.A * s.D || s.T <= 0)
+    return false;
+  return panelGeometry(s, g);
+}
+
+#define CKL_PANEL_SELECT(fn)                                                                   \
+  [](const void *spec) -> const void * {                                                       \
+    switch (tc::chooseWidth(specOf<GemmSpec>(spec))) {                                         \
+    case 128: return reinterpret_cast<const void *>(&fn<128>);                                 \
+    case 64: return reinterpret_cast<const void *>(&fn<64>);                                   \
+    default: return reinterpret_cast<const void *>(&fn<32>);                                  \
+    }                                                                                          \
+  }
+
+} // namespace
+
+CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPanelKernel),
+                    "PPPFS", sizeof(RmsApplySpec), rmsPanelGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.fused.swiglu_panel", reinterpret_cast<const void *>(&swigluPanelKernel),
+                    "PPPS", sizeof(RowsSpec), swigluPanelGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32>),
+                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope",
+                    reinterpret_cast<const void *>(&panelLinearRopeTc<32>), "PPPPPS",
+                    sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append",
+                    reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32>), "PPPPPS",
+                    sizeof(GemmSpec), panelAppendGeometry,
+                    CKL_PANEL_SELECT(panelLinearRopeAppendTc));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append",
+                    reinterpret_cast<const void *>(&panelLinearAppendTc<32>), "PPPPS",
+                    sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual",
+                    reinterpret_cast<const void *>(&panelLinearResidualTc<32>), "PPPPS",
+                    sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax",
+                    reinterpret_cast<const void *>(&panelLinearArgmaxTc<32>), "PPPPS",
+                    sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc));
+
+} // namespace ckl::kernels
+
+// Fault word of the tensor-core kernels: bit 0 a bounded wait expired, bit 1 a panel operand
+// was not 16-byte aligned.  `reset` clears it after reading.
+extern "C" int ckl_library_faults(uint32_t *out, int reset) {
+  unsigned value = 0;
+  cudaError_t status = cudaMemcpyFromSymbol(&value, ckl::kernels::tc::g_libraryFaults, sizeof(value));
+  if (status == cudaSuccess && reset) {
+    const unsigned zero = 0;
+    status = cudaMemcpyToSymbol(ckl::kernels::tc::g_libraryFaults, &zero, sizeof(zero));
+  }
+  if (status != cudaSuccess) {
+    cudaGetLastError();
+    return CKL_RUNTIME_ERROR;
+  }
+  if (out)
+    *out = value;
+  return CKL_OK;
+}

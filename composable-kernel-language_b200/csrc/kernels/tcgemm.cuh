@@ -1,45 +1,53 @@
 // Tensor-core (tcgen05) projection kernel with FP32-level accuracy (3xTF32).
 //
-// out = epilogue(prologue(A) @ W[layer]) for batched decode (M >= 128 requests), where a
-// projection is a true dense contraction.  Each FP32 operand is split into a TF32 high part
-// and a TF32 low part (x = hi + lo, both rounded to nearest); hi*hi accumulates in one FP32
-// tensor-memory accumulator and the two correction products hi*lo + lo*hi in a second one,
-// summed in FP32 by the epilogue (the dropped lo*lo term is ~2^-22 relative).  This keeps
-// the decoder's 1e-4 relative tolerance and greedy-token parity that plain TF32 breaks.
+// out = epilogue(A @ W[layer]) for batched decode (M >= 128 requests), A given as a split
+// panel (panel.cuh: TF32 hi/lo parts in the tensor cores' shared-memory layout, produced
+// once by the kernel that computes A), W the FP32 weights [K, N] of one layer, read as stored.
+// hi*hi accumulates in one FP32 tensor-memory accumulator and the correction products
+// hi*lo + lo*hi in a second one, summed in FP32 by the epilogue (the dropped lo*lo term is
+// ~2^-22 relative).  This keeps the decoder's 1e-4 relative tolerance and greedy-token parity
+// that plain TF32 breaks.
 //
-// CTA: 256 threads (8 warps), tile 128 rows x BN columns, K in slices of 32.
-//   * raw FP32 slices of A, W (and the RMSNorm gain) stream from global memory into a ring
-//     of S shared-memory stages with 16-byte cp.async copies, S-1 slices ahead (when shapes
-//     and pointers allow; otherwise each slice is loaded synchronously into stage 0);
-//   * all threads convert a landed slice into one of two canonical stages: prologue (RMSNorm
-//     gain; the row scale is applied in the epilogue from sums of squares accumulated here),
-//     TF32 hi/lo split by integer rounding, K-major no-swizzle layout: element (row, k) at
-//     byte ((k / 4) * rows + row) * 16 + (k % 4) * 4 (8-row x 16-byte core matrices, K-chunks
-//     `rows * 16` bytes apart = LBO, 8-row groups 128 bytes apart = SBO);
-//   * one thread issues 4 k-steps x 3 `tcgen05.mma.cta_group::1.kind::tf32` (M=128, N=BN,
-//     K=8) per slice and commits them to the stage's mbarrier; a canonical stage is reused
-//     only after those MMAs completed;
-//   * the epilogue reads the accumulators with `tcgen05.ld.32x32b` (warps w and w+4 share
-//     TMEM lanes 32(w%4).., one row per thread, half the columns each).
-// Every mbarrier wait is bounded by time: on expiry the kernel records a fault bit
-// (ckl_library_faults), waits (again bounded) for its in-flight MMAs, frees its tensor memory
-// and returns; it never spins without a limit.
+// CTA: one 128 x BN output tile, K in slices of 32, six warps with fixed roles:
+//   warp 0 (producer): per slice one 32 KB bulk copy of the panel block (hi + lo) and one
+//     bulk copy per weight row (BN floats) into a ring of S stages, completing on the
+//     stage's `full` mbarrier; a stage is refilled after the MMAs that read it completed;
+//   warp 1 (MMA): allocates 2*BN tensor-memory columns; per slice, once the panel block has
+//     landed and the weight slice is converted, one thread issues up to 4 k-steps x 3
+//     `tcgen05.mma.cta_group::1.kind::tf32` (M=128, N=BN, K=8) and commits them to the
+//     stage's `empty` and the weight buffer's `bEmpty` mbarriers;
+//   warps 2-5 (converters, then epilogue): split each landed weight slice into TF32 hi/lo in
+//     K-major no-swizzle layout (two buffers), then read the accumulators with
+//     `tcgen05.ld.32x32b` (warp w reads TMEM lanes 32 (w % 4).., one output row per thread)
+//     and apply the fused epilogue.
+// Weight slices whose rows or pointer do not allow 16-byte copies are read by the converters
+// straight from global memory instead.
+//
+// Every mbarrier wait is bounded by time.  A wait that expires records a fault bit
+// (ckl_library_faults) and raises a CTA-wide abort flag that ends the other roles' waits; the
+// CTA then waits (again bounded) for its in-flight copies and MMAs, frees its tensor memory
+// and returns.  No wait spins without a limit.
 #pragma once
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "panel.cuh"
 
 namespace ckl::kernels::tc {
 
-constexpr int BM = 128;
-constexpr int BK = 32;
-constexpr int kThreads = 256; // 8 warps: two per accumulator lane quarter
+constexpr int BM = panel::kRows;
+constexpr int BK = panel::kSlice;
+constexpr int kProducerWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kConverterWarps = 4; // warps 2..5; also the epilogue
+constexpr int kConverterThreads = kConverterWarps * kWarp;
+constexpr int kThreads = (2 + kConverterWarps) * kWarp;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull; // 2 s
+constexpr std::size_t kMaxDynamicSmem = 227 * 1024;
 
 // Fault word of the library (bit 0: a tensor-core wait expired).  One translation unit
-// (decoder_fused.cu) instantiates these kernels and reports the word (ckl_library_faults).
+// instantiates these kernels and reports the word (ckl_library_faults).
 static __device__ unsigned g_libraryFaults = 0;
-
 
 __device__ __forceinline__ unsigned smemAddress(const void *p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -61,19 +69,19 @@ template <int BN> __host__ __device__ constexpr unsigned instructionDescriptor()
   return (1u << 4) | (2u << 7) | (2u << 10) | (unsigned(BN >> 3) << 17) | (unsigned(BM >> 4) << 24);
 }
 
-// Round to the nearest TF32 value (10 explicit mantissa bits) with integer operations
-// (ties away from zero, as cvt.rna); keeps the conversion off the transcendental pipe.
-__device__ __forceinline__ float toTf32(float x) {
-  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-
-__device__ __forceinline__ void split(float x, float &hi, float &lo) {
-  hi = toTf32(x);
-  lo = toTf32(x - hi);
-}
-
 __device__ __forceinline__ void mbarrierInit(unsigned long long *bar, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smemAddress(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbarrierArrive(unsigned long long *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemAddress(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbarrierArriveExpectTx(unsigned long long *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               ::"r"(smemAddress(bar)), "r"(bytes)
                : "memory");
 }
 
@@ -94,17 +102,33 @@ __device__ __forceinline__ unsigned long long globalTimer() {
   return t;
 }
 
-// Bounded wait for an mbarrier phase; false when the time limit expired.
-__device__ __forceinline__ bool mbarrierWait(unsigned long long *bar, unsigned phase) {
+// Bounded wait for an mbarrier phase.  Gives up when `abort` is raised by another thread, or
+// raises it (and the fault bit) when the time limit expires.
+__device__ __forceinline__ bool waitPhase(unsigned long long *bar, unsigned phase,
+                                          volatile int *abort) {
   if (mbarrierTryWait(bar, phase))
     return true;
   const unsigned long long start = globalTimer();
   while (true) {
     if (mbarrierTryWait(bar, phase))
       return true;
-    if (globalTimer() - start > kWaitLimitNs)
+    if (abort != nullptr && *abort)
       return false;
+    if (globalTimer() - start > kWaitLimitNs) {
+      atomicOr(&g_libraryFaults, 1u);
+      if (abort != nullptr)
+        *abort = 1;
+      return false;
+    }
   }
+}
+
+__device__ __forceinline__ void bulkCopy(void *dst, const void *src, unsigned bytes,
+                                         unsigned long long *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+               "[%0], [%1], %2, [%3];" ::"r"(smemAddress(dst)),
+               "l"(src), "r"(bytes), "r"(smemAddress(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void fenceAsyncShared() {
@@ -160,7 +184,6 @@ __device__ __forceinline__ void tmemLoad16(unsigned address, float (&v)[16]) {
     v[i] = __uint_as_float(r[i]);
 }
 
-
 // Column width of the tile for a specialization: enough CTAs to fill the GPU when possible.
 inline int chooseWidth(const GemmSpec &s) {
   const int64_t rowTiles = (s.M + BM - 1) / BM;
@@ -170,33 +193,22 @@ inline int chooseWidth(const GemmSpec &s) {
   return 32;
 }
 
-constexpr std::size_t kMaxDynamicSmem = 227 * 1024;
-
 template <int BN, int S> struct Smem {
-  float aHi[2][BK / 4][BM][4];
-  float aLo[2][BK / 4][BM][4];
-  float bHi[2][BK / 4][BN][4];
+  float a[S][2][BK / 4][BM][4]; // panel blocks (hi, lo) as copied
+  float bHi[2][BK / 4][BN][4];  // converted weight slices, K-major
   float bLo[2][BK / 4][BN][4];
-  float rawA[S][BM][BK + 4]; // padded rows: conflict-free 16-byte reads per row
-  float rawB[S][BK][BN + 4];
-  float rawG[S][BK];         // RMSNorm gain slice
-  float squares[2][BM];      // per-row partial sums of squares (RMSNorm)
-  unsigned long long mmaDone[2];
-  unsigned long long accDone;
+  float rawB[S][BK][BN];        // weight rows as copied
+  unsigned long long full[S], empty[S], bFull[2], bEmpty[2], accDone;
   unsigned tmemBase;
+  int abort;
 };
 
-template <int BN, int S = 8> constexpr int stages() {
-  if constexpr (S < 2)
-    return 1;
-  else if constexpr (sizeof(Smem<BN, S>) + 1024 <= kMaxDynamicSmem)
-    return S;
-  else
-    return stages<BN, S - 1>();
+template <int BN> constexpr int stages() {
+  return sizeof(Smem<BN, 4>) <= kMaxDynamicSmem ? 4 : (sizeof(Smem<BN, 3>) <= kMaxDynamicSmem ? 3 : 2);
 }
+static_assert(sizeof(Smem<128, stages<128>()>) <= kMaxDynamicSmem, "shared memory budget");
 
-// Dynamic shared memory of the asynchronous pipeline at a column width (the synchronous one
-// needs less).
+// Dynamic shared memory of the kernel at a column width.
 inline std::size_t sharedBytes(int width) {
   switch (width) {
   case 128: return sizeof(Smem<128, stages<128>()>);
@@ -205,72 +217,57 @@ inline std::size_t sharedBytes(int width) {
   }
 }
 
-__device__ __forceinline__ void cpAsync16(void *dst, const void *src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smemAddress(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cpAsyncCommit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N> __device__ __forceinline__ void cpAsyncWait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-template <int BN, class Layout>
-__device__ __forceinline__ void issueSlice(Layout &sm, int stage, unsigned tmem, bool first) {
-  constexpr unsigned idesc = instructionDescriptor<BN>();
-#pragma unroll
-  for (int ks = 0; ks < BK / 8; ++ks) {
-    const unsigned long long aHi = matrixDescriptor(sm.aHi[stage][2 * ks], BM * 16, 128);
-    const unsigned long long aLo = matrixDescriptor(sm.aLo[stage][2 * ks], BM * 16, 128);
-    const unsigned long long bHi = matrixDescriptor(sm.bHi[stage][2 * ks], BN * 16, 128);
-    const unsigned long long bLo = matrixDescriptor(sm.bLo[stage][2 * ks], BN * 16, 128);
-    // Main products and correction products accumulate separately: the corrections are
-    // ~2^-11 of the main term and keep their precision in their own accumulator.
-    mma(tmem, aHi, bHi, idesc, (first && ks == 0) ? 0u : 1u);
-    mma(tmem + BN, aHi, bLo, idesc, (first && ks == 0) ? 0u : 1u);
-    mma(tmem + BN, aLo, bHi, idesc, 1u);
-  }
-}
-
-// Epilogue: warps w and w+4 read TMEM lanes 32(w%4).. (one row per thread), columns
-// [half*BN/2, (half+1)*BN/2); main + correction accumulators summed in FP32, optional row
-// scale (RMSNorm), then the fused epilogue.
+// Epilogue of one output row (this thread's) over the tile's BN columns: main + correction
+// accumulators summed in FP32, then the fused epilogue.
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue(const gemm::Params &p, unsigned tmem, int64_t m0,
-                                         int64_t n0, int position, float rowScale,
-                                         float2 *rowBest) {
+__device__ __forceinline__ void epilogue(const gemm::Params &p, unsigned rowAddress, int64_t m,
+                                         int64_t n0, int position) {
   const GemmSpec &s = p.s;
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  const int quarter = warp % 4, half = warp / 4;
   const int64_t M = s.M, N = s.N;
-  const int64_t m = m0 + quarter * 32 + lane;
-  const unsigned rowAddress = tmem + (unsigned(quarter * 32) << 16);
+  const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
+                    (EPI != gemm::kResidual || aligned16(p.residual));
   float best = -CUDART_INF_F;
   int bestIndex = 0x7fffffff;
 #pragma unroll 1
-  for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
+  for (int c0 = 0; c0 < BN; c0 += 16) {
     float v[16], correction[16];
     tmemLoad16(rowAddress + unsigned(c0), v);
     tmemLoad16(rowAddress + unsigned(BN + c0), correction);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      v[j] = __fmul_rn(v[j] + correction[j], rowScale);
-    if (m >= M)
-      continue;
+      v[j] = __fadd_rn(v[j], correction[j]);
     const int64_t nBase = n0 + c0;
+    if (m >= M || nBase >= N)
+      continue;
     if constexpr (EPI == gemm::kStore || EPI == gemm::kResidual || EPI == gemm::kArgmax) {
+      if (vec4 && nBase + 16 <= N) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int64_t n = nBase + j;
-        if (n < N) {
-          float value = v[j];
-          if constexpr (EPI == gemm::kResidual)
-            value = __fadd_rn(p.residual[m * N + n], value);
-          p.out[m * N + n] = value;
-          if constexpr (EPI == gemm::kArgmax)
-            argmaxMerge(best, bestIndex, v[j], int(n));
+        for (int j = 0; j < 16; j += 4) {
+          float4 value = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          if constexpr (EPI == gemm::kResidual) {
+            const float4 r = *reinterpret_cast<const float4 *>(p.residual + m * N + nBase + j);
+            value = make_float4(__fadd_rn(r.x, value.x), __fadd_rn(r.y, value.y),
+                                __fadd_rn(r.z, value.z), __fadd_rn(r.w, value.w));
+          }
+          *reinterpret_cast<float4 *>(p.out + m * N + nBase + j) = value;
+        }
+        if constexpr (EPI == gemm::kArgmax) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            argmaxMerge(best, bestIndex, v[j], int(nBase + j));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int64_t n = nBase + j;
+          if (n < N) {
+            float value = v[j];
+            if constexpr (EPI == gemm::kResidual)
+              value = __fadd_rn(p.residual[m * N + n], value);
+            p.out[m * N + n] = value;
+            if constexpr (EPI == gemm::kArgmax)
+              argmaxMerge(best, bestIndex, v[j], int(n));
+          }
         }
       }
     } else {
@@ -302,213 +299,167 @@ __device__ __forceinline__ void epilogue(const gemm::Params &p, unsigned tmem, i
     }
   }
   if constexpr (EPI == gemm::kArgmax) {
-    // The two column halves of a row meet in shared memory; the lower index wins ties.
-    rowBest[half * BM + quarter * 32 + lane] = make_float2(best, __int_as_float(bestIndex));
-    __syncthreads();
-    if (half == 0 && m < M) {
-      const float2 other = rowBest[BM + quarter * 32 + lane];
-      argmaxMerge(best, bestIndex, other.x, __float_as_int(other.y));
+    if (m < M)
       p.partials[m * s.tiles + blockIdx.x] = make_float2(best, __int_as_float(bestIndex));
-    }
   }
 }
 
-template <int BN, int PRO, int EPI, bool ASYNC> __device__ void body(const gemm::Params &p) {
-  static_assert(PRO != gemm::kSwiGlu, "the tensor-core path takes a materialised SwiGLU input");
-  constexpr int S = ASYNC ? stages<BN>() : 1;
+// One 128 x BN tile.  p.a is the panel of A [M, K]; p.w the weights [layers, K, N].
+template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
+  constexpr int S = stages<BN>();
   using Layout = Smem<BN, S>;
   extern __shared__ __align__(1024) unsigned char raw[];
   Layout &sm = *reinterpret_cast<Layout *>(raw);
   const GemmSpec &s = p.s;
-  const int tid = threadIdx.x, warp = tid / kWarp;
-  const int64_t m0 = int64_t(blockIdx.y) * BM, n0 = int64_t(blockIdx.x) * BN;
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int64_t M = s.M, K = s.K, N = s.N;
+  const int64_t m0 = int64_t(blockIdx.y) * BM, n0 = int64_t(blockIdx.x) * BN;
+  const int64_t slices = panel::slices(K);
   const float *W = p.w + s.layer * K * N;
-  const float *gain = p.gain + s.layer * K;
+  const float *blocks = p.a + int64_t(blockIdx.y) * slices * panel::kBlock;
 
   int position = 0;
   if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend) {
     position = p.position[0];
     if (position < 0 || position >= s.T)
-      return;
+      return; // outside cache capacity: the step writes nothing
   }
-  const int64_t slices = (K + BK - 1) / BK;
-
-  // Raw slice kt -> ring slot kt % S.
-  auto fetch = [&](int64_t kt) {
-    const int slot = int(kt % S);
-    const int64_t k0 = kt * BK;
-    for (int e = tid; e < BM * (BK / 4); e += kThreads) {
-      const int r = e / (BK / 4), c = e % (BK / 4);
-      const int64_t m = m0 + r, k = k0 + 4 * c;
-      float *dst = &sm.rawA[slot][r][4 * c];
-      if constexpr (ASYNC) {
-        const bool valid = m < M && k < K;
-        cpAsync16(dst, valid ? p.a + m * K + k : p.a, valid);
-      } else {
-        for (int i = 0; i < 4; ++i)
-          dst[i] = (m < M && k + i < K) ? p.a[m * K + k + i] : 0.f;
-      }
-    }
-    for (int e = tid; e < BK * (BN / 4); e += kThreads) {
-      const int r = e / (BN / 4), c = e % (BN / 4);
-      const int64_t k = k0 + r, n = n0 + 4 * c;
-      float *dst = &sm.rawB[slot][r][4 * c];
-      if constexpr (ASYNC) {
-        const bool valid = k < K && n < N;
-        cpAsync16(dst, valid ? W + k * N + n : W, valid);
-      } else {
-        for (int i = 0; i < 4; ++i)
-          dst[i] = (k < K && n + i < N) ? W[k * N + n + i] : 0.f;
-      }
-    }
-    if constexpr (PRO == gemm::kRms) {
-      if (tid < BK / 4) {
-        const int64_t k = k0 + 4 * tid;
-        float *dst = &sm.rawG[slot][4 * tid];
-        if constexpr (ASYNC) {
-          cpAsync16(dst, k < K ? gain + k : gain, k < K);
-        } else {
-          for (int i = 0; i < 4; ++i)
-            dst[i] = k + i < K ? gain[k + i] : 0.f;
-        }
-      }
-    }
-  };
-
-  if constexpr (ASYNC) {
-    for (int64_t i = 0; i < S - 1; ++i) {
-      if (i < slices)
-        fetch(i);
-      cpAsyncCommit();
-    }
+  if (!aligned16(p.a)) {
+    if (threadIdx.x == 0)
+      atomicOr(&g_libraryFaults, 2u); // panel operands are 16-byte aligned by construction
+    return;
   }
-  if (warp == 0)
+  // Weight rows by bulk copy when every row slice is a 16-byte multiple at a 16-byte address.
+  const bool copyRows = N % 4 == 0 && aligned16(W);
+
+  if (warp == kMmaWarp)
     tmemAlloc<2 * BN>(&sm.tmemBase);
-  if (tid == 0) {
-    mbarrierInit(&sm.mmaDone[0], 1);
-    mbarrierInit(&sm.mmaDone[1], 1);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbarrierInit(&sm.full[i], 1);
+      mbarrierInit(&sm.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbarrierInit(&sm.bFull[i], kConverterWarps);
+      mbarrierInit(&sm.bEmpty[i], 1);
+    }
     mbarrierInit(&sm.accDone, 1);
+    sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fenceBeforeSync();
   __syncthreads();
   fenceAfterSync();
   const unsigned tmem = sm.tmemBase;
+  volatile int *abort = &sm.abort;
 
-  // Conversion: thread tid takes A row tid % 128, chunks of its half, and a run of one B
-  // column.  The RMSNorm row statistic accumulates here from the raw values.
-  const int row = tid % BM, half = tid / BM;
-  float squares = 0.f;
-  auto convert = [&](int slot, int stage) {
-#pragma unroll
-    for (int cc = 0; cc < BK / 8; ++cc) {
-      const int c = half * (BK / 8) + cc;
-      float4 v = *reinterpret_cast<const float4 *>(&sm.rawA[slot][row][4 * c]);
-      if constexpr (PRO == gemm::kRms) {
-        squares += v.x * v.x;
-        squares += v.y * v.y;
-        squares += v.z * v.z;
-        squares += v.w * v.w;
-        const float4 g = *reinterpret_cast<const float4 *>(&sm.rawG[slot][4 * c]);
-        v.x = __fmul_rn(v.x, g.x);
-        v.y = __fmul_rn(v.y, g.y);
-        v.z = __fmul_rn(v.z, g.z);
-        v.w = __fmul_rn(v.w, g.w);
+  if (warp == kProducerWarp) {
+    const unsigned rowBytes = unsigned((N - n0 < BN ? N - n0 : BN) * 4);
+    int64_t issued = 0;
+    for (int64_t kt = 0; kt < slices; ++kt) {
+      const int slot = int(kt % S);
+      bool ok = true;
+      if (lane == 0 && kt >= S)
+        ok = waitPhase(&sm.empty[slot], unsigned((kt / S - 1) & 1), abort);
+      if (!__shfl_sync(0xffffffffu, ok, 0))
+        break;
+      const int64_t k0 = kt * BK;
+      const int rows = int(K - k0 < BK ? K - k0 : BK);
+      if (lane == 0)
+        mbarrierArriveExpectTx(&sm.full[slot],
+                               unsigned(2 * panel::kPart * 4) + (copyRows ? rows * rowBytes : 0u));
+      __syncwarp();
+      if (lane == 0)
+        bulkCopy(&sm.a[slot][0][0][0][0], blocks + kt * panel::kBlock,
+                 unsigned(2 * panel::kPart * 4), &sm.full[slot]);
+      if (copyRows && lane < rows)
+        bulkCopy(&sm.rawB[slot][lane][0], W + (k0 + lane) * N + n0, rowBytes, &sm.full[slot]);
+      issued = kt + 1;
+    }
+    // Leave no copy in flight: wait (bounded, regardless of abort) for the last use of each
+    // stage.  In a completed pipeline these phases are long done.
+    if (lane == 0)
+      for (int64_t kt = issued > S ? issued - S : 0; kt < issued; ++kt)
+        waitPhase(&sm.full[kt % S], unsigned((kt / S) & 1), nullptr);
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr unsigned idesc = instructionDescriptor<BN>();
+      for (int64_t kt = 0; kt < slices; ++kt) {
+        const int slot = int(kt % S), buffer = int(kt & 1);
+        if (!waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort) ||
+            !waitPhase(&sm.bFull[buffer], unsigned((kt / 2) & 1), abort))
+          break;
+        fenceAfterSync();
+        const int64_t remaining = K - kt * BK;
+        const int steps = int(remaining >= BK ? BK / 8 : (remaining + 7) / 8);
+        for (int ks = 0; ks < steps; ++ks) {
+          const unsigned long long aHi = matrixDescriptor(sm.a[slot][0][2 * ks], BM * 16, 128);
+          const unsigned long long aLo = matrixDescriptor(sm.a[slot][1][2 * ks], BM * 16, 128);
+          const unsigned long long bHi = matrixDescriptor(sm.bHi[buffer][2 * ks], BN * 16, 128);
+          const unsigned long long bLo = matrixDescriptor(sm.bLo[buffer][2 * ks], BN * 16, 128);
+          const unsigned first = (kt == 0 && ks == 0) ? 0u : 1u;
+          mma(tmem, aHi, bHi, idesc, first);
+          mma(tmem + BN, aHi, bLo, idesc, first);
+          mma(tmem + BN, aLo, bHi, idesc, 1u);
+        }
+        commit(&sm.empty[slot]);
+        commit(&sm.bEmpty[buffer]);
       }
-      float4 hi, lo;
-      split(v.x, hi.x, lo.x);
-      split(v.y, hi.y, lo.y);
-      split(v.z, hi.z, lo.z);
-      split(v.w, hi.w, lo.w);
-      *reinterpret_cast<float4 *>(sm.aHi[stage][c][row]) = hi;
-      *reinterpret_cast<float4 *>(sm.aLo[stage][c][row]) = lo;
+      // Tracks every MMA issued above, on success and on abort alike.
+      commit(&sm.accDone);
     }
-    constexpr int kPerThread = BK * BN / kThreads; // k values of one column per thread
-    const int col = tid % BN, kb = (tid / BN) * kPerThread;
+    __syncwarp();
+  } else {
+    const int t = threadIdx.x - 2 * kWarp;
+    for (int64_t kt = 0; kt < slices; ++kt) {
+      const int slot = int(kt % S), buffer = int(kt & 1);
+      bool ok = !copyRows || waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort);
+      if (ok && kt >= 2)
+        ok = waitPhase(&sm.bEmpty[buffer], unsigned((kt / 2 - 1) & 1), abort);
+      if (!__all_sync(0xffffffffu, ok))
+        break;
+      const int64_t k0 = kt * BK;
+      // Group i: four consecutive k (chunk c) of column n.
+      for (int i = t; i < (BK / 4) * BN; i += kConverterThreads) {
+        const int c = i / BN, n = i % BN;
+        float4 v;
+        float *lanes = &v.x;
 #pragma unroll
-    for (int j = 0; j < kPerThread; j += 4) {
-      float4 hi, lo;
-      split(sm.rawB[slot][kb + j][col], hi.x, lo.x);
-      split(sm.rawB[slot][kb + j + 1][col], hi.y, lo.y);
-      split(sm.rawB[slot][kb + j + 2][col], hi.z, lo.z);
-      split(sm.rawB[slot][kb + j + 3][col], hi.w, lo.w);
-      *reinterpret_cast<float4 *>(sm.bHi[stage][(kb + j) / 4][col]) = hi;
-      *reinterpret_cast<float4 *>(sm.bLo[stage][(kb + j) / 4][col]) = lo;
-    }
-  };
-
-  bool ok = true;
-  unsigned phase[2] = {0, 0};
-  for (int64_t kt = 0; kt < slices && ok; ++kt) {
-    if constexpr (ASYNC) {
-      if (kt + S - 1 < slices)
-        fetch(kt + S - 1);
-      cpAsyncCommit();
-      cpAsyncWait<S - 1>(); // this thread's copies of slice kt have landed
-    } else {
-      fetch(kt);
-    }
-    const int stage = int(kt & 1);
-    if (kt >= 2) {
-      ok = mbarrierWait(&sm.mmaDone[stage], phase[stage]);
-      phase[stage] ^= 1;
-    }
-    __syncthreads(); // slice kt visible to every thread
-    if (ok) {
-      convert(int(kt % S), stage);
+        for (int j = 0; j < 4; ++j) {
+          const int64_t k = k0 + 4 * c + j;
+          float value = 0.f;
+          if (k < K) {
+            if (copyRows)
+              value = sm.rawB[slot][4 * c + j][n];
+            else if (n0 + n < N)
+              value = W[k * N + n0 + n];
+          }
+          lanes[j] = value;
+        }
+        float4 hi, lo;
+        panel::split4(v, hi, lo);
+        *reinterpret_cast<float4 *>(sm.bHi[buffer][c][n]) = hi;
+        *reinterpret_cast<float4 *>(sm.bLo[buffer][c][n]) = lo;
+      }
       fenceAsyncShared();
+      __syncwarp();
+      if (lane == 0)
+        mbarrierArrive(&sm.bFull[buffer]);
     }
-    ok = __syncthreads_and(ok);
-    if (ok && tid == 0) {
-      fenceAfterSync();
-      issueSlice<BN, Layout>(sm, stage, tmem, kt == 0);
-      commit(&sm.mmaDone[stage]);
+    // Epilogue: wait (bounded) for every issued MMA, then read this warp's TMEM lanes.
+    const bool done = waitPhase(&sm.accDone, 0, nullptr);
+    fenceAfterSync();
+    if (__all_sync(0xffffffffu, done && !*abort)) { // warp-uniform: tcgen05.ld is .aligned
+      const int quarter = warp % 4;
+      epilogue<BN, EPI>(p, tmem + (unsigned(quarter * 32) << 16), m0 + quarter * 32 + lane, n0,
+                        position);
     }
   }
-  if constexpr (ASYNC)
-    cpAsyncWait<0>();
-  if (tid == 0)
-    commit(&sm.accDone);
-  bool done = mbarrierWait(&sm.accDone, 0);
-  if constexpr (PRO == gemm::kRms)
-    sm.squares[half][row] = squares;
-  done = __syncthreads_and(done);
-  if (!ok || !done) {
-    if (tid == 0)
-      atomicOr(&g_libraryFaults, 1u);
-    fenceBeforeSync();
-    __syncthreads();
-    if (warp == 0)
-      tmemFree<2 * BN>(tmem);
-    return;
-  }
-  fenceAfterSync();
-  float rowScale = 1.f;
-  if constexpr (PRO == gemm::kRms) {
-    const int r = (warp % 4) * 32 + tid % kWarp;
-    rowScale = rsqrtf((sm.squares[0][r] + sm.squares[1][r]) / float(K) + p.eps);
-  }
-  // The argmax epilogue reuses the (now idle) raw A ring to merge column halves.
-  epilogue<BN, EPI>(p, tmem, m0, n0, position, rowScale,
-                    reinterpret_cast<float2 *>(&sm.rawA[0][0][0]));
   fenceBeforeSync();
   __syncthreads();
-  if (warp == 0)
+  if (warp == kMmaWarp)
     tmemFree<2 * BN>(tmem);
-}
-
-// Entry used by the kernel wrappers: the asynchronous pipeline when shapes and pointers
-// allow 16-byte copies, the synchronous one otherwise.
-template <int BN, int PRO, int EPI> __device__ void run(const gemm::Params &p) {
-  const GemmSpec &s = p.s;
-  const float *W = p.w + s.layer * s.K * s.N;
-  const bool vec = s.K % 4 == 0 && s.N % 4 == 0 && aligned16(p.a) && aligned16(W) &&
-                   (PRO != gemm::kRms || aligned16(p.gain + s.layer * s.K));
-  if (vec)
-    body<BN, PRO, EPI, true>(p);
-  else
-    body<BN, PRO, EPI, false>(p);
 }
 
 } // namespace ckl::kernels::tc

@@ -205,6 +205,11 @@ _ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
 _TENSOR_CORE_ROWS = 128
 
 
+def _panel_floats(M: int, K: int) -> int:
+    """Size of a split tensor-core operand: 128-row tiles x 32-column slices x (hi, lo)."""
+    return -(-M // 128) * -(-K // 32) * 2 * 128 * 32
+
+
 class _NoMatch(Exception):
     pass
 
@@ -278,6 +283,14 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
     embedding = dispatches[0]
     x = res(embedding, 2)
     new_nodes = [embedding]
+    added: list[int] = []
+
+    def panel_resource(M, K, name):
+        rid = _add_resource(resources, "temporary", BufferSpec((_panel_floats(M, K),), f32), name)
+        added.append(rid)
+        return rid
+
+    tensor_cores = config == 0 and shape(x)[0] >= _TENSOR_CORE_ROWS
     eliminated: dict[int, list] = {}
     position = sincos = kc = vc = None
     for layer_index in range(layers):
@@ -351,57 +364,100 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
 
         R = lambda r: Slot("resource", resource=r)
         pos_read = (position, READ, POSITION)
-        new_nodes.append(node("ckl.fused.norm_linear_rope",
-                              [R(x), R(g1), R(wq), R(sincos), R(position), R(qr), eps1],
-                              gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                              [x, g1, wq, sincos], [pos_read, (qr, WRITE, "whole")], "q projection"))
-        new_nodes.append(node("ckl.fused.norm_linear_rope_append",
-                              [R(x), R(g1), R(wk), R(sincos), R(position), R(kc), eps1],
-                              gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                              [x, g1, wk, sincos], [pos_read, (kc, WRITE, "whole")], "k projection"))
-        new_nodes.append(node("ckl.fused.norm_linear_append",
-                              [R(x), R(g1), R(wv), R(position), R(vc), eps1],
-                              gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                              [x, g1, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
-        new_nodes.append(node("ckl.fused.attention",
-                              [R(qr), R(kc), R(vc), R(position), R(context), scale],
-                              pack(B, A, T, D, L_, layer, 1, 0),
-                              [qr, kc, vc], [pos_read, (context, WRITE, "whole")], "attention"))
-        new_nodes.append(node("ckl.fused.linear_residual",
-                              [R(context), R(wo), R(x), R(residual)],
-                              gemm_spec(B, Cdim, Cdim, Lw, layer),
-                              [context, wo, x], [(residual, WRITE, "whole")], "o projection"))
-        new_nodes.append(node("ckl.fused.norm_linear", [R(residual), R(g2), R(wg), R(gate), eps2],
-                              gemm_spec(B, Cdim, F, shape(wg)[0], layer),
-                              [residual, g2, wg], [(gate, WRITE, "whole")], "gate projection"))
-        new_nodes.append(node("ckl.fused.norm_linear", [R(residual), R(g2), R(wu), R(up), eps2],
-                              gemm_spec(B, Cdim, F, shape(wu)[0], layer),
-                              [residual, g2, wu], [(up, WRITE, "whole")], "up projection"))
         eliminated_here = [(inv, (d[0], d[1])), (normed, (d[1], d[2], d[3], d[4])),
                            (q, (d[2], d[5])), (k, (d[3], d[6])), (v, (d[4], d[7])),
                            (kr, (d[6], d[7])), (scores, (d[8], d[9])), (probs, (d[9], d[10])),
                            (projected, (d[11], d[12])), (inv2, (d[13], d[14])),
                            (normed2, (d[14], d[15], d[16])), (activated, (d[17], d[18])),
-                           (down, (d[19], d[20]))]
-        if config == 0 and B >= _TENSOR_CORE_ROWS:
-            # Tensor-core down projection: the activation is materialised once (in the
-            # program's own `product` temporary) and the GEMM takes it as a plain operand.
-            if shape(product) != (B, F):
-                raise _NoMatch
-            new_nodes.append(node("ckl.fused.swiglu", [R(gate), R(up), R(product)], pack(B, F),
-                                  [gate, up], [(product, WRITE, "whole")], "swiglu"))
-            new_nodes.append(node("ckl.fused.linear_residual",
-                                  [R(product), R(wd), R(residual), R(next_x)],
+                           (product, (d[18], d[19])), (down, (d[19], d[20]))]
+        if tensor_cores:
+            # Each activation operand is split into a TF32 hi/lo panel once, by its producer,
+            # and the projections read the panels on the tensor cores.
+            x_panel = panel_resource(B, Cdim, "x_panel")
+            context_panel = panel_resource(B, Cdim, "context_panel")
+            r_panel = panel_resource(B, Cdim, "residual_panel")
+            p_panel = panel_resource(B, F, "swiglu_panel")
+            new_nodes.append(node("ckl.fused.rms_panel", [R(x), R(g1), R(x_panel), eps1],
+                                  pack(B, Cdim, shape(g1)[0], layer), [x, g1],
+                                  [(x_panel, WRITE, "whole")], "attention norm"))
+            new_nodes.append(node("ckl.fused.panel_linear_rope",
+                                  [R(x_panel), R(wq), R(sincos), R(position), R(qr)],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                                  [x_panel, wq, sincos], [pos_read, (qr, WRITE, "whole")],
+                                  "q projection"))
+            new_nodes.append(node("ckl.fused.panel_linear_rope_append",
+                                  [R(x_panel), R(wk), R(sincos), R(position), R(kc)],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                                  [x_panel, wk, sincos], [pos_read, (kc, WRITE, "whole")],
+                                  "k projection"))
+            new_nodes.append(node("ckl.fused.panel_linear_append",
+                                  [R(x_panel), R(wv), R(position), R(vc)],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                                  [x_panel, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
+            new_nodes.append(node("ckl.fused.attention",
+                                  [R(qr), R(kc), R(vc), R(position), R(context_panel), scale],
+                                  pack(B, A, T, D, L_, layer, 1, 0, 1),
+                                  [qr, kc, vc], [pos_read, (context_panel, WRITE, "whole")],
+                                  "attention"))
+            new_nodes.append(node("ckl.fused.panel_linear_residual",
+                                  [R(context_panel), R(wo), R(x), R(residual)],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer),
+                                  [context_panel, wo, x], [(residual, WRITE, "whole")],
+                                  "o projection"))
+            new_nodes.append(node("ckl.fused.rms_panel", [R(residual), R(g2), R(r_panel), eps2],
+                                  pack(B, Cdim, shape(g2)[0], layer), [residual, g2],
+                                  [(r_panel, WRITE, "whole")], "mlp norm"))
+            new_nodes.append(node("ckl.fused.panel_linear", [R(r_panel), R(wg), R(gate)],
+                                  gemm_spec(B, Cdim, F, shape(wg)[0], layer),
+                                  [r_panel, wg], [(gate, WRITE, "whole")], "gate projection"))
+            new_nodes.append(node("ckl.fused.panel_linear", [R(r_panel), R(wu), R(up)],
+                                  gemm_spec(B, Cdim, F, shape(wu)[0], layer),
+                                  [r_panel, wu], [(up, WRITE, "whole")], "up projection"))
+            new_nodes.append(node("ckl.fused.swiglu_panel", [R(gate), R(up), R(p_panel)],
+                                  pack(B, F), [gate, up], [(p_panel, WRITE, "whole")], "swiglu"))
+            new_nodes.append(node("ckl.fused.panel_linear_residual",
+                                  [R(p_panel), R(wd), R(residual), R(next_x)],
                                   gemm_spec(B, F, Cdim, shape(wd)[0], layer),
-                                  [product, wd, residual], [(next_x, WRITE, "whole")],
+                                  [p_panel, wd, residual], [(next_x, WRITE, "whole")],
                                   "down projection"))
+            eliminated_here.append((context, (d[10], d[11])))
         else:
+            new_nodes.append(node("ckl.fused.norm_linear_rope",
+                                  [R(x), R(g1), R(wq), R(sincos), R(position), R(qr), eps1],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                                  [x, g1, wq, sincos], [pos_read, (qr, WRITE, "whole")],
+                                  "q projection"))
+            new_nodes.append(node("ckl.fused.norm_linear_rope_append",
+                                  [R(x), R(g1), R(wk), R(sincos), R(position), R(kc), eps1],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                                  [x, g1, wk, sincos], [pos_read, (kc, WRITE, "whole")],
+                                  "k projection"))
+            new_nodes.append(node("ckl.fused.norm_linear_append",
+                                  [R(x), R(g1), R(wv), R(position), R(vc), eps1],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
+                                  [x, g1, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
+            new_nodes.append(node("ckl.fused.attention",
+                                  [R(qr), R(kc), R(vc), R(position), R(context), scale],
+                                  pack(B, A, T, D, L_, layer, 1, 0, 0),
+                                  [qr, kc, vc], [pos_read, (context, WRITE, "whole")],
+                                  "attention"))
+            new_nodes.append(node("ckl.fused.linear_residual",
+                                  [R(context), R(wo), R(x), R(residual)],
+                                  gemm_spec(B, Cdim, Cdim, Lw, layer),
+                                  [context, wo, x], [(residual, WRITE, "whole")], "o projection"))
+            new_nodes.append(node("ckl.fused.norm_linear",
+                                  [R(residual), R(g2), R(wg), R(gate), eps2],
+                                  gemm_spec(B, Cdim, F, shape(wg)[0], layer),
+                                  [residual, g2, wg], [(gate, WRITE, "whole")], "gate projection"))
+            new_nodes.append(node("ckl.fused.norm_linear",
+                                  [R(residual), R(g2), R(wu), R(up), eps2],
+                                  gemm_spec(B, Cdim, F, shape(wu)[0], layer),
+                                  [residual, g2, wu], [(up, WRITE, "whole")], "up projection"))
             new_nodes.append(node("ckl.fused.swiglu_linear_residual",
                                   [R(gate), R(up), R(wd), R(residual), R(next_x)],
                                   gemm_spec(B, F, Cdim, shape(wd)[0], layer),
                                   [gate, up, wd, residual], [(next_x, WRITE, "whole")],
                                   "down projection"))
-            eliminated_here.append((product, (d[18], d[19])))
         for rid, users in eliminated_here:
             eliminated[rid] = list(users)
         x = next_x
@@ -420,19 +476,31 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
     B, Cdim = shape(x)
     V = shape(lm)[2]
     T = shape(history)[0]
+    head_name = "ckl.fused.panel_linear_argmax" if tensor_cores else "ckl.fused.norm_linear_argmax"
     head_spec = gemm_spec(B, Cdim, V, shape(lm)[0], const(h[2]))
-    geometry = library_geometry("ckl.fused.norm_linear_argmax", head_spec)
+    geometry = library_geometry(head_name, head_spec)
     tiles = geometry[0][0]
     head_spec = gemm_spec(B, Cdim, V, shape(lm)[0], const(h[2]), tiles=tiles)
     partials = _add_resource(resources, "temporary", BufferSpec((B, tiles, 2), f32), "partials")
     counter = _add_resource(resources, "persistent", BufferSpec((1,), i32), "counter")
     R = lambda r: Slot("resource", resource=r)
     eps = _scalar_slot(op(h[0], 2))
-    new_nodes.append(Node("ckl.fused.norm_linear_argmax",
-                          [R(x), R(fgain), R(lm), R(logits), R(partials), eps], head_spec,
-                          [(x, READ, "whole"), (fgain, READ, "whole"), (lm, READ, "whole"),
-                           (logits, WRITE, "whole"), (partials, WRITE, "whole")],
-                          "lm head"))
+    if tensor_cores:
+        f_panel = panel_resource(B, Cdim, "final_panel")
+        new_nodes.append(Node("ckl.fused.rms_panel", [R(x), R(fgain), R(f_panel), eps],
+                              pack(B, Cdim, shape(fgain)[0], const(h[1])),
+                              [(x, READ, "whole"), (fgain, READ, "whole"),
+                               (f_panel, WRITE, "whole")], "final norm"))
+        new_nodes.append(Node(head_name, [R(f_panel), R(lm), R(logits), R(partials)], head_spec,
+                              [(f_panel, READ, "whole"), (lm, READ, "whole"),
+                               (logits, WRITE, "whole"), (partials, WRITE, "whole")],
+                              "lm head"))
+    else:
+        new_nodes.append(Node(head_name,
+                              [R(x), R(fgain), R(lm), R(logits), R(partials), eps], head_spec,
+                              [(x, READ, "whole"), (fgain, READ, "whole"), (lm, READ, "whole"),
+                               (logits, WRITE, "whole"), (partials, WRITE, "whole")],
+                              "lm head"))
     new_nodes.append(Node("ckl.fused.greedy_combine",
                           [R(partials), R(logits), R(tokens), R(history), R(position), R(counter)],
                           pack(B, tiles, T, V),
@@ -442,7 +510,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
                           "greedy + advance"))
     eliminated[finv] = [h[0], h[1]]
     eliminated[final_x] = [h[1], h[2]]
-    return new_nodes, eliminated, [partials]
+    return new_nodes, eliminated, added + [partials]
 
 
 def _add_resource(resources, kind, spec, name) -> int:

@@ -1,9 +1,11 @@
 """Batched projections on tcgen05 tensor cores (3xTF32) match the FP32 oracle.
 
-Fused decoder kernels switch to the tensor-core path at 128 or more requests.  These cases
-cover full and ragged row tiles, K not a multiple of the 32-wide slice, N not a multiple of
-the column tile, every epilogue (RoPE, KV append, residual, SwiGLU prologue, argmax head), and
-check that no kernel reported an expired wait.
+The fused decoder switches to the tensor-core path at 128 or more requests: RMSNorm, attention
+and SwiGLU write split operand panels and the projections read them with the FP32 weights.
+These cases cover full and ragged row tiles, K not a multiple of the 32-wide slice (and not of
+the 8-wide MMA step), N not a multiple of the column tile or of 4 (weights read without bulk
+copies), every epilogue (RoPE, KV append, residual, argmax head), and check that no kernel
+reported an expired wait or a misaligned panel.
 """
 from __future__ import annotations
 
@@ -37,6 +39,8 @@ def faults():
     (300, 128, 2, 1, 96, 1000, 3),     # ragged rows, K = 96, N tails
     (512, 1024, 16, 1, 4096, 4000, 2), # cfg5 layer shapes, 4 row tiles (smaller vocab)
     (128, 1024, 16, 4, 4096, 32000, 2),  # cfg5 depth and vocabulary
+    (200, 64, 2, 1, 98, 1001, 2),      # K = 98 (ragged MMA step), N % 4 != 0, head dim 32
+    (129, 96, 3, 2, 160, 520, 2),      # one row in the second tile, C = 96, head dim 32
 ])
 def test_tensor_core_decoder_matches_oracle(device, batch, hidden, heads, layers, ffn, vocab, steps):
     faults()

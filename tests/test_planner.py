@@ -129,6 +129,33 @@ def test_fused_decoder_plan_shape():
     assert topology[gate] == topology[up]
 
 
+def test_tensor_core_decoder_plan_shape():
+    """Batches of 128+ requests: split-operand panels feed tensor-core projections."""
+    config = ref.Config(batch=256, hidden=128, heads=2, layers=2, ffn=256, vocab=512, context=8,
+                        steps=8)
+    lowered = decoder.decode.lower(signature=decoder_signature(config))
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+    names = plans.primary.node_names
+    layer = ["ckl.fused.rms_panel", "ckl.fused.panel_linear_rope",
+             "ckl.fused.panel_linear_rope_append", "ckl.fused.panel_linear_append",
+             "ckl.fused.attention", "ckl.fused.panel_linear_residual", "ckl.fused.rms_panel",
+             "ckl.fused.panel_linear", "ckl.fused.panel_linear", "ckl.fused.swiglu_panel",
+             "ckl.fused.panel_linear_residual"]
+    head = ["ckl.fused.rms_panel", "ckl.fused.panel_linear_argmax", "ckl.fused.greedy_combine"]
+    assert names == ["ckl.decoder.embedding"] + layer * 2 + head
+    topology = plans.primary.topology
+    ids = sorted(topology)
+    norm, q, k, v = ids[1:5]
+    assert topology[q] == topology[k] == topology[v] == [norm]
+    gate, up = ids[8], ids[9]
+    assert topology[gate] == topology[up] == [ids[7]]
+    # FFMA projections when tensor cores are switched off.
+    ffma = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
+                        tensor_cores=False)
+    assert ffma.primary.nodes == 1 + 8 * 2 + 2
+    assert not any("panel" in n for n in ffma.primary.node_names)
+
+
 def test_vector_pipeline_plans():
     """tests/Runtime/test_frontend_runtime.py:66-69 and test_pointwise_fusion.py:43-45."""
     lowered = vector_pipeline.lower()
