@@ -11,6 +11,9 @@
 //   fused epilogues as the FFMA kernels.
 // The normalised and activated values are rounded exactly as in the FFMA kernels
 // (x * rsqrt(mean(x^2) + eps) * gain, silu(g) * u) before the split.
+#include <cstring>
+#include <mutex>
+
 #include "ckl_b200.h"
 #include "common.cuh"
 #include "gemm.cuh"
@@ -26,7 +29,15 @@ using gemm::Params;
 constexpr int kPanelWarps = 8;
 
 // One warp per row: sum of squares, then the normalised row split into the panel.  Columns
-// between K and the next multiple of 32 are written as zeros.
+// between K and the next multiple of 32 are written as zeros.  Rows of up to 1024 columns are
+// held in registers between the two passes.
+constexpr int kRmsHeld = 8; // float4 per lane
+
+__device__ __forceinline__ float4 rmsScale(const float4 &a, float inv, const float4 &g) {
+  return make_float4(__fmul_rn(__fmul_rn(a.x, inv), g.x), __fmul_rn(__fmul_rn(a.y, inv), g.y),
+                     __fmul_rn(__fmul_rn(a.z, inv), g.z), __fmul_rn(__fmul_rn(a.w, inv), g.w));
+}
+
 __global__ void __launch_bounds__(kPanelWarps *kWarp)
     rmsPanelKernel(const float *x, const float *gain, float *out, float eps, RmsApplySpec s) {
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
@@ -37,7 +48,31 @@ __global__ void __launch_bounds__(kPanelWarps *kWarp)
   const float *row = x + m * K;
   const float *g = gain + s.layer * K;
   const bool vec = K % 4 == 0 && aligned16(row) && aligned16(g);
+  const int64_t padded = panel::slices(K) * panel::kSlice;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   float total = 0.f;
+  if (vec && padded <= 4 * kWarp * kRmsHeld) {
+    const float4 *row4 = reinterpret_cast<const float4 *>(row);
+    float4 held[kRmsHeld];
+#pragma unroll
+    for (int i = 0; i < kRmsHeld; ++i) {
+      const int64_t q = lane + i * kWarp;
+      held[i] = q < K / 4 ? row4[q] : zero;
+      total += held[i].x * held[i].x + held[i].y * held[i].y + held[i].z * held[i].z +
+               held[i].w * held[i].w;
+    }
+    total = warpSum(total);
+    const float inv = rsqrtf(total / float(K) + eps);
+#pragma unroll
+    for (int i = 0; i < kRmsHeld; ++i) {
+      const int64_t k = 4 * (lane + int64_t(i) * kWarp);
+      if (k < padded)
+        panel::store4(out, m, k, K,
+                      k < K ? rmsScale(held[i], inv, reinterpret_cast<const float4 *>(g)[k / 4])
+                            : zero);
+    }
+    return;
+  }
   if (vec) {
     for (int64_t q = lane; q < K / 4; q += kWarp) {
       const float4 v = reinterpret_cast<const float4 *>(row)[q];
@@ -49,14 +84,11 @@ __global__ void __launch_bounds__(kPanelWarps *kWarp)
   }
   total = warpSum(total);
   const float inv = rsqrtf(total / float(K) + eps);
-  const int64_t padded = panel::slices(K) * panel::kSlice;
   for (int64_t k = 4 * int64_t(lane); k < padded; k += 4 * kWarp) {
     float4 v;
     if (vec && k < K) {
-      const float4 a = reinterpret_cast<const float4 *>(row)[k / 4];
-      const float4 b = reinterpret_cast<const float4 *>(g)[k / 4];
-      v = make_float4(__fmul_rn(__fmul_rn(a.x, inv), b.x), __fmul_rn(__fmul_rn(a.y, inv), b.y),
-                      __fmul_rn(__fmul_rn(a.z, inv), b.z), __fmul_rn(__fmul_rn(a.w, inv), b.w));
+      v = rmsScale(reinterpret_cast<const float4 *>(row)[k / 4], inv,
+                   reinterpret_cast<const float4 *>(g)[k / 4]);
     } else {
       float *lanes = &v.x;
 #pragma unroll
@@ -117,57 +149,82 @@ bool swigluPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
 }
 
 // ---- projections on a panel ------------------------------------------------------------------
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelLinearTc(const float *a, const float *w, float *dst, GemmSpec s) {
-  Params p;
-  p.a = a, p.w = w, p.out = dst, p.s = s;
-  tc::body<BN, gemm::kStore>(p);
+// Every projection takes the panel of A, the weights [layers, K, N], its outputs, the
+// specialization and (last, added at bind time) the weights' tensor map.  SPLITS > 1 splits
+// K over a cluster of that many CTAs per output tile.
+#define CKL_PANEL_KERNEL(fn, EPI, params, assign)                                               \
+  template <int BN, int SPLITS>                                                                \
+  __global__ void __cluster_dims__(1, 1, SPLITS) __launch_bounds__(tc::kThreads)               \
+      fn(const float *a, const float *w, CKL_UNPACK params, GemmSpec s,                         \
+         const __grid_constant__ tc::WeightMap weights) {                                      \
+    Params p;                                                                                  \
+    p.a = a, p.w = w, p.s = s;                                                                 \
+    CKL_UNPACK assign;                                                                         \
+    tc::body<BN, EPI, SPLITS>(p, weights);                                                     \
+  }
+#define CKL_UNPACK(...) __VA_ARGS__
+
+CKL_PANEL_KERNEL(panelLinearTc, gemm::kStore, (float *dst), (p.out = dst))
+CKL_PANEL_KERNEL(panelLinearRopeTc, gemm::kRope,
+                 (const float *table, const int *position, float *dst),
+                 (p.table = table, p.position = position, p.out = dst))
+CKL_PANEL_KERNEL(panelLinearRopeAppendTc, gemm::kRopeAppend,
+                 (const float *table, const int *position, float *cache),
+                 (p.table = table, p.position = position, p.out = cache))
+CKL_PANEL_KERNEL(panelLinearAppendTc, gemm::kAppend, (const int *position, float *cache),
+                 (p.position = position, p.out = cache))
+CKL_PANEL_KERNEL(panelLinearResidualTc, gemm::kResidual, (const float *residual, float *dst),
+                 (p.residual = residual, p.out = dst))
+CKL_PANEL_KERNEL(panelLinearArgmaxTc, gemm::kArgmax, (float *logits, float2 *partials),
+                 (p.out = logits, p.partials = partials))
+
+// Tensor map of the weights [layers, K, N] for the kernel's column width, built once per bound
+// node from the resolved weight pointer (slot 1 of every panel projection).  Weights whose
+// shape or address admit no map get valid == 0 and are read with plain loads.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encodeTiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *entry = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &entry, cudaEnableDefault, &found) ==
+            cudaSuccess &&
+        found == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(entry);
+    else
+      cudaGetLastError();
+  });
+  return fn;
 }
 
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelLinearRopeTc(const float *a, const float *w, const float *table, const int *position,
-                      float *dst, GemmSpec s) {
-  Params p;
-  p.a = a, p.w = w, p.table = table, p.position = position, p.out = dst, p.s = s;
-  tc::body<BN, gemm::kRope>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelLinearRopeAppendTc(const float *a, const float *w, const float *table,
-                            const int *position, float *cache, GemmSpec s) {
-  Params p;
-  p.a = a, p.w = w, p.table = table, p.position = position, p.out = cache, p.s = s;
-  tc::body<BN, gemm::kRopeAppend>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelLinearAppendTc(const float *a, const float *w, const int *position, float *cache,
-                        GemmSpec s) {
-  Params p;
-  p.a = a, p.w = w, p.position = position, p.out = cache, p.s = s;
-  tc::body<BN, gemm::kAppend>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelLinearResidualTc(const float *a, const float *w, const float *residual, float *dst,
-                          GemmSpec s) {
-  Params p;
-  p.a = a, p.w = w, p.residual = residual, p.out = dst, p.s = s;
-  tc::body<BN, gemm::kResidual>(p);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelLinearArgmaxTc(const float *a, const float *w, float *logits, float2 *partials,
-                        GemmSpec s) {
-  Params p;
-  p.a = a, p.w = w, p.out = logits, p.partials = partials, p.s = s;
-  tc::body<BN, gemm::kArgmax>(p);
+bool prepareWeights(const void *spec, const void *const *arguments, std::size_t count,
+                    void *extra) {
+  if (spec == nullptr || count < 2)
+    return false;
+  const GemmSpec &s = specOf<GemmSpec>(spec);
+  tc::WeightMap local;
+  std::memset(&local, 0, sizeof(local));
+  uint64_t w = 0;
+  std::memcpy(&w, arguments[1], sizeof(w));
+  const EncodeTiledFn encode = encodeTiled();
+  if (encode != nullptr && s.N % 4 == 0 && w % 16 == 0 && s.K > 0 && s.N > 0 && s.layers > 0) {
+    const cuuint64_t dims[3] = {cuuint64_t(s.N), cuuint64_t(s.K), cuuint64_t(s.layers)};
+    const cuuint64_t strides[2] = {cuuint64_t(s.N) * 4, cuuint64_t(s.K) * cuuint64_t(s.N) * 4};
+    const cuuint32_t box[3] = {cuuint32_t(tc::chooseWidth(s)), cuuint32_t(tc::BK), 1};
+    const cuuint32_t unit[3] = {1, 1, 1};
+    const CUresult status =
+        encode(&local.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, reinterpret_cast<void *>(w), dims,
+               strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    local.valid = status == CUDA_SUCCESS ? 1 : 0;
+  }
+  std::memcpy(extra, &local, sizeof(local));
+  return true;
 }
 
 bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
@@ -176,6 +233,7 @@ bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
   const int width = tc::chooseWidth(s);
   g->grid[0] = ceilDiv(s.N, width);
   g->grid[1] = ceilDiv(s.M, tc::BM);
+  g->grid[2] = unsigned(tc::chooseSplits(s));
   g->block[0] = tc::kThreads;
   g->sharedBytes = unsigned(tc::sharedBytes(width));
   return g->grid[1] <= 65535;
@@ -201,10 +259,17 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
 
 #define CKL_PANEL_SELECT(fn)                                                                   \
   [](const void *spec) -> const void * {                                                       \
-    switch (tc::chooseWidth(specOf<GemmSpec>(spec))) {                                         \
-    case 128: return reinterpret_cast<const void *>(&fn<128>);                                 \
-    case 64: return reinterpret_cast<const void *>(&fn<64>);                                   \
-    default: return reinterpret_cast<const void *>(&fn<32>);                                  \
+    const GemmSpec &s = specOf<GemmSpec>(spec);                                                \
+    switch (tc::chooseWidth(s)) {                                                              \
+    case 128:                                                                                  \
+      switch (tc::chooseSplits(s)) {                                                           \
+      case 8: return reinterpret_cast<const void *>(&fn<128, 8>);                              \
+      case 4: return reinterpret_cast<const void *>(&fn<128, 4>);                              \
+      case 2: return reinterpret_cast<const void *>(&fn<128, 2>);                              \
+      default: return reinterpret_cast<const void *>(&fn<128, 1>);                             \
+      }                                                                                        \
+    case 64: return reinterpret_cast<const void *>(&fn<64, 1>);                                \
+    default: return reinterpret_cast<const void *>(&fn<32, 1>);                                \
     }                                                                                          \
   }
 
@@ -214,29 +279,29 @@ CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPa
                     "PPPFS", sizeof(RmsApplySpec), rmsPanelGeometry, nullptr);
 CKL_REGISTER_KERNEL("ckl.fused.swiglu_panel", reinterpret_cast<const void *>(&swigluPanelKernel),
                     "PPPS", sizeof(RowsSpec), swigluPanelGeometry, nullptr);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32>),
-                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc));
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope",
-                    reinterpret_cast<const void *>(&panelLinearRopeTc<32>), "PPPPPS",
-                    sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc));
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append",
-                    reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32>), "PPPPPS",
-                    sizeof(GemmSpec), panelAppendGeometry,
-                    CKL_PANEL_SELECT(panelLinearRopeAppendTc));
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append",
-                    reinterpret_cast<const void *>(&panelLinearAppendTc<32>), "PPPPS",
-                    sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc));
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual",
-                    reinterpret_cast<const void *>(&panelLinearResidualTc<32>), "PPPPS",
-                    sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc));
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax",
-                    reinterpret_cast<const void *>(&panelLinearArgmaxTc<32>), "PPPPS",
-                    sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1>),
+                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc),
+                    prepareWeights, sizeof(tc::WeightMap));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope", reinterpret_cast<const void *>(&panelLinearRopeTc<32, 1>),
+                    "PPPPPS", sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc),
+                    prepareWeights, sizeof(tc::WeightMap));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append", reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32, 1>),
+                    "PPPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearRopeAppendTc),
+                    prepareWeights, sizeof(tc::WeightMap));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append", reinterpret_cast<const void *>(&panelLinearAppendTc<32, 1>),
+                    "PPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc),
+                    prepareWeights, sizeof(tc::WeightMap));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const void *>(&panelLinearResidualTc<32, 1>),
+                    "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc),
+                    prepareWeights, sizeof(tc::WeightMap));
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1>),
+                    "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc),
+                    prepareWeights, sizeof(tc::WeightMap));
 
 } // namespace ckl::kernels
 
-// Fault word of the tensor-core kernels: bit 0 a bounded wait expired, bit 1 a panel operand
-// was not 16-byte aligned.  `reset` clears it after reading.
+// Fault word of the tensor-core kernels: bit 0 a bounded wait expired, bit 1 a panel operand or
+// the shared-memory ring was misaligned.  `reset` clears it after reading.
 extern "C" int ckl_library_faults(uint32_t *out, int reset) {
   unsigned value = 0;
   cudaError_t status = cudaMemcpyFromSymbol(&value, ckl::kernels::tc::g_libraryFaults, sizeof(value));

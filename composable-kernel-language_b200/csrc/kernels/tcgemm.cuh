@@ -9,9 +9,11 @@
 // that plain TF32 breaks.
 //
 // CTA: one 128 x BN output tile, K in slices of 32, six warps with fixed roles:
-//   warp 0 (producer): per slice one 32 KB bulk copy of the panel block (hi + lo) and one
-//     bulk copy per weight row (BN floats) into a ring of S stages, completing on the
-//     stage's `full` mbarrier; a stage is refilled after the MMAs that read it completed;
+//   warp 0 (producer): per slice one 32 KB bulk copy of the panel block (hi + lo) and one TMA
+//     tensor copy of the 32 x BN weight box (zero-filled beyond K and N; the tensor map is
+//     built at bind time and passed as a __grid_constant__ parameter) into a ring of S
+//     stages, completing on the stage's `full` mbarrier; a stage is refilled after the MMAs
+//     that read it completed;
 //   warp 1 (MMA): allocates 2*BN tensor-memory columns; per slice, once the panel block has
 //     landed and the weight slice is converted, one thread issues up to 4 k-steps x 3
 //     `tcgen05.mma.cta_group::1.kind::tf32` (M=128, N=BN, K=8) and commits them to the
@@ -20,14 +22,21 @@
 //     K-major no-swizzle layout (two buffers), then read the accumulators with
 //     `tcgen05.ld.32x32b` (warp w reads TMEM lanes 32 (w % 4).., one output row per thread)
 //     and apply the fused epilogue.
-// Weight slices whose rows or pointer do not allow 16-byte copies are read by the converters
-// straight from global memory instead.
+// A tf32 MMA costs about the same at N = 32 as at N = 128, so tiles are 128 columns wide
+// (narrower only for narrow outputs) and the K loop is split over gridDim.z CTAs when the
+// output has too few tiles to fill the GPU.  Each split writes its partial tile to a
+// workspace; the last split to arrive (per-tile counter) sums the partials in split order,
+// which keeps the result deterministic, applies the epilogue and resets the counter.
+// Weights whose rows or pointer do not allow a tensor map (N % 4 != 0, unaligned base) are read
+// by the converters straight from global memory instead.
 //
 // Every mbarrier wait is bounded by time.  A wait that expires records a fault bit
 // (ckl_library_faults) and raises a CTA-wide abort flag that ends the other roles' waits; the
 // CTA then waits (again bounded) for its in-flight copies and MMAs, frees its tensor memory
 // and returns.  No wait spins without a limit.
 #pragma once
+
+#include <cuda.h>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -44,6 +53,13 @@ constexpr int kConverterThreads = kConverterWarps * kWarp;
 constexpr int kThreads = (2 + kConverterWarps) * kWarp;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull; // 2 s
 constexpr std::size_t kMaxDynamicSmem = 227 * 1024;
+
+// TMA tensor map of a weight buffer [layers, K, N] with a box of BN x 32 x 1 (N innermost),
+// or valid == 0 when the buffer does not admit one.
+struct WeightMap {
+  CUtensorMap map;
+  int valid;
+};
 
 // Fault word of the library (bit 0: a tensor-core wait expired).  One translation unit
 // instantiates these kernels and reports the word (ckl_library_faults).
@@ -131,6 +147,16 @@ __device__ __forceinline__ void bulkCopy(void *dst, const void *src, unsigned by
                : "memory");
 }
 
+// TMA copy of the weight box at (n0, k0, layer) into shared memory.
+__device__ __forceinline__ void tensorCopy(void *dst, const CUtensorMap *map, int n0, int k0,
+                                           int layer, unsigned long long *bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+               "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smemAddress(dst)),
+               "l"(reinterpret_cast<unsigned long long>(map)), "r"(n0), "r"(k0), "r"(layer),
+               "r"(smemAddress(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void fenceAsyncShared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -184,27 +210,45 @@ __device__ __forceinline__ void tmemLoad16(unsigned address, float (&v)[16]) {
     v[i] = __uint_as_float(r[i]);
 }
 
-// Column width of the tile for a specialization: enough CTAs to fill the GPU when possible.
-inline int chooseWidth(const GemmSpec &s) {
-  const int64_t rowTiles = (s.M + BM - 1) / BM;
-  for (int width : {128, 64})
-    if (rowTiles * ((s.N + width - 1) / width) >= 120)
-      return width;
-  return 32;
+// Column width of the tile for a specialization.
+inline int chooseWidth(const GemmSpec &s) { return s.N <= 32 ? 32 : (s.N <= 64 ? 64 : 128); }
+
+constexpr int64_t kTargetCtas = 148; // one CTA per SM
+
+// K splits (1, 2, 4 or 8; the CTAs of one tile form a cluster): about one wave of CTAs over
+// the SMs, at least two slices per split, full-width tiles only.  A split whose slice range
+// is empty contributes zeros.
+inline int chooseSplits(const GemmSpec &s) {
+  const int width = chooseWidth(s);
+  if (width != 128)
+    return 1;
+  const int64_t tiles = ((s.M + BM - 1) / BM) * ((s.N + width - 1) / width);
+  const int64_t slices = panel::slices(s.K);
+  int64_t wanted = kTargetCtas / (tiles > 0 ? tiles : 1);
+  if (wanted > slices / 2)
+    wanted = slices / 2;
+  int splits = 1;
+  while (splits * 2 <= wanted && splits < 8)
+    splits *= 2;
+  return splits;
 }
 
 template <int BN, int S> struct Smem {
   float a[S][2][BK / 4][BM][4]; // panel blocks (hi, lo) as copied
   float bHi[2][BK / 4][BN][4];  // converted weight slices, K-major
   float bLo[2][BK / 4][BN][4];
-  float rawB[S][BK][BN];        // weight rows as copied
+  float rawB[S][BK][BN];        // weight box as copied (128-byte aligned)
   unsigned long long full[S], empty[S], bFull[2], bEmpty[2], accDone;
   unsigned tmemBase;
   int abort;
 };
 
-template <int BN> constexpr int stages() {
-  return sizeof(Smem<BN, 4>) <= kMaxDynamicSmem ? 4 : (sizeof(Smem<BN, 3>) <= kMaxDynamicSmem ? 3 : 2);
+// Deepest ring (at most 6 stages) that fits the shared-memory budget.
+template <int BN, int S = 6> constexpr int stages() {
+  if constexpr (S <= 2 || sizeof(Smem<BN, S>) <= kMaxDynamicSmem)
+    return S;
+  else
+    return stages<BN, S - 1>();
 }
 static_assert(sizeof(Smem<128, stages<128>()>) <= kMaxDynamicSmem, "shared memory budget");
 
@@ -217,106 +261,179 @@ inline std::size_t sharedBytes(int width) {
   }
 }
 
-// Epilogue of one output row (this thread's) over the tile's BN columns: main + correction
-// accumulators summed in FP32, then the fused epilogue.
-template <int BN, int EPI>
-__device__ __forceinline__ void epilogue(const gemm::Params &p, unsigned rowAddress, int64_t m,
-                                         int64_t n0, int position) {
+// Fused epilogue of four consecutive output values v of row m starting at column n (a multiple
+// of 4); columns at or beyond N are skipped.
+template <int EPI>
+__device__ __forceinline__ void storeQuad(const gemm::Params &p, int64_t m, int64_t n, float4 v,
+                                          int position, bool vec4, float &best, int &bestIndex) {
   const GemmSpec &s = p.s;
   const int64_t M = s.M, N = s.N;
-  const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
-                    (EPI != gemm::kResidual || aligned16(p.residual));
-  float best = -CUDART_INF_F;
-  int bestIndex = 0x7fffffff;
-#pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 16) {
-    float v[16], correction[16];
-    tmemLoad16(rowAddress + unsigned(c0), v);
-    tmemLoad16(rowAddress + unsigned(BN + c0), correction);
+  float *lanes = &v.x;
+  if constexpr (EPI == gemm::kStore || EPI == gemm::kResidual || EPI == gemm::kArgmax) {
+    if constexpr (EPI == gemm::kArgmax) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      v[j] = __fadd_rn(v[j], correction[j]);
-    const int64_t nBase = n0 + c0;
-    if (m >= M || nBase >= N)
-      continue;
-    if constexpr (EPI == gemm::kStore || EPI == gemm::kResidual || EPI == gemm::kArgmax) {
-      if (vec4 && nBase + 16 <= N) {
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          float4 value = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          if constexpr (EPI == gemm::kResidual) {
-            const float4 r = *reinterpret_cast<const float4 *>(p.residual + m * N + nBase + j);
-            value = make_float4(__fadd_rn(r.x, value.x), __fadd_rn(r.y, value.y),
-                                __fadd_rn(r.z, value.z), __fadd_rn(r.w, value.w));
-          }
-          *reinterpret_cast<float4 *>(p.out + m * N + nBase + j) = value;
-        }
-        if constexpr (EPI == gemm::kArgmax) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            argmaxMerge(best, bestIndex, v[j], int(nBase + j));
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int64_t n = nBase + j;
-          if (n < N) {
-            float value = v[j];
-            if constexpr (EPI == gemm::kResidual)
-              value = __fadd_rn(p.residual[m * N + n], value);
-            p.out[m * N + n] = value;
-            if constexpr (EPI == gemm::kArgmax)
-              argmaxMerge(best, bestIndex, v[j], int(n));
-          }
-        }
+      for (int j = 0; j < 4; ++j)
+        if (n + j < N)
+          argmaxMerge(best, bestIndex, lanes[j], int(n + j));
+    }
+    if (vec4 && n + 4 <= N) {
+      if constexpr (EPI == gemm::kResidual) {
+        const float4 r = *reinterpret_cast<const float4 *>(p.residual + m * N + n);
+        v = make_float4(__fadd_rn(r.x, v.x), __fadd_rn(r.y, v.y), __fadd_rn(r.z, v.z),
+                        __fadd_rn(r.w, v.w));
       }
+      *reinterpret_cast<float4 *>(p.out + m * N + n) = v;
     } else {
-      const int64_t D = s.D, R = s.D / 2;
 #pragma unroll
-      for (int j = 0; j < 16; j += 2) {
-        const int64_t n = nBase + j;
-        if (n >= N)
+      for (int j = 0; j < 4; ++j) {
+        if (n + j >= N)
           continue;
-        float first = v[j], second = v[j + 1];
-        const int64_t h = n / D, d = n % D;
-        if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend) {
-          const float *cs = p.table + (int64_t(position) * R + d / 2) * 2;
-          const float cosine = cs[0], sine = cs[1];
-          const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
-          const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
-          first = x;
-          second = y;
-        }
-        if constexpr (EPI == gemm::kRope) {
-          p.out[m * N + n] = first;
-          p.out[m * N + n + 1] = second;
-        } else {
-          float *slot = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
-          slot[0] = first;
-          slot[1] = second;
-        }
+        float value = lanes[j];
+        if constexpr (EPI == gemm::kResidual)
+          value = __fadd_rn(p.residual[m * N + n + j], value);
+        p.out[m * N + n + j] = value;
+      }
+    }
+  } else {
+    const int64_t D = s.D, R = s.D / 2;
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const int64_t c = n + j;
+      if (c >= N)
+        continue;
+      float first = lanes[j], second = lanes[j + 1];
+      const int64_t h = c / D, d = c % D;
+      if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend) {
+        const float *cs = p.table + (int64_t(position) * R + d / 2) * 2;
+        const float cosine = cs[0], sine = cs[1];
+        const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
+        const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
+        first = x;
+        second = y;
+      }
+      if constexpr (EPI == gemm::kRope) {
+        p.out[m * N + c] = first;
+        p.out[m * N + c + 1] = second;
+      } else {
+        float *slot = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
+        slot[0] = first;
+        slot[1] = second;
       }
     }
   }
-  if constexpr (EPI == gemm::kArgmax) {
-    if (m < M)
-      p.partials[m * s.tiles + blockIdx.x] = make_float2(best, __int_as_float(bestIndex));
+}
+
+// Named barrier over the epilogue warps that also ANDs a predicate across them.
+__device__ __forceinline__ bool epilogueAll(bool value) {
+  unsigned out;
+  asm volatile("{\n\t.reg .pred p, q;\n\t"
+               "setp.ne.u32 p, %1, 0;\n\t"
+               "barrier.cta.red.and.pred q, 1, %2, p;\n\t"
+               "selp.u32 %0, 1, 0, q;\n\t}"
+               : "=r"(out)
+               : "r"(unsigned(value)), "n"(kConverterThreads)
+               : "memory");
+  return out != 0;
+}
+
+// Barrier over every thread of every CTA of the cluster (the K splits of one tile).
+__device__ __forceinline__ void clusterSync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Four floats at the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ float4 loadCluster(const float *local, unsigned rank) {
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smemAddress(local)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+// Accumulators staged in shared memory, one padded row per output row (conflict-free row-wise
+// writes and column-wise reads); aliases the idle panel ring after the main loop.
+template <int BN> using Staging = float[BM][BN + 4];
+
+// Output rows [rank * 128 / SPLITS, (rank + 1) * 128 / SPLITS) of the tile: each epilogue warp
+// takes a row at a time, each lane four consecutive columns, summing the K splits' staged
+// partials in rank order (deterministic), and stores them through the fused epilogue.
+template <int BN, int EPI, int SPLITS>
+__device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN> &stage,
+                                               int64_t m0, int64_t nt, int position) {
+  const GemmSpec &s = p.s;
+  const int64_t M = s.M, N = s.N, n0 = nt * BN;
+  const int warp = threadIdx.x / kWarp - 2, lane = threadIdx.x % kWarp;
+  const unsigned rank = blockIdx.z;
+  constexpr int kRows = BM / SPLITS;
+  const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
+                    (EPI != gemm::kResidual || aligned16(p.residual));
+  for (int r = warp; r < kRows; r += kConverterWarps) {
+    const int row = int(rank) * kRows + r;
+    const int64_t m = m0 + row;
+    if (m >= M)
+      break; // rows increase with r
+    float best = -CUDART_INF_F;
+    int bestIndex = 0x7fffffff;
+    for (int c = 4 * lane; c < BN; c += 4 * kWarp) {
+      float4 sum;
+      if constexpr (SPLITS == 1) {
+        sum = *reinterpret_cast<const float4 *>(&stage[row][c]);
+      } else {
+        sum = loadCluster(&stage[row][c], 0);
+#pragma unroll
+        for (unsigned q = 1; q < SPLITS; ++q) {
+          const float4 part = loadCluster(&stage[row][c], q);
+          sum = make_float4(__fadd_rn(sum.x, part.x), __fadd_rn(sum.y, part.y),
+                            __fadd_rn(sum.z, part.z), __fadd_rn(sum.w, part.w));
+        }
+      }
+      if (n0 + c < N)
+        storeQuad<EPI>(p, m, n0 + c, sum, position, vec4, best, bestIndex);
+    }
+    if constexpr (EPI == gemm::kArgmax) {
+#pragma unroll
+      for (int o = kWarp / 2; o > 0; o >>= 1) {
+        const float otherBest = __shfl_xor_sync(0xffffffffu, best, o);
+        const int otherIndex = __shfl_xor_sync(0xffffffffu, bestIndex, o);
+        argmaxMerge(best, bestIndex, otherBest, otherIndex);
+      }
+      if (lane == 0)
+        p.partials[m * s.tiles + nt] = make_float2(best, __int_as_float(bestIndex));
+    }
   }
 }
 
 // One 128 x BN tile.  p.a is the panel of A [M, K]; p.w the weights [layers, K, N].
-template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
+template <int BN, int EPI, int SPLITS>
+__device__ void body(const gemm::Params &p, const WeightMap &weights) {
+  static_assert(SPLITS == 1 || BN == 128, "K splits use full-width tiles");
+  static_assert(sizeof(Staging<BN>) <= sizeof(Smem<BN, stages<BN>()>::a), "staging fits the ring");
   constexpr int S = stages<BN>();
   using Layout = Smem<BN, S>;
   extern __shared__ __align__(1024) unsigned char raw[];
   Layout &sm = *reinterpret_cast<Layout *>(raw);
   const GemmSpec &s = p.s;
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  const int64_t M = s.M, K = s.K, N = s.N;
-  const int64_t m0 = int64_t(blockIdx.y) * BM, n0 = int64_t(blockIdx.x) * BN;
-  const int64_t slices = panel::slices(K);
+  const int64_t K = s.K, N = s.N;
+  // Tiles in launch order with the row tile varying fastest: the CTAs that share a weight tile
+  // run together and read it from HBM once.
+  const int64_t rowTiles = gridDim.y;
+  const int64_t tile = int64_t(blockIdx.y) * gridDim.x + blockIdx.x;
+  const int64_t mt = tile % rowTiles, nt = tile / rowTiles;
+  const int64_t m0 = mt * BM, n0 = nt * BN;
+  // This split's K slices [kBegin, kEnd).
+  const int64_t allSlices = panel::slices(K);
+  const int64_t perSplit = (allSlices + SPLITS - 1) / SPLITS;
+  const int64_t kBegin = perSplit * blockIdx.z;
+  const int64_t kEnd = kBegin + perSplit < allSlices ? kBegin + perSplit : allSlices;
+  const int64_t slices = kEnd > kBegin ? kEnd - kBegin : 0;
+  const bool hasWork = slices > 0;
   const float *W = p.w + s.layer * K * N;
-  const float *blocks = p.a + int64_t(blockIdx.y) * slices * panel::kBlock;
+  const float *blocks = p.a + mt * allSlices * panel::kBlock;
 
   int position = 0;
   if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend) {
@@ -324,13 +441,13 @@ template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
     if (position < 0 || position >= s.T)
       return; // outside cache capacity: the step writes nothing
   }
-  if (!aligned16(p.a)) {
+  if (!aligned16(p.a) || smemAddress(raw) % 128 != 0) {
     if (threadIdx.x == 0)
-      atomicOr(&g_libraryFaults, 2u); // panel operands are 16-byte aligned by construction
+      atomicOr(&g_libraryFaults, 2u); // panels and the shared ring are aligned by construction
     return;
   }
-  // Weight rows by bulk copy when every row slice is a 16-byte multiple at a 16-byte address.
-  const bool copyRows = N % 4 == 0 && aligned16(W);
+  // Weight boxes by TMA when the buffer admits a tensor map.
+  const bool copyRows = weights.valid != 0;
 
   if (warp == kMmaWarp)
     tmemAlloc<2 * BN>(&sm.tmemBase);
@@ -354,8 +471,11 @@ template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
   volatile int *abort = &sm.abort;
 
   if (warp == kProducerWarp) {
-    const unsigned rowBytes = unsigned((N - n0 < BN ? N - n0 : BN) * 4);
+    const unsigned boxBytes = copyRows ? unsigned(BK * BN * 4) : 0u; // full box, OOB zero-filled
     int64_t issued = 0;
+    if (lane == 0 && copyRows)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&weights.map))
+                   : "memory");
     for (int64_t kt = 0; kt < slices; ++kt) {
       const int slot = int(kt % S);
       bool ok = true;
@@ -363,17 +483,15 @@ template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
         ok = waitPhase(&sm.empty[slot], unsigned((kt / S - 1) & 1), abort);
       if (!__shfl_sync(0xffffffffu, ok, 0))
         break;
-      const int64_t k0 = kt * BK;
-      const int rows = int(K - k0 < BK ? K - k0 : BK);
-      if (lane == 0)
-        mbarrierArriveExpectTx(&sm.full[slot],
-                               unsigned(2 * panel::kPart * 4) + (copyRows ? rows * rowBytes : 0u));
-      __syncwarp();
-      if (lane == 0)
-        bulkCopy(&sm.a[slot][0][0][0][0], blocks + kt * panel::kBlock,
+      if (lane == 0) {
+        mbarrierArriveExpectTx(&sm.full[slot], unsigned(2 * panel::kPart * 4) + boxBytes);
+        bulkCopy(&sm.a[slot][0][0][0][0], blocks + (kBegin + kt) * panel::kBlock,
                  unsigned(2 * panel::kPart * 4), &sm.full[slot]);
-      if (copyRows && lane < rows)
-        bulkCopy(&sm.rawB[slot][lane][0], W + (k0 + lane) * N + n0, rowBytes, &sm.full[slot]);
+        if (copyRows)
+          tensorCopy(&sm.rawB[slot][0][0], &weights.map, int(n0), int((kBegin + kt) * BK),
+                     int(s.layer),
+                     &sm.full[slot]);
+      }
       issued = kt + 1;
     }
     // Leave no copy in flight: wait (bounded, regardless of abort) for the last use of each
@@ -391,7 +509,7 @@ template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
             !waitPhase(&sm.bFull[buffer], unsigned((kt / 2) & 1), abort))
           break;
         fenceAfterSync();
-        const int64_t remaining = K - kt * BK;
+        const int64_t remaining = K - (kBegin + kt) * BK;
         const int steps = int(remaining >= BK ? BK / 8 : (remaining + 7) / 8);
         for (int ks = 0; ks < steps; ++ks) {
           const unsigned long long aHi = matrixDescriptor(sm.a[slot][0][2 * ks], BM * 16, 128);
@@ -419,9 +537,11 @@ template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
         ok = waitPhase(&sm.bEmpty[buffer], unsigned((kt / 2 - 1) & 1), abort);
       if (!__all_sync(0xffffffffu, ok))
         break;
-      const int64_t k0 = kt * BK;
+      const int64_t k0 = (kBegin + kt) * BK;
       // Group i: four consecutive k (chunk c) of column n.
-      for (int i = t; i < (BK / 4) * BN; i += kConverterThreads) {
+#pragma unroll
+      for (int g = 0; g < (BK / 4) * BN / kConverterThreads; ++g) {
+        const int i = t + g * kConverterThreads;
         const int c = i / BN, n = i % BN;
         float4 v;
         float *lanes = &v.x;
@@ -447,17 +567,43 @@ template <int BN, int EPI> __device__ void body(const gemm::Params &p) {
       if (lane == 0)
         mbarrierArrive(&sm.bFull[buffer]);
     }
-    // Epilogue: wait (bounded) for every issued MMA, then read this warp's TMEM lanes.
+    // Epilogue: wait (bounded) for every issued MMA, then stage this warp's TMEM lanes (main +
+    // correction, one row per thread) in shared memory over the idle panel ring.
     const bool done = waitPhase(&sm.accDone, 0, nullptr);
     fenceAfterSync();
-    if (__all_sync(0xffffffffu, done && !*abort)) { // warp-uniform: tcgen05.ld is .aligned
-      const int quarter = warp % 4;
-      epilogue<BN, EPI>(p, tmem + (unsigned(quarter * 32) << 16), m0 + quarter * 32 + lane, n0,
-                        position);
+    Staging<BN> &stage = *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0]);
+    const int row = (warp % 4) * 32 + lane;
+    const unsigned rowAddress = tmem + (unsigned((warp % 4) * 32) << 16);
+    const bool valid = epilogueAll(done && !*abort) && hasWork; // uniform over these warps
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16], correction[16];
+      if (valid) {
+        tmemLoad16(rowAddress + unsigned(c0), v);
+        tmemLoad16(rowAddress + unsigned(BN + c0), correction);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4 *>(&stage[row][c0 + j]) =
+            valid ? make_float4(__fadd_rn(v[j], correction[j]), __fadd_rn(v[j + 1], correction[j + 1]),
+                                __fadd_rn(v[j + 2], correction[j + 2]),
+                                __fadd_rn(v[j + 3], correction[j + 3]))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
+  // Every thread of every split CTA of the tile takes part in the same two barriers.
+  if constexpr (SPLITS > 1)
+    clusterSync();
+  else
+    __syncthreads();
+  if (warp >= 2 && __all_sync(0xffffffffu, !*abort))
+    reduceAndStore<BN, EPI, SPLITS>(p, *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0]),
+                                    m0, nt, position);
   fenceBeforeSync();
-  __syncthreads();
+  if constexpr (SPLITS > 1)
+    clusterSync(); // peers read this CTA's staging until here
+  else
+    __syncthreads();
   if (warp == kMmaWarp)
     tmemFree<2 * BN>(tmem);
 }

@@ -23,6 +23,12 @@ using GeometryFn = bool (*)(const void *spec, std::size_t specBytes, Geometry *o
 // entry has several compiled tile configurations.
 using SelectFn = const void *(*)(const void *spec);
 
+// Optional: bytes of one extra trailing kernel parameter derived from the bound arguments
+// (`arguments[i]` points at slot i's bytes, pointers already resolved), e.g. a TMA tensor map
+// of a weight buffer.  Returns false when the arguments are invalid for the kernel.
+using PrepareFn = bool (*)(const void *spec, const void *const *arguments, std::size_t count,
+                           void *extra);
+
 struct Kernel {
   const char *name;
   const void *function;     // host stub of the __global__ function (default configuration)
@@ -30,6 +36,8 @@ struct Kernel {
   std::size_t specBytes;    // size of the trailing specialization struct (0 if none)
   GeometryFn geometry;
   SelectFn select;          // may be null
+  PrepareFn prepare = nullptr;
+  std::size_t prepareBytes = 0; // size of the parameter `prepare` writes
 };
 
 // All entries, defined by the kernel translation units (registered at static init time).

@@ -1112,6 +1112,18 @@ void ckl_commit(void *frame, uint64_t id) {
                 "cudaFuncSetAttribute");
         }
       }
+      if (k->prepare) {
+        const void *spec = k->specBytes ? f.pending.arguments.back().data() : nullptr;
+        std::vector<const void *> slots;
+        for (const auto &a : f.pending.arguments)
+          slots.push_back(a.data());
+        std::vector<unsigned char> extra(k->prepareBytes);
+        f.device->current();
+        if (!k->prepare(spec, slots.data(), slots.size(), extra.data()))
+          throw std::invalid_argument(std::string("arguments not supported by library kernel ") +
+                                      k->name);
+        f.pending.arguments.push_back(std::move(extra));
+      }
     }
     f.nodes[id] = f.plan.add(std::move(f.pending), std::move(f.pendingDeps));
     f.pending = KernelLaunch{};

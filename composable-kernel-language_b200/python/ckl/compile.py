@@ -393,7 +393,8 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
             new_nodes.append(node("ckl.fused.panel_linear_append",
                                   [R(x_panel), R(wv), R(position), R(vc)],
                                   gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                                  [x_panel, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
+                                  [x_panel, wv], [pos_read, (vc, WRITE, "whole")],
+                                  "v projection"))
             new_nodes.append(node("ckl.fused.attention",
                                   [R(qr), R(kc), R(vc), R(position), R(context_panel), scale],
                                   pack(B, A, T, D, L_, layer, 1, 0, 1),
@@ -409,10 +410,12 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
                                   [(r_panel, WRITE, "whole")], "mlp norm"))
             new_nodes.append(node("ckl.fused.panel_linear", [R(r_panel), R(wg), R(gate)],
                                   gemm_spec(B, Cdim, F, shape(wg)[0], layer),
-                                  [r_panel, wg], [(gate, WRITE, "whole")], "gate projection"))
+                                  [r_panel, wg], [(gate, WRITE, "whole")],
+                                  "gate projection"))
             new_nodes.append(node("ckl.fused.panel_linear", [R(r_panel), R(wu), R(up)],
                                   gemm_spec(B, Cdim, F, shape(wu)[0], layer),
-                                  [r_panel, wu], [(up, WRITE, "whole")], "up projection"))
+                                  [r_panel, wu], [(up, WRITE, "whole")],
+                                  "up projection"))
             new_nodes.append(node("ckl.fused.swiglu_panel", [R(gate), R(up), R(p_panel)],
                                   pack(B, F), [gate, up], [(p_panel, WRITE, "whole")], "swiglu"))
             new_nodes.append(node("ckl.fused.panel_linear_residual",
