@@ -277,7 +277,8 @@ def gpu_arm(args, workload, world, rank, local, group):
     position = int(sess.read("position")[0])
     per_node = inv.profile_nodes(1)
     names = inv.node_names
-    attention = [t for n, t in zip(names, per_node) if n == "ckl.fused.attention"]
+    attention_kernel = "ckl.fused.attention"
+    attention = [t for n, t in zip(names, per_node) if n == attention_kernel]
     hbm, peak_kind = peaks()
     roofline = None
     if attention:
@@ -285,7 +286,7 @@ def gpu_arm(args, workload, world, rank, local, group):
         algorithmic = 2 * b * a * n_rows * (h // a) * 4 + 2 * b * h * 4
         launch_ms = statistics.mean(attention)
         achieved = algorithmic / (launch_ms / 1000.0) / 1e9
-        roofline = {"bound": "hbm", "kernel": "ckl.fused.attention", "achieved": achieved,
+        roofline = {"bound": "hbm", "kernel": attention_kernel, "achieved": achieved,
                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
                     "traffic": None, "algorithmic_bytes_per_launch": algorithmic,
                     "launch_ms": launch_ms, "launches_profiled": len(attention),

@@ -90,13 +90,18 @@ struct GreedySpec {
 //   M rows (requests), K inner, N outputs; W holds `layers` matrices [K, N].
 //   Cache-writing epilogues address cache[L=layers, M, A, T, D] at position[0].
 //   `tiles` is the number of column tiles of the argmax epilogue (partials per row).
+//   `cache` is the request count of the cache's batch dimension (M when 0): a projection over
+//   a slice of the requests passes the cache pointer offset to its first request.
 struct GemmSpec {
-  int64_t M, K, N, layers, layer, A, D, T, tiles, config;
+  int64_t M, K, N, layers, layer, A, D, T, tiles, config, cache;
 };
 // Flash-decoding attention over cache[L, B, A, T, D] at positions 0..position[0].
 // `panel` 1 writes the context as a split tensor-core operand (panel.cuh) instead of [B, A*D].
+// `rows` requests (B when 0) are processed, starting at the request the q, cache and context
+// pointers point to; B is the cache's batch dimension.  `grid` caps the CTAs (0: one per
+// request and head), which then loop over (request, head) pairs.
 struct AttentionSpec {
-  int64_t B, A, T, D, L, layer, splits, chunk, panel;
+  int64_t B, A, T, D, L, layer, splits, chunk, panel, rows, grid;
 };
 // Greedy combine of per-tile argmax partials [B, tiles] of (value, index).
 struct CombineSpec {

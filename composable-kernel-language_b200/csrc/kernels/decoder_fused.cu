@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "panel.cuh"
+#include "softmax.cuh"
 
 namespace ckl::kernels {
 namespace {
@@ -133,36 +134,6 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
 // One CTA per (request, head): WARPS warps stream the K and V rows 0..p of the cache with
 // 16-byte loads, D/4 lanes per row; each lane group keeps an online softmax state
 // (running max, normaliser, weighted V) and the states merge across groups and warps.
-struct SoftmaxState {
-  float m, l;
-  float4 acc;
-};
-
-__device__ __forceinline__ void mergeState(SoftmaxState &a, const SoftmaxState &b) {
-  const float M = fmaxf(a.m, b.m);
-  if (M == -CUDART_INF_F)
-    return; // both empty
-  const float ca = a.m == -CUDART_INF_F ? 0.f : expf(a.m - M);
-  const float cb = b.m == -CUDART_INF_F ? 0.f : expf(b.m - M);
-  a.l = a.l * ca + b.l * cb;
-  a.acc.x = a.acc.x * ca + b.acc.x * cb;
-  a.acc.y = a.acc.y * ca + b.acc.y * cb;
-  a.acc.z = a.acc.z * ca + b.acc.z * cb;
-  a.acc.w = a.acc.w * ca + b.acc.w * cb;
-  a.m = M;
-}
-
-__device__ __forceinline__ SoftmaxState shuffleState(const SoftmaxState &s, int offset) {
-  SoftmaxState o;
-  o.m = __shfl_xor_sync(0xffffffffu, s.m, offset);
-  o.l = __shfl_xor_sync(0xffffffffu, s.l, offset);
-  o.acc.x = __shfl_xor_sync(0xffffffffu, s.acc.x, offset);
-  o.acc.y = __shfl_xor_sync(0xffffffffu, s.acc.y, offset);
-  o.acc.z = __shfl_xor_sync(0xffffffffu, s.acc.z, offset);
-  o.acc.w = __shfl_xor_sync(0xffffffffu, s.acc.w, offset);
-  return o;
-}
-
 constexpr int kAttentionWarps = 4;
 constexpr int kAttentionUnroll = 4;
 
@@ -175,81 +146,84 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
   constexpr int STEP = kAttentionWarps * RPW;
   __shared__ SoftmaxState warpState[kAttentionWarps][LPR];
 
-  const int64_t bh = blockIdx.x;
-  const int64_t h = bh % s.A, b = bh / s.A;
+  const int64_t rows = s.rows > 0 ? s.rows : s.B;
   const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
   const int group = lane / LPR, sub = lane % LPR;
   const int64_t C = s.A * D;
   const int p = position[0];
   const int64_t end = int64_t(p) + 1;
   const int64_t n = end < 0 ? 0 : (end < s.T ? end : s.T);
-
-  const float4 qv = *reinterpret_cast<const float4 *>(q + b * C + h * D + 4 * sub);
-  const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D + 4 * sub;
-  const float4 *kRows = reinterpret_cast<const float4 *>(kc + base);
-  const float4 *vRows = reinterpret_cast<const float4 *>(vc + base);
   constexpr int ROW4 = D / 4; // float4 per row
 
-  SoftmaxState st{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
-  for (int64_t t0 = int64_t(warp) * RPW; t0 < n; t0 += int64_t(STEP) * kAttentionUnroll) {
-    float4 kv[kAttentionUnroll], vv[kAttentionUnroll];
-    bool valid[kAttentionUnroll];
+  for (int64_t bh = blockIdx.x; bh < rows * s.A; bh += gridDim.x) {
+    const int64_t h = bh % s.A, b = bh / s.A;
+    const float4 qv = *reinterpret_cast<const float4 *>(q + b * C + h * D + 4 * sub);
+    const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D + 4 * sub;
+    const float4 *kRows = reinterpret_cast<const float4 *>(kc + base);
+    const float4 *vRows = reinterpret_cast<const float4 *>(vc + base);
+
+    SoftmaxState st{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int64_t t0 = int64_t(warp) * RPW; t0 < n; t0 += int64_t(STEP) * kAttentionUnroll) {
+      float4 kv[kAttentionUnroll], vv[kAttentionUnroll];
+      bool valid[kAttentionUnroll];
 #pragma unroll
-    for (int u = 0; u < kAttentionUnroll; ++u) {
-      const int64_t t = t0 + int64_t(u) * STEP + group;
-      valid[u] = t < n;
-      if (valid[u]) {
-        kv[u] = __ldcs(kRows + t * ROW4);
-        vv[u] = __ldcs(vRows + t * ROW4);
-      } else {
-        kv[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < kAttentionUnroll; ++u) {
+        const int64_t t = t0 + int64_t(u) * STEP + group;
+        valid[u] = t < n;
+        if (valid[u]) {
+          kv[u] = __ldcs(kRows + t * ROW4);
+          vv[u] = __ldcs(vRows + t * ROW4);
+        } else {
+          kv[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kAttentionUnroll; ++u) {
+        float dot = qv.x * kv[u].x + qv.y * kv[u].y + qv.z * kv[u].z + qv.w * kv[u].w;
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1)
+          dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (valid[u]) {
+          const float score = dot * scale;
+          const float M = fmaxf(st.m, score);
+          const float c = st.m == -CUDART_INF_F ? 0.f : expf(st.m - M);
+          const float e = expf(score - M);
+          st.l = st.l * c + e;
+          st.acc.x = st.acc.x * c + e * vv[u].x;
+          st.acc.y = st.acc.y * c + e * vv[u].y;
+          st.acc.z = st.acc.z * c + e * vv[u].z;
+          st.acc.w = st.acc.w * c + e * vv[u].w;
+          st.m = M;
+        }
       }
     }
+    // Merge the lane groups of the warp (same `sub`, different rows).
 #pragma unroll
-    for (int u = 0; u < kAttentionUnroll; ++u) {
-      float dot = qv.x * kv[u].x + qv.y * kv[u].y + qv.z * kv[u].z + qv.w * kv[u].w;
+    for (int o = LPR; o < kWarp; o <<= 1) {
+      const SoftmaxState other = shuffleState(st, o);
+      mergeState(st, other);
+    }
+    if (group == 0)
+      warpState[warp][sub] = st;
+    __syncthreads();
+    if (warp == 0 && group == 0) {
+      SoftmaxState total = warpState[0][sub];
 #pragma unroll
-      for (int o = LPR / 2; o > 0; o >>= 1)
-        dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      if (valid[u]) {
-        const float score = dot * scale;
-        const float M = fmaxf(st.m, score);
-        const float c = st.m == -CUDART_INF_F ? 0.f : expf(st.m - M);
-        const float e = expf(score - M);
-        st.l = st.l * c + e;
-        st.acc.x = st.acc.x * c + e * vv[u].x;
-        st.acc.y = st.acc.y * c + e * vv[u].y;
-        st.acc.z = st.acc.z * c + e * vv[u].z;
-        st.acc.w = st.acc.w * c + e * vv[u].w;
-        st.m = M;
+      for (int w = 1; w < kAttentionWarps; ++w)
+        mergeState(total, warpState[w][sub]);
+      float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (total.l > 0.f) {
+        out.x = total.acc.x / total.l;
+        out.y = total.acc.y / total.l;
+        out.z = total.acc.z / total.l;
+        out.w = total.acc.w / total.l;
       }
+      if (s.panel)
+        panel::store4(ctx, b, h * D + 4 * sub, C, out); // split operand of the o projection
+      else
+        *reinterpret_cast<float4 *>(ctx + b * C + h * D + 4 * sub) = out;
     }
-  }
-  // Merge the lane groups of the warp (same `sub`, different rows).
-#pragma unroll
-  for (int o = LPR; o < kWarp; o <<= 1) {
-    const SoftmaxState other = shuffleState(st, o);
-    mergeState(st, other);
-  }
-  if (group == 0)
-    warpState[warp][sub] = st;
-  __syncthreads();
-  if (warp == 0 && group == 0) {
-    SoftmaxState total = warpState[0][sub];
-#pragma unroll
-    for (int w = 1; w < kAttentionWarps; ++w)
-      mergeState(total, warpState[w][sub]);
-    float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (total.l > 0.f) {
-      out.x = total.acc.x / total.l;
-      out.y = total.acc.y / total.l;
-      out.z = total.acc.z / total.l;
-      out.w = total.acc.w / total.l;
-    }
-    if (s.panel)
-      panel::store4(ctx, b, h * D + 4 * sub, C, out); // split operand of the o projection
-    else
-      *reinterpret_cast<float4 *>(ctx + b * C + h * D + 4 * sub) = out;
+    __syncthreads(); // warpState is reused by the next (request, head)
   }
 }
 
@@ -259,9 +233,11 @@ bool attentionGeometry(const void *spec, std::size_t, library::Geometry *g) {
     return false;
   if (s.D != 16 && s.D != 32 && s.D != 64 && s.D != 128)
     return false;
-  if (s.B * s.A >= (int64_t(1) << 31))
+  const int64_t rows = s.rows > 0 ? s.rows : s.B;
+  if (s.rows < 0 || rows > s.B || s.grid < 0 || rows * s.A >= (int64_t(1) << 31))
     return false;
-  g->grid[0] = unsigned(s.B * s.A);
+  const int64_t pairs = rows * s.A;
+  g->grid[0] = unsigned(s.grid > 0 && s.grid < pairs ? s.grid : pairs);
   g->block[0] = kAttentionWarps * kWarp;
   return true;
 }

@@ -5,8 +5,8 @@
 // that produces it, and every projection then runs the tcgen05 3xTF32 kernel (tcgemm.cuh) on
 // that panel with the layer's FP32 weights:
 //   rms_panel:    panel = split(RMSNorm(x) * gain)        (feeds q/k/v, gate/up, lm head)
-//   swiglu_panel: panel = split(silu(gate) * up)          (feeds the down projection)
 //   attention writes its context rows as a panel           (feeds the o projection)
+//   panel_gate_up: panel = split(silu(a @ wg) * (a @ wu))  (feeds the down projection)
 //   panel_linear{,_rope,_rope_append,_append,_residual,_argmax}: the projections with the same
 //   fused epilogues as the FFMA kernels.
 // The normalised and activated values are rounded exactly as in the FFMA kernels
@@ -108,46 +108,6 @@ bool rmsPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
   return true;
 }
 
-__device__ __forceinline__ float swiglu(float g, float u) {
-  return __fmul_rn(g / (1.0f + expf(-g)), u);
-}
-
-// One thread per four consecutive columns of a row (rows [B], columns padded to 32).
-__global__ void __launch_bounds__(256)
-    swigluPanelKernel(const float *gate, const float *up, float *out, RowsSpec s) {
-  const int64_t K = s.C;
-  const int64_t quads = panel::slices(K) * (panel::kSlice / 4);
-  const int64_t total = s.B * quads;
-  const bool vec = K % 4 == 0 && aligned16(gate) && aligned16(up);
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t m = i / quads, k = 4 * (i % quads);
-    float4 v;
-    if (vec && k < K) {
-      const float4 a = reinterpret_cast<const float4 *>(gate + m * K)[k / 4];
-      const float4 b = reinterpret_cast<const float4 *>(up + m * K)[k / 4];
-      v = make_float4(swiglu(a.x, b.x), swiglu(a.y, b.y), swiglu(a.z, b.z), swiglu(a.w, b.w));
-    } else {
-      float *lanes = &v.x;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        lanes[j] = k + j < K ? swiglu(gate[m * K + k + j], up[m * K + k + j]) : 0.f;
-    }
-    panel::store4(out, m, k, K, v);
-  }
-}
-
-bool swigluPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
-  const auto &s = specOf<RowsSpec>(spec);
-  if (s.B <= 0 || s.C <= 0)
-    return false;
-  const int64_t wanted = ceilDiv(s.B * panel::slices(s.C) * (panel::kSlice / 4), 256 * 4);
-  const int64_t cap = 148 * 8 * 4;
-  g->grid[0] = unsigned(wanted > cap ? cap : wanted);
-  g->block[0] = 256;
-  return true;
-}
-
 // ---- projections on a panel ------------------------------------------------------------------
 // Every projection takes the panel of A, the weights [layers, K, N], its outputs, the
 // specialization and (last, added at bind time) the weights' tensor map.  SPLITS > 1 splits
@@ -178,6 +138,26 @@ CKL_PANEL_KERNEL(panelLinearResidualTc, gemm::kResidual, (const float *residual,
 CKL_PANEL_KERNEL(panelLinearArgmaxTc, gemm::kArgmax, (float *logits, float2 *partials),
                  (p.out = logits, p.partials = partials))
 
+// Fused gate/up/SwiGLU: out is the panel of silu(a @ wg) * (a @ wu) [M, N].
+__global__ void __launch_bounds__(tc::kThreads)
+    panelGateUpTc(const float *a, const float *wg, const float *wu, float *out, GemmSpec s,
+                  const __grid_constant__ tc::WeightMapPair maps) {
+  Params p;
+  p.a = a, p.w = wg, p.w2 = wu, p.out = out, p.s = s;
+  tc::body<128, gemm::kSwiGluPanel, 1>(p, maps.gate, &maps.up);
+}
+
+bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
+    return false;
+  g->grid[0] = ceilDiv(s.N, tc::BM / 2);
+  g->grid[1] = ceilDiv(s.M, tc::BM);
+  g->block[0] = tc::kThreads;
+  g->sharedBytes = unsigned(tc::sharedBytes(128));
+  return g->grid[1] <= 65535;
+}
+
 // Tensor map of the weights [layers, K, N] for the kernel's column width, built once per bound
 // node from the resolved weight pointer (slot 1 of every panel projection).  Weights whose
 // shape or address admit no map get valid == 0 and are read with plain loads.
@@ -202,28 +182,53 @@ EncodeTiledFn encodeTiled() {
   return fn;
 }
 
+// Map of the weights at `address` with a box of `width` columns x 32 rows x 1 layer.
+tc::WeightMap weightMap(uint64_t address, const GemmSpec &s, int width) {
+  tc::WeightMap local;
+  std::memset(&local, 0, sizeof(local));
+  const EncodeTiledFn encode = encodeTiled();
+  if (encode != nullptr && s.N % 4 == 0 && address % 16 == 0 && s.K > 0 && s.N > 0 &&
+      s.layers > 0) {
+    const cuuint64_t dims[3] = {cuuint64_t(s.N), cuuint64_t(s.K), cuuint64_t(s.layers)};
+    const cuuint64_t strides[2] = {cuuint64_t(s.N) * 4, cuuint64_t(s.K) * cuuint64_t(s.N) * 4};
+    const cuuint32_t box[3] = {cuuint32_t(width), cuuint32_t(tc::BK), 1};
+    const cuuint32_t unit[3] = {1, 1, 1};
+    const CUresult status =
+        encode(&local.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, reinterpret_cast<void *>(address),
+               dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    local.valid = status == CUDA_SUCCESS ? 1 : 0;
+  }
+  return local;
+}
+
+uint64_t pointerSlot(const void *const *arguments, std::size_t index) {
+  uint64_t address = 0;
+  std::memcpy(&address, arguments[index], sizeof(address));
+  return address;
+}
+
 bool prepareWeights(const void *spec, const void *const *arguments, std::size_t count,
                     void *extra) {
   if (spec == nullptr || count < 2)
     return false;
   const GemmSpec &s = specOf<GemmSpec>(spec);
-  tc::WeightMap local;
-  std::memset(&local, 0, sizeof(local));
-  uint64_t w = 0;
-  std::memcpy(&w, arguments[1], sizeof(w));
-  const EncodeTiledFn encode = encodeTiled();
-  if (encode != nullptr && s.N % 4 == 0 && w % 16 == 0 && s.K > 0 && s.N > 0 && s.layers > 0) {
-    const cuuint64_t dims[3] = {cuuint64_t(s.N), cuuint64_t(s.K), cuuint64_t(s.layers)};
-    const cuuint64_t strides[2] = {cuuint64_t(s.N) * 4, cuuint64_t(s.K) * cuuint64_t(s.N) * 4};
-    const cuuint32_t box[3] = {cuuint32_t(tc::chooseWidth(s)), cuuint32_t(tc::BK), 1};
-    const cuuint32_t unit[3] = {1, 1, 1};
-    const CUresult status =
-        encode(&local.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, reinterpret_cast<void *>(w), dims,
-               strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    local.valid = status == CUDA_SUCCESS ? 1 : 0;
-  }
-  std::memcpy(extra, &local, sizeof(local));
+  const tc::WeightMap map = weightMap(pointerSlot(arguments, 1), s, tc::chooseWidth(s));
+  std::memcpy(extra, &map, sizeof(map));
+  return true;
+}
+
+// Gate weights in slot 1, up weights in slot 2; boxes of half a tile each.
+bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t count,
+                   void *extra) {
+  if (spec == nullptr || count < 3)
+    return false;
+  const GemmSpec &s = specOf<GemmSpec>(spec);
+  tc::WeightMapPair maps;
+  maps.gate = weightMap(pointerSlot(arguments, 1), s, tc::BM / 2);
+  maps.up = weightMap(pointerSlot(arguments, 2), s, tc::BM / 2);
+  std::memcpy(extra, &maps, sizeof(maps));
   return true;
 }
 
@@ -277,8 +282,9 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
 
 CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPanelKernel),
                     "PPPFS", sizeof(RmsApplySpec), rmsPanelGeometry, nullptr);
-CKL_REGISTER_KERNEL("ckl.fused.swiglu_panel", reinterpret_cast<const void *>(&swigluPanelKernel),
-                    "PPPS", sizeof(RowsSpec), swigluPanelGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&panelGateUpTc),
+                    "PPPPS", sizeof(GemmSpec), gateUpGeometry, nullptr, prepareGateUp,
+                    sizeof(tc::WeightMapPair));
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc),
                     prepareWeights, sizeof(tc::WeightMap));

@@ -18,13 +18,18 @@
 namespace ckl::kernels::gemm {
 
 enum Prologue : int { kPlain = 0, kRms = 1, kSwiGlu = 2 };
-enum Epilogue : int { kStore = 0, kResidual = 1, kRope = 2, kRopeAppend = 3, kAppend = 4, kArgmax = 5 };
+// kSwiGluPanel (tensor-core path only): the tile's columns are gate and up projections of the
+// same outputs; the epilogue writes silu(gate) * up as a split operand panel.
+enum Epilogue : int {
+  kStore = 0, kResidual = 1, kRope = 2, kRopeAppend = 3, kAppend = 4, kArgmax = 5, kSwiGluPanel = 6
+};
 
 struct Params {
   const float *a = nullptr;        // [M, K]
   const float *a2 = nullptr;       // [M, K] up projection (SwiGLU)
   const float *gain = nullptr;     // [layers, K] (RMSNorm)
   const float *w = nullptr;        // [layers, K, N]
+  const float *w2 = nullptr;       // [layers, K, N] up projection (kSwiGluPanel)
   const float *residual = nullptr; // [M, N]
   const float *table = nullptr;    // [T, D/2, 2]
   const int *position = nullptr;   // [1]

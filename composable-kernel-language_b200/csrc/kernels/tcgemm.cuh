@@ -61,6 +61,21 @@ struct WeightMap {
   int valid;
 };
 
+// Gate and up weights of the fused gate/up/SwiGLU projection, each with a box of BN/2 columns.
+struct WeightMapPair {
+  WeightMap gate, up;
+};
+
+// Output columns of one tile: the gate/up tile holds BN/2 gate and BN/2 up columns of the same
+// BN/2 outputs.
+template <int BN, int EPI> constexpr int tileColumns() {
+  return EPI == gemm::kSwiGluPanel ? BN / 2 : BN;
+}
+
+__device__ __forceinline__ float swigluValue(float g, float u) {
+  return __fmul_rn(g / (1.0f + expf(-g)), u);
+}
+
 // Fault word of the library (bit 0: a tensor-core wait expired).  One translation unit
 // instantiates these kernels and reports the word (ckl_library_faults).
 static __device__ unsigned g_libraryFaults = 0;
@@ -315,7 +330,8 @@ __device__ __forceinline__ void storeQuad(const gemm::Params &p, int64_t m, int6
         p.out[m * N + c] = first;
         p.out[m * N + c + 1] = second;
       } else {
-        float *slot = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
+        const int64_t rows = s.cache > 0 ? s.cache : M;
+        float *slot = p.out + (((s.layer * rows + m) * s.A + h) * s.T + position) * D + d;
         slot[0] = first;
         slot[1] = second;
       }
@@ -365,7 +381,7 @@ template <int BN, int EPI, int SPLITS>
 __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN> &stage,
                                                int64_t m0, int64_t nt, int position) {
   const GemmSpec &s = p.s;
-  const int64_t M = s.M, N = s.N, n0 = nt * BN;
+  const int64_t M = s.M, N = s.N, n0 = nt * tileColumns<BN, EPI>();
   const int warp = threadIdx.x / kWarp - 2, lane = threadIdx.x % kWarp;
   const unsigned rank = blockIdx.z;
   constexpr int kRows = BM / SPLITS;
@@ -391,8 +407,27 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
                             __fadd_rn(sum.z, part.z), __fadd_rn(sum.w, part.w));
         }
       }
-      if (n0 + c < N)
+      if constexpr (EPI == gemm::kSwiGluPanel) {
+        // Lanes 0-15 hold gate columns, lanes 16-31 the up columns of the same outputs.
+        static_assert(BN == 4 * kWarp, "one quad of columns per lane");
+        const float4 up = make_float4(__shfl_down_sync(0xffffffffu, sum.x, 16),
+                                      __shfl_down_sync(0xffffffffu, sum.y, 16),
+                                      __shfl_down_sync(0xffffffffu, sum.z, 16),
+                                      __shfl_down_sync(0xffffffffu, sum.w, 16));
+        const int64_t k = n0 + c; // output column (the panel's K)
+        const int64_t padded = panel::slices(N) * panel::kSlice;
+        if (lane < 16 && k < padded) {
+          const float *g = &sum.x, *u = &up.x;
+          float4 v;
+          float *out = &v.x;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            out[j] = k + j < N ? swigluValue(g[j], u[j]) : 0.f;
+          panel::store4(p.out, m, k, N, v);
+        }
+      } else if (n0 + c < N) {
         storeQuad<EPI>(p, m, n0 + c, sum, position, vec4, best, bestIndex);
+      }
     }
     if constexpr (EPI == gemm::kArgmax) {
 #pragma unroll
@@ -409,7 +444,9 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
 
 // One 128 x BN tile.  p.a is the panel of A [M, K]; p.w the weights [layers, K, N].
 template <int BN, int EPI, int SPLITS>
-__device__ void body(const gemm::Params &p, const WeightMap &weights) {
+__device__ void body(const gemm::Params &p, const WeightMap &weights,
+                     const WeightMap *upWeights = nullptr) {
+  static_assert(EPI != gemm::kSwiGluPanel || (SPLITS == 1 && BN == 128), "gate/up tiles");
   static_assert(SPLITS == 1 || BN == 128, "K splits use full-width tiles");
   static_assert(sizeof(Staging<BN>) <= sizeof(Smem<BN, stages<BN>()>::a), "staging fits the ring");
   constexpr int S = stages<BN>();
@@ -424,7 +461,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights) {
   const int64_t rowTiles = gridDim.y;
   const int64_t tile = int64_t(blockIdx.y) * gridDim.x + blockIdx.x;
   const int64_t mt = tile % rowTiles, nt = tile / rowTiles;
-  const int64_t m0 = mt * BM, n0 = nt * BN;
+  const int64_t m0 = mt * BM, n0 = nt * tileColumns<BN, EPI>();
   // This split's K slices [kBegin, kEnd).
   const int64_t allSlices = panel::slices(K);
   const int64_t perSplit = (allSlices + SPLITS - 1) / SPLITS;
@@ -447,7 +484,9 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights) {
     return;
   }
   // Weight boxes by TMA when the buffer admits a tensor map.
-  const bool copyRows = weights.valid != 0;
+  const bool copyRows =
+      weights.valid != 0 && (EPI != gemm::kSwiGluPanel || upWeights->valid != 0);
+  const float *W2 = EPI == gemm::kSwiGluPanel ? p.w2 + s.layer * K * N : nullptr;
 
   if (warp == kMmaWarp)
     tmemAlloc<2 * BN>(&sm.tmemBase);
@@ -473,9 +512,14 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights) {
   if (warp == kProducerWarp) {
     const unsigned boxBytes = copyRows ? unsigned(BK * BN * 4) : 0u; // full box, OOB zero-filled
     int64_t issued = 0;
-    if (lane == 0 && copyRows)
+    if (lane == 0 && copyRows) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&weights.map))
                    : "memory");
+      if constexpr (EPI == gemm::kSwiGluPanel)
+        asm volatile("prefetch.tensormap [%0];"
+                     ::"l"(reinterpret_cast<unsigned long long>(&upWeights->map))
+                     : "memory");
+    }
     for (int64_t kt = 0; kt < slices; ++kt) {
       const int slot = int(kt % S);
       bool ok = true;
@@ -487,10 +531,19 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights) {
         mbarrierArriveExpectTx(&sm.full[slot], unsigned(2 * panel::kPart * 4) + boxBytes);
         bulkCopy(&sm.a[slot][0][0][0][0], blocks + (kBegin + kt) * panel::kBlock,
                  unsigned(2 * panel::kPart * 4), &sm.full[slot]);
-        if (copyRows)
-          tensorCopy(&sm.rawB[slot][0][0], &weights.map, int(n0), int((kBegin + kt) * BK),
-                     int(s.layer),
-                     &sm.full[slot]);
+        if (copyRows) {
+          const int k0 = int((kBegin + kt) * BK);
+          if constexpr (EPI == gemm::kSwiGluPanel) {
+            // Gate box, then up box: [2][BK][BN / 2] in the stage.
+            tensorCopy(&sm.rawB[slot][0][0], &weights.map, int(n0), k0, int(s.layer),
+                       &sm.full[slot]);
+            tensorCopy(&sm.rawB[slot][0][0] + BK * (BN / 2), &upWeights->map, int(n0), k0,
+                       int(s.layer), &sm.full[slot]);
+          } else {
+            tensorCopy(&sm.rawB[slot][0][0], &weights.map, int(n0), k0, int(s.layer),
+                       &sm.full[slot]);
+          }
+        }
       }
       issued = kt + 1;
     }
@@ -550,10 +603,18 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights) {
           const int64_t k = k0 + 4 * c + j;
           float value = 0.f;
           if (k < K) {
-            if (copyRows)
-              value = sm.rawB[slot][4 * c + j][n];
-            else if (n0 + n < N)
-              value = W[k * N + n0 + n];
+            if constexpr (EPI == gemm::kSwiGluPanel) {
+              const int half = n / (BN / 2), col = n % (BN / 2);
+              if (copyRows)
+                value = (&sm.rawB[slot][0][0])[(half * BK + 4 * c + j) * (BN / 2) + col];
+              else if (n0 + col < N)
+                value = (half ? W2 : W)[k * N + n0 + col];
+            } else {
+              if (copyRows)
+                value = sm.rawB[slot][4 * c + j][n];
+              else if (n0 + n < N)
+                value = W[k * N + n0 + n];
+            }
           }
           lanes[j] = value;
         }

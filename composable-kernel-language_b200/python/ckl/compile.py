@@ -278,7 +278,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
             raise _NoMatch
 
     def gemm_spec(M, K, N, layers_, layer, A=0, D=0, T=0, tiles=0):
-        return pack(M, K, N, layers_, layer, A, D, T, tiles, config)
+        return pack(M, K, N, layers_, layer, A, D, T, tiles, config, M)
 
     embedding = dispatches[0]
     x = res(embedding, 2)
@@ -397,7 +397,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
                                   "v projection"))
             new_nodes.append(node("ckl.fused.attention",
                                   [R(qr), R(kc), R(vc), R(position), R(context_panel), scale],
-                                  pack(B, A, T, D, L_, layer, 1, 0, 1),
+                                  pack(B, A, T, D, L_, layer, 1, 0, 1, B, 0),
                                   [qr, kc, vc], [pos_read, (context_panel, WRITE, "whole")],
                                   "attention"))
             new_nodes.append(node("ckl.fused.panel_linear_residual",
@@ -408,22 +408,18 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
             new_nodes.append(node("ckl.fused.rms_panel", [R(residual), R(g2), R(r_panel), eps2],
                                   pack(B, Cdim, shape(g2)[0], layer), [residual, g2],
                                   [(r_panel, WRITE, "whole")], "mlp norm"))
-            new_nodes.append(node("ckl.fused.panel_linear", [R(r_panel), R(wg), R(gate)],
+            new_nodes.append(node("ckl.fused.panel_gate_up",
+                                  [R(r_panel), R(wg), R(wu), R(p_panel)],
                                   gemm_spec(B, Cdim, F, shape(wg)[0], layer),
-                                  [r_panel, wg], [(gate, WRITE, "whole")],
-                                  "gate projection"))
-            new_nodes.append(node("ckl.fused.panel_linear", [R(r_panel), R(wu), R(up)],
-                                  gemm_spec(B, Cdim, F, shape(wu)[0], layer),
-                                  [r_panel, wu], [(up, WRITE, "whole")],
-                                  "up projection"))
-            new_nodes.append(node("ckl.fused.swiglu_panel", [R(gate), R(up), R(p_panel)],
-                                  pack(B, F), [gate, up], [(p_panel, WRITE, "whole")], "swiglu"))
+                                  [r_panel, wg, wu], [(p_panel, WRITE, "whole")],
+                                  "gate/up projection + swiglu"))
             new_nodes.append(node("ckl.fused.panel_linear_residual",
                                   [R(p_panel), R(wd), R(residual), R(next_x)],
                                   gemm_spec(B, F, Cdim, shape(wd)[0], layer),
                                   [p_panel, wd, residual], [(next_x, WRITE, "whole")],
                                   "down projection"))
-            eliminated_here.append((context, (d[10], d[11])))
+            eliminated_here += [(context, (d[10], d[11])), (gate, (d[15], d[17])),
+                                (up, (d[16], d[18]))]
         else:
             new_nodes.append(node("ckl.fused.norm_linear_rope",
                                   [R(x), R(g1), R(wq), R(sincos), R(position), R(qr), eps1],
@@ -441,7 +437,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
                                   [x, g1, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
             new_nodes.append(node("ckl.fused.attention",
                                   [R(qr), R(kc), R(vc), R(position), R(context), scale],
-                                  pack(B, A, T, D, L_, layer, 1, 0, 0),
+                                  pack(B, A, T, D, L_, layer, 1, 0, 0, B, 0),
                                   [qr, kc, vc], [pos_read, (context, WRITE, "whole")],
                                   "attention"))
             new_nodes.append(node("ckl.fused.linear_residual",

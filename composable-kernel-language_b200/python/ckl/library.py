@@ -41,7 +41,7 @@ def _extents(grid, block):
 
 
 def _gemm(M, K, N, layers, layer, A=0, D=0, T=0, tiles=0, config=0):
-    return pack(M, K, N, layers, layer, A, D, T, tiles, config)
+    return pack(M, K, N, layers, layer, A, D, T, tiles, config, M)
 
 
 # Shapes are the runtime buffer operands' shapes in parameter order; constants are the

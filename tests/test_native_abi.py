@@ -53,7 +53,7 @@ def test_library_catalogue_and_geometry():
     lib = _native.load()
     names = {lib.ckl_library_name(i).decode() for i in range(lib.ckl_library_count())}
     assert {"ckl.pointwise.add_scalar", "ckl.fused.attention", "ckl.decoder.greedy"} <= names
-    grid, block, shared = library_geometry("ckl.decoder.linear", pack(512, 1024, 4096, 4, 1, 0, 0, 0, 0, 0))
+    grid, block, shared = library_geometry("ckl.decoder.linear", pack(512, 1024, 4096, 4, 1, 0, 0, 0, 0, 0, 512))
     assert grid[0] >= 1 and block[0] in (128, 256) and shared == 0
     with pytest.raises(Exception):
         library_geometry("ckl.decoder.linear", pack(1, 2, 3))          # wrong spec size

@@ -139,16 +139,15 @@ def test_tensor_core_decoder_plan_shape():
     layer = ["ckl.fused.rms_panel", "ckl.fused.panel_linear_rope",
              "ckl.fused.panel_linear_rope_append", "ckl.fused.panel_linear_append",
              "ckl.fused.attention", "ckl.fused.panel_linear_residual", "ckl.fused.rms_panel",
-             "ckl.fused.panel_linear", "ckl.fused.panel_linear", "ckl.fused.swiglu_panel",
-             "ckl.fused.panel_linear_residual"]
+             "ckl.fused.panel_gate_up", "ckl.fused.panel_linear_residual"]
     head = ["ckl.fused.rms_panel", "ckl.fused.panel_linear_argmax", "ckl.fused.greedy_combine"]
     assert names == ["ckl.decoder.embedding"] + layer * 2 + head
     topology = plans.primary.topology
     ids = sorted(topology)
     norm, q, k, v = ids[1:5]
     assert topology[q] == topology[k] == topology[v] == [norm]
-    gate, up = ids[8], ids[9]
-    assert topology[gate] == topology[up] == [ids[7]]
+    gate_up, down = ids[8], ids[9]
+    assert topology[gate_up] == [ids[7]] and topology[down] == [gate_up]
     # FFMA projections when tensor cores are switched off.
     ffma = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
                         tensor_cores=False)
