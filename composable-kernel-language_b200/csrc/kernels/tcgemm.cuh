@@ -18,10 +18,10 @@
 //     landed and the weight slice is converted, one thread issues up to 4 k-steps x 3
 //     `tcgen05.mma.cta_group::1.kind::tf32` (M=128, N=BN, K=8) and commits them to the
 //     stage's `empty` and the weight buffer's `bEmpty` mbarriers;
-//   warps 2-5 (converters, then epilogue): split each landed weight slice into TF32 hi/lo in
+//   warps 2-9 (converters, then epilogue): split each landed weight slice into TF32 hi/lo in
 //     K-major no-swizzle layout (two buffers), then read the accumulators with
-//     `tcgen05.ld.32x32b` (warp w reads TMEM lanes 32 (w % 4).., one output row per thread)
-//     and apply the fused epilogue.
+//     `tcgen05.ld.32x32b` (warp w reads TMEM lanes 32 (w % 4).., one output row per thread,
+//     half of the columns each) and apply the fused epilogue.
 // A tf32 MMA costs about the same at N = 32 as at N = 128, so tiles are 128 columns wide
 // (narrower only for narrow outputs) and the K loop is split over gridDim.z CTAs when the
 // output has too few tiles to fill the GPU.  Each split writes its partial tile to a
@@ -48,7 +48,7 @@ constexpr int BM = panel::kRows;
 constexpr int BK = panel::kSlice;
 constexpr int kProducerWarp = 0;
 constexpr int kMmaWarp = 1;
-constexpr int kConverterWarps = 4; // warps 2..5; also the epilogue
+constexpr int kConverterWarps = 8; // warps 2..9; also the epilogue (two warps per TMEM lane quarter)
 constexpr int kConverterThreads = kConverterWarps * kWarp;
 constexpr int kThreads = (2 + kConverterWarps) * kWarp;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull; // 2 s
@@ -591,7 +591,28 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       if (!__all_sync(0xffffffffu, ok))
         break;
       const int64_t k0 = (kBegin + kt) * BK;
-      // Group i: four consecutive k (chunk c) of column n.
+      // Group i: four consecutive k (chunk c) of column n.  Full slices of copied boxes need no
+      // bounds checks (the box is zero-filled beyond N).
+      if (copyRows && k0 + BK <= K) {
+#pragma unroll
+        for (int g = 0; g < (BK / 4) * BN / kConverterThreads; ++g) {
+          const int i = t + g * kConverterThreads;
+          const int c = i / BN, n = i % BN;
+          float4 v;
+          if constexpr (EPI == gemm::kSwiGluPanel) {
+            const float *box = &sm.rawB[slot][0][0] + (n / (BN / 2)) * BK * (BN / 2) + n % (BN / 2);
+            v = make_float4(box[(4 * c) * (BN / 2)], box[(4 * c + 1) * (BN / 2)],
+                            box[(4 * c + 2) * (BN / 2)], box[(4 * c + 3) * (BN / 2)]);
+          } else {
+            v = make_float4(sm.rawB[slot][4 * c][n], sm.rawB[slot][4 * c + 1][n],
+                            sm.rawB[slot][4 * c + 2][n], sm.rawB[slot][4 * c + 3][n]);
+          }
+          float4 hi, lo;
+          panel::split4(v, hi, lo);
+          *reinterpret_cast<float4 *>(sm.bHi[buffer][c][n]) = hi;
+          *reinterpret_cast<float4 *>(sm.bLo[buffer][c][n]) = lo;
+        }
+      } else {
 #pragma unroll
       for (int g = 0; g < (BK / 4) * BN / kConverterThreads; ++g) {
         const int i = t + g * kConverterThreads;
@@ -623,21 +644,23 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
         *reinterpret_cast<float4 *>(sm.bHi[buffer][c][n]) = hi;
         *reinterpret_cast<float4 *>(sm.bLo[buffer][c][n]) = lo;
       }
+      }
       fenceAsyncShared();
       __syncwarp();
       if (lane == 0)
         mbarrierArrive(&sm.bFull[buffer]);
     }
     // Epilogue: wait (bounded) for every issued MMA, then stage this warp's TMEM lanes (main +
-    // correction, one row per thread) in shared memory over the idle panel ring.
+    // correction, one row per thread, half of the columns) in shared memory over the idle ring.
     const bool done = waitPhase(&sm.accDone, 0, nullptr);
     fenceAfterSync();
     Staging<BN> &stage = *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0]);
     const int row = (warp % 4) * 32 + lane;
     const unsigned rowAddress = tmem + (unsigned((warp % 4) * 32) << 16);
+    const int half = (warp - 2) / 4;
     const bool valid = epilogueAll(done && !*abort) && hasWork; // uniform over these warps
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
+    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
       float v[16], correction[16];
       if (valid) {
         tmemLoad16(rowAddress + unsigned(c0), v);
