@@ -48,6 +48,13 @@ WORKLOADS = {
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
+# DRAM bytes per algorithmic byte of one attention launch, from an ncu capture of the same
+# kernel on the 32-request cfg5 shard at position 2049 (read 537.02 MB + write 3.85 MB for
+# 537.4 MB of K/V rows).  The traffic grows with the rows read, so the ratio scales it to the
+# bench workload.
+ATTENTION_TRAFFIC_RATIO = (537.02e6 + 3.85e6) / 537.4e6
+
+
 def peaks():
     if PEAKS.exists():
         data = json.loads(PEAKS.read_text())
@@ -288,7 +295,11 @@ def gpu_arm(args, workload, world, rank, local, group):
         achieved = algorithmic / (launch_ms / 1000.0) / 1e9
         roofline = {"bound": "hbm", "kernel": attention_kernel, "achieved": achieved,
                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
-                    "traffic": None, "algorithmic_bytes_per_launch": algorithmic,
+                    "traffic": algorithmic * ATTENTION_TRAFFIC_RATIO,
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                      "32-request shard at position 2049, scaled by algorithmic "
+                                      "bytes",
+                    "algorithmic_bytes_per_launch": algorithmic,
                     "launch_ms": launch_ms, "launches_profiled": len(attention),
                     "kv_rows_per_head": n_rows}
     share = {}
