@@ -147,9 +147,22 @@ def barrier(group):
 
 
 # ---- CPU leg: the reference algorithm on the host --------------------------------------
+def host_threads() -> int:
+    """Let NumPy's BLAS use every host thread (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(cores)
+    except ImportError:
+        pass
+    return cores
+
+
 def cpu_decode_rate(workload, budget_s: float, min_steps: int, max_steps: int, sample: int):
     """Tokens/s of the NumPy decoder (oracle restatement) on `sample` requests."""
     from oracle import decoder as ref
+
+    host_threads()
 
     b, h, a, l, f, v, ctx, steps, seed, eps = workload
     config = ref.Config(batch=sample, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
