@@ -44,6 +44,8 @@ WORKLOADS = {
     "cfg1": (1, 64, 4, 2, 256, 512, 16, 16, 0, 1e-6),
     "cfg3": (64, 256, 8, 2, 1024, 512, 16, 16, 2, 1e-6),
     "cfg4": (256, 64, 4, 8, 256, 512, 16, 16, 3, 1e-6),
+    # dst = (src + 0.5) + 0.5 over 2^28 float32 elements per GPU, seed 1.
+    "vector": (1 << 28, 0, 0, 0, 0, 0, 0, 0, 1, 0.5),
 }
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
@@ -158,6 +160,28 @@ def host_threads() -> int:
     return cores
 
 
+def cpu_vector_rate(workload, budget_s: float, min_steps: int, max_steps: int,
+                    sample: int = 1 << 26):
+    """Elements/s of the NumPy vector pipeline (oracle restatement) on `sample` elements."""
+    from oracle import vector_pipeline as ref
+
+    src = ref.make_source(sample, workload[8])
+    out = np.empty_like(src)
+    times = []
+    begin = time.perf_counter()
+    while len(times) < max_steps and (len(times) < min_steps or time.perf_counter() - begin < budget_s):
+        t0 = time.perf_counter()
+        ref.pipeline(src, workload[9], out)
+        times.append(time.perf_counter() - t0)
+    return sample / statistics.mean(times), len(times), sample
+
+
+def cpu_rate(args, workload, budget_s, min_steps, max_steps, sample):
+    if args.workload == "vector":
+        return cpu_vector_rate(workload, budget_s, min_steps, max_steps)
+    return cpu_decode_rate(workload, budget_s, min_steps, max_steps, sample)
+
+
 def cpu_decode_rate(workload, budget_s: float, min_steps: int, max_steps: int, sample: int):
     """Tokens/s of the NumPy decoder (oracle restatement) on `sample` requests."""
     from oracle import decoder as ref
@@ -188,26 +212,50 @@ def cpu_decode_rate(workload, budget_s: float, min_steps: int, max_steps: int, s
     return sample / statistics.mean(times), len(times), sample
 
 
+def cpu_baseline(args, workload) -> dict:
+    """The NumPy restatement of the reference algorithm on a bounded sample, all host threads
+    and one thread."""
+    if args.workload == "vector":
+        rate, done, sample = cpu_vector_rate(workload, 10.0, 3, 40)
+        return {"value": rate, "unit": "elements/s", "cores": 1, "kind": "port",
+                "sample": f"{sample} elements, {done} passes of (src + b) + b, NumPy (one thread)"}
+    sample = min(8, workload[0])
+    rate, done, sample = cpu_decode_rate(workload, 15.0, 3, 40, sample)
+    cores = host_threads()
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(1):
+        rate1, done1, _ = cpu_decode_rate(workload, 8.0, 2, 20, sample)
+    host_threads()
+    return {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "value_one_thread": rate1,
+            "sample": f"{sample} requests at position {workload[6] - 1}, {done} decode steps of "
+                      f"the NumPy decoder (reference algorithm) with {cores} host threads; "
+                      f"{done1} steps with one thread give value_one_thread"}
+
+
 def reference_arm(args, workload, world, rank):
     if rank != 0:
         return 0
     sample = 8 if workload[0] >= 8 else workload[0]
     steps = max(args.steps, 1)
     # Warm-up steps, then `steps` timed steps of the bounded sample.
-    cpu_decode_rate(workload, 0.0, args.warmup, args.warmup, sample) if args.warmup else None
-    rate, done, sample = cpu_decode_rate(workload, 1e9, steps, steps, sample)
-    cores = os.cpu_count()
+    cpu_rate(args, workload, 0.0, args.warmup, args.warmup, sample) if args.warmup else None
+    rate, done, sample = cpu_rate(args, workload, 1e9, steps, steps, sample)
+    vector = args.workload == "vector"
+    cores = 1 if vector else host_threads()
+    unit = "elements/s" if vector else "tokens/s"
+    what = (f"{sample} elements, {done} pipeline passes, NumPy (one thread)" if vector else
+            f"{sample} requests at position {workload[6] - 1}, {done} decode steps, NumPy with "
+            f"{cores} host threads")
     line = {
         "impl": "reference", "metric": metric_name(args.workload), "value": rate,
-        "unit": "tokens/s", "n_gpus": args.gpus, "steps": done, "warmup": args.warmup,
+        "unit": unit, "n_gpus": args.gpus, "steps": done, "warmup": args.warmup,
         "ms_per_step": 1000.0 * sample / rate, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, workload, world),
-        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} requests at position {workload[6] - 1}, "
-                                   f"{done} decode steps, NumPy with {cores} host threads"},
-        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": rate, "unit": unit, "cores": cores, "kind": "port",
+                         "sample": what},
+        "e2e": {"value": rate, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -219,6 +267,11 @@ def metric_name(workload: str) -> str:
 
 def workload_config(args, workload, world):
     b, h, a, l, f, v, ctx, steps, seed, eps = workload
+    if args.workload == "vector":
+        return {"workload": "vector pipeline (BASELINE config 2): dst = (src + b) + b, fused "
+                            "into one launch", "elements_per_gpu": b, "total_elements": b * world,
+                "bias": eps, "seed": seed, "parallelism": f"elements x{world}, no collective",
+                "l2": "no flush: 2 GiB of src + dst per GPU exceed the 126 MB L2"}
     return {"workload": f"{args.workload} decoder (BASELINE config "
                         f"{ {'cfg5': 5, 'cfg1': 1, 'cfg3': 3, 'cfg4': 4}[args.workload]}), "
                         f"{b} requests per GPU, request-sharded",
@@ -230,6 +283,78 @@ def workload_config(args, workload, world):
 
 
 # ---- GPU leg ----------------------------------------------------------------------------
+def vector_arm(args, workload, world, rank, local, group):
+    """the two-launch vector pipeline, fused into one streaming launch."""
+    import ckl
+    from ckl.workloads import vector_pipeline
+
+    n, seed, bias = workload[0], workload[8], workload[9]
+    device = ckl.Device(local)
+    spec = ckl.BufferSpec((n,), ckl.f32)
+    src, dst = device.empty(spec), device.empty(spec)
+    # Each GPU's slice of the job: U(-1, 1) from the seed, offset by the rank.
+    host = np.random.default_rng(seed + rank).uniform(-1.0, 1.0, n).astype(np.float32)
+    src.copy_from_host(host)
+    compiled = vector_pipeline.lower(n).compile(target=ckl.NVIDIATarget("sm_100a"),
+                                                fuse_pointwise=True)
+    inv = compiled.bind(src, dst, float(bias))
+    nodes = inv.node_count
+    clocks = ClockSampler(local).__enter__()
+    for _ in range(args.warmup):
+        inv.run(mode="graph")
+    barrier(group)
+    inv.synchronize()
+    elapsed_ms = inv.time_launches(args.steps, mode="graph")
+    inv.synchronize()
+    barrier(group)
+    elapsed_ms = reduce_max(group, elapsed_ms)
+    value = n * world * args.steps / (elapsed_ms / 1000.0)
+
+    # End to end: the step's source copied in from pinned memory, the result copied out.
+    pinned_in, pinned_out = ckl.cuda.PinnedHostBuffer(4 * n), ckl.cuda.PinnedHostBuffer(4 * n)
+    np.frombuffer(pinned_in.view(), dtype=np.float32)[:] = host
+    barrier(group)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        inv.copy_in_async(src, pinned_in.pointer, 4 * n)
+        inv.launch(mode="graph")
+        inv.copy_out_async(dst, pinned_out.pointer, 4 * n)
+        inv.synchronize()
+    e2e_s = reduce_max(group, time.perf_counter() - t0)
+    e2e = n * world * args.steps / e2e_s
+    clocks.__exit__(None, None, None)
+
+    per_node = inv.profile_nodes(3)
+    hbm, peak_kind = peaks()
+    launch_ms = per_node[0] / 3 if per_node else None
+    roofline = None
+    if launch_ms:
+        algorithmic = 8 * n  # read src, write dst
+        achieved = algorithmic / (launch_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "kernel": inv.node_names[0], "achieved": achieved,
+                    "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": None, "algorithmic_bytes_per_launch": algorithmic,
+                    "launch_ms": launch_ms}
+    line = None
+    if rank == 0:
+        line = {
+            "metric": metric_name(args.workload), "value": value, "unit": "elements/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: U(-1, 1) float32 (seed 1 + rank)",
+            "config": workload_config(args, workload, world),
+            "roofline": roofline,
+            "e2e": {"value": e2e, "unit": "elements/s", "h2d_bytes_per_step": 4 * n * world,
+                    "d2h_bytes_per_step": 4 * n * world},
+            "gpu_launches": nodes * args.steps,
+            "graph_nodes_per_step": nodes,
+            "clocks": clocks.summary(),
+        }
+    return line
+
+
+
 def gpu_arm(args, workload, world, rank, local, group):
     import ckl
     from ckl.workloads import session as S
@@ -371,15 +496,11 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         return reference_arm(args, workload, world, int(os.environ.get("RANK", "0")))
     world, rank, local, group = distributed()
-    line = gpu_arm(args, workload, world, rank, local, group)
+    arm = vector_arm if args.workload == "vector" else gpu_arm
+    line = arm(args, workload, world, rank, local, group)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            rate, done, sample = cpu_decode_rate(workload, 15.0, 3, 40, min(8, workload[0]))
-            cores = os.cpu_count()
-            line["cpu_baseline"] = {
-                "value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-                "sample": f"{sample} requests at position {workload[6] - 1}, {done} decode steps "
-                          f"of the NumPy decoder (reference algorithm) with {cores} host threads"}
+            line["cpu_baseline"] = cpu_baseline(args, workload)
         print(json.dumps(line), flush=True)
     if group is not None:
         group.barrier()

@@ -45,6 +45,25 @@ __device__ __forceinline__ bool aligned16(const void *p) {
 
 inline unsigned ceilDiv(int64_t a, int64_t b) { return unsigned((a + b - 1) / b); }
 
+// Programmatic dependent launch: wait until every kernel this one depends on has completed and
+// its memory is visible, then allow the kernels that depend on this one to be scheduled (they
+// wait in turn).  Both are no-ops for a kernel launched without a programmatic dependency.
+// Library kernels registered as dependent-launch aware call this before any global access.
+__device__ __forceinline__ void dependentLaunchEntry() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// The same for a long multi-wave kernel: wait at entry, and let the dependents be scheduled
+// only as this CTA finishes (dependentLaunchExit), so they do not compete with this kernel's
+// later waves for SM slots.
+__device__ __forceinline__ void dependentLaunchWait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void dependentLaunchExit() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <typename Spec> const Spec &specOf(const void *spec) {
   return *static_cast<const Spec *>(spec);
 }

@@ -31,6 +31,7 @@ using gemm::Small;
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     linearKernel(const float *x, const float *w, float *dst, GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.w = w, p.out = dst, p.s = s;
   gemm::body<Cfg, gemm::kPlain, gemm::kStore>(p);
@@ -40,6 +41,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     normLinearKernel(const float *x, const float *gain, const float *w, float *dst, float eps,
                      GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.out = dst, p.eps = eps, p.s = s;
   gemm::body<Cfg, gemm::kRms, gemm::kStore>(p);
@@ -49,6 +51,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     normLinearRopeKernel(const float *x, const float *gain, const float *w, const float *table,
                          const int *position, float *dst, float eps, GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = dst;
   p.eps = eps, p.s = s;
@@ -60,6 +63,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
     normLinearRopeAppendKernel(const float *x, const float *gain, const float *w,
                                const float *table, const int *position, float *cache, float eps,
                                GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = cache;
   p.eps = eps, p.s = s;
@@ -70,6 +74,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     normLinearAppendKernel(const float *x, const float *gain, const float *w, const int *position,
                            float *cache, float eps, GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.position = position, p.out = cache, p.eps = eps, p.s = s;
   gemm::body<Cfg, gemm::kRms, gemm::kAppend>(p);
@@ -79,6 +84,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     linearResidualKernel(const float *x, const float *w, const float *residual, float *dst,
                          GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.w = w, p.residual = residual, p.out = dst, p.s = s;
   gemm::body<Cfg, gemm::kPlain, gemm::kResidual>(p);
@@ -88,6 +94,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     swigluLinearResidualKernel(const float *gate, const float *up, const float *w,
                                const float *residual, float *dst, GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = gate, p.a2 = up, p.w = w, p.residual = residual, p.out = dst, p.s = s;
   gemm::body<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
@@ -97,6 +104,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::kThreads)
     normLinearArgmaxKernel(const float *x, const float *gain, const float *w, float *logits,
                            float2 *partials, float eps, GemmSpec s) {
+  dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.out = logits, p.partials = partials, p.eps = eps, p.s = s;
   gemm::body<Cfg, gemm::kRms, gemm::kArgmax>(p);
@@ -137,10 +145,14 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
 constexpr int kAttentionWarps = 4;
 constexpr int kAttentionUnroll = 4;
 
+// Attention is registered without dependent launch: started early behind its q/k/v
+// producers, its many waiting CTAs cost ~15 % of its own run time on B200.  It still lets its
+// dependents (the o projection) be scheduled as its CTAs finish.
 template <int D>
 __global__ void __launch_bounds__(kAttentionWarps *kWarp)
     attentionKernel(const float *q, const float *kc, const float *vc, const int *position,
                     float *ctx, float scale, AttentionSpec s) {
+  dependentLaunchWait();
   constexpr int LPR = D / 4;             // lanes per cache row
   constexpr int RPW = kWarp / LPR;       // rows per warp per iteration
   constexpr int STEP = kAttentionWarps * RPW;
@@ -225,6 +237,7 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
     }
     __syncthreads(); // warpState is reused by the next (request, head)
   }
+  dependentLaunchExit();
 }
 
 bool attentionGeometry(const void *spec, std::size_t, library::Geometry *g) {
@@ -261,6 +274,7 @@ constexpr int kCombineWarps = 8;
 __global__ void __launch_bounds__(kCombineWarps *kWarp)
     greedyCombineKernel(const float2 *partials, const float *logits, int *tokens, int *history,
                         int *position, unsigned *counter, CombineSpec s) {
+  dependentLaunchEntry();
   const int p = position[0];
   const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
   const int64_t row = int64_t(blockIdx.x) * kCombineWarps + warp;
@@ -311,34 +325,43 @@ CKL_REGISTER_KERNEL("ckl.decoder.linear", reinterpret_cast<const void *>(&linear
                     "PPPS", sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(linearKernel));
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear", reinterpret_cast<const void *>(&normLinearKernel<Medium>),
                     "PPPPFS", sizeof(GemmSpec), gemmGeometry,
-                    CKL_GEMM_SELECT(normLinearKernel));
+                    CKL_GEMM_SELECT(normLinearKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_rope",
                     reinterpret_cast<const void *>(&normLinearRopeKernel<Medium>), "PPPPPPFS",
                     sizeof(GemmSpec), ropeGemmGeometry,
-                    CKL_GEMM_SELECT(normLinearRopeKernel));
+                    CKL_GEMM_SELECT(normLinearRopeKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_rope_append",
                     reinterpret_cast<const void *>(&normLinearRopeAppendKernel<Medium>), "PPPPPPFS",
                     sizeof(GemmSpec), appendGemmGeometry,
-                    CKL_GEMM_SELECT(normLinearRopeAppendKernel));
+                    CKL_GEMM_SELECT(normLinearRopeAppendKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_append",
                     reinterpret_cast<const void *>(&normLinearAppendKernel<Medium>), "PPPPPFS",
                     sizeof(GemmSpec), appendGemmGeometry,
-                    CKL_GEMM_SELECT(normLinearAppendKernel));
+                    CKL_GEMM_SELECT(normLinearAppendKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.linear_residual",
                     reinterpret_cast<const void *>(&linearResidualKernel<Medium>), "PPPPS",
                     sizeof(GemmSpec), gemmGeometry,
-                    CKL_GEMM_SELECT(linearResidualKernel));
+                    CKL_GEMM_SELECT(linearResidualKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.swiglu_linear_residual",
                     reinterpret_cast<const void *>(&swigluLinearResidualKernel<Medium>), "PPPPPS",
-                    sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(swigluLinearResidualKernel));
+                    sizeof(GemmSpec), gemmGeometry, CKL_GEMM_SELECT(swigluLinearResidualKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.norm_linear_argmax",
                     reinterpret_cast<const void *>(&normLinearArgmaxKernel<Medium>), "PPPPPFS",
                     sizeof(GemmSpec), gemmGeometry,
-                    CKL_GEMM_SELECT(normLinearArgmaxKernel));
+                    CKL_GEMM_SELECT(normLinearArgmaxKernel),
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.attention", reinterpret_cast<const void *>(&attentionKernel<64>),
-                    "PPPPPFS", sizeof(AttentionSpec), attentionGeometry, attentionSelect);
+                    "PPPPPFS", sizeof(AttentionSpec), attentionGeometry, attentionSelect,
+                    nullptr, 0, false);
 CKL_REGISTER_KERNEL("ckl.fused.greedy_combine",
                     reinterpret_cast<const void *>(&greedyCombineKernel), "PPPPPPS",
-                    sizeof(CombineSpec), combineGeometry, nullptr);
+                    sizeof(CombineSpec), combineGeometry, nullptr,
+                    nullptr, 0, true);
 
 } // namespace ckl::kernels

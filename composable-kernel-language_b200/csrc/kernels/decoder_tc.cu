@@ -40,6 +40,7 @@ __device__ __forceinline__ float4 rmsScale(const float4 &a, float inv, const flo
 
 __global__ void __launch_bounds__(kPanelWarps *kWarp)
     rmsPanelKernel(const float *x, const float *gain, float *out, float eps, RmsApplySpec s) {
+  dependentLaunchEntry();
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int64_t m = int64_t(blockIdx.x) * kPanelWarps + warp;
   if (m >= s.B)
@@ -117,6 +118,7 @@ bool rmsPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
   __global__ void __cluster_dims__(1, 1, SPLITS) __launch_bounds__(tc::kThreads)               \
       fn(const float *a, const float *w, CKL_UNPACK params, GemmSpec s,                         \
          const __grid_constant__ tc::WeightMap weights) {                                      \
+    dependentLaunchEntry();                                                                    \
     Params p;                                                                                  \
     p.a = a, p.w = w, p.s = s;                                                                 \
     CKL_UNPACK assign;                                                                         \
@@ -142,6 +144,7 @@ CKL_PANEL_KERNEL(panelLinearArgmaxTc, gemm::kArgmax, (float *logits, float2 *par
 __global__ void __launch_bounds__(tc::kThreads)
     panelGateUpTc(const float *a, const float *wg, const float *wu, float *out, GemmSpec s,
                   const __grid_constant__ tc::WeightMapPair maps) {
+  dependentLaunchEntry();
   Params p;
   p.a = a, p.w = wg, p.w2 = wu, p.out = out, p.s = s;
   tc::body<128, gemm::kSwiGluPanel, 1>(p, maps.gate, &maps.up);
@@ -281,28 +284,29 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
 } // namespace
 
 CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPanelKernel),
-                    "PPPFS", sizeof(RmsApplySpec), rmsPanelGeometry, nullptr);
+                    "PPPFS", sizeof(RmsApplySpec), rmsPanelGeometry, nullptr,
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&panelGateUpTc),
                     "PPPPS", sizeof(GemmSpec), gateUpGeometry, nullptr, prepareGateUp,
-                    sizeof(tc::WeightMapPair));
+                    sizeof(tc::WeightMapPair), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc),
-                    prepareWeights, sizeof(tc::WeightMap));
+                    prepareWeights, sizeof(tc::WeightMap), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope", reinterpret_cast<const void *>(&panelLinearRopeTc<32, 1>),
                     "PPPPPS", sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc),
-                    prepareWeights, sizeof(tc::WeightMap));
+                    prepareWeights, sizeof(tc::WeightMap), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append", reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32, 1>),
                     "PPPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearRopeAppendTc),
-                    prepareWeights, sizeof(tc::WeightMap));
+                    prepareWeights, sizeof(tc::WeightMap), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append", reinterpret_cast<const void *>(&panelLinearAppendTc<32, 1>),
                     "PPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc),
-                    prepareWeights, sizeof(tc::WeightMap));
+                    prepareWeights, sizeof(tc::WeightMap), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const void *>(&panelLinearResidualTc<32, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc),
-                    prepareWeights, sizeof(tc::WeightMap));
+                    prepareWeights, sizeof(tc::WeightMap), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc),
-                    prepareWeights, sizeof(tc::WeightMap));
+                    prepareWeights, sizeof(tc::WeightMap), true);
 
 } // namespace ckl::kernels
 

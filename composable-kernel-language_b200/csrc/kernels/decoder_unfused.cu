@@ -16,6 +16,7 @@ namespace {
 // bounds there).
 __global__ void embeddingKernel(const int *tokens, const float *table, float *dst,
                                 EmbeddingSpec s) {
+  dependentLaunchEntry();
   const int64_t total = s.B * s.C;
   for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += int64_t(gridDim.x) * blockDim.x) {
@@ -312,7 +313,8 @@ bool singleThreadGeometry(const void *, std::size_t, library::Geometry *g) { ret
 } // namespace
 
 CKL_REGISTER_KERNEL("ckl.decoder.embedding", reinterpret_cast<const void *>(&embeddingKernel),
-                    "PPPS", sizeof(EmbeddingSpec), embeddingGeometry, nullptr);
+                    "PPPS", sizeof(EmbeddingSpec), embeddingGeometry, nullptr,
+                    nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.decoder.rms_stats", reinterpret_cast<const void *>(&rmsStatsKernel),
                     "PPFS", sizeof(RowsSpec), rowsGeometry, nullptr);
 CKL_REGISTER_KERNEL("ckl.decoder.rms_apply", reinterpret_cast<const void *>(&rmsApplyKernel),

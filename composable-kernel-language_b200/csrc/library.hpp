@@ -38,6 +38,9 @@ struct Kernel {
   SelectFn select;          // may be null
   PrepareFn prepare = nullptr;
   std::size_t prepareBytes = 0; // size of the parameter `prepare` writes
+  // The kernel calls dependentLaunchEntry() first: it may be launched with a programmatic
+  // dependency on its predecessors (scheduled while they finish).
+  bool dependentLaunch = false;
 };
 
 // All entries, defined by the kernel translation units (registered at static init time).

@@ -17,6 +17,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -161,10 +162,55 @@ struct GraphExec {
   }
 };
 
+// Programmatic dependent launch for library kernels that wait on their predecessors
+// themselves (griddepcontrol.wait at entry): such a kernel is scheduled while the kernel before
+// it finishes, hiding most of the launch gap between dependent nodes.  CKL_B200_DEPENDENT_LAUNCH=0
+// turns it off (every edge then waits for full completion); CKL_B200_DEPENDENT_LAUNCH_EXCLUDE
+// lists comma-separated kernel-name fragments to leave out (tuning).
+bool dependentLaunch(const KernelLaunch &k) {
+  static const bool enabled = [] {
+    const char *value = std::getenv("CKL_B200_DEPENDENT_LAUNCH");
+    return !(value && value[0] == '0');
+  }();
+  static const std::vector<std::string> excluded = [] {
+    std::vector<std::string> out;
+    if (const char *value = std::getenv("CKL_B200_DEPENDENT_LAUNCH_EXCLUDE")) {
+      std::string list(value);
+      for (std::size_t start = 0; start <= list.size();) {
+        const std::size_t end = std::min(list.find(',', start), list.size());
+        if (end > start)
+          out.push_back(list.substr(start, end - start));
+        start = end + 1;
+      }
+    }
+    return out;
+  }();
+  if (!enabled || !k.function.entry || !k.function.entry->dependentLaunch)
+    return false;
+  for (const std::string &fragment : excluded)
+    if (std::strstr(k.function.entry->name, fragment.c_str()))
+      return false;
+  return true;
+}
+
 void launchOne(const KernelLaunch &k, cudaStream_t stream) {
   auto args = k.pointers();
-  check(cudaLaunchKernel(k.function.address, k.grid, k.block, args.data(), k.shared, stream),
-        "cudaLaunchKernel");
+  if (!dependentLaunch(k)) {
+    check(cudaLaunchKernel(k.function.address, k.grid, k.block, args.data(), k.shared, stream),
+          "cudaLaunchKernel");
+    return;
+  }
+  cudaLaunchConfig_t config{};
+  config.gridDim = k.grid;
+  config.blockDim = k.block;
+  config.dynamicSmemBytes = k.shared;
+  config.stream = stream;
+  cudaLaunchAttribute attribute{};
+  attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute.val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = &attribute;
+  config.numAttrs = 1;
+  check(cudaLaunchKernelExC(&config, k.function.address, args.data()), "cudaLaunchKernelEx");
 }
 
 void launchOrdinary(const Plan &plan, cudaStream_t stream) {
@@ -181,9 +227,6 @@ std::shared_ptr<GraphExec> instantiate(const Plan &plan, const std::shared_ptr<D
   g->nodes.reserve(plan.nodes.size());
   for (std::size_t i = 0; i < plan.nodes.size(); ++i) {
     const KernelLaunch &k = plan.nodes[i];
-    std::vector<cudaGraphNode_t> deps;
-    for (std::size_t d : plan.dependencies[i])
-      deps.push_back(g->nodes.at(d));
     auto args = k.pointers();
     cudaKernelNodeParams p{};
     p.func = const_cast<void *>(k.function.address);
@@ -192,9 +235,22 @@ std::shared_ptr<GraphExec> instantiate(const Plan &plan, const std::shared_ptr<D
     p.sharedMemBytes = k.shared;
     p.kernelParams = args.data();
     cudaGraphNode_t node{};
-    check(cudaGraphAddKernelNode(&node, g->graph, deps.data(), deps.size(), &p),
-          "cudaGraphAddKernelNode");
+    check(cudaGraphAddKernelNode(&node, g->graph, nullptr, 0, &p), "cudaGraphAddKernelNode");
     g->nodes.push_back(node);
+    // Edges into a dependent-launch-aware kernel are programmatic: it may start once every
+    // predecessor has triggered (griddepcontrol.launch_dependents) and waits for their
+    // completion itself.
+    const bool programmatic = dependentLaunch(k);
+    for (std::size_t d : plan.dependencies[i]) {
+      cudaGraphEdgeData edge{};
+      if (programmatic) {
+        edge.from_port = cudaGraphKernelNodePortProgrammatic;
+        edge.type = cudaGraphDependencyTypeProgrammatic;
+      }
+      const cudaGraphNode_t from = g->nodes.at(d);
+      check(cudaGraphAddDependencies_v2(g->graph, &from, &node, &edge, 1),
+            "cudaGraphAddDependencies");
+    }
   }
   check(cudaGraphInstantiate(&g->exec, g->graph, 0), "cudaGraphInstantiate");
   return g;
