@@ -34,7 +34,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.w = w, p.out = dst, p.s = s;
-  gemm::body<Cfg, gemm::kPlain, gemm::kStore>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kPlain, gemm::kStore>(p);
+  else
+    gemm::body<Cfg, gemm::kPlain, gemm::kStore>(p);
 }
 
 template <class Cfg>
@@ -44,7 +47,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.out = dst, p.eps = eps, p.s = s;
-  gemm::body<Cfg, gemm::kRms, gemm::kStore>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kRms, gemm::kStore>(p);
+  else
+    gemm::body<Cfg, gemm::kRms, gemm::kStore>(p);
 }
 
 template <class Cfg>
@@ -55,7 +61,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = dst;
   p.eps = eps, p.s = s;
-  gemm::body<Cfg, gemm::kRms, gemm::kRope>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kRms, gemm::kRope>(p);
+  else
+    gemm::body<Cfg, gemm::kRms, gemm::kRope>(p);
 }
 
 template <class Cfg>
@@ -67,7 +76,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = cache;
   p.eps = eps, p.s = s;
-  gemm::body<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
+  else
+    gemm::body<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
 }
 
 template <class Cfg>
@@ -77,7 +89,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.position = position, p.out = cache, p.eps = eps, p.s = s;
-  gemm::body<Cfg, gemm::kRms, gemm::kAppend>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kRms, gemm::kAppend>(p);
+  else
+    gemm::body<Cfg, gemm::kRms, gemm::kAppend>(p);
 }
 
 template <class Cfg>
@@ -87,7 +102,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.w = w, p.residual = residual, p.out = dst, p.s = s;
-  gemm::body<Cfg, gemm::kPlain, gemm::kResidual>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kPlain, gemm::kResidual>(p);
+  else
+    gemm::body<Cfg, gemm::kPlain, gemm::kResidual>(p);
 }
 
 template <class Cfg>
@@ -97,7 +115,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = gate, p.a2 = up, p.w = w, p.residual = residual, p.out = dst, p.s = s;
-  gemm::body<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
+  else
+    gemm::body<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
 }
 
 template <class Cfg>
@@ -107,7 +128,10 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.out = logits, p.partials = partials, p.eps = eps, p.s = s;
-  gemm::body<Cfg, gemm::kRms, gemm::kArgmax>(p);
+  if constexpr (gemm::IsRows<Cfg>::value)
+    gemm::rowsBody<Cfg, gemm::kRms, gemm::kArgmax>(p);
+  else
+    gemm::body<Cfg, gemm::kRms, gemm::kArgmax>(p);
 }
 
 bool gemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
@@ -134,6 +158,9 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
     case 0: return reinterpret_cast<const void *>(&fn<Small>);                                 \
     case 1: return reinterpret_cast<const void *>(&fn<Medium>);                                \
     case 2: return reinterpret_cast<const void *>(&fn<Large>);                                 \
+    case 6: return reinterpret_cast<const void *>(&fn<gemm::Rows1>);                           \
+    case 7: return reinterpret_cast<const void *>(&fn<gemm::Rows4>);                           \
+    case 8: return reinterpret_cast<const void *>(&fn<gemm::Rows16>);                          \
     default: return nullptr;                                                                   \
     }                                                                                          \
   }

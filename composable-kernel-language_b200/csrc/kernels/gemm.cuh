@@ -13,6 +13,8 @@
 // append; store + per-row argmax partials for the greedy head.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace ckl::kernels::gemm {
@@ -52,13 +54,18 @@ using Small = Config<16, 64, 16, 2, 4>;    // 128 threads, M <= 16
 using Medium = Config<64, 64, 16, 4, 4>;   // 256 threads
 using Large = Config<128, 128, 8, 8, 8>;   // 256 threads, M >= 256 and wide N
 
-// Tile configuration for a specialization: 0 small, 1 medium, 2 large.  `config` 1-3 forces
-// one of them; 0 (automatic) and 5 (FFMA only) choose by shape.
+// Tile configuration for a specialization: 0 small, 1 medium, 2 large, 6/7/8 the few-row
+// kernel for 1 / 4 / 16 rows.  `config` 1-3 forces a tile; 0 (automatic) and 5 (FFMA only)
+// choose by shape.
 inline int chooseConfig(const GemmSpec &s) {
   if (s.config > 0 && s.config <= 3)
     return int(s.config - 1);
+  if (s.M <= 1)
+    return 6;
+  if (s.M <= 4)
+    return 7;
   if (s.M <= 16)
-    return 0;
+    return 8;
   if (s.M >= 256 && s.N >= 2048)
     return 2;
   return 1;
@@ -77,6 +84,13 @@ inline bool geometry(const GemmSpec &s, library::Geometry *g) {
   case 0: tileGrid<Small>(s, g); break;
   case 1: tileGrid<Medium>(s, g); break;
   case 2: tileGrid<Large>(s, g); break;
+  case 6:
+  case 7:
+  case 8:
+    g->grid[0] = ceilDiv(s.N, 32);
+    g->grid[1] = 1;
+    g->block[0] = 256;
+    break;
   default: return false;
   }
   return g->grid[1] <= 65535;
@@ -309,6 +323,135 @@ template <class Cfg, int PRO, int EPI> __device__ void body(const Params &p) {
         const int64_t h = n / D, d = n % D;
         if constexpr (EPI == kRope || EPI == kRopeAppend) {
           const float *cs = p.table + (int64_t(position) * R + d / 2) * 2;
+          const float cosine = cs[0], sine = cs[1];
+          const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
+          const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
+          first = x;
+          second = y;
+        }
+        if constexpr (EPI == kRope) {
+          p.out[m * N + n] = first;
+          p.out[m * N + n + 1] = second;
+        } else {
+          float *slot = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
+          slot[0] = first;
+          slot[1] = second;
+        }
+      }
+    }
+  }
+}
+
+// ---- few-row projections (decode with up to 16 requests) -------------------------------
+// The batch-1 decode GEMVs: a CTA owns 32 output columns (one per lane) for all rows; its 8
+// warps split K.  Rows of A go through the prologue once per CTA into shared memory, a chunk
+// of K at a time (k-major, read as broadcasts); each thread keeps one accumulator per row for
+// its column and its K range, reading the weights as coalesced 128-byte rows; the warps'
+// partial sums are added in warp order (deterministic) before the fused epilogue.
+template <int ROWS> struct Rows {
+  static constexpr int kRows = ROWS, kThreads = 256, kWarps = 8, kCols = 32, kChunk = 256;
+};
+using Rows1 = Rows<1>;
+using Rows4 = Rows<4>;
+using Rows16 = Rows<16>;
+
+template <class Cfg> struct IsRows : std::false_type {};
+template <int R> struct IsRows<Rows<R>> : std::true_type {};
+
+template <class Cfg, int PRO, int EPI> __device__ void rowsBody(const Params &p) {
+  constexpr int R = Cfg::kRows, KC = Cfg::kChunk, WARPS = Cfg::kWarps;
+  constexpr int SLAB = KC / WARPS; // k per warp per chunk
+  __shared__ float As[KC][R + 1];
+  __shared__ float partial[WARPS][R][kWarp];
+  __shared__ float rowInv[R];
+
+  const GemmSpec &s = p.s;
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  const int64_t M = s.M, K = s.K, N = s.N;
+  const int64_t n = int64_t(blockIdx.x) * Cfg::kCols + lane;
+  const float *A = p.a;
+  const float *W = p.w + s.layer * K * N;
+
+  int position = 0;
+  if constexpr (EPI == kRope || EPI == kRopeAppend || EPI == kAppend) {
+    position = p.position[0];
+    if (position < 0 || position >= s.T)
+      return; // outside cache capacity: the step writes nothing
+  }
+  if constexpr (PRO == kRms) {
+    for (int m = warp; m < R; m += WARPS) {
+      float total = 0.f;
+      if (m < M)
+        for (int64_t k = lane; k < K; k += kWarp) {
+          const float v = A[m * K + k];
+          total += v * v;
+        }
+      total = warpSum(total);
+      if (lane == 0)
+        rowInv[m] = rsqrtf(total / float(K) + p.eps);
+    }
+    __syncthreads();
+  }
+
+  float acc[R];
+#pragma unroll
+  for (int m = 0; m < R; ++m)
+    acc[m] = 0.f;
+  for (int64_t k0 = 0; k0 < K; k0 += KC) {
+    for (int e = tid; e < KC * R; e += Cfg::kThreads) {
+      const int m = e / KC, kk = e % KC;
+      const int64_t k = k0 + kk;
+      As[kk][m] = (m < M && k < K) ? prologue<PRO>(p, A[m * K + k], m, k, rowInv, m) : 0.f;
+    }
+    __syncthreads();
+    const int64_t kEnd = K - k0 < KC ? K - k0 : KC;
+#pragma unroll 8
+    for (int kk = warp * SLAB; kk < (warp + 1) * SLAB; ++kk) {
+      if (kk >= kEnd)
+        break;
+      const float w = n < N ? __ldg(W + (k0 + kk) * N + n) : 0.f;
+#pragma unroll
+      for (int m = 0; m < R; ++m)
+        acc[m] = fmaf(As[kk][m], w, acc[m]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int m = 0; m < R; ++m)
+    partial[warp][m][lane] = acc[m];
+  __syncthreads();
+
+  // One warp per row: lane = column.
+  for (int m = warp; m < R && m < M; m += WARPS) {
+    float v = partial[0][m][lane];
+#pragma unroll
+    for (int w = 1; w < WARPS; ++w)
+      v = __fadd_rn(v, partial[w][m][lane]);
+    if constexpr (EPI == kStore || EPI == kResidual || EPI == kArgmax) {
+      if (n < N) {
+        float out = v;
+        if constexpr (EPI == kResidual)
+          out = __fadd_rn(p.residual[m * N + n], v);
+        p.out[m * N + n] = out;
+      }
+      if constexpr (EPI == kArgmax) {
+        float best = n < N ? v : -CUDART_INF_F;
+        int bestIndex = n < N ? int(n) : 0x7fffffff;
+#pragma unroll
+        for (int o = kWarp / 2; o > 0; o >>= 1)
+          argmaxMerge(best, bestIndex, __shfl_xor_sync(0xffffffffu, best, o),
+                      __shfl_xor_sync(0xffffffffu, bestIndex, o));
+        if (lane == 0)
+          p.partials[m * s.tiles + blockIdx.x] = make_float2(best, __int_as_float(bestIndex));
+      }
+    } else {
+      // Adjacent columns (even n, n + 1) pair up across neighbouring lanes.
+      const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+      if (lane % 2 == 0 && n < N) {
+        float first = v, second = other;
+        const int64_t D = s.D, R2 = s.D / 2, h = n / D, d = n % D;
+        if constexpr (EPI == kRope || EPI == kRopeAppend) {
+          const float *cs = p.table + (int64_t(position) * R2 + d / 2) * 2;
           const float cosine = cs[0], sine = cs[1];
           const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
           const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));

@@ -132,7 +132,8 @@ extern "C" int ckl_greedy_head_noalloc(const float *x, const float *gain, const 
     if (batch <= 0 || hidden <= 0 || vocab <= 0 || capacity <= 0)
       throw std::invalid_argument("greedy head: sizes must be positive");
     GemmSpec s{batch, hidden, vocab, 1, 0, 0, 0, 0, 0, 0};
-    const int config = gemm::chooseConfig(s);
+    // Tiles of the shared FFMA kernel: 16x64 up to 16 rows, otherwise the shape-based choice.
+    const int config = batch <= 16 ? 0 : gemm::chooseConfig(s);
     const int width = config == 0 ? gemm::Small::BN : config == 1 ? gemm::Medium::BN
                                                                   : gemm::Large::BN;
     const int64_t tiles = (vocab + width - 1) / width;
