@@ -1,7 +1,7 @@
 // Fused decode-step kernels for the decoder program (benchmarks/decoder/workloads.py:191-254).
 //
-// One layer of the reference runs 21 dependent launches.  With FFMA projections (fewer than
-// 128 requests) it is eight graph nodes in five dependency levels:
+// One layer of the reference runs 21 dependent launches.  With FFMA projections (up to 16
+// requests, or with tensor cores switched off) it is eight graph nodes in five dependency levels:
 //   q: RMSNorm -> x @ wq -> RoPE                       (norm_linear_rope)
 //   k: RMSNorm -> x @ wk -> RoPE -> append to kc at p  (norm_linear_rope_append)
 //   v: RMSNorm -> x @ wv -> append to vc at p          (norm_linear_append)
@@ -10,7 +10,7 @@
 //   gate, up: RMSNorm -> x @ wg / wu                   (norm_linear, two concurrent nodes)
 //   next_x = residual + (silu(gate) * up) @ wd         (swiglu_linear_residual)
 // and the head is RMSNorm -> x @ lm with per-tile argmax partials, followed by a combine
-// that writes tokens and history and advances the position.  Batches of 128 or more requests
+// that writes tokens and history and advances the position.  Batches of 17 or more requests
 // run the projections on the tensor cores instead (decoder_tc.cu); attention then writes its
 // context as a split operand panel (AttentionSpec::panel).
 #include "ckl_b200.h"

@@ -1,5 +1,5 @@
 // Tensor-core path of the decoder's batched projections (benchmarks/decoder/workloads.py:191-254
-// with 128 or more requests).
+// with 17 or more requests).
 //
 // Each projection's activation operand is split into a TF32 hi/lo panel once, by the kernel
 // that produces it, and every projection then runs the tcgen05 3xTF32 kernel (tcgemm.cuh) on

@@ -1,6 +1,6 @@
 // Tensor-core (tcgen05) projection kernel with FP32-level accuracy (3xTF32).
 //
-// out = epilogue(A @ W[layer]) for batched decode (M >= 128 requests), A given as a split
+// out = epilogue(A @ W[layer]) for batched decode (17 or more requests), A given as a split
 // panel (panel.cuh: TF32 hi/lo parts in the tensor cores' shared-memory layout, produced
 // once by the kernel that computes A), W the FP32 weights [K, N] of one layer, read as stored.
 // hi*hi accumulates in one FP32 tensor-memory accumulator and the correction products
@@ -8,7 +8,7 @@
 // ~2^-22 relative).  This keeps the decoder's 1e-4 relative tolerance and greedy-token parity
 // that plain TF32 breaks.
 //
-// CTA: one 128 x BN output tile, K in slices of 32, six warps with fixed roles:
+// CTA: one 128 x BN output tile, K in slices of 32, ten warps with fixed roles:
 //   warp 0 (producer): per slice one 32 KB bulk copy of the panel block (hi + lo) and one TMA
 //     tensor copy of the 32 x BN weight box (zero-filled beyond K and N; the tensor map is
 //     built at bind time and passed as a __grid_constant__ parameter) into a ring of S
@@ -24,9 +24,10 @@
 //     half of the columns each) and apply the fused epilogue.
 // A tf32 MMA costs about the same at N = 32 as at N = 128, so tiles are 128 columns wide
 // (narrower only for narrow outputs) and the K loop is split over gridDim.z CTAs when the
-// output has too few tiles to fill the GPU.  Each split writes its partial tile to a
-// workspace; the last split to arrive (per-tile counter) sums the partials in split order,
-// which keeps the result deterministic, applies the epilogue and resets the counter.
+// output has too few tiles to fill the GPU.  The splits of a tile form a thread-block
+// cluster: each stages its summed accumulators in shared memory, and after a cluster barrier
+// each reduces a slice of the tile's rows by reading its peers' staging through distributed
+// shared memory in rank order (deterministic), then applies the fused epilogue.
 // Weights whose rows or pointer do not allow a tensor map (N % 4 != 0, unaligned base) are read
 // by the converters straight from global memory instead.
 //

@@ -200,9 +200,10 @@ _LAYER = ("rms_stats", "rms_apply", "linear", "linear", "linear", "rope", "rope"
           "rms_apply", "linear", "linear", "silu", "multiply", "linear", "add")
 _HEAD = ("rms_stats", "rms_apply", "linear", "greedy", "advance")
 _ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
-# Projections with at least one 128-row tile of requests run on tcgen05 tensor cores (GemmSpec
-# config 0); config 5 keeps every projection on FFMA.
-_TENSOR_CORE_ROWS = 128
+# Batches of 17 or more requests run the projections on tcgen05 tensor cores (GemmSpec config
+# 0; partial 128-row tiles with split-K still beat FFMA tiles from 17 rows); up to 16 the
+# few-row FFMA kernel is faster.  Config 5 keeps every projection on FFMA.
+_TENSOR_CORE_ROWS = 17
 
 
 def _panel_floats(M: int, K: int) -> int:

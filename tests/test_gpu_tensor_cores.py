@@ -1,6 +1,6 @@
 """Batched projections on tcgen05 tensor cores (3xTF32) match the FP32 oracle.
 
-The fused decoder switches to the tensor-core path at 128 or more requests: RMSNorm, attention
+The fused decoder switches to the tensor-core path at 17 or more requests: RMSNorm, attention
 and SwiGLU write split operand panels and the projections read them with the FP32 weights.
 These cases cover full and ragged row tiles, K not a multiple of the 32-wide slice (and not of
 the 8-wide MMA step), N not a multiple of the column tile or of 4 (weights read without bulk
