@@ -122,6 +122,22 @@ struct GemmSpec {
 struct AttentionSpec {
   int64_t B, A, T, D, L, layer, splits, chunk, panel, rows, grid;
 };
+// Batched prefill: row m of a chunk is request m % B at prompt position position[0] + m / B.
+//   PrefillRowsSpec: M rows, embedding [V, C], prompts [T, B].
+//   PrefillAttentionSpec: cache [L, B, A, T, D]; P positions per chunk (M = P * B rows).
+//   PrefillHistorySpec: argmax partials [M, tiles], history [T, B].
+struct PrefillRowsSpec {
+  int64_t M, B, C, V, T;
+};
+struct PrefillAttentionSpec {
+  int64_t B, A, T, D, L, layer, P;
+};
+struct PrefillHistorySpec {
+  int64_t M, B, tiles, T;
+};
+struct PositionAddSpec {
+  int64_t delta;
+};
 // Greedy combine of per-tile argmax partials [B, tiles] of (value, index).
 struct CombineSpec {
   int64_t B, tiles, T, V;

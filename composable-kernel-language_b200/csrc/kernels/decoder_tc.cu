@@ -139,6 +139,10 @@ CKL_PANEL_KERNEL(panelLinearResidualTc, gemm::kResidual, (const float *residual,
                  (p.residual = residual, p.out = dst))
 CKL_PANEL_KERNEL(panelLinearArgmaxTc, gemm::kArgmax, (float *logits, float2 *partials),
                  (p.out = logits, p.partials = partials))
+// Argmax partials only, no logits (the batched prefill's heads: only the greedy tokens of the
+// prompt positions are kept, as history).
+CKL_PANEL_KERNEL(panelArgmaxTc, gemm::kArgmax, (float2 *partials),
+                 (p.out = nullptr, p.partials = partials))
 
 // Fused gate/up/SwiGLU: out is the panel of silu(a @ wg) * (a @ wu) [M, N].
 __global__ void __launch_bounds__(tc::kThreads)
@@ -306,6 +310,9 @@ CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const vo
                     prepareWeights, sizeof(tc::WeightMap), true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc),
+                    prepareWeights, sizeof(tc::WeightMap), true);
+CKL_REGISTER_KERNEL("ckl.fused.panel_argmax", reinterpret_cast<const void *>(&panelArgmaxTc<32, 1>),
+                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelArgmaxTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
 
 } // namespace ckl::kernels

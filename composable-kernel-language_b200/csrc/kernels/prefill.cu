@@ -1,0 +1,282 @@
+// Batched prompt prefill for the decoder (the reference prefills by replaying the decode step
+// once per prompt token with the next prompt token forced, benchmarks/decoder/reference.py:98-108).
+//
+// A prefill chunk processes P prompt positions of all B requests at once: row m of every
+// chunk-sized activation is request m % B at position position[0] + m / B.  The projections are
+// the tensor-core panel kernels (their RoPE / KV-append epilogues place each row at its own
+// position, and an argmax-only head produces the greedy token of every row); the kernels here
+// are the rest of the chunk:
+//   prefill.embedding: rows from the prompts buffer [T, B];
+//   prefill.attention: causal flash attention of the chunk's queries over the KV cache rows
+//     0..position (earlier chunks and this chunk's appends), written as the o projection's panel;
+//   prefill.history:   the greedy token of each row into history[position, request];
+//   prefill.advance:   position[0] += P once the chunk is done.
+#include "ckl_b200.h"
+#include "common.cuh"
+#include "panel.cuh"
+
+namespace ckl::kernels {
+namespace {
+
+// ---- embedding -----------------------------------------------------------------------------
+// Rows whose prompt token lies outside the table are left unwritten, like the decode step's.
+__global__ void prefillEmbeddingKernel(const int *prompts, const int *position, const float *table,
+                                       float *dst, PrefillRowsSpec s) {
+  const int64_t p0 = position[0];
+  const int64_t total = s.M * s.C;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = e / s.C, c = e % s.C;
+    const int64_t at = p0 + m / s.B;
+    if (at < 0 || at >= s.T)
+      continue;
+    const int token = prompts[at * s.B + m % s.B];
+    if (token >= 0 && token < s.V)
+      dst[e] = table[int64_t(token) * s.C + c];
+  }
+}
+
+bool prefillEmbeddingGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<PrefillRowsSpec>(spec);
+  if (s.M <= 0 || s.B <= 0 || s.C <= 0 || s.V <= 0 || s.T <= 0)
+    return false;
+  const int64_t wanted = ceilDiv(s.M * s.C, 256 * 4);
+  g->grid[0] = unsigned(wanted < 148 * 16 ? wanted : 148 * 16);
+  g->block[0] = 256;
+  return true;
+}
+
+// ---- causal attention over the cache ---------------------------------------------------------
+// One CTA per (request, head, block of QB chunk positions); 8 threads per query row.  Keys
+// stream through shared memory KB rows at a time from 0 to the block's last position; each row
+// keeps an online softmax (running maximum, normaliser, weighted V in float4 groups of the head
+// dimension) with keys after the query's own position masked.  FFMA throughout.
+constexpr int kPrefillQueries = 32;
+constexpr int kPrefillKeys = 64;
+constexpr int kPrefillThreads = 256;
+constexpr int kPrefillRowThreads = kPrefillThreads / kPrefillQueries; // 8
+
+template <int D> struct PrefillSmem {
+  float q[kPrefillQueries][D + 1];
+  float k[kPrefillKeys][D + 1];
+  float4 v[kPrefillKeys][D / 4];
+  float p[kPrefillQueries][kPrefillKeys + 1];
+};
+
+template <int D>
+__global__ void __launch_bounds__(kPrefillThreads)
+    prefillAttentionKernel(const float *q, const float *kc, const float *vc, const int *position,
+                           float *ctx, float scale, PrefillAttentionSpec s) {
+  constexpr int QB = kPrefillQueries, KB = kPrefillKeys, TPR = kPrefillRowThreads;
+  constexpr int G = D / 4;                      // float4 groups of a row
+  constexpr int GPT = (G + TPR - 1) / TPR;      // groups per thread
+  constexpr int KPT = KB / TPR;                 // keys per thread per block
+  extern __shared__ __align__(16) unsigned char raw[];
+  auto &sm = *reinterpret_cast<PrefillSmem<D> *>(raw);
+
+  const int64_t blocks = (s.P + QB - 1) / QB;
+  const int64_t qb = blockIdx.x % blocks, bh = blockIdx.x / blocks;
+  const int64_t h = bh % s.A, b = bh / s.A;
+  const int64_t C = s.A * D, i0 = qb * QB;
+  const int64_t p0 = position[0];
+  const int tid = threadIdx.x, row = tid / TPR, sub = tid % TPR;
+
+  for (int e = tid; e < QB * D; e += kPrefillThreads) {
+    const int i = e / D, d = e % D;
+    sm.q[i][d] = i0 + i < s.P ? q[((i0 + i) * s.B + b) * C + h * D + d] : 0.f;
+  }
+  const bool live = i0 + row < s.P;
+  const int64_t mine = p0 + i0 + row; // this row's position
+  const int64_t lastLocal = (i0 + QB < s.P ? i0 + QB : s.P) - 1;
+  int64_t last = p0 + lastLocal;
+  if (last >= s.T)
+    last = s.T - 1;
+  const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D;
+
+  float m = -CUDART_INF_F, l = 0.f;
+  float4 acc[GPT];
+#pragma unroll
+  for (int j = 0; j < GPT; ++j)
+    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int64_t t0 = 0; t0 <= last; t0 += KB) {
+    __syncthreads(); // previous block's keys fully consumed (and the queries staged)
+    for (int e = tid; e < KB * G; e += kPrefillThreads) {
+      const int r = e / G, g = e % G;
+      const int64_t t = t0 + r;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (t <= last) {
+        const float *kr = kc + base + t * D + 4 * g, *vr = vc + base + t * D + 4 * g;
+        if (aligned16(kr) && aligned16(vr)) {
+          kv = *reinterpret_cast<const float4 *>(kr);
+          vv = *reinterpret_cast<const float4 *>(vr);
+        } else {
+          kv = make_float4(kr[0], kr[1], kr[2], kr[3]);
+          vv = make_float4(vr[0], vr[1], vr[2], vr[3]);
+        }
+      }
+      sm.k[r][4 * g] = kv.x;
+      sm.k[r][4 * g + 1] = kv.y;
+      sm.k[r][4 * g + 2] = kv.z;
+      sm.k[r][4 * g + 3] = kv.w;
+      sm.v[r][g] = vv;
+    }
+    __syncthreads();
+    float score[KPT];
+    float blockMax = -CUDART_INF_F;
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) {
+      const int kj = sub + TPR * u;
+      float dot = 0.f;
+#pragma unroll 16
+      for (int d = 0; d < D; ++d)
+        dot = fmaf(sm.q[row][d], sm.k[kj][d], dot);
+      const bool visible = live && t0 + kj <= mine && t0 + kj <= last;
+      score[u] = visible ? dot * scale : -CUDART_INF_F;
+      blockMax = fmaxf(blockMax, score[u]);
+    }
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1)
+      blockMax = fmaxf(blockMax, __shfl_xor_sync(0xffffffffu, blockMax, o));
+    const float next = fmaxf(m, blockMax);
+    const float correction = m == -CUDART_INF_F ? 0.f : expf(m - next);
+    float sum = 0.f;
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) {
+      const float e = score[u] == -CUDART_INF_F ? 0.f : expf(score[u] - next);
+      sm.p[row][sub + TPR * u] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1)
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    l = l * correction + sum;
+    m = next;
+    __syncwarp(); // the row's probabilities come from the 8 threads of this warp
+#pragma unroll
+    for (int j = 0; j < GPT; ++j) {
+      const int g = sub + TPR * j;
+      if (g >= G)
+        continue;
+      float4 a = acc[j];
+      a.x *= correction;
+      a.y *= correction;
+      a.z *= correction;
+      a.w *= correction;
+#pragma unroll 8
+      for (int kj = 0; kj < KB; ++kj) {
+        const float w = sm.p[row][kj];
+        const float4 v = sm.v[kj][g];
+        a.x = fmaf(w, v.x, a.x);
+        a.y = fmaf(w, v.y, a.y);
+        a.z = fmaf(w, v.z, a.z);
+        a.w = fmaf(w, v.w, a.w);
+      }
+      acc[j] = a;
+    }
+  }
+  if (!live || mine >= s.T)
+    return;
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int g = sub + TPR * j;
+    if (g >= G)
+      continue;
+    float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (l > 0.f)
+      out = make_float4(acc[j].x / l, acc[j].y / l, acc[j].z / l, acc[j].w / l);
+    panel::store4(ctx, (i0 + row) * s.B + b, h * D + 4 * g, C, out);
+  }
+}
+
+bool prefillAttentionGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<PrefillAttentionSpec>(spec);
+  if (s.B <= 0 || s.A <= 0 || s.T <= 0 || s.P <= 0 || s.layer < 0 || s.layer >= s.L)
+    return false;
+  std::size_t bytes = 0;
+  switch (s.D) {
+  case 16: bytes = sizeof(PrefillSmem<16>); break;
+  case 32: bytes = sizeof(PrefillSmem<32>); break;
+  case 64: bytes = sizeof(PrefillSmem<64>); break;
+  case 128: bytes = sizeof(PrefillSmem<128>); break;
+  default: return false;
+  }
+  const int64_t ctas = s.B * s.A * ((s.P + kPrefillQueries - 1) / kPrefillQueries);
+  if (ctas >= (int64_t(1) << 31))
+    return false;
+  g->grid[0] = unsigned(ctas);
+  g->block[0] = kPrefillThreads;
+  g->sharedBytes = unsigned(bytes);
+  return true;
+}
+
+const void *prefillAttentionSelect(const void *spec) {
+  switch (specOf<PrefillAttentionSpec>(spec).D) {
+  case 16: return reinterpret_cast<const void *>(&prefillAttentionKernel<16>);
+  case 32: return reinterpret_cast<const void *>(&prefillAttentionKernel<32>);
+  case 64: return reinterpret_cast<const void *>(&prefillAttentionKernel<64>);
+  case 128: return reinterpret_cast<const void *>(&prefillAttentionKernel<128>);
+  default: return nullptr;
+  }
+}
+
+// ---- greedy tokens of the prompt positions --------------------------------------------------
+// One warp per row: the first index of the row's maximum over its tiles' partials (the decode
+// step's greedy rule) goes to history[position, request].
+constexpr int kHistoryWarps = 8;
+
+__global__ void __launch_bounds__(kHistoryWarps *kWarp)
+    prefillHistoryKernel(const float2 *partials, const int *position, int *history,
+                         PrefillHistorySpec s) {
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  const int64_t m = int64_t(blockIdx.x) * kHistoryWarps + warp;
+  if (m >= s.M)
+    return;
+  float best = -CUDART_INF_F;
+  int index = 0x7fffffff;
+  for (int64_t t = lane; t < s.tiles; t += kWarp) {
+    const float2 candidate = partials[m * s.tiles + t];
+    argmaxMerge(best, index, candidate.x, __float_as_int(candidate.y));
+  }
+#pragma unroll
+  for (int o = kWarp / 2; o > 0; o >>= 1)
+    argmaxMerge(best, index, __shfl_xor_sync(0xffffffffu, best, o),
+                __shfl_xor_sync(0xffffffffu, index, o));
+  const int64_t at = int64_t(position[0]) + m / s.B;
+  if (lane == 0 && at >= 0 && at < s.T)
+    history[at * s.B + m % s.B] = index;
+}
+
+bool prefillHistoryGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<PrefillHistorySpec>(spec);
+  if (s.M <= 0 || s.B <= 0 || s.tiles <= 0 || s.T <= 0)
+    return false;
+  g->grid[0] = ceilDiv(s.M, kHistoryWarps);
+  g->block[0] = kHistoryWarps * kWarp;
+  return true;
+}
+
+__global__ void prefillAdvanceKernel(int *position, PositionAddSpec s) {
+  position[0] = int(position[0] + s.delta);
+}
+
+bool prefillAdvanceGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  (void)specOf<PositionAddSpec>(spec);
+  g->grid[0] = 1;
+  g->block[0] = 1;
+  return true;
+}
+
+} // namespace
+
+CKL_REGISTER_KERNEL("ckl.prefill.embedding", reinterpret_cast<const void *>(&prefillEmbeddingKernel),
+                    "PPPPS", sizeof(PrefillRowsSpec), prefillEmbeddingGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.prefill.attention",
+                    reinterpret_cast<const void *>(&prefillAttentionKernel<64>), "PPPPPFS",
+                    sizeof(PrefillAttentionSpec), prefillAttentionGeometry, prefillAttentionSelect);
+CKL_REGISTER_KERNEL("ckl.prefill.history", reinterpret_cast<const void *>(&prefillHistoryKernel),
+                    "PPPS", sizeof(PrefillHistorySpec), prefillHistoryGeometry, nullptr);
+CKL_REGISTER_KERNEL("ckl.prefill.advance", reinterpret_cast<const void *>(&prefillAdvanceKernel),
+                    "PS", sizeof(PositionAddSpec), prefillAdvanceGeometry, nullptr);
+
+} // namespace ckl::kernels

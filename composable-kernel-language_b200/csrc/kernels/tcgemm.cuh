@@ -292,6 +292,8 @@ __device__ __forceinline__ void storeQuad(const gemm::Params &p, int64_t m, int6
         if (n + j < N)
           argmaxMerge(best, bestIndex, lanes[j], int(n + j));
     }
+    if (EPI == gemm::kArgmax && p.out == nullptr)
+      return; // argmax partials only (batched prefill heads)
     if (vec4 && n + 4 <= N) {
       if constexpr (EPI == gemm::kResidual) {
         const float4 r = *reinterpret_cast<const float4 *>(p.residual + m * N + n);
@@ -311,7 +313,13 @@ __device__ __forceinline__ void storeQuad(const gemm::Params &p, int64_t m, int6
       }
     }
   } else {
+    // Row m is request m % cache at position position[0] + m / cache (decode: M == cache, so
+    // every row is at position[0]; batched prefill: several positions per launch).
     const int64_t D = s.D, R = s.D / 2;
+    const int64_t rows = s.cache > 0 ? s.cache : M;
+    const int64_t request = m % rows, at = position + m / rows;
+    if (at >= s.T)
+      return;
 #pragma unroll
     for (int j = 0; j < 4; j += 2) {
       const int64_t c = n + j;
@@ -320,7 +328,7 @@ __device__ __forceinline__ void storeQuad(const gemm::Params &p, int64_t m, int6
       float first = lanes[j], second = lanes[j + 1];
       const int64_t h = c / D, d = c % D;
       if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend) {
-        const float *cs = p.table + (int64_t(position) * R + d / 2) * 2;
+        const float *cs = p.table + (at * R + d / 2) * 2;
         const float cosine = cs[0], sine = cs[1];
         const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
         const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
@@ -331,8 +339,7 @@ __device__ __forceinline__ void storeQuad(const gemm::Params &p, int64_t m, int6
         p.out[m * N + c] = first;
         p.out[m * N + c + 1] = second;
       } else {
-        const int64_t rows = s.cache > 0 ? s.cache : M;
-        float *slot = p.out + (((s.layer * rows + m) * s.A + h) * s.T + position) * D + d;
+        float *slot = p.out + (((s.layer * rows + request) * s.A + h) * s.T + at) * D + d;
         slot[0] = first;
         slot[1] = second;
       }

@@ -224,6 +224,18 @@ class CompiledProgram(_ContextManager):
                                   tensor_cores=tensor_cores)
         self._resource = _NativeProgram(self._lib, self.plans)
 
+    @classmethod
+    def from_plans(cls, signature, plans, target: NVIDIATarget | None = None) -> "CompiledProgram":
+        """A program from plans built directly on library kernels (e.g. the batched prefill),
+        bound and run like a compiled DSL program."""
+        self = cls.__new__(cls)
+        self.signature, self.target = signature, target or NVIDIATarget("sm_100a")
+        self.lowered = None
+        self._lib = _abi.load()
+        self.plans = plans
+        self._resource = _NativeProgram(self._lib, plans)
+        return self
+
     @property
     def prepared_ir(self) -> str:
         return self.plans.prepared_ir

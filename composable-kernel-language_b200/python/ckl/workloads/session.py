@@ -93,7 +93,9 @@ class DecoderSession:
                  tensor_cores: bool = True,
                  shared_weights: "DecoderSession | None" = None):
         self.device = device
+        self.epsilon, self.attention_scale = epsilon, attention_scale
         self.owners, self.buffers, self.shapes = {}, {}, {}
+        self._batched_prefill = None
         self.tails = tails
         for name in decoder.ARGUMENTS[:-2]:
             values = arrays[name]
@@ -158,8 +160,20 @@ class DecoderSession:
         for _ in range(count // batch_size):
             self.invocation.run(mode=mode, batch_size=batch_size)
 
-    def prefill(self, prompts: np.ndarray, *, mode: str = "graph") -> None:
-        """Teacher-forced prefill: ``context - 1`` steps, next prompt token after each."""
+    def prefill(self, prompts: np.ndarray, *, mode: str = "graph", batched: bool = False) -> None:
+        """Teacher-forced prefill: ``context - 1`` steps, next prompt token after each.
+
+        ``batched`` runs the prompt positions in chunks of all requests at once
+        (:mod:`ckl.workloads.prefill`) instead of one decode step per position; the resulting
+        state is the same up to floating-point rounding."""
+        if batched:
+            from .prefill import BatchedPrefill
+
+            context = prompts.shape[0]
+            if self._batched_prefill is None or self._batched_prefill.context != context:
+                self._batched_prefill = BatchedPrefill(self, context)
+            self._batched_prefill.run(prompts, mode=mode)
+            return
         self.write("tokens", prompts[0])
         self.write("position", np.zeros(1, np.int32))
         for i in range(prompts.shape[0] - 1):
