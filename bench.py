@@ -379,11 +379,14 @@ def gpu_arm(args, workload, world, rank, local, group):
     t_setup = time.perf_counter()
     sess = S.DecoderSession(device, arrays, epsilon=eps, attention_scale=(h // a) ** -0.5,
                             tails=False, tensor_cores=args.projections == "tensor")
-    if args.prefill == "graph":
-        sess.prefill(prompts)
+    t_prefill = time.perf_counter()
+    if args.prefill in ("batched", "graph"):
+        sess.prefill(prompts, batched=args.prefill == "batched")
+        sess.invocation.synchronize()
     else:
         sess.write("tokens", prompts[-1])
         sess.write("position", np.array([ctx - 1], np.int32))
+    prefill_s = time.perf_counter() - t_prefill
     setup_s = time.perf_counter() - t_setup
     inv = sess.invocation
     nodes = inv.node_count
@@ -463,6 +466,7 @@ def gpu_arm(args, workload, world, rank, local, group):
             "prefill": args.prefill,
             "projections": args.projections,
             "prefill_setup_s": round(setup_s, 2),
+            "prefill_s": round(prefill_s, 3),
             "clocks": clocks.summary(),
         }
     return line
@@ -480,8 +484,9 @@ def main():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--projections", choices=("tensor", "ffma"), default="tensor",
                         help="batched projections on tcgen05 tensor cores (3xTF32) or FFMA")
-    parser.add_argument("--prefill", choices=("graph", "synthetic"), default="graph",
-                        help="graph: teacher-forced prefill through the decode graph; synthetic: "
+    parser.add_argument("--prefill", choices=("batched", "graph", "synthetic"), default="batched",
+                        help="batched: chunked prefill of all prompt positions (library graph); "
+                             "graph: one teacher-forced decode step per prompt token; synthetic: "
                              "zero KV prefix and position at the last prompt token (profiling)")
     args = parser.parse_args()
     if args.warmup < 0 or args.steps < 1:
