@@ -47,30 +47,33 @@ bool prefillEmbeddingGeometry(const void *spec, std::size_t, library::Geometry *
 }
 
 // ---- causal attention over the cache ---------------------------------------------------------
-// One CTA per (request, head, block of QB chunk positions); 8 threads per query row.  Keys
-// stream through shared memory KB rows at a time from 0 to the block's last position; each row
-// keeps an online softmax (running maximum, normaliser, weighted V in float4 groups of the head
-// dimension) with keys after the query's own position masked.  FFMA throughout.
+// One CTA per (request, head, block of QB chunk positions).  Keys stream through shared memory
+// KB rows at a time from 0 to the block's last position.  Scores: each thread owns 2 queries x
+// 4 keys (keys 16 apart, so the 16-byte loads of a warp hit distinct banks) and accumulates
+// them over the head dimension in float4 steps; each query row keeps an online softmax
+// (running maximum and normaliser, shared by the 16 threads of its row pair through shuffles)
+// with keys after the query's own position masked.  Values: each thread owns the same 2 queries
+// x float4 groups of the head dimension.  FFMA throughout.
 constexpr int kPrefillQueries = 32;
 constexpr int kPrefillKeys = 64;
 constexpr int kPrefillThreads = 256;
-constexpr int kPrefillRowThreads = kPrefillThreads / kPrefillQueries; // 8
+constexpr int kPrefillGroup = 16; // threads sharing a query pair
 
 template <int D> struct PrefillSmem {
-  float q[kPrefillQueries][D + 1];
-  float k[kPrefillKeys][D + 1];
+  float q[kPrefillQueries][D + 4];
+  float k[kPrefillKeys][D + 4];
   float4 v[kPrefillKeys][D / 4];
-  float p[kPrefillQueries][kPrefillKeys + 1];
+  float p[kPrefillQueries][kPrefillKeys + 4];
 };
 
 template <int D>
 __global__ void __launch_bounds__(kPrefillThreads)
     prefillAttentionKernel(const float *q, const float *kc, const float *vc, const int *position,
                            float *ctx, float scale, PrefillAttentionSpec s) {
-  constexpr int QB = kPrefillQueries, KB = kPrefillKeys, TPR = kPrefillRowThreads;
-  constexpr int G = D / 4;                      // float4 groups of a row
-  constexpr int GPT = (G + TPR - 1) / TPR;      // groups per thread
-  constexpr int KPT = KB / TPR;                 // keys per thread per block
+  constexpr int QB = kPrefillQueries, KB = kPrefillKeys, TG = kPrefillGroup;
+  constexpr int G = D / 4;                    // float4 groups of a row
+  constexpr int KPT = KB / TG;                // keys per thread (4), 16 apart
+  constexpr int GPT = (G + TG - 1) / TG;      // value groups per thread
   extern __shared__ __align__(16) unsigned char raw[];
   auto &sm = *reinterpret_cast<PrefillSmem<D> *>(raw);
 
@@ -79,28 +82,40 @@ __global__ void __launch_bounds__(kPrefillThreads)
   const int64_t h = bh % s.A, b = bh / s.A;
   const int64_t C = s.A * D, i0 = qb * QB;
   const int64_t p0 = position[0];
-  const int tid = threadIdx.x, row = tid / TPR, sub = tid % TPR;
+  const int tid = threadIdx.x, pair = tid / TG, lane16 = tid % TG;
 
-  for (int e = tid; e < QB * D; e += kPrefillThreads) {
-    const int i = e / D, d = e % D;
-    sm.q[i][d] = i0 + i < s.P ? q[((i0 + i) * s.B + b) * C + h * D + d] : 0.f;
+  for (int e = tid; e < QB * G; e += kPrefillThreads) {
+    const int i = e / G, g = e % G;
+    float4 value = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i0 + i < s.P) {
+      const float *src = q + ((i0 + i) * s.B + b) * C + h * D + 4 * g;
+      value = make_float4(src[0], src[1], src[2], src[3]);
+    }
+    *reinterpret_cast<float4 *>(&sm.q[i][4 * g]) = value;
   }
-  const bool live = i0 + row < s.P;
-  const int64_t mine = p0 + i0 + row; // this row's position
+  bool live[2];
+  int64_t mine[2];
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    live[a] = i0 + 2 * pair + a < s.P;
+    mine[a] = p0 + i0 + 2 * pair + a;
+  }
   const int64_t lastLocal = (i0 + QB < s.P ? i0 + QB : s.P) - 1;
   int64_t last = p0 + lastLocal;
   if (last >= s.T)
     last = s.T - 1;
   const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D;
 
-  float m = -CUDART_INF_F, l = 0.f;
-  float4 acc[GPT];
+  float m[2] = {-CUDART_INF_F, -CUDART_INF_F}, l[2] = {0.f, 0.f};
+  float4 acc[2][GPT];
 #pragma unroll
-  for (int j = 0; j < GPT; ++j)
-    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int j = 0; j < GPT; ++j)
+      acc[a][j] = make_float4(0.f, 0.f, 0.f, 0.f);
 
   for (int64_t t0 = 0; t0 <= last; t0 += KB) {
-    __syncthreads(); // previous block's keys fully consumed (and the queries staged)
+    __syncthreads(); // previous block's keys consumed (and the queries staged)
     for (int e = tid; e < KB * G; e += kPrefillThreads) {
       const int r = e / G, g = e % G;
       const int64_t t = t0 + r;
@@ -115,77 +130,104 @@ __global__ void __launch_bounds__(kPrefillThreads)
           vv = make_float4(vr[0], vr[1], vr[2], vr[3]);
         }
       }
-      sm.k[r][4 * g] = kv.x;
-      sm.k[r][4 * g + 1] = kv.y;
-      sm.k[r][4 * g + 2] = kv.z;
-      sm.k[r][4 * g + 3] = kv.w;
+      *reinterpret_cast<float4 *>(&sm.k[r][4 * g]) = kv;
       sm.v[r][g] = vv;
     }
     __syncthreads();
-    float score[KPT];
-    float blockMax = -CUDART_INF_F;
+    float score[2][KPT];
 #pragma unroll
-    for (int u = 0; u < KPT; ++u) {
-      const int kj = sub + TPR * u;
-      float dot = 0.f;
-#pragma unroll 16
-      for (int d = 0; d < D; ++d)
-        dot = fmaf(sm.q[row][d], sm.k[kj][d], dot);
-      const bool visible = live && t0 + kj <= mine && t0 + kj <= last;
-      score[u] = visible ? dot * scale : -CUDART_INF_F;
-      blockMax = fmaxf(blockMax, score[u]);
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int u = 0; u < KPT; ++u)
+        score[a][u] = 0.f;
+#pragma unroll 4
+    for (int g = 0; g < G; ++g) {
+      const float4 q0 = *reinterpret_cast<const float4 *>(&sm.q[2 * pair][4 * g]);
+      const float4 q1 = *reinterpret_cast<const float4 *>(&sm.q[2 * pair + 1][4 * g]);
+#pragma unroll
+      for (int u = 0; u < KPT; ++u) {
+        const float4 kv = *reinterpret_cast<const float4 *>(&sm.k[lane16 + TG * u][4 * g]);
+        score[0][u] = fmaf(q0.x, kv.x, score[0][u]);
+        score[0][u] = fmaf(q0.y, kv.y, score[0][u]);
+        score[0][u] = fmaf(q0.z, kv.z, score[0][u]);
+        score[0][u] = fmaf(q0.w, kv.w, score[0][u]);
+        score[1][u] = fmaf(q1.x, kv.x, score[1][u]);
+        score[1][u] = fmaf(q1.y, kv.y, score[1][u]);
+        score[1][u] = fmaf(q1.z, kv.z, score[1][u]);
+        score[1][u] = fmaf(q1.w, kv.w, score[1][u]);
+      }
     }
+    float correction[2];
 #pragma unroll
-    for (int o = 1; o < TPR; o <<= 1)
-      blockMax = fmaxf(blockMax, __shfl_xor_sync(0xffffffffu, blockMax, o));
-    const float next = fmaxf(m, blockMax);
-    const float correction = m == -CUDART_INF_F ? 0.f : expf(m - next);
-    float sum = 0.f;
+    for (int a = 0; a < 2; ++a) {
+      float blockMax = -CUDART_INF_F;
 #pragma unroll
-    for (int u = 0; u < KPT; ++u) {
-      const float e = score[u] == -CUDART_INF_F ? 0.f : expf(score[u] - next);
-      sm.p[row][sub + TPR * u] = e;
-      sum += e;
+      for (int u = 0; u < KPT; ++u) {
+        const int64_t t = t0 + lane16 + TG * u;
+        score[a][u] = live[a] && t <= mine[a] && t <= last ? score[a][u] * scale : -CUDART_INF_F;
+        blockMax = fmaxf(blockMax, score[a][u]);
+      }
+#pragma unroll
+      for (int o = 1; o < TG; o <<= 1)
+        blockMax = fmaxf(blockMax, __shfl_xor_sync(0xffffffffu, blockMax, o));
+      const float next = fmaxf(m[a], blockMax);
+      correction[a] = m[a] == -CUDART_INF_F ? 0.f : expf(m[a] - next);
+      float sum = 0.f;
+#pragma unroll
+      for (int u = 0; u < KPT; ++u) {
+        const float e = score[a][u] == -CUDART_INF_F ? 0.f : expf(score[a][u] - next);
+        sm.p[2 * pair + a][lane16 + TG * u] = e;
+        sum += e;
+      }
+#pragma unroll
+      for (int o = 1; o < TG; o <<= 1)
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l[a] = l[a] * correction[a] + sum;
+      m[a] = next;
     }
-#pragma unroll
-    for (int o = 1; o < TPR; o <<= 1)
-      sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    l = l * correction + sum;
-    m = next;
-    __syncwarp(); // the row's probabilities come from the 8 threads of this warp
+    __syncwarp(); // a row pair's probabilities come from the 16 threads of this half-warp
 #pragma unroll
     for (int j = 0; j < GPT; ++j) {
-      const int g = sub + TPR * j;
+      const int g = lane16 + TG * j;
       if (g >= G)
         continue;
-      float4 a = acc[j];
-      a.x *= correction;
-      a.y *= correction;
-      a.z *= correction;
-      a.w *= correction;
+      float4 a0 = acc[0][j], a1 = acc[1][j];
+      a0 = make_float4(a0.x * correction[0], a0.y * correction[0], a0.z * correction[0],
+                       a0.w * correction[0]);
+      a1 = make_float4(a1.x * correction[1], a1.y * correction[1], a1.z * correction[1],
+                       a1.w * correction[1]);
 #pragma unroll 8
       for (int kj = 0; kj < KB; ++kj) {
-        const float w = sm.p[row][kj];
+        const float w0 = sm.p[2 * pair][kj], w1 = sm.p[2 * pair + 1][kj];
         const float4 v = sm.v[kj][g];
-        a.x = fmaf(w, v.x, a.x);
-        a.y = fmaf(w, v.y, a.y);
-        a.z = fmaf(w, v.z, a.z);
-        a.w = fmaf(w, v.w, a.w);
+        a0.x = fmaf(w0, v.x, a0.x);
+        a0.y = fmaf(w0, v.y, a0.y);
+        a0.z = fmaf(w0, v.z, a0.z);
+        a0.w = fmaf(w0, v.w, a0.w);
+        a1.x = fmaf(w1, v.x, a1.x);
+        a1.y = fmaf(w1, v.y, a1.y);
+        a1.z = fmaf(w1, v.z, a1.z);
+        a1.w = fmaf(w1, v.w, a1.w);
       }
-      acc[j] = a;
+      acc[0][j] = a0;
+      acc[1][j] = a1;
     }
   }
-  if (!live || mine >= s.T)
-    return;
 #pragma unroll
-  for (int j = 0; j < GPT; ++j) {
-    const int g = sub + TPR * j;
-    if (g >= G)
+  for (int a = 0; a < 2; ++a) {
+    if (!live[a] || mine[a] >= s.T)
       continue;
-    float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (l > 0.f)
-      out = make_float4(acc[j].x / l, acc[j].y / l, acc[j].z / l, acc[j].w / l);
-    panel::store4(ctx, (i0 + row) * s.B + b, h * D + 4 * g, C, out);
+#pragma unroll
+    for (int j = 0; j < GPT; ++j) {
+      const int g = lane16 + TG * j;
+      if (g >= G)
+        continue;
+      float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (l[a] > 0.f)
+        out = make_float4(acc[a][j].x / l[a], acc[a][j].y / l[a], acc[a][j].z / l[a],
+                          acc[a][j].w / l[a]);
+      panel::store4(ctx, (i0 + 2 * pair + a) * s.B + b, h * D + 4 * g, C, out);
+    }
   }
 }
 
