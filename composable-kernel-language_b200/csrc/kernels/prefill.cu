@@ -47,23 +47,26 @@ bool prefillEmbeddingGeometry(const void *spec, std::size_t, library::Geometry *
 }
 
 // ---- causal attention over the cache ---------------------------------------------------------
-// One CTA per (request, head, block of QB chunk positions).  Keys stream through shared memory
-// KB rows at a time from 0 to the block's last position.  Scores: each thread owns 2 queries x
-// 4 keys (keys 16 apart, so the 16-byte loads of a warp hit distinct banks) and accumulates
-// them over the head dimension in float4 steps; each query row keeps an online softmax
-// (running maximum and normaliser, shared by the 16 threads of its row pair through shuffles)
-// with keys after the query's own position masked.  Values: each thread owns the same 2 queries
-// x float4 groups of the head dimension.  FFMA throughout.
+// One CTA of 128 threads per (request, head, block of QB chunk positions).  Keys stream through
+// shared memory KB rows at a time from 0 to the block's last position.  Thread (quad, lane)
+// owns queries 4 quad .. 4 quad + 3.  Scores: it accumulates those 4 queries x keys lane,
+// lane + 16, lane + 32, lane + 48 over the head dimension in float4 steps (rows padded to D + 4
+// floats, so a warp's 16-byte key loads hit distinct banks and its query loads broadcast); each
+// query row keeps an online softmax (running maximum and normaliser, shared by the 16 threads
+// of the row's quad through shuffles) with keys after the query's own position masked.  The
+// probabilities go to shared memory key-major, so the value pass reads a query quad's four with
+// one 16-byte load; there the thread owns the same 4 queries x float4 groups lane, lane + 16 ..
+// of the head dimension.  FFMA throughout.
 constexpr int kPrefillQueries = 32;
 constexpr int kPrefillKeys = 64;
-constexpr int kPrefillThreads = 256;
-constexpr int kPrefillGroup = 16; // threads sharing a query pair
+constexpr int kPrefillThreads = 128;
+constexpr int kPrefillGroup = 16; // threads sharing a query quad
 
 template <int D> struct PrefillSmem {
   float q[kPrefillQueries][D + 4];
   float k[kPrefillKeys][D + 4];
   float4 v[kPrefillKeys][D / 4];
-  float p[kPrefillQueries][kPrefillKeys + 4];
+  float p[kPrefillKeys][kPrefillQueries + 4]; // probabilities, key-major
 };
 
 template <int D>
@@ -71,9 +74,9 @@ __global__ void __launch_bounds__(kPrefillThreads)
     prefillAttentionKernel(const float *q, const float *kc, const float *vc, const int *position,
                            float *ctx, float scale, PrefillAttentionSpec s) {
   constexpr int QB = kPrefillQueries, KB = kPrefillKeys, TG = kPrefillGroup;
-  constexpr int G = D / 4;                    // float4 groups of a row
-  constexpr int KPT = KB / TG;                // keys per thread (4), 16 apart
-  constexpr int GPT = (G + TG - 1) / TG;      // value groups per thread
+  constexpr int G = D / 4;               // float4 groups of a row
+  constexpr int KPT = KB / TG;           // keys per thread (4), 16 apart
+  constexpr int GPT = (G + TG - 1) / TG; // value groups per thread
   extern __shared__ __align__(16) unsigned char raw[];
   auto &sm = *reinterpret_cast<PrefillSmem<D> *>(raw);
 
@@ -82,7 +85,7 @@ __global__ void __launch_bounds__(kPrefillThreads)
   const int64_t h = bh % s.A, b = bh / s.A;
   const int64_t C = s.A * D, i0 = qb * QB;
   const int64_t p0 = position[0];
-  const int tid = threadIdx.x, pair = tid / TG, lane16 = tid % TG;
+  const int tid = threadIdx.x, quad = tid / TG, lane16 = tid % TG;
 
   for (int e = tid; e < QB * G; e += kPrefillThreads) {
     const int i = e / G, g = e % G;
@@ -93,12 +96,12 @@ __global__ void __launch_bounds__(kPrefillThreads)
     }
     *reinterpret_cast<float4 *>(&sm.q[i][4 * g]) = value;
   }
-  bool live[2];
-  int64_t mine[2];
+  bool live[4];
+  int64_t mine[4];
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    live[a] = i0 + 2 * pair + a < s.P;
-    mine[a] = p0 + i0 + 2 * pair + a;
+  for (int a = 0; a < 4; ++a) {
+    live[a] = i0 + 4 * quad + a < s.P;
+    mine[a] = p0 + i0 + 4 * quad + a;
   }
   const int64_t lastLocal = (i0 + QB < s.P ? i0 + QB : s.P) - 1;
   int64_t last = p0 + lastLocal;
@@ -106,16 +109,19 @@ __global__ void __launch_bounds__(kPrefillThreads)
     last = s.T - 1;
   const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D;
 
-  float m[2] = {-CUDART_INF_F, -CUDART_INF_F}, l[2] = {0.f, 0.f};
-  float4 acc[2][GPT];
+  float m[4], l[4];
+  float4 acc[4][GPT];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+  for (int a = 0; a < 4; ++a) {
+    m[a] = -CUDART_INF_F;
+    l[a] = 0.f;
 #pragma unroll
     for (int j = 0; j < GPT; ++j)
       acc[a][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 
   for (int64_t t0 = 0; t0 <= last; t0 += KB) {
-    __syncthreads(); // previous block's keys consumed (and the queries staged)
+    __syncthreads(); // previous block's keys and probabilities consumed (queries staged)
     for (int e = tid; e < KB * G; e += kPrefillThreads) {
       const int r = e / G, g = e % G;
       const int64_t t = t0 + r;
@@ -134,32 +140,34 @@ __global__ void __launch_bounds__(kPrefillThreads)
       sm.v[r][g] = vv;
     }
     __syncthreads();
-    float score[2][KPT];
+    float score[4][KPT];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < 4; ++a)
 #pragma unroll
       for (int u = 0; u < KPT; ++u)
         score[a][u] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
     for (int g = 0; g < G; ++g) {
-      const float4 q0 = *reinterpret_cast<const float4 *>(&sm.q[2 * pair][4 * g]);
-      const float4 q1 = *reinterpret_cast<const float4 *>(&sm.q[2 * pair + 1][4 * g]);
+      float4 qv[4], kv[KPT];
 #pragma unroll
-      for (int u = 0; u < KPT; ++u) {
-        const float4 kv = *reinterpret_cast<const float4 *>(&sm.k[lane16 + TG * u][4 * g]);
-        score[0][u] = fmaf(q0.x, kv.x, score[0][u]);
-        score[0][u] = fmaf(q0.y, kv.y, score[0][u]);
-        score[0][u] = fmaf(q0.z, kv.z, score[0][u]);
-        score[0][u] = fmaf(q0.w, kv.w, score[0][u]);
-        score[1][u] = fmaf(q1.x, kv.x, score[1][u]);
-        score[1][u] = fmaf(q1.y, kv.y, score[1][u]);
-        score[1][u] = fmaf(q1.z, kv.z, score[1][u]);
-        score[1][u] = fmaf(q1.w, kv.w, score[1][u]);
-      }
+      for (int a = 0; a < 4; ++a)
+        qv[a] = *reinterpret_cast<const float4 *>(&sm.q[4 * quad + a][4 * g]);
+#pragma unroll
+      for (int u = 0; u < KPT; ++u)
+        kv[u] = *reinterpret_cast<const float4 *>(&sm.k[lane16 + TG * u][4 * g]);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int u = 0; u < KPT; ++u) {
+          score[a][u] = fmaf(qv[a].x, kv[u].x, score[a][u]);
+          score[a][u] = fmaf(qv[a].y, kv[u].y, score[a][u]);
+          score[a][u] = fmaf(qv[a].z, kv[u].z, score[a][u]);
+          score[a][u] = fmaf(qv[a].w, kv[u].w, score[a][u]);
+        }
     }
-    float correction[2];
+    float correction[4], e[4][KPT];
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < 4; ++a) {
       float blockMax = -CUDART_INF_F;
 #pragma unroll
       for (int u = 0; u < KPT; ++u) {
@@ -175,9 +183,8 @@ __global__ void __launch_bounds__(kPrefillThreads)
       float sum = 0.f;
 #pragma unroll
       for (int u = 0; u < KPT; ++u) {
-        const float e = score[a][u] == -CUDART_INF_F ? 0.f : expf(score[a][u] - next);
-        sm.p[2 * pair + a][lane16 + TG * u] = e;
-        sum += e;
+        e[a][u] = score[a][u] == -CUDART_INF_F ? 0.f : expf(score[a][u] - next);
+        sum += e[a][u];
       }
 #pragma unroll
       for (int o = 1; o < TG; o <<= 1)
@@ -185,36 +192,41 @@ __global__ void __launch_bounds__(kPrefillThreads)
       l[a] = l[a] * correction[a] + sum;
       m[a] = next;
     }
-    __syncwarp(); // a row pair's probabilities come from the 16 threads of this half-warp
+#pragma unroll
+    for (int u = 0; u < KPT; ++u)
+      *reinterpret_cast<float4 *>(&sm.p[lane16 + TG * u][4 * quad]) =
+          make_float4(e[0][u], e[1][u], e[2][u], e[3][u]);
+    __syncwarp(); // a quad's probabilities come from the 16 threads of this half-warp
 #pragma unroll
     for (int j = 0; j < GPT; ++j) {
       const int g = lane16 + TG * j;
       if (g >= G)
         continue;
-      float4 a0 = acc[0][j], a1 = acc[1][j];
-      a0 = make_float4(a0.x * correction[0], a0.y * correction[0], a0.z * correction[0],
-                       a0.w * correction[0]);
-      a1 = make_float4(a1.x * correction[1], a1.y * correction[1], a1.z * correction[1],
-                       a1.w * correction[1]);
-#pragma unroll 8
+      float4 r[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+        r[a] = make_float4(acc[a][j].x * correction[a], acc[a][j].y * correction[a],
+                           acc[a][j].z * correction[a], acc[a][j].w * correction[a]);
+#pragma unroll 4
       for (int kj = 0; kj < KB; ++kj) {
-        const float w0 = sm.p[2 * pair][kj], w1 = sm.p[2 * pair + 1][kj];
+        const float4 w = *reinterpret_cast<const float4 *>(&sm.p[kj][4 * quad]);
         const float4 v = sm.v[kj][g];
-        a0.x = fmaf(w0, v.x, a0.x);
-        a0.y = fmaf(w0, v.y, a0.y);
-        a0.z = fmaf(w0, v.z, a0.z);
-        a0.w = fmaf(w0, v.w, a0.w);
-        a1.x = fmaf(w1, v.x, a1.x);
-        a1.y = fmaf(w1, v.y, a1.y);
-        a1.z = fmaf(w1, v.z, a1.z);
-        a1.w = fmaf(w1, v.w, a1.w);
+        const float ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          r[a].x = fmaf(ws[a], v.x, r[a].x);
+          r[a].y = fmaf(ws[a], v.y, r[a].y);
+          r[a].z = fmaf(ws[a], v.z, r[a].z);
+          r[a].w = fmaf(ws[a], v.w, r[a].w);
+        }
       }
-      acc[0][j] = a0;
-      acc[1][j] = a1;
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+        acc[a][j] = r[a];
     }
   }
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
+  for (int a = 0; a < 4; ++a) {
     if (!live[a] || mine[a] >= s.T)
       continue;
 #pragma unroll
@@ -226,7 +238,7 @@ __global__ void __launch_bounds__(kPrefillThreads)
       if (l[a] > 0.f)
         out = make_float4(acc[a][j].x / l[a], acc[a][j].y / l[a], acc[a][j].z / l[a],
                           acc[a][j].w / l[a]);
-      panel::store4(ctx, (i0 + 2 * pair + a) * s.B + b, h * D + 4 * g, C, out);
+      panel::store4(ctx, (i0 + 4 * quad + a) * s.B + b, h * D + 4 * g, C, out);
     }
   }
 }
