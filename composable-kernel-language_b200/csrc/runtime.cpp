@@ -1094,8 +1094,11 @@ void ckl_kernel(void *frame, const char *name, uint64_t gx, uint64_t gy, uint64_
     Function fn;
     fn.module = f.module;
     fn.name = name;
-    if (f.module->library) {
-      fn.entry = ckl::library::find(name);
+    // Library kernels resolve by name in every plan; a plan with a CUBIN (generated kernels
+    // or a hand-written module) resolves its other names in that module.
+    const ckl::library::Kernel *entry = ckl::library::find(name);
+    if (entry || f.module->library) {
+      fn.entry = entry;
       if (!fn.entry)
         throw std::invalid_argument(std::string("unknown library kernel: ") + name);
       fn.address = fn.entry->function;
@@ -1111,6 +1114,10 @@ void ckl_kernel(void *frame, const char *name, uint64_t gx, uint64_t gy, uint64_
       f.device->current();
       check(cudaLibraryGetKernel(&kernel, f.module->handle, name), "cudaLibraryGetKernel");
       fn.address = reinterpret_cast<const void *>(kernel);
+      if (shared > 48 * 1024)
+        check(cudaKernelSetAttributeForDevice(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(shared), f.device->ordinal),
+              "cudaKernelSetAttributeForDevice");
     }
     f.pending = KernelLaunch{};
     f.pending.function = fn;

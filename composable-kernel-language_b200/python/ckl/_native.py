@@ -92,6 +92,9 @@ _PROTOTYPES = {
     "ckl_library_faults": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
     "ckl_library_count": (C.c_uint32, []),
     "ckl_library_name": (C.c_char_p, [C.c_uint32]),
+    "ckl_cuda_compile": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p),
+                                   C.POINTER(C.c_uint64)]),
+    "ckl_binary_free": (None, [C.c_void_p]),
     "ckl_graph_plan_create": (C.c_int, [C.c_uint32, C.POINTER(GraphNode), C.c_uint32,
                                         C.POINTER(GraphAccess), C.c_uint32,
                                         C.POINTER(GraphResource), C.c_uint32,
@@ -147,6 +150,18 @@ def load():
         function.argtypes = argtypes
     _LIBRARY = lib
     return lib
+
+
+def compile_cuda(source: str, name: str = "ckl_generated.cu") -> bytes:
+    """sm_100a CUBIN of CUDA C++ source (NVRTC through the native library)."""
+    lib = load()
+    binary, size = C.c_void_p(), C.c_uint64()
+    check(lib.ckl_cuda_compile(source.encode(), name.encode(), C.byref(binary), C.byref(size)),
+          "ckl_cuda_compile")
+    try:
+        return C.string_at(binary, size.value)
+    finally:
+        lib.ckl_binary_free(binary)
 
 
 def message() -> str:

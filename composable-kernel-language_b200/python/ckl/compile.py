@@ -18,10 +18,11 @@ Stages (the reference's ``ckl-fuse-pointwise``, ``ckl-prepare-cuda``, ``ckl-buil
 from __future__ import annotations
 
 import ctypes as C
+import hashlib
 import struct
 from dataclasses import dataclass, field
 
-from . import _native
+from . import _native, codegen
 from .compiler import CompilationError
 from .frontend import analysis
 from .frontend.tracer import LoweredProgram, Resource
@@ -58,6 +59,7 @@ class Node:
     chain: tuple = None
     source: object = None     # the traced dispatch (1:1 nodes)
     selection: Selection = None
+    generated: object = None  # codegen.GeneratedKernel for kernels outside the library
 
 
 @dataclass
@@ -100,8 +102,16 @@ def _scalar_slot(operand) -> Slot:
     return Slot("value", data=struct.pack(code, operand.value))
 
 
-def _one_to_one(dispatch) -> Node:
-    selection = select(dispatch)
+def _one_to_one(dispatch, library: bool = True) -> Node:
+    """The node of one dispatch: its library kernel when the library implements the kernel
+    body over the launch's whole index space (and `library` is set), else a generated kernel
+    launched with the dispatch's own geometry."""
+    selection = None
+    if library:
+        try:
+            selection = select(dispatch)
+        except CompilationError:
+            selection = None
     spec = dispatch.specialization
     summary = analysis.summarize(spec.definition, spec.signature)
     slots, accesses = [], []
@@ -113,8 +123,13 @@ def _one_to_one(dispatch) -> Node:
                 accesses.append((operand.resource, bits, region))
         else:
             slots.append(_scalar_slot(operand))
-    node = Node(selection.entry.native, slots, selection.spec, accesses,
-                f"{spec.definition.name} @ {dispatch.location}", source=dispatch,
+    label = f"{spec.definition.name} @ {dispatch.location}"
+    if selection is None:
+        kernel = codegen.generate(spec.definition, spec.signature, spec.identity)
+        node = Node(kernel.symbol, slots, b"", accesses, label, source=dispatch, generated=kernel)
+        node.grid, node.block, node.shared = dispatch.grid, dispatch.block, dispatch.shared_memory
+        return node
+    node = Node(selection.entry.native, slots, selection.spec, accesses, label, source=dispatch,
                 selection=selection)
     node.grid, node.block = dispatch.grid, dispatch.block
     if selection.entry.pointwise_op >= 0 and dispatch.shared_memory == 0:
@@ -545,7 +560,7 @@ def _region(resources, rid, region):
 
 
 def _plan(lowered: LoweredProgram, events, resources, *, reuse_storage: bool,
-          externals_disjoint: bool, fused: bool) -> Plan:
+          externals_disjoint: bool, fused: bool, binary: bytes | None = None) -> Plan:
     lib = _native.load()
     nodes, accesses = [], []
     labels = []
@@ -577,12 +592,12 @@ def _plan(lowered: LoweredProgram, events, resources, *, reuse_storage: bool,
     if status:
         raise CompilationError(("ckl-b200", "plan"), _native.message())
     try:
-        return _emit(lowered, lib, handle, events, resources, fused)
+        return _emit(lowered, lib, handle, events, resources, fused, binary)
     finally:
         lib.ckl_graph_plan_release(handle)
 
 
-def _emit(lowered, lib, handle, events, resources, fused) -> Plan:
+def _emit(lowered, lib, handle, events, resources, fused, binary=None) -> Plan:
     count = lib.ckl_graph_plan_resource_count(handle)
     order = (C.c_uint32 * max(count, 1))()
     lib.ckl_graph_plan_resources(handle, order)
@@ -602,7 +617,7 @@ def _emit(lowered, lib, handle, events, resources, fused) -> Plan:
             text.append(f"arg {position} buffer {parameter.dtype.nbytes}")
         else:
             text.append(f"arg {position} scalar {parameter.dtype.name}")
-    text.append("binary library")
+    text.append(f"binary hex {binary.hex()}" if binary else "binary library")
     for h in range(heap_count.value):
         text.append(f"heap {h} {heaps[h]}")
         ir.append(f'  "ckl_exec.heap"() {{id = {h} : i64, bytes = {heaps[h]} : i64, alignment = '
@@ -631,7 +646,10 @@ def _emit(lowered, lib, handle, events, resources, fused) -> Plan:
         if event.kind != "dispatch":
             continue
         node = event.node
-        grid, block, shared = library_geometry(node.name, node.spec)
+        if node.generated is not None:
+            grid, block, shared = node.grid, node.block, node.shared
+        else:
+            grid, block, shared = library_geometry(node.name, node.spec)
         deps_count = lib.ckl_graph_plan_dependency_count(handle, node_id)
         deps = (C.c_uint32 * max(deps_count, 1))()
         lib.ckl_graph_plan_dependencies(handle, node_id, deps)
@@ -664,27 +682,51 @@ def _emit(lowered, lib, handle, events, resources, fused) -> Plan:
                 temporaries, int(planned.value), int(baseline.value), topology, fused)
 
 
-def _initial_events(lowered: LoweredProgram):
+def _initial_events(lowered: LoweredProgram, library: bool = True):
     trace = lowered.trace
     resources = [Resource(r.id, r.kind, r.spec, r.argument, r.base, r.byte_offset, r.name)
                  for r in trace.resources]
     events = []
     for e in trace.events:
         if e.kind == "dispatch":
-            events.append(Event("dispatch", node=_one_to_one(e.dispatch)))
+            events.append(Event("dispatch", node=_one_to_one(e.dispatch, library)))
         else:
             events.append(Event(e.kind, resource=e.resource))
     return events, resources
 
 
+_BINARIES: dict = {}
+
+
+def device_binary(kernels) -> tuple[str, bytes | None]:
+    """The translation unit of a program's generated kernels and its sm_100a CUBIN (None when
+    every dispatch runs a library kernel).  CUBINs are cached by source."""
+    kernels = list(kernels)
+    if not kernels:
+        return "", None
+    unit = codegen.translation_unit(kernels)
+    key = hashlib.sha256(unit.encode()).hexdigest()
+    if key not in _BINARIES:
+        try:
+            _BINARIES[key] = _native.compile_cuda(unit, "ckl_generated.cu")
+        except (ValueError, RuntimeError) as error:
+            raise CompilationError(("ckl-b200", "nvrtc", "sm_100a"), str(error)) from error
+    return unit, _BINARIES[key]
+
+
 def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library: bool,
-                 reuse_storage: bool, tensor_cores: bool = True) -> CompiledPlans:
-    events, resources = _initial_events(lowered)
+                 reuse_storage: bool, tensor_cores: bool = True,
+                 library: bool = True) -> CompiledPlans:
+    """Plans of a lowered program.  `library=False` generates every kernel from its body (the
+    reference's naive code path) instead of selecting library kernels."""
+    events, resources = _initial_events(lowered, library)
     if not any(e.kind == "dispatch" for e in events):
         raise CompilationError(("ckl-b200", "plan"), "program launches no kernels")
+    unit, binary = device_binary(e.node.generated for e in events
+                                 if e.kind == "dispatch" and e.node.generated is not None)
     baseline = _plan(lowered, [Event(e.kind, e.resource, e.node) for e in events],
                      list(resources), reuse_storage=reuse_storage, externals_disjoint=False,
-                     fused=False)
+                     fused=False, binary=binary)
     fused = False
     if fuse_pointwise:
         fused |= _fuse_pointwise(events, resources)
@@ -693,34 +735,43 @@ def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library:
     plans = CompiledPlans(baseline)
     if fused:
         primary = _plan(lowered, events, resources, reuse_storage=reuse_storage,
-                        externals_disjoint=True, fused=True)
+                        externals_disjoint=True, fused=True, binary=binary)
         plans = CompiledPlans(primary, baseline)
     plans.prepared_ir = lowered.mlir
-    plans.device_ir = _device_text(plans)
-    plans.host_ir = _host_text(plans.primary)
+    plans.device_ir = _device_text(plans, unit)
+    plans.host_ir = _host_text(plans.primary, binary)
     return plans
 
 
-def _device_text(plans: CompiledPlans) -> str:
+def _device_text(plans: CompiledPlans, generated: str = "") -> str:
     lib = _native.load()
     used = sorted(set(plans.primary.node_names) |
                   set(plans.fallback.node_names if plans.fallback else []))
     lines = ["// sm_100a kernel library entries used by this program (signature codes: "
              "P pointer, F f32, S specialization)"]
     for name in used:
+        if name.startswith(codegen.SYMBOL_PREFIX):
+            continue
         signature = C.create_string_buffer(64)
         lib.ckl_library_signature(name.encode(), signature, 64)
         lines.append(f"ckl.library.kernel @{name} signature \"{signature.value.decode()}\" "
                      "target \"sm_100a\"")
+    if generated:
+        lines += ["// generated kernels (CUDA C++, compiled by NVRTC for sm_100a):", generated]
     return "\n".join(lines) + "\n"
 
 
-def _host_text(plan: Plan) -> str:
+def _host_text(plan: Plan, binary: bytes | None = None) -> str:
     """The callback sequence the native entry replays, in LLVM-like text."""
-    lines = [f'@ckl.binary = internal constant [{len(LIBRARY_BINARY) + 1} x i8] '
-             f'c"{LIBRARY_BINARY}\\00"',
-             "define void @ckl_entry(ptr %frame, ptr %arguments) {",
-             f"  call void @ckl_begin(ptr %frame, ptr @ckl.binary, i64 {len(LIBRARY_BINARY)})"]
+    if binary:
+        lines = [f'@ckl.binary = internal constant [{len(binary)} x i8] c"<sm_100a CUBIN>"',
+                 "define void @ckl_entry(ptr %frame, ptr %arguments) {",
+                 f"  call void @ckl_begin(ptr %frame, ptr @ckl.binary, i64 {len(binary)})"]
+    else:
+        lines = [f'@ckl.binary = internal constant [{len(LIBRARY_BINARY) + 1} x i8] '
+                 f'c"{LIBRARY_BINARY}\\00"',
+                 "define void @ckl_entry(ptr %frame, ptr %arguments) {",
+                 f"  call void @ckl_begin(ptr %frame, ptr @ckl.binary, i64 {len(LIBRARY_BINARY)})"]
     current = None
     for line in plan.text.splitlines():
         parts = line.split()

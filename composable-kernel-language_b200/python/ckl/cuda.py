@@ -200,16 +200,18 @@ class _NativeProgram:
 
 
 class CompiledProgram(_ContextManager):
-    """A program resolved onto the sm_100a kernel library with its planned graph and storage."""
+    """A program resolved onto the sm_100a kernel library (and kernels generated from the bodies
+    the library does not implement) with its planned graph and storage."""
 
     def __init__(self, program, target: NVIDIATarget, *, fuse_pointwise=True, reuse_storage=True,
-                 fuse_library=True, tensor_cores=True):
+                 fuse_library=True, tensor_cores=True, library=True):
         if type(fuse_pointwise) is not bool:
             raise TypeError("fuse_pointwise must be bool")
         if type(reuse_storage) is not bool:
             raise TypeError("reuse_storage must be bool")
-        if type(fuse_library) is not bool or type(tensor_cores) is not bool:
-            raise TypeError("fuse_library and tensor_cores must be bool")
+        if type(fuse_library) is not bool or type(tensor_cores) is not bool \
+                or type(library) is not bool:
+            raise TypeError("fuse_library, tensor_cores and library must be bool")
         if not isinstance(target, NVIDIATarget) or target.binary_format != "bin":
             raise ValueError("CKL CUDA compilation requires a binary target")
         if target.chip not in SUPPORTED_CHIPS:
@@ -221,7 +223,7 @@ class CompiledProgram(_ContextManager):
         self._lib = _abi.load()
         self.plans = plan_program(program, fuse_pointwise=fuse_pointwise,
                                   fuse_library=fuse_library, reuse_storage=reuse_storage,
-                                  tensor_cores=tensor_cores)
+                                  tensor_cores=tensor_cores, library=library)
         self._resource = _NativeProgram(self._lib, self.plans)
 
     @classmethod

@@ -129,16 +129,18 @@ class LoweredProgram:
         return self
 
     def compile(self, *, target, fuse_pointwise=True, reuse_storage=True, fuse_library=True,
-                tensor_cores=True):
+                tensor_cores=True, library=True):
         """Select sm_100a kernels, infer the dependency graph and plan temporary storage.
 
-        ``tensor_cores=False`` keeps batched fused projections on FFMA instead of tcgen05.
+        Kernel bodies the library does not implement are generated (CUDA C++, compiled by
+        NVRTC for sm_100a).  ``tensor_cores=False`` keeps batched fused projections on FFMA
+        instead of tcgen05; ``library=False`` generates every kernel from its body.
         """
         from ..cuda import CompiledProgram
 
         return CompiledProgram(self, target, fuse_pointwise=fuse_pointwise,
                                reuse_storage=reuse_storage, fuse_library=fuse_library,
-                               tensor_cores=tensor_cores)
+                               tensor_cores=tensor_cores, library=library)
 
 
 @dataclass(frozen=True)
@@ -523,6 +525,11 @@ def lower_program(definition: Definition, signature, constants, *, verify=False,
     program_identity = identity(definition, bound)
     tracer = ProgramTracer(definition, bound)
     trace = tracer.trace()
+    # Kernel bodies are type-checked when the program is lowered, as the reference's emitter
+    # does; the generated source is kept for kernels the library does not implement.
+    from ..codegen import generate
+    for spec in tracer.specializations.values():
+        generate(spec.definition, spec.signature, spec.identity)
     symbol = "program_" + program_identity[:24]
     text = render(trace, symbol)
     for spec in tracer.specializations.values():

@@ -196,6 +196,16 @@ int ckl_greedy_head_noalloc(const float *x, const float *gain, const float *lm, 
                             float *logits, int32_t *tokens, int32_t *history, int32_t *position,
                             void *stream);
 
+/* ---- generated kernels (no GPU needed) ---------------------------------------------------- */
+/* Compiles CUDA C++ source (the frontend's translation of kernel bodies the library does not
+ * implement) for sm_100a with NVRTC, loaded at run time: no multiply-add contraction, IEEE
+ * division and square root, denormals kept.  On success *binary is a malloc'd CUBIN of *bytes
+ * bytes (release with ckl_binary_free); a compile error is CKL_INVALID_ARGUMENT with NVRTC's
+ * log in ckl_last_error().  Replaces: the NVVM lowering and gpu-module-to-binary serializer of
+ * the reference's device pipeline, python/ckl/_jit.py:32-52. */
+int ckl_cuda_compile(const char *source, const char *name, void **binary, uint64_t *bytes);
+void ckl_binary_free(void *binary);
+
 /* ---- planning (no GPU needed) ------------------------------------------------------------ */
 /* Inference of the dependency graph, its transitive reduction onto dispatch nodes and the
  * temporary-storage plan of one traced program.  Replaces: buildGraph + attachMemoryPlan

@@ -9,6 +9,7 @@ import pytest
 import ckl
 from ckl.compile import plan_program
 from ckl.compiler import CompilationError
+from ckl.library import select
 from ckl.frontend import FrontendError
 from ckl.frontend.analysis import canonical_key, summarize
 from ckl.workloads import decoder, vector_pipeline
@@ -54,10 +55,18 @@ def uses_unknown(src: Vector, dst: Vector) -> None:
     ckl.launch(unknown_kernel, src, dst, grid=(1,), block=(32,))
 
 
-def test_unknown_kernel_is_rejected_not_emulated():
+def test_unknown_kernel_is_generated_not_emulated():
+    """A kernel outside the library becomes generated sm_100a code launched with the program's
+    own geometry; selection alone still refuses it."""
     lowered = uses_unknown.lower(signature={"src": SPEC, "dst": SPEC})
     with pytest.raises(CompilationError, match="no sm_100a library implementation"):
-        plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+        select(lowered.trace.dispatches[0])
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+    (name,) = plans.primary.node_names
+    assert name.startswith("ckl_gen_unknown_kernel_")
+    assert f"kernel 0 {name} 1 1 1 32 1 1 0" in plans.primary.text
+    assert "binary hex 7f454c46" in plans.primary.text  # an ELF CUBIN
+    assert f'extern "C" __global__ void {name}(float *p_src, float *p_dst)' in plans.device_ir
 
 
 @ckl.program
@@ -66,12 +75,17 @@ def short_linear(x: ckl.Buffer[ckl.f32, (2, 64)], w: ckl.Buffer[ckl.f32, (1, 64,
     ckl.launch(linear, x, w, y, 0, grid=(1, 2), block=(64,))
 
 
-def test_partial_launch_coverage_is_rejected():
+def test_partial_launch_runs_generated_code_with_its_own_geometry():
     lowered = short_linear.lower(signature={"x": ckl.BufferSpec((2, 64), ckl.f32),
                                             "w": ckl.BufferSpec((1, 64, 256), ckl.f32),
                                             "y": ckl.BufferSpec((2, 256), ckl.f32)})
     with pytest.raises(CompilationError, match="does not cover"):
-        plan_program(lowered, fuse_pointwise=False, fuse_library=False, reuse_storage=True)
+        select(lowered.trace.dispatches[0])
+    plan = plan_program(lowered, fuse_pointwise=False, fuse_library=False,
+                        reuse_storage=True).primary
+    (name,) = plan.node_names
+    assert name.startswith("ckl_gen_linear_")
+    assert f"kernel 0 {name} 1 2 1 64 1 1 0" in plan.text
 
 
 @ckl.program
