@@ -17,6 +17,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <thread>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -75,7 +76,15 @@ struct Device {
   int ordinal = 0;
   uint64_t id = 0;
   std::string name;
+  // Set before asynchronous work is enqueued on this device (ckl_launch, asynchronous
+  // copies); a synchronous buffer copy then waits for the device first, so it never races
+  // with a submission still in flight.
+  mutable std::atomic<bool> asyncPending{false};
   void current() const { check(cudaSetDevice(ordinal), "cudaSetDevice"); }
+  void settle() const {
+    if (asyncPending.exchange(false))
+      check(cudaDeviceSynchronize(), "cudaDeviceSynchronize(settle)");
+  }
 };
 
 struct Allocation {
@@ -567,6 +576,19 @@ struct ckl_program {
 struct ckl_invocation {
   std::shared_ptr<InvocationState> state;
 };
+// A point on an invocation's stream.  It shares the invocation's state, so the stream, heaps
+// and bound buffers outlive every completion still held (the state's destructor also waits
+// for its stream).
+struct ckl_completion {
+  std::shared_ptr<InvocationState> state;
+  cudaEvent_t event = nullptr;
+  ~ckl_completion() {
+    if (event) {
+      cudaSetDevice(state->device->ordinal);
+      cudaEventDestroy(event);
+    }
+  }
+};
 struct ckl_graph_plan {
   ckl::planning::ProgramGraph graph;
   std::vector<uint32_t> resourceTemporary;
@@ -673,6 +695,7 @@ int ckl_buffer_copy_from_host(const ckl_buffer *buffer, const void *source, uint
     if (!buffer || !source || bytes > buffer->bytes)
       throw std::out_of_range("host-to-device copy exceeds the buffer");
     buffer->allocation->device->current();
+    buffer->allocation->device->settle();
     check(cudaMemcpy(reinterpret_cast<void *>(buffer->address()), source, bytes,
                      cudaMemcpyHostToDevice),
           "cudaMemcpy(host-to-device)");
@@ -687,6 +710,7 @@ int ckl_buffer_copy_to_host(const ckl_buffer *buffer, void *destination, uint64_
     if (!buffer || !destination || bytes > buffer->bytes)
       throw std::out_of_range("device-to-host copy exceeds the buffer");
     buffer->allocation->device->current();
+    buffer->allocation->device->settle();
     check(cudaMemcpy(destination, reinterpret_cast<void *>(buffer->address()), bytes,
                      cudaMemcpyDeviceToHost),
           "cudaMemcpy(device-to-host)");
@@ -828,6 +852,7 @@ int ckl_launch(ckl_invocation *invocation, int mode, uint64_t batch) {
     std::lock_guard<std::mutex> lock(f.runMutex);
     validateExecution(f, mode, batch);
     f.device->current();
+    f.device->asyncPending = true;
     submit(f, mode, batch);
   });
 }
@@ -849,6 +874,7 @@ int ckl_copy_in_async(ckl_invocation *invocation, const ckl_buffer *buffer, cons
       throw std::out_of_range("asynchronous host-to-device copy exceeds the buffer");
     auto &f = *invocation->state;
     f.device->current();
+    f.device->asyncPending = true;
     check(cudaMemcpyAsync(reinterpret_cast<void *>(buffer->address()), source, bytes,
                           cudaMemcpyHostToDevice, f.stream),
           "cudaMemcpyAsync(host-to-device)");
@@ -862,11 +888,87 @@ int ckl_copy_out_async(ckl_invocation *invocation, const ckl_buffer *buffer, voi
       throw std::out_of_range("asynchronous device-to-host copy exceeds the buffer");
     auto &f = *invocation->state;
     f.device->current();
+    f.device->asyncPending = true;
     check(cudaMemcpyAsync(destination, reinterpret_cast<void *>(buffer->address()), bytes,
                           cudaMemcpyDeviceToHost, f.stream),
           "cudaMemcpyAsync(device-to-host)");
   });
 }
+
+int ckl_record(ckl_invocation *invocation, ckl_completion **out) {
+  return guarded([&] {
+    if (!invocation || !out)
+      throw std::invalid_argument("null invocation or completion output");
+    *out = nullptr;
+    auto &f = *invocation->state;
+    std::lock_guard<std::mutex> lock(f.runMutex);
+    f.device->current();
+    auto completion = std::make_unique<ckl_completion>();
+    completion->state = invocation->state;
+    check(cudaEventCreateWithFlags(&completion->event, cudaEventDisableTiming),
+          "cudaEventCreateWithFlags");
+    check(cudaEventRecord(completion->event, f.stream), "cudaEventRecord");
+    *out = completion.release();
+  });
+}
+
+int ckl_wait_for(ckl_invocation *invocation, const ckl_completion *completion) {
+  return guarded([&] {
+    if (!invocation || !completion)
+      throw std::invalid_argument("null invocation or completion");
+    auto &f = *invocation->state;
+    std::lock_guard<std::mutex> lock(f.runMutex);
+    f.device->current();
+    f.device->asyncPending = true;
+    check(cudaStreamWaitEvent(f.stream, completion->event, 0), "cudaStreamWaitEvent");
+  });
+}
+
+int ckl_completion_query(const ckl_completion *completion, int *done) {
+  return guarded([&] {
+    if (!completion || !done)
+      throw std::invalid_argument("null completion or output");
+    completion->state->device->current();
+    const cudaError_t status = cudaEventQuery(completion->event);
+    if (status == cudaErrorNotReady) {
+      cudaGetLastError();
+      *done = 0;
+      return;
+    }
+    check(status, "cudaEventQuery");
+    *done = 1;
+  });
+}
+
+int ckl_completion_wait(const ckl_completion *completion, uint64_t timeout_us, int *done) {
+  return guarded([&] {
+    if (!completion || !done)
+      throw std::invalid_argument("null completion or output");
+    completion->state->device->current();
+    *done = 0;
+    if (timeout_us == UINT64_MAX) {
+      check(cudaEventSynchronize(completion->event), "cudaEventSynchronize");
+      *done = 1;
+      return;
+    }
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(timeout_us);
+    for (;;) {
+      const cudaError_t status = cudaEventQuery(completion->event);
+      if (status == cudaSuccess) {
+        *done = 1;
+        return;
+      }
+      if (status != cudaErrorNotReady)
+        check(status, "cudaEventQuery");
+      cudaGetLastError();
+      if (std::chrono::steady_clock::now() >= deadline)
+        return;
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+  });
+}
+
+void ckl_completion_release(ckl_completion *completion) { delete completion; }
 
 int ckl_benchmark(ckl_invocation *invocation, int mode, uint64_t iterations, uint64_t batch,
                   double out[3]) {

@@ -2,8 +2,10 @@
 from .compiler import (CompilationError, CompiledModule, CompilerOptions, GPUObject,
                        NVIDIATarget, extract_gpu_objects)
 from .frontend import FrontendError, LoweredProgram, kernel, program
-from .cuda import CompiledProgram, Device, DeviceBuffer, Invocation
+from .cuda import (CompiledProgram, Completion, Device, DeviceBuffer, Invocation,
+                   PinnedHostBuffer)
 from .frontend.source import INTRINSICS as _intrinsics
+from .plan_io import load as load_program
 from .types import Buffer, BufferSpec, constexpr, dim, f32, f64, i32, i64, index
 from .types import bool_ as bool
 
@@ -11,7 +13,8 @@ globals().update(_intrinsics)
 
 __all__ = [
     "CompilationError", "CompiledModule", "CompilerOptions", "GPUObject", "NVIDIATarget",
-    "CompiledProgram", "Device", "DeviceBuffer", "Invocation", "extract_gpu_objects",
+    "CompiledProgram", "Completion", "Device", "DeviceBuffer", "Invocation", "PinnedHostBuffer",
+    "extract_gpu_objects", "load_program",
     "Buffer", "BufferSpec", "constexpr", "dim", "f32", "f64", "i32", "i64", "index", "bool",
     "FrontendError", "LoweredProgram", "kernel", "program", *_intrinsics,
 ]

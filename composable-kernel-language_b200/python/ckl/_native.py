@@ -76,6 +76,11 @@ _PROTOTYPES = {
     "ckl_synchronize": (C.c_int, [C.c_void_p]),
     "ckl_copy_in_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]),
     "ckl_copy_out_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]),
+    "ckl_record": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "ckl_wait_for": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "ckl_completion_query": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "ckl_completion_wait": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_int)]),
+    "ckl_completion_release": (None, [C.c_void_p]),
     "ckl_time_launches": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_uint64,
                                     C.POINTER(C.c_double)]),
     "ckl_profile_nodes": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_double), C.c_uint64]),

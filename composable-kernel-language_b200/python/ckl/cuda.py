@@ -238,6 +238,23 @@ class CompiledProgram(_ContextManager):
         self._resource = _NativeProgram(self._lib, plans)
         return self
 
+    def to_json(self) -> str:
+        """Signature, native plans (with any generated device code) and ``ckl_exec`` text as
+        JSON; :func:`ckl.load_program` / :func:`ckl.plan_io.from_json` rebuild the program."""
+        from .plan_io import to_json
+        return to_json(self)
+
+    def save(self, path) -> None:
+        from .plan_io import save
+        save(self, path)
+
+    @property
+    def plan_stats(self) -> dict:
+        """The reference harness's statistics (nodes, edges, topology, temporaries, heap
+        bytes) of the primary plan."""
+        from .plan_io import plan_stats
+        return plan_stats(self.executable_ir)
+
     @property
     def prepared_ir(self) -> str:
         return self.plans.prepared_ir
@@ -387,6 +404,47 @@ class Invocation(_ContextManager):
                                                    buffer._native_resource.value,
                                                    destination_pointer, nbytes), "copy_out_async")
 
+    def record(self) -> "Completion":
+        """A completion at the current end of this invocation's stream."""
+        handle = C.c_void_p()
+        _abi.check(self._lib.ckl_record(self._native_resource.value, C.byref(handle)), "record")
+        return Completion(self, _Handle(handle.value, self._lib.ckl_completion_release))
+
+    def wait_for(self, completion: "Completion") -> None:
+        """Make this invocation's later work wait (on the device) for `completion`."""
+        if not isinstance(completion, Completion):
+            raise TypeError("wait_for requires a Completion")
+        _abi.check(self._lib.ckl_wait_for(self._native_resource.value,
+                                          completion._native_resource.value), "wait_for")
+
+    def submit(self, *, graph=False, mode=None, batch_size=1, after=(),
+               observe=()) -> "Completion":
+        """Enqueue one execution of ``batch_size`` programs and return its completion without
+        waiting.  ``after``: completions (of this or other invocations, on any device) the
+        execution waits for on the device.  ``observe``: ``(buffer, host)`` pairs copied to
+        page-locked host memory (:class:`PinnedHostBuffer` or a numpy view of one) after the
+        execution, in stream order; :meth:`Completion.wait` makes them readable.  Submissions
+        on one invocation run in order; the completion keeps the invocation, its buffers and
+        the observed host memory alive."""
+        execution = self._execution(graph, mode, batch_size)
+        observed = []
+        for buffer, host in observe:
+            if not isinstance(buffer, DeviceBuffer):
+                raise TypeError("observe takes (DeviceBuffer, host memory) pairs")
+            pointer, nbytes, keep = _pinned_pointer(host)
+            if nbytes < buffer.nbytes:
+                raise ValueError("observed host memory is smaller than the buffer")
+            observed.append((buffer, pointer, keep))
+        for completion in after:
+            self.wait_for(completion)
+        _abi.check(self._lib.ckl_launch(self._native_resource.value, execution, batch_size),
+                   "submit")
+        for buffer, pointer, _ in observed:
+            self.copy_out_async(buffer, pointer, buffer.nbytes)
+        completion = self.record()
+        completion._keep = (tuple(after), tuple(observed))
+        return completion
+
     def profile_nodes(self, iterations: int = 1) -> list:
         """Per-node device milliseconds over ``iterations`` ordinary executions (state advances)."""
         count = self.node_count
@@ -403,6 +461,44 @@ class Invocation(_ContextManager):
         return out.value
 
 
+class Completion(_ContextManager):
+    """A point on an invocation's stream (asynchronous invocation/completion interface).
+
+    Holding it keeps the invocation's stream, temporaries and bound buffers alive; ``done``
+    polls, ``wait`` blocks (optionally up to ``timeout`` seconds) and returns whether the work
+    before it has finished."""
+
+    def __init__(self, invocation, resource):
+        self.invocation = invocation
+        self._lib = invocation._lib
+        self._resource = resource
+        self._keep = ()
+
+    def done(self) -> bool:
+        flag = C.c_int()
+        _abi.check(self._lib.ckl_completion_query(self._native_resource.value, C.byref(flag)),
+                   "completion query")
+        return bool(flag.value)
+
+    def wait(self, timeout: float | None = None) -> bool:
+        if timeout is not None and (not math.isfinite(timeout) or timeout < 0):
+            raise ValueError("timeout must be a finite nonnegative number of seconds")
+        micros = (1 << 64) - 1 if timeout is None else int(timeout * 1e6)
+        flag = C.c_int()
+        _abi.check(self._lib.ckl_completion_wait(self._native_resource.value, micros,
+                                                 C.byref(flag)), "completion wait")
+        return bool(flag.value)
+
+
+def _pinned_pointer(host):
+    """(pointer, nbytes, keepalive) of page-locked host memory: a PinnedHostBuffer or a
+    contiguous writable array viewing one."""
+    if isinstance(host, PinnedHostBuffer):
+        return host.pointer, host.nbytes, host
+    pointer, nbytes, keep = _host_pointer(host, writable=True)
+    return pointer, nbytes, (host, keep)
+
+
 class PinnedHostBuffer:
     """Page-locked host memory for asynchronous copies."""
 
@@ -415,6 +511,14 @@ class PinnedHostBuffer:
 
     def view(self):
         return (C.c_char * self.nbytes).from_address(self.pointer)
+
+    def array(self, dtype, shape):
+        """A numpy array over this memory (the buffer must outlive it)."""
+        import numpy as np
+        count = int(np.prod(shape))
+        if count * np.dtype(dtype).itemsize > self.nbytes:
+            raise ValueError("array exceeds the pinned buffer")
+        return np.frombuffer(self.view(), dtype=dtype, count=count).reshape(shape)
 
 
 def cuda_available() -> bool:

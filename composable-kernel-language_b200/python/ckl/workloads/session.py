@@ -160,6 +160,43 @@ class DecoderSession:
         for _ in range(count // batch_size):
             self.invocation.run(mode=mode, batch_size=batch_size)
 
+    def generate(self, steps: int, *, group: int = 1, depth: int = 2, mode: str = "graph"):
+        """Greedy decode `steps` steps asynchronously; yields ``(position, tokens)`` per group
+        of `group` steps, ``tokens[g, b]`` being request b's token at ``position + g``.
+
+        Each group is one submission of `group` decode steps (the program repeated inside one
+        graph launch: fewer submissions, later observation), followed on the same stream by a
+        copy of the group's history rows into page-locked memory; up to `depth` groups are in
+        flight while the host consumes earlier ones.  The device state afterwards equals
+        ``step(steps)``."""
+        if steps % group or group <= 0 or depth <= 0:
+            raise ValueError("steps must be a positive multiple of group; depth positive")
+        from collections import deque
+
+        history = self.buffers["history"]
+        capacity, batch = history.spec.shape
+        position = int(self.read("position")[0])
+        if position + steps > capacity:
+            raise ValueError("generation would run past the history capacity")
+        slots = [ckl.PinnedHostBuffer(group * batch * 4) for _ in range(depth)]
+        pending = deque()
+        for index in range(steps // group):
+            if len(pending) == depth:
+                yield self._observed(*pending.popleft())
+            at = position + index * group
+            rows = history.subview(offset=at * batch, shape=(group, batch))
+            slot = slots[index % depth]
+            completion = self.invocation.submit(mode=mode, batch_size=group,
+                                                observe=[(rows, slot)])
+            pending.append((completion, at, slot, group, batch))
+        while pending:
+            yield self._observed(*pending.popleft())
+
+    @staticmethod
+    def _observed(completion, at, slot, group, batch):
+        completion.wait()
+        return at, slot.array(np.int32, (group, batch)).copy()
+
     def prefill(self, prompts: np.ndarray, *, mode: str = "graph", batched: bool = False) -> None:
         """Teacher-forced prefill: ``context - 1`` steps, next prompt token after each.
 

@@ -125,6 +125,22 @@ int ckl_copy_in_async(ckl_invocation *invocation, const ckl_buffer *buffer, cons
                       uint64_t bytes);
 int ckl_copy_out_async(ckl_invocation *invocation, const ckl_buffer *buffer, void *destination,
                        uint64_t bytes);
+
+/* Completions: the asynchronous invocation/completion interface the reference names as next
+ * work (benchmarks/decoder/results/deep-dive/REPORT.md:155-159; its runs are synchronous,
+ * lib/Runtime/NvidiaProgram.cpp:217-229).  ckl_record marks the current end of the
+ * invocation's stream (after ckl_launch and asynchronous copies); the completion keeps the
+ * invocation's stream, heaps and bound buffers alive until released.  ckl_wait_for makes an
+ * invocation's later work wait on the device for another invocation's completion (also
+ * across devices).  ckl_completion_wait polls up to timeout_us microseconds (UINT64_MAX:
+ * blocks) and sets *done.  Synchronous buffer copies wait for a device's outstanding
+ * asynchronous work before they touch its memory. */
+typedef struct ckl_completion ckl_completion;
+int ckl_record(ckl_invocation *invocation, ckl_completion **out);
+int ckl_wait_for(ckl_invocation *invocation, const ckl_completion *completion);
+int ckl_completion_query(const ckl_completion *completion, int *done);
+int ckl_completion_wait(const ckl_completion *completion, uint64_t timeout_us, int *done);
+void ckl_completion_release(ckl_completion *completion);
 /* Device time of `steps` submissions of (mode, batch) bracketed by events on the invocation
  * stream; nothing else is enqueued in between.  out_ms receives the elapsed milliseconds. */
 int ckl_time_launches(ckl_invocation *invocation, int mode, uint64_t batch, uint64_t steps,
