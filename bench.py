@@ -361,7 +361,7 @@ def gpu_arm(args, workload, world, rank, local, group):
 
     b, h, a, l, f, v, ctx, steps, seed, eps = workload
     total_steps = args.warmup + args.steps
-    capacity_steps = max(steps, 2 * total_steps + 4)
+    capacity_steps = max(steps, 2 * total_steps + 4 + NAIVE_STEPS + 1)
     shape = S.DecoderShape(batch=b, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
                            steps=capacity_steps)
     arrays, rng = S.make_weights(shape, seed)
@@ -378,7 +378,8 @@ def gpu_arm(args, workload, world, rank, local, group):
     device = ckl.Device(local)
     t_setup = time.perf_counter()
     sess = S.DecoderSession(device, arrays, epsilon=eps, attention_scale=(h // a) ** -0.5,
-                            tails=False, tensor_cores=args.projections == "tensor")
+                            tails=False, tensor_cores=args.projections == "tensor",
+                            whole_step=args.whole_step == "on")
     t_prefill = time.perf_counter()
     if args.prefill in ("batched", "graph"):
         sess.prefill(prompts, batched=args.prefill == "batched")
@@ -447,6 +448,7 @@ def gpu_arm(args, workload, world, rank, local, group):
     for n, t in zip(names, per_node):
         share[n] = share.get(n, 0.0) + t
     total = sum(per_node)
+    naive = None if args.no_naive else naive_graph(sess, elapsed_ms / args.steps, group)
     line = None
     if rank == 0:
         line = {
@@ -463,13 +465,43 @@ def gpu_arm(args, workload, world, rank, local, group):
             "graph_nodes_per_step": nodes,
             "kernel_share": {k: round(t / total, 4) for k, t in sorted(share.items(),
                                                                        key=lambda kv: -kv[1])},
+            "naive_graph": naive,
             "prefill": args.prefill,
             "projections": args.projections,
+            "whole_step": args.whole_step,
             "prefill_setup_s": round(setup_s, 2),
             "prefill_s": round(prefill_s, 3),
             "clocks": clocks.summary(),
         }
     return line
+
+
+NAIVE_STEPS = 3
+
+
+def naive_graph(sess, ms_per_step, group):
+    """The reference's own code path on this GPU: every kernel generated from its
+    ``workloads.py`` body (naive FP32 code, no library, no fusion), the unfused 21L+6-node DAG
+    with the reference's may-alias edges, replayed as an inferred CUDA graph on the session's
+    buffers after the timed region.  It stands in for the reference's MLIR-compiled graph,
+    which needs an LLVM/MLIR toolchain absent here."""
+    import ckl
+    from ckl.workloads import decoder
+
+    t0 = time.perf_counter()
+    program = sess.lowered.compile(target=ckl.NVIDIATarget("sm_100a"), fuse_pointwise=False,
+                                   fuse_library=False, library=False)
+    compile_s = time.perf_counter() - t0
+    arguments = [sess.buffers[name] for name in decoder.ARGUMENTS[:-2]]
+    inv = program.bind(*arguments, float(sess.epsilon), float(sess.attention_scale))
+    inv.run(mode="graph")
+    inv.synchronize()
+    barrier(group)
+    naive_ms = reduce_max(group, inv.time_launches(NAIVE_STEPS, mode="graph")) / NAIVE_STEPS
+    return {"ms_per_step": naive_ms, "steps": NAIVE_STEPS, "graph_nodes_per_step": inv.node_count,
+            "speedup": naive_ms / ms_per_step, "compile_s": round(compile_s, 2),
+            "what": "reference kernel bodies compiled naively (ckl codegen + NVRTC, sm_100a), "
+                    "reference DAG, inferred graph, same buffers and GPU"}
 
 
 def main():
@@ -482,6 +514,12 @@ def main():
     parser.add_argument("--requests-per-gpu", type=int)
     parser.add_argument("--context", type=int, help="override the prompt length (profiling)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--whole-step", choices=("on", "off"), default="on",
+                        help="small decoders: the whole decode step as one kernel (on) or the "
+                             "per-layer fused graph (off)")
+    parser.add_argument("--no-naive", action="store_true",
+                        help="skip timing the reference's naive code path (all kernels generated "
+                             "from their bodies) on the same GPU")
     parser.add_argument("--projections", choices=("tensor", "ffma"), default="tensor",
                         help="batched projections on tcgen05 tensor cores (3xTF32) or FFMA")
     parser.add_argument("--prefill", choices=("batched", "graph", "synthetic"), default="batched",

@@ -142,5 +142,11 @@ struct PositionAddSpec {
 struct CombineSpec {
   int64_t B, tiles, T, V;
 };
+// Whole decode step in one launch (small decoders): B requests, hidden C = A x D, FFN width F,
+// vocabulary V, L layers (weights of layers 0..L-1 of arrays holding `weightLayers`), cache
+// capacity T, norm/head layer indices of the final norm and LM head, G requests per cluster.
+struct DecodeStepSpec {
+  int64_t B, C, A, D, F, V, L, T, weightLayers, normLayers, finalLayer, headLayer, G, clusters;
+};
 
 } // namespace ckl::kernels

@@ -1,0 +1,511 @@
+// Whole decode step of a small decoder in one launch.
+//
+// For decoders whose weights stay resident in L2 (a few MB: the latency-bound configurations),
+// a step of 19-76 dependent graph nodes costs mostly launch and drain latency.  This kernel runs
+// the entire step (embedding, every layer, final norm, LM head, greedy selection and the
+// position advance) as one launch of 8-CTA thread-block clusters:
+//   * requests are partitioned across clusters (G rows each); clusters never wait for one
+//     another: the last cluster to finish advances `position` (a last-arriver counter);
+//   * inside a cluster every CTA keeps a full copy of its rows' activations in shared memory;
+//     each projection splits its output columns over the 8 CTAs, and every CTA writes its
+//     columns into all 8 copies through distributed shared memory, followed by one cluster
+//     barrier (barrier.cluster arrive/wait, release/acquire at cluster scope);
+//   * projections read their weights straight from L2 (they stay resident there), each thread
+//     reusing every weight load for up to eight requests held in registers;
+//   * RMSNorm statistics are recomputed by every CTA from its own copy (no exchange);
+//   * attention gives one warp to each (request, head) of the cluster: scores over the cache
+//     rows 0..p, softmax in shared memory, then the weighted value sum, each lane a head dim.
+// FFMA throughout; per output the K range is split over threads and reduced in a fixed order.
+#include "ckl_b200.h"
+#include "common.cuh"
+
+#include <cooperative_groups.h>
+
+namespace ckl::kernels {
+namespace {
+
+namespace cg = cooperative_groups;
+
+constexpr int kStepCtas = 8;      // CTAs per cluster
+constexpr int kStepThreads = 256; // threads per CTA
+constexpr int kStepWarps = kStepThreads / kWarp;
+constexpr int kMaxRows = 16;      // rows (requests) per cluster
+constexpr int kRowBlock = 8;              // rows per projection pass (accumulator registers)
+constexpr int kReduceFloats = kStepWarps * kRowBlock * 128; // partials of one pass
+constexpr int kMaxCacheRows = 1024;
+constexpr int kMaxLayers = 32;
+constexpr int kProjections = 7;           // q, k, v, o, gate, up, down per layer
+constexpr int kMaxSlices = kMaxLayers * kProjections + 1;
+
+__device__ __forceinline__ float4 f4(float a, float b, float c, float d) {
+  return make_float4(a, b, c, d);
+}
+
+__device__ __forceinline__ void fma4(float4 &acc, float a, const float4 &w) {
+  acc.x = fmaf(a, w.x, acc.x);
+  acc.y = fmaf(a, w.y, acc.y);
+  acc.z = fmaf(a, w.z, acc.z);
+  acc.w = fmaf(a, w.w, acc.w);
+}
+
+__device__ __forceinline__ float4 add4(const float4 &a, const float4 &b) {
+  return f4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// ---- the projections ---------------------------------------------------------------------------
+// One projection of the step as this CTA sees it: its column slice [o0, o0 + width) of a
+// K x O row-major matrix.
+struct Slice {
+  const float *w;
+  int K, O, o0, width;
+};
+
+// The step's slices in order (per layer q, k, v, o, gate, up, down; then the LM head).
+struct StreamTable {
+  Slice slices[kMaxSlices];
+};
+
+struct Cursor {
+  int slice = 0;
+};
+
+__device__ Slice makeSlice(const float *w, int64_t K, int64_t O, int rank) {
+  Slice s;
+  s.w = w;
+  s.K = int(K);
+  s.O = int(O);
+  s.width = int(O / kStepCtas);
+  s.o0 = rank * s.width;
+  return s;
+}
+
+// tile[r][4q .. 4q+3] = sum_k in[r][k] * W[k][o0 + 4q ..] for r < rows and the quads of the
+// next slice (tile row stride = slice width).  Rows go kRowBlock at a time, each thread holding
+// a float4 accumulator per row so that every weight load serves all rows of the block.  Thread
+// t owns quad t % nq and the K rows k = t / nq (mod 256 / nq), read straight from L2; partial
+// sums reduce within the warp (nq < 32) and then across warps in a fixed order.  For
+// nq >= 256 a thread owns whole quads.  One out-of-line copy serves every projection.
+__device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const float *in, int ldIn,
+                                     int rows, float *red, float *tile) {
+  const int tid = threadIdx.x, lane = tid % kWarp, warp = tid / kWarp;
+  const Slice sl = t.slices[cur.slice++];
+  const int nq = sl.width / 4, K = sl.K;
+  const int64_t O4 = sl.O / 4;
+  const float4 *w0 = reinterpret_cast<const float4 *>(sl.w + sl.o0);
+  for (int rb = 0; rb < rows; rb += kRowBlock) {
+    const int rr = rows - rb < kRowBlock ? rows - rb : kRowBlock;
+    const float *x = in + rb * ldIn;
+    float *out = tile + rb * nq * 4;
+    if (nq >= kStepThreads) {
+      for (int q = tid; q < nq; q += kStepThreads) {
+        float4 acc[kRowBlock];
+#pragma unroll
+        for (int r = 0; r < kRowBlock; ++r)
+          acc[r] = f4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int k = 0; k < K; ++k) {
+          const float4 wk = __ldg(w0 + k * O4 + q);
+#pragma unroll
+          for (int r = 0; r < kRowBlock; ++r)
+            if (r < rr)
+              fma4(acc[r], x[r * ldIn + k], wk);
+        }
+#pragma unroll
+        for (int r = 0; r < kRowBlock; ++r)
+          if (r < rr)
+            *reinterpret_cast<float4 *>(out + (r * nq + q) * 4) = acc[r];
+      }
+      __syncthreads();
+      continue;
+    }
+    const int q = tid % nq, kp = tid / nq, kparts = kStepThreads / nq;
+    float4 acc[kRowBlock];
+#pragma unroll
+    for (int r = 0; r < kRowBlock; ++r)
+      acc[r] = f4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int k = kp; k < K; k += kparts) {
+      const float4 wk = __ldg(w0 + k * O4 + q);
+#pragma unroll
+      for (int r = 0; r < kRowBlock; ++r)
+        if (r < rr)
+          fma4(acc[r], x[r * ldIn + k], wk);
+    }
+    int groups;
+    if (nq < kWarp) {
+#pragma unroll
+      for (int r = 0; r < kRowBlock; ++r) {
+        if (r >= rr)
+          break;
+        for (int o = nq; o < kWarp; o <<= 1) {
+          acc[r].x += __shfl_xor_sync(0xffffffffu, acc[r].x, o);
+          acc[r].y += __shfl_xor_sync(0xffffffffu, acc[r].y, o);
+          acc[r].z += __shfl_xor_sync(0xffffffffu, acc[r].z, o);
+          acc[r].w += __shfl_xor_sync(0xffffffffu, acc[r].w, o);
+        }
+      }
+      groups = kStepWarps;
+      if (lane < nq)
+#pragma unroll
+        for (int r = 0; r < kRowBlock; ++r)
+          if (r < rr)
+            *reinterpret_cast<float4 *>(red + ((warp * kRowBlock + r) * nq + q) * 4) = acc[r];
+    } else {
+      groups = kparts;
+#pragma unroll
+      for (int r = 0; r < kRowBlock; ++r)
+        if (r < rr)
+          *reinterpret_cast<float4 *>(red + ((kp * kRowBlock + r) * nq + q) * 4) = acc[r];
+    }
+    __syncthreads();
+    for (int e = tid; e < rr * nq; e += kStepThreads) {
+      const int r = e / nq, qq = e % nq;
+      float4 v = *reinterpret_cast<const float4 *>(red + (r * nq + qq) * 4);
+      for (int g = 1; g < groups; ++g)
+        v = add4(v, *reinterpret_cast<const float4 *>(red + ((g * kRowBlock + r) * nq + qq) * 4));
+      *reinterpret_cast<float4 *>(out + e * 4) = v;
+    }
+    __syncthreads();
+  }
+}
+
+// fn(r, column, value) for every (row, quad) of a projection tile.
+template <class Fn>
+__device__ __forceinline__ void eachQuad(int rows, int nq, int o0, const float *tile, Fn fn) {
+  for (int e = threadIdx.x; e < rows * nq; e += kStepThreads)
+    fn(e / nq, o0 + 4 * (e % nq), *reinterpret_cast<const float4 *>(tile + e * 4));
+}
+
+// Store one value at the same shared-memory offset in every CTA of the cluster.
+__device__ __forceinline__ void storeAll(cg::cluster_group &cluster, float *local, float4 v) {
+#pragma unroll
+  for (int rank = 0; rank < kStepCtas; ++rank)
+    *reinterpret_cast<float4 *>(cluster.map_shared_rank(local, rank)) = v;
+}
+
+__device__ __forceinline__ void storeAll(cg::cluster_group &cluster, float *local, float v) {
+#pragma unroll
+  for (int rank = 0; rank < kStepCtas; ++rank)
+    *cluster.map_shared_rank(local, rank) = v;
+}
+
+// act[g][:] = x[g][:] * rsqrt(mean(x[g]^2) + eps) * gain, one warp per row (row stride ld).
+__device__ void rmsRows(const float *x, const float *gain, float *act, int rows, int C, int ld,
+                        float eps) {
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  for (int g = warp; g < rows; g += kStepWarps) {
+    float total = 0.f;
+    for (int c = lane; c < C; c += kWarp) {
+      const float v = x[g * ld + c];
+      total += v * v;
+    }
+    total = warpSum(total);
+    const float inv = rsqrtf(total / float(C) + eps);
+    for (int c = lane; c < C; c += kWarp)
+      act[g * ld + c] = __fmul_rn(__fmul_rn(x[g * ld + c], inv), gain[c]);
+  }
+  __syncthreads();
+}
+
+// Activation rows are padded by four floats so that the rows read together in a projection
+// start in different shared-memory banks (and stay 16-byte aligned).
+__host__ __device__ constexpr int64_t rowStride(int64_t columns) { return columns + 4; }
+
+// Widest per-CTA column slice of any projection (the projection output tile's row stride).
+__host__ __device__ inline int64_t tileColumns(const DecodeStepSpec &s) {
+  int64_t widest = s.C > s.F ? s.C : s.F;
+  widest = widest > s.V ? widest : s.V;
+  return widest / kStepCtas;
+}
+
+constexpr std::size_t kTableBytes = (sizeof(StreamTable) + 15) / 16 * 16;
+
+struct StepBuffers {
+  StreamTable *table;
+  float *x, *act, *q, *ctx, *h, *red, *probs, *tile, *partValue, *first;
+  int *partIndex;
+};
+
+__device__ StepBuffers carve(unsigned char *base, const DecodeStepSpec &s) {
+  StepBuffers b;
+  const int64_t G = s.G, C = s.C;
+  b.table = reinterpret_cast<StreamTable *>(base);
+  b.x = reinterpret_cast<float *>(base + kTableBytes);
+  b.act = b.x + G * rowStride(C);
+  b.q = b.act + G * rowStride(C);
+  b.ctx = b.q + G * rowStride(C);
+  b.h = b.ctx + G * rowStride(C);
+  b.red = b.h + G * rowStride(s.F);
+  b.probs = b.red + kReduceFloats;
+  b.tile = b.probs + kStepWarps * s.T;
+  b.partValue = b.tile + G * tileColumns(s);
+  b.partIndex = reinterpret_cast<int *>(b.partValue + kStepCtas * kMaxRows);
+  b.first = reinterpret_cast<float *>(b.partIndex + kStepCtas * kMaxRows);
+  return b;
+}
+
+std::size_t stepSharedBytes(const DecodeStepSpec &s) {
+  const int64_t floats = 4 * s.G * rowStride(s.C) + s.G * rowStride(s.F) + kReduceFloats +
+                         kStepWarps * s.T +
+                         s.G * tileColumns(s) + 3 * kStepCtas * kMaxRows;
+  return kTableBytes + std::size_t(floats) * sizeof(float);
+}
+
+__global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads)
+    decodeStepKernel(int *tokens, int *position, int *history, const float *emb,
+                     const float *norm1, const float *norm2, const float *finalNorm,
+                     const float *wq, const float *wk, const float *wv, const float *wo,
+                     const float *wg, const float *wu, const float *wd, const float *lm,
+                     const float *sincos, float *kc, float *vc, float *logits, unsigned *counter,
+                     float eps, float scale, DecodeStepSpec s) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = int(cluster.block_rank());
+  const int tid = threadIdx.x, lane = tid % kWarp, warp = tid / kWarp;
+  extern __shared__ float4 sharedRaw[];
+  const StepBuffers sb = carve(reinterpret_cast<unsigned char *>(sharedRaw), s);
+  StreamTable &table = *sb.table;
+  const int64_t B = s.B, C = s.C, A = s.A, D = s.D, F = s.F, V = s.V, T = s.T;
+  const int64_t r0 = int64_t(blockIdx.x / kStepCtas) * s.G;
+  const int rows = int(s.G < B - r0 ? s.G : B - r0);
+  const int ldC = int(rowStride(C)), ldF = int(rowStride(F));
+  const int p = position[0];
+  const bool inside = p >= 0 && p < T;
+  // Every CTA of the cluster has read the position before any of them can finish (and so
+  // before the last cluster can advance it).
+  cluster.sync();
+
+  Cursor cur;
+  if (inside) {
+    // The step's weight slices in consumption order: per layer q, k, v, o, gate, up, down;
+    // then the LM head.
+    const int count = int(s.L) * kProjections + 1;
+    for (int i = tid; i < count; i += kStepThreads) {
+      const int64_t l = i / kProjections;
+      Slice sl;
+      switch (i == count - 1 ? -1 : i % kProjections) {
+      case 0: sl = makeSlice(wq + l * C * C, C, C, rank); break;
+      case 1: sl = makeSlice(wk + l * C * C, C, C, rank); break;
+      case 2: sl = makeSlice(wv + l * C * C, C, C, rank); break;
+      case 3: sl = makeSlice(wo + l * C * C, C, C, rank); break;
+      case 4: sl = makeSlice(wg + l * C * F, C, F, rank); break;
+      case 5: sl = makeSlice(wu + l * C * F, C, F, rank); break;
+      case 6: sl = makeSlice(wd + l * F * C, F, C, rank); break;
+      default: sl = makeSlice(lm + s.headLayer * C * V, C, V, rank); break;
+      }
+      table.slices[i] = sl;
+    }
+    __syncthreads();
+
+    for (int64_t e = tid; e < rows * C; e += kStepThreads) {
+      const int64_t g = e / C, c = e % C;
+      const int token = tokens[r0 + g];
+      sb.x[g * ldC + c] = token >= 0 && token < V ? emb[int64_t(token) * C + c] : 0.f;
+    }
+    __syncthreads();
+
+    const int nqC = int(C / kStepCtas / 4), nqF = int(F / kStepCtas / 4);
+    const int oC = rank * int(C / kStepCtas), oF = rank * int(F / kStepCtas);
+    const int64_t R = D / 2;
+    const float *cs = sincos + int64_t(p) * R * 2;
+    auto rope = [&](int col, float4 v) {
+      const int d = int(col % D);
+      const float c0 = cs[(d / 2) * 2], s0 = cs[(d / 2) * 2 + 1];
+      const float c1 = cs[(d / 2 + 1) * 2], s1 = cs[(d / 2 + 1) * 2 + 1];
+      return f4(__fsub_rn(__fmul_rn(v.x, c0), __fmul_rn(v.y, s0)),
+                __fadd_rn(__fmul_rn(v.x, s0), __fmul_rn(v.y, c0)),
+                __fsub_rn(__fmul_rn(v.z, c1), __fmul_rn(v.w, s1)),
+                __fadd_rn(__fmul_rn(v.z, s1), __fmul_rn(v.w, c1)));
+    };
+    auto residual = [&](int r, int col, float4 v) {
+      float *x = sb.x + r * ldC + col;
+      const float4 old = *reinterpret_cast<const float4 *>(x);
+      storeAll(cluster, x, f4(__fadd_rn(old.x, v.x), __fadd_rn(old.y, v.y),
+                              __fadd_rn(old.z, v.z), __fadd_rn(old.w, v.w)));
+    };
+    for (int64_t l = 0; l < s.L; ++l) {
+      auto cacheSlot = [&](float *cache, int r, int col) {
+        const int64_t b = r0 + r, h = col / D, d = col % D;
+        return reinterpret_cast<float4 *>(cache + (((l * B + b) * A + h) * T + p) * D + d);
+      };
+      rmsRows(sb.x, norm1 + l * C, sb.act, rows, int(C), ldC, eps);
+      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      eachQuad(rows, nqC, oC, sb.tile, [&](int r, int col, float4 v) {
+        storeAll(cluster, sb.q + r * ldC + col, rope(col, v));
+      });
+      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      eachQuad(rows, nqC, oC, sb.tile,
+               [&](int r, int col, float4 v) { *cacheSlot(kc, r, col) = rope(col, v); });
+      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      eachQuad(rows, nqC, oC, sb.tile,
+               [&](int r, int col, float4 v) { *cacheSlot(vc, r, col) = v; });
+      cluster.sync();
+
+      // Attention: one warp per (row, head) of the cluster.
+      const int64_t n = int64_t(p) + 1;
+      float *probs = sb.probs + warp * T;
+      for (int64_t pair = int64_t(rank) * kStepWarps + warp; pair < rows * A;
+           pair += kStepCtas * kStepWarps) {
+        const int64_t g = pair / A, h = pair % A, b = r0 + g;
+        const float *qv = sb.q + g * ldC + h * D;
+        const int64_t base = ((l * B + b) * A + h) * T * D;
+        float best = -CUDART_INF_F;
+        for (int64_t t = lane; t < n; t += kWarp) {
+          const float4 *krow = reinterpret_cast<const float4 *>(kc + base + t * D);
+          float dot = 0.f;
+          for (int64_t d4 = 0; d4 < D / 4; ++d4) {
+            const float4 kv = __ldcg(krow + d4);
+            dot = fmaf(qv[4 * d4], kv.x, dot);
+            dot = fmaf(qv[4 * d4 + 1], kv.y, dot);
+            dot = fmaf(qv[4 * d4 + 2], kv.z, dot);
+            dot = fmaf(qv[4 * d4 + 3], kv.w, dot);
+          }
+          const float score = dot * scale;
+          probs[t] = score;
+          best = fmaxf(best, score);
+        }
+        best = warpMax(best);
+        float total = 0.f;
+        for (int64_t t = lane; t < n; t += kWarp) {
+          const float e = expf(probs[t] - best);
+          probs[t] = e;
+          total += e;
+        }
+        total = warpSum(total);
+        __syncwarp();
+        for (int64_t d = lane; d < D; d += kWarp) {
+          const float *column = vc + base + d;
+          float acc = 0.f;
+          int64_t t = 0;
+          for (; t + 8 <= n; t += 8) { // eight independent loads in flight per lane
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              v[u] = __ldcg(column + (t + u) * D);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              acc = fmaf(probs[t + u], v[u], acc);
+          }
+          for (; t < n; ++t)
+            acc = fmaf(probs[t], __ldcg(column + t * D), acc);
+          storeAll(cluster, sb.ctx + g * ldC + h * D + d, acc / total);
+        }
+        __syncwarp();
+      }
+      cluster.sync();
+
+      // o projection + residual.
+      project(table, cur, sb.ctx, ldC, rows, sb.red, sb.tile);
+      eachQuad(rows, nqC, oC, sb.tile, residual);
+      cluster.sync();
+
+      // MLP: gate, then up with the SwiGLU product, then down + residual.
+      rmsRows(sb.x, norm2 + l * C, sb.act, rows, int(C), ldC, eps);
+      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 v) {
+        *reinterpret_cast<float4 *>(sb.h + r * ldF + col) = v;
+      });
+      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 v) {
+        float *hp = sb.h + r * ldF + col;
+        const float4 gate = *reinterpret_cast<const float4 *>(hp);
+        auto act = [](float gv, float uv) { return __fmul_rn(gv / (1.0f + expf(-gv)), uv); };
+        storeAll(cluster, hp, f4(act(gate.x, v.x), act(gate.y, v.y), act(gate.z, v.z),
+                                 act(gate.w, v.w)));
+      });
+      cluster.sync();
+      project(table, cur, sb.h, ldF, rows, sb.red, sb.tile);
+      eachQuad(rows, nqC, oC, sb.tile, residual);
+      cluster.sync();
+    }
+
+    // Head: final norm, logits of this CTA's vocabulary columns and their per-row maximum.
+    rmsRows(sb.x, finalNorm + s.finalLayer * C, sb.act, rows, int(C), ldC, eps);
+    const int64_t Wv = V / kStepCtas;
+    const int oV = rank * int(Wv);
+    project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+    eachQuad(rows, int(Wv / 4), oV, sb.tile, [&](int r, int col, float4 v) {
+      *reinterpret_cast<float4 *>(logits + (r0 + r) * V + col) = v;
+    });
+    for (int r = warp; r < rows; r += kStepWarps) {
+      float best = -CUDART_INF_F;
+      int index = 0x7fffffff;
+      for (int64_t j = lane; j < Wv; j += kWarp)
+        argmaxMerge(best, index, sb.tile[r * Wv + j], int(oV + j));
+#pragma unroll
+      for (int o = kWarp / 2; o > 0; o >>= 1)
+        argmaxMerge(best, index, __shfl_xor_sync(0xffffffffu, best, o),
+                    __shfl_xor_sync(0xffffffffu, index, o));
+      if (lane == 0) {
+        *cluster.map_shared_rank(sb.partValue + rank * kMaxRows + r, 0) = best;
+        *cluster.map_shared_rank(sb.partIndex + rank * kMaxRows + r, 0) = index;
+        if (rank == 0)
+          sb.first[r] = sb.tile[r * Wv];
+      }
+    }
+    cluster.sync();
+    if (rank == 0) {
+      for (int g = tid; g < rows; g += kStepThreads) {
+        float best = -CUDART_INF_F;
+        int index = 0x7fffffff;
+        for (int k = 0; k < kStepCtas; ++k)
+          argmaxMerge(best, index, sb.partValue[k * kMaxRows + g], sb.partIndex[k * kMaxRows + g]);
+        const float first = sb.first[g];
+        if (first != first || index == 0x7fffffff)
+          index = 0; // a NaN first score wins the reference's strict scan outright
+        tokens[r0 + g] = index;
+        history[int64_t(p) * B + r0 + g] = index;
+      }
+    }
+  }
+  // The last cluster to finish advances the position (clusters never wait for each other).
+  if (rank == 0) {
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      const unsigned done = atomicAdd(counter, 1u);
+      if (done == unsigned(s.clusters) - 1) {
+        position[0] = p + 1;
+        atomicExch(counter, 0u);
+        __threadfence();
+      }
+    }
+  }
+}
+
+bool decodeStepGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<DecodeStepSpec>(spec);
+  // Column quads per CTA: a power of two below 256 (the warp reduction pairs lanes by xor)
+  // or a multiple of 256.
+  auto quadsOk = [](int64_t columns) {
+    if (columns <= 0 || columns % (kStepCtas * 4))
+      return false;
+    const int64_t nq = columns / (kStepCtas * 4);
+    return nq % kStepThreads == 0 || (nq < kStepThreads && (nq & (nq - 1)) == 0);
+  };
+  if (s.B <= 0 || s.L <= 0 || s.L > kMaxLayers || s.A <= 0 || s.D <= 0 || s.D % 4 ||
+      s.A * s.D != s.C)
+    return false;
+  if (!quadsOk(s.C) || !quadsOk(s.F) || !quadsOk(s.V) || s.T <= 0 || s.T > kMaxCacheRows)
+    return false;
+  if (s.G <= 0 || s.G > kMaxRows || s.clusters <= 0 || s.clusters * s.G < s.B ||
+      (s.clusters - 1) * s.G >= s.B)
+    return false;
+  if (s.L > s.weightLayers || s.L > s.normLayers || s.finalLayer < 0 || s.headLayer < 0)
+    return false;
+  const std::size_t bytes = stepSharedBytes(s);
+  if (bytes > 227 * 1024)
+    return false;
+  g->grid[0] = unsigned(s.clusters * kStepCtas);
+  g->block[0] = kStepThreads;
+  g->sharedBytes = unsigned(bytes);
+  return true;
+}
+
+} // namespace
+
+CKL_REGISTER_KERNEL("ckl.fused.decode_step", reinterpret_cast<const void *>(&decodeStepKernel),
+                    "PPPPPPPPPPPPPPPPPPPPFFS", sizeof(DecodeStepSpec), decodeStepGeometry,
+                    nullptr, nullptr, 0, false);
+
+
+} // namespace ckl::kernels

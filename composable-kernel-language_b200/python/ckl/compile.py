@@ -234,7 +234,8 @@ def _short(node: Node) -> str:
     return node.name.rsplit(".", 1)[-1] if node.name.startswith("ckl.decoder.") else node.name
 
 
-def _fuse_decoder(events, resources: list, tensor_cores: bool = True) -> bool:
+def _fuse_decoder(events, resources: list, tensor_cores: bool = True,
+                  whole_step: bool = True) -> bool:
     dispatches = [e.node for e in events if e.kind == "dispatch"]
     names = [_short(n) for n in dispatches]
     if len(names) < 1 + len(_LAYER) + len(_HEAD) or (len(names) - 1 - len(_HEAD)) % len(_LAYER):
@@ -243,6 +244,12 @@ def _fuse_decoder(events, resources: list, tensor_cores: bool = True) -> bool:
     expected = ("embedding",) + _LAYER * layers + _HEAD
     if tuple(names) != expected:
         return False
+    if whole_step:
+        node = _whole_step(dispatches, layers, resources)
+        if node is not None:
+            # The program is exactly one decode step: every temporary lives inside the kernel.
+            events[:] = [Event("dispatch", node=node)]
+            return True
     try:
         new_nodes, eliminated, added = _decoder_nodes(dispatches, layers, resources,
                                                       0 if tensor_cores else 5)
@@ -273,7 +280,7 @@ def _fuse_decoder(events, resources: list, tensor_cores: bool = True) -> bool:
     return True
 
 
-def _decoder_nodes(dispatches, layers, resources, config=0):
+def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
     def op(node, i):
         return node.source.operands[i]
 
@@ -475,6 +482,10 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
                                   "down projection"))
         for rid, users in eliminated_here:
             eliminated[rid] = list(users)
+        if collect is not None:
+            collect.setdefault("layers", []).append(dict(
+                layer=layer, weights=(g1, g2, wq, wk, wv, wo, wg, wu, wd),
+                scalars=(eps1, eps2, scale), cache=(kc, vc), sincos=sincos, position=position))
         x = next_x
     h = dispatches[1 + layers * len(_LAYER):]
     same(res(h[0], 0), res(h[1], 0), x)
@@ -525,7 +536,77 @@ def _decoder_nodes(dispatches, layers, resources, config=0):
                           "greedy + advance"))
     eliminated[finv] = [h[0], h[1]]
     eliminated[final_x] = [h[1], h[2]]
+    if collect is not None:
+        collect["head"] = dict(tokens=tokens, history=history, logits=logits, fgain=fgain, lm=lm,
+                               final=const(h[1]), head=const(h[2]), eps=eps,
+                               embedding=(res(embedding, 0), res(embedding, 1)))
     return new_nodes, eliminated, added + [partials]
+
+
+# Whole-step kernel limits (csrc/kernels/decode_step.cu): weights small enough to stay in L2
+# while every cluster streams them, at most 16 requests per 8-CTA cluster and 18 clusters.
+_WHOLE_STEP_WEIGHT_BYTES = 24 << 20
+_WHOLE_STEP_CLUSTERS = 18
+_WHOLE_STEP_ROWS = 16
+
+
+def _whole_step(dispatches, layers, resources):
+    """One ``ckl.fused.decode_step`` node for a whole small decode step, or None."""
+    info: dict = {}
+    try:
+        _decoder_nodes(dispatches, layers, list(resources), 5, collect=info)
+    except _NoMatch:
+        return None
+    per_layer, head = info.get("layers", []), info.get("head")
+    if head is None or len(per_layer) != layers:
+        return None
+    first = per_layer[0]
+    for index, entry in enumerate(per_layer):
+        if entry["layer"] != index or entry["weights"] != first["weights"] or \
+                entry["cache"] != first["cache"] or entry["sincos"] != first["sincos"]:
+            return None
+        if any(not _same_slot(a, first["scalars"][0]) for a in entry["scalars"][:2]) or \
+                not _same_slot(entry["scalars"][2], first["scalars"][2]):
+            return None
+    if not _same_slot(head["eps"], first["scalars"][0]):
+        return None
+    tokens, emb = head["embedding"]
+    if tokens != head["tokens"]:
+        return None
+    g1, g2, wq, wk, wv, wo, wg, wu, wd = first["weights"]
+    kc, vc = first["cache"]
+    shape = lambda rid: resources[rid].spec.shape
+    _, B, A, T, D = shape(kc)
+    C, F, V = shape(wq)[1], shape(wg)[2], shape(head["lm"])[2]
+    weight_bytes = 4 * (layers * (4 * C * C + 3 * C * F) + 2 * V * C)
+    if weight_bytes > _WHOLE_STEP_WEIGHT_BYTES or B > _WHOLE_STEP_CLUSTERS * _WHOLE_STEP_ROWS:
+        return None
+    G = -(-B // min(_WHOLE_STEP_CLUSTERS, B))
+    clusters = -(-B // G)
+    spec = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
+                head["head"], G, clusters)
+    try:
+        library_geometry("ckl.fused.decode_step", spec)
+    except CompilationError:
+        return None
+    counter = _add_resource(resources, "persistent", BufferSpec((1,), i32), "counter")
+    position, sincos = first["position"], first["sincos"]
+    R = lambda rid: Slot("resource", resource=rid)
+    operands = [tokens, position, head["history"], emb, g1, g2, head["fgain"], wq, wk, wv, wo,
+                wg, wu, wd, head["lm"], sincos, kc, vc, head["logits"], counter]
+    reads = [emb, g1, g2, head["fgain"], wq, wk, wv, wo, wg, wu, wd, head["lm"], sincos]
+    accesses = [(r, READ, "whole") for r in reads]
+    accesses += [(tokens, READ | WRITE, "whole"), (position, READ | WRITE, POSITION),
+                 (head["history"], WRITE, "whole"), (kc, READ | WRITE, "whole"),
+                 (vc, READ | WRITE, "whole"), (head["logits"], WRITE, "whole"),
+                 (counter, READ | WRITE, "whole")]
+    return Node("ckl.fused.decode_step",
+                [R(r) for r in operands] + [first["scalars"][0], first["scalars"][2]], spec,
+                accesses, f"whole decode step ({layers} layers, {clusters} clusters)")
+
+
+def _same_slot(a, b) -> bool:
+    return (a.kind, a.argument, a.data) == (b.kind, b.argument, b.data)
 
 
 def _add_resource(resources, kind, spec, name) -> int:
@@ -716,7 +797,7 @@ def device_binary(kernels) -> tuple[str, bytes | None]:
 
 def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library: bool,
                  reuse_storage: bool, tensor_cores: bool = True,
-                 library: bool = True) -> CompiledPlans:
+                 library: bool = True, whole_step: bool = True) -> CompiledPlans:
     """Plans of a lowered program.  `library=False` generates every kernel from its body (the
     reference's naive code path) instead of selecting library kernels."""
     events, resources = _initial_events(lowered, library)
@@ -731,7 +812,7 @@ def plan_program(lowered: LoweredProgram, *, fuse_pointwise: bool, fuse_library:
     if fuse_pointwise:
         fused |= _fuse_pointwise(events, resources)
     if fuse_library:
-        fused |= _fuse_decoder(events, resources, tensor_cores)
+        fused |= _fuse_decoder(events, resources, tensor_cores, whole_step)
     plans = CompiledPlans(baseline)
     if fused:
         primary = _plan(lowered, events, resources, reuse_storage=reuse_storage,

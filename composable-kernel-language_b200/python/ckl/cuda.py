@@ -204,14 +204,13 @@ class CompiledProgram(_ContextManager):
     the library does not implement) with its planned graph and storage."""
 
     def __init__(self, program, target: NVIDIATarget, *, fuse_pointwise=True, reuse_storage=True,
-                 fuse_library=True, tensor_cores=True, library=True):
+                 fuse_library=True, tensor_cores=True, library=True, whole_step=True):
         if type(fuse_pointwise) is not bool:
             raise TypeError("fuse_pointwise must be bool")
         if type(reuse_storage) is not bool:
             raise TypeError("reuse_storage must be bool")
-        if type(fuse_library) is not bool or type(tensor_cores) is not bool \
-                or type(library) is not bool:
-            raise TypeError("fuse_library, tensor_cores and library must be bool")
+        if any(type(v) is not bool for v in (fuse_library, tensor_cores, library, whole_step)):
+            raise TypeError("fuse_library, tensor_cores, library and whole_step must be bool")
         if not isinstance(target, NVIDIATarget) or target.binary_format != "bin":
             raise ValueError("CKL CUDA compilation requires a binary target")
         if target.chip not in SUPPORTED_CHIPS:
@@ -223,7 +222,8 @@ class CompiledProgram(_ContextManager):
         self._lib = _abi.load()
         self.plans = plan_program(program, fuse_pointwise=fuse_pointwise,
                                   fuse_library=fuse_library, reuse_storage=reuse_storage,
-                                  tensor_cores=tensor_cores, library=library)
+                                  tensor_cores=tensor_cores, library=library,
+                                  whole_step=whole_step)
         self._resource = _NativeProgram(self._lib, self.plans)
 
     @classmethod

@@ -129,18 +129,21 @@ class LoweredProgram:
         return self
 
     def compile(self, *, target, fuse_pointwise=True, reuse_storage=True, fuse_library=True,
-                tensor_cores=True, library=True):
+                tensor_cores=True, library=True, whole_step=True):
         """Select sm_100a kernels, infer the dependency graph and plan temporary storage.
 
         Kernel bodies the library does not implement are generated (CUDA C++, compiled by
         NVRTC for sm_100a).  ``tensor_cores=False`` keeps batched fused projections on FFMA
-        instead of tcgen05; ``library=False`` generates every kernel from its body.
+        instead of tcgen05; ``library=False`` generates every kernel from its body;
+        ``whole_step=False`` keeps a small decode step as per-layer nodes instead of one
+        whole-step kernel.
         """
         from ..cuda import CompiledProgram
 
         return CompiledProgram(self, target, fuse_pointwise=fuse_pointwise,
                                reuse_storage=reuse_storage, fuse_library=fuse_library,
-                               tensor_cores=tensor_cores, library=library)
+                               tensor_cores=tensor_cores, library=library,
+                               whole_step=whole_step)
 
 
 @dataclass(frozen=True)

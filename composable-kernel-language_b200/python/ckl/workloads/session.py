@@ -90,7 +90,7 @@ class DecoderSession:
 
     def __init__(self, device: ckl.Device, arrays: dict, *, epsilon: float, attention_scale: float,
                  fuse_library: bool = True, reuse_storage: bool = True, tails: bool = True,
-                 tensor_cores: bool = True, library: bool = True,
+                 tensor_cores: bool = True, library: bool = True, whole_step: bool = True,
                  shared_weights: "DecoderSession | None" = None):
         self.device = device
         self.epsilon, self.attention_scale = epsilon, attention_scale
@@ -125,7 +125,8 @@ class DecoderSession:
         self.lowered = decoder.decode.lower(signature=signature)
         self.program = self.lowered.compile(target=ckl.NVIDIATarget("sm_100a"),
                                             fuse_library=fuse_library, reuse_storage=reuse_storage,
-                                            tensor_cores=tensor_cores, library=library)
+                                            tensor_cores=tensor_cores, library=library,
+                                            whole_step=whole_step)
         arguments = [self.buffers[name] for name in decoder.ARGUMENTS[:-2]]
         self.invocation = self.program.bind(*arguments, float(epsilon), float(attention_scale))
 

@@ -52,13 +52,15 @@ def verify(session, initial, expected, config):
                 assert np.allclose(actual, expected[name], rtol=RTOL, atol=ATOL), name
 
 
-@pytest.mark.parametrize("fuse", [True, False], ids=["fused", "unfused"])
+@pytest.mark.parametrize("fuse,whole,nodes", [(True, True, 1), (True, False, 19),
+                                              (False, False, 48)],
+                         ids=["whole-step", "fused-layers", "unfused"])
 @pytest.mark.parametrize("eps", [1e-6, 1e-5])
-def test_cfg1_sixteen_steps_match_oracle(device, fuse, eps):
+def test_cfg1_sixteen_steps_match_oracle(device, fuse, whole, nodes, eps):
     initial, _ = ref.make_inputs(CFG1, 0, eps=eps)
     expected = ref.expected(initial, CFG1, CFG1.steps, eps=eps)
-    session = open_session(device, CFG1, initial, eps, fuse_library=fuse)
-    assert session.invocation.node_count == (19 if fuse else 48)
+    session = open_session(device, CFG1, initial, eps, fuse_library=fuse, whole_step=whole)
+    assert session.invocation.node_count == nodes
     session.step(CFG1.steps)
     verify(session, initial, expected, CFG1)
 
@@ -98,13 +100,34 @@ def test_published_tokens_with_gpu_prefill(device, case):
     (256, 64, 4, 8, 256, 3, 3),      # cfg4 shape
     (33, 128, 2, 1, 96, 5, 3),       # ragged batch, head dim 64
 ])
-def test_batched_shapes_match_oracle(device, batch, hidden, heads, layers, ffn, seed, steps):
+@pytest.mark.parametrize("whole", [True, False], ids=["whole-step", "layers"])
+def test_batched_shapes_match_oracle(device, batch, hidden, heads, layers, ffn, seed, steps, whole):
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn, vocab=512,
                         context=16, steps=steps)
     initial, _ = ref.make_inputs(config, seed, eps=1e-6)
     expected = ref.expected(initial, config, steps, eps=1e-6)
-    session = open_session(device, config, initial, 1e-6)
+    session = open_session(device, config, initial, 1e-6, whole_step=whole)
     session.step(steps)
+    verify(session, initial, expected, config)
+
+
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,context,steps", [
+    (1, 64, 4, 2, 256, 512, 16, 16),       # one cluster, one request
+    (7, 128, 4, 3, 512, 1024, 40, 6),      # rows per cluster 1
+    (40, 64, 2, 2, 128, 8192, 20, 4),      # 256 vocabulary quads per CTA, D 32
+    (200, 128, 1, 1, 256, 256, 12, 3),     # one head of dim 128, ragged last cluster
+    (288, 64, 4, 1, 256, 512, 8, 3),       # 18 clusters x 16 requests (two row blocks)
+])
+def test_whole_step_kernel_matches_oracle(device, batch, hidden, heads, layers, ffn, vocab,
+                                          context, steps):
+    config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
+                        vocab=vocab, context=context, steps=steps)
+    initial, _ = ref.make_inputs(config, 11, eps=1e-5)
+    expected = ref.expected(initial, config, steps, eps=1e-5)
+    session = open_session(device, config, initial, 1e-5)
+    assert session.invocation.node_names == ["ckl.fused.decode_step"]
+    for mode in ("graph", "ordinary"):
+        session.step(steps // 2 if mode == "graph" else steps - steps // 2, mode=mode)
     verify(session, initial, expected, config)
 
 

@@ -114,7 +114,11 @@ def test_decoder_plan_matches_published(case):
 def test_fused_decoder_plan_shape():
     config = ref.Config(batch=1, hidden=64, heads=4, layers=2, ffn=256, vocab=512, context=16, steps=16)
     lowered = decoder.decode.lower(signature=decoder_signature(config))
-    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+    whole = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+    assert whole.primary.node_names == ["ckl.fused.decode_step"]
+    assert whole.fallback.nodes == 21 * 2 + 6
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
+                         whole_step=False)
     assert plans.primary.fused and plans.fallback is not None
     assert plans.primary.nodes == 1 + 8 * 2 + 2
     assert plans.fallback.nodes == 21 * 2 + 6
@@ -134,7 +138,8 @@ def test_tensor_core_decoder_plan_shape():
     config = ref.Config(batch=256, hidden=128, heads=2, layers=2, ffn=256, vocab=512, context=8,
                         steps=8)
     lowered = decoder.decode.lower(signature=decoder_signature(config))
-    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
+                         whole_step=False)
     names = plans.primary.node_names
     layer = ["ckl.fused.rms_panel", "ckl.fused.panel_linear_rope",
              "ckl.fused.panel_linear_rope_append", "ckl.fused.panel_linear_append",
@@ -150,9 +155,30 @@ def test_tensor_core_decoder_plan_shape():
     assert topology[gate_up] == [ids[7]] and topology[down] == [gate_up]
     # FFMA projections when tensor cores are switched off.
     ffma = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
-                        tensor_cores=False)
+                        tensor_cores=False, whole_step=False)
     assert ffma.primary.nodes == 1 + 8 * 2 + 2
     assert not any("panel" in n for n in ffma.primary.node_names)
+
+
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,context,whole", [
+    (1, 64, 4, 2, 256, 512, 16, True),
+    (64, 256, 8, 2, 1024, 512, 16, True),     # config 3
+    (256, 64, 4, 8, 256, 512, 16, True),      # config 4
+    (288, 64, 4, 1, 256, 512, 8, True),       # 18 clusters x 16 requests
+    (289, 64, 4, 1, 256, 512, 8, False),      # too many requests per cluster
+    (3, 48, 3, 1, 80, 129, 6, False),         # columns do not split into 8 x float4
+    (33, 128, 2, 1, 96, 512, 6, False),       # three FFN quads per CTA (not a power of two)
+    (4, 1024, 16, 4, 4096, 32000, 8, False),  # weights do not stay in L2
+])
+def test_whole_step_kernel_selection(batch, hidden, heads, layers, ffn, vocab, context, whole):
+    config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
+                        vocab=vocab, context=context, steps=4)
+    lowered = decoder.decode.lower(signature=decoder_signature(config))
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
+    assert (plans.primary.node_names == ["ckl.fused.decode_step"]) == whole
+    if whole:
+        # The whole step replaces every node; nothing but the cross-cluster counter persists.
+        assert plans.primary.temporaries == 0 and plans.primary.edges == 0
 
 
 def test_vector_pipeline_plans():
