@@ -31,8 +31,10 @@ constexpr int kStepThreads = 256; // threads per CTA
 constexpr int kStepWarps = kStepThreads / kWarp;
 constexpr int kMaxRows = 16;      // rows (requests) per cluster
 constexpr int kRowBlock = 8;              // rows per projection pass (accumulator registers)
-constexpr int kReduceFloats = kStepWarps * kRowBlock * 128; // partials of one pass
+// Partials of one pass (every thread's rows) plus the segment sums.
+constexpr int kReduceFloats = 4 * (kStepThreads * kRowBlock + kStepThreads);
 constexpr int kMaxCacheRows = 1024;
+constexpr std::size_t kMaxSharedPerCta = 113 * 1024; // two CTAs per SM
 constexpr int kMaxLayers = 32;
 constexpr int kProjections = 7;           // q, k, v, o, gate, up, down per layer
 constexpr int kMaxSlices = kMaxLayers * kProjections + 1;
@@ -131,38 +133,33 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
         if (r < rr)
           fma4(acc[r], x[r * ldIn + k], wk);
     }
-    int groups;
-    if (nq < kWarp) {
+    // Partials of every (K slice, row, quad) to shared memory, then a two-level sum in a fixed
+    // order: segments of K slices per output, then the segments (no warp shuffles: the
+    // shuffle pipe is the scarcer resource here).
+    const int outputs = rr * nq;
+    float4 *partial = reinterpret_cast<float4 *>(red);
 #pragma unroll
-      for (int r = 0; r < kRowBlock; ++r) {
-        if (r >= rr)
-          break;
-        for (int o = nq; o < kWarp; o <<= 1) {
-          acc[r].x += __shfl_xor_sync(0xffffffffu, acc[r].x, o);
-          acc[r].y += __shfl_xor_sync(0xffffffffu, acc[r].y, o);
-          acc[r].z += __shfl_xor_sync(0xffffffffu, acc[r].z, o);
-          acc[r].w += __shfl_xor_sync(0xffffffffu, acc[r].w, o);
-        }
-      }
-      groups = kStepWarps;
-      if (lane < nq)
-#pragma unroll
-        for (int r = 0; r < kRowBlock; ++r)
-          if (r < rr)
-            *reinterpret_cast<float4 *>(red + ((warp * kRowBlock + r) * nq + q) * 4) = acc[r];
-    } else {
-      groups = kparts;
-#pragma unroll
-      for (int r = 0; r < kRowBlock; ++r)
-        if (r < rr)
-          *reinterpret_cast<float4 *>(red + ((kp * kRowBlock + r) * nq + q) * 4) = acc[r];
+    for (int r = 0; r < kRowBlock; ++r)
+      if (r < rr)
+        partial[kp * outputs + r * nq + q] = acc[r];
+    __syncthreads();
+    int segments = 1; // about sqrt(kparts): both levels sum a few terms each
+    while (outputs * segments * 2 <= kStepThreads && segments * segments < kparts)
+      segments *= 2;
+    const int span = kparts / segments;
+    float4 *level = partial + kparts * outputs;
+    if (tid < outputs * segments) {
+      const int o = tid % outputs, seg = tid / outputs;
+      float4 v = partial[seg * span * outputs + o];
+      for (int j = 1; j < span; ++j)
+        v = add4(v, partial[(seg * span + j) * outputs + o]);
+      level[seg * outputs + o] = v;
     }
     __syncthreads();
-    for (int e = tid; e < rr * nq; e += kStepThreads) {
-      const int r = e / nq, qq = e % nq;
-      float4 v = *reinterpret_cast<const float4 *>(red + (r * nq + qq) * 4);
-      for (int g = 1; g < groups; ++g)
-        v = add4(v, *reinterpret_cast<const float4 *>(red + ((g * kRowBlock + r) * nq + qq) * 4));
+    for (int e = tid; e < outputs; e += kStepThreads) {
+      float4 v = level[e];
+      for (int g = 1; g < segments; ++g)
+        v = add4(v, level[g * outputs + e]);
       *reinterpret_cast<float4 *>(out + e * 4) = v;
     }
     __syncthreads();
@@ -251,7 +248,10 @@ std::size_t stepSharedBytes(const DecodeStepSpec &s) {
   return kTableBytes + std::size_t(floats) * sizeof(float);
 }
 
-__global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads)
+// Two CTAs per SM (at most 128 registers a thread and half of an SM's shared memory each):
+// with one CTA per SM only about 15 eight-CTA clusters fit on the GPU at once, and the last
+// clusters of a larger grid would wait for a second wave.
+__global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads, 2)
     decodeStepKernel(int *tokens, int *position, int *history, const float *emb,
                      const float *norm1, const float *norm2, const float *finalNorm,
                      const float *wq, const float *wk, const float *wv, const float *wo,
@@ -493,7 +493,7 @@ bool decodeStepGeometry(const void *spec, std::size_t, library::Geometry *g) {
   if (s.L > s.weightLayers || s.L > s.normLayers || s.finalLayer < 0 || s.headLayer < 0)
     return false;
   const std::size_t bytes = stepSharedBytes(s);
-  if (bytes > 227 * 1024)
+  if (bytes > kMaxSharedPerCta)
     return false;
   g->grid[0] = unsigned(s.clusters * kStepCtas);
   g->block[0] = kStepThreads;
