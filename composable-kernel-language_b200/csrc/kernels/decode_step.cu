@@ -120,28 +120,36 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
       __syncthreads();
       continue;
     }
-    const int q = tid % nq, kp = tid / nq, kparts = kStepThreads / nq;
+    // K split kparts ways, each slice at least four K rows (fewer partials to reduce).
+    int kparts = kStepThreads / nq;
+    while (kparts > 1 && kparts * 4 > K)
+      kparts >>= 1;
+    const int q = tid % nq, kp = tid / nq;
+    const bool busy = kp < kparts;
     float4 acc[kRowBlock];
 #pragma unroll
     for (int r = 0; r < kRowBlock; ++r)
       acc[r] = f4(0.f, 0.f, 0.f, 0.f);
+    if (busy) {
 #pragma unroll 4
-    for (int k = kp; k < K; k += kparts) {
-      const float4 wk = __ldg(w0 + k * O4 + q);
+      for (int k = kp; k < K; k += kparts) {
+        const float4 wk = __ldg(w0 + k * O4 + q);
 #pragma unroll
-      for (int r = 0; r < kRowBlock; ++r)
-        if (r < rr)
-          fma4(acc[r], x[r * ldIn + k], wk);
+        for (int r = 0; r < kRowBlock; ++r)
+          if (r < rr)
+            fma4(acc[r], x[r * ldIn + k], wk);
+      }
     }
     // Partials of every (K slice, row, quad) to shared memory, then a two-level sum in a fixed
     // order: segments of K slices per output, then the segments (no warp shuffles: the
     // shuffle pipe is the scarcer resource here).
     const int outputs = rr * nq;
     float4 *partial = reinterpret_cast<float4 *>(red);
+    if (busy)
 #pragma unroll
-    for (int r = 0; r < kRowBlock; ++r)
-      if (r < rr)
-        partial[kp * outputs + r * nq + q] = acc[r];
+      for (int r = 0; r < kRowBlock; ++r)
+        if (r < rr)
+          partial[kp * outputs + r * nq + q] = acc[r];
     __syncthreads();
     int segments = 1; // about sqrt(kparts): both levels sum a few terms each
     while (outputs * segments * 2 <= kStepThreads && segments * segments < kparts)
