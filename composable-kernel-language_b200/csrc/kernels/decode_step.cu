@@ -84,12 +84,12 @@ __device__ Slice makeSlice(const float *w, int64_t K, int64_t O, int rank) {
 // tile[r][4q .. 4q+3] = sum_k in[r][k] * W[k][o0 + 4q ..] for r < rows and the quads of the
 // next slice (tile row stride = slice width).  Rows go kRowBlock at a time, each thread holding
 // a float4 accumulator per row so that every weight load serves all rows of the block.  Thread
-// t owns quad t % nq and the K rows k = t / nq (mod 256 / nq), read straight from L2; partial
-// sums reduce within the warp (nq < 32) and then across warps in a fixed order.  For
-// nq >= 256 a thread owns whole quads.  One out-of-line copy serves every projection.
+// t owns quad t % nq and the K rows k = t / nq (mod kparts), read straight from L2; the
+// partials reduce through shared memory in two fixed-order levels.  For nq >= 256 a thread owns
+// whole quads.  One out-of-line copy serves every projection.
 __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const float *in, int ldIn,
                                      int rows, float *red, float *tile) {
-  const int tid = threadIdx.x, lane = tid % kWarp, warp = tid / kWarp;
+  const int tid = threadIdx.x;
   const Slice sl = t.slices[cur.slice++];
   const int nq = sl.width / 4, K = sl.K;
   const int64_t O4 = sl.O / 4;
