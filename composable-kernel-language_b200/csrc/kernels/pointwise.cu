@@ -34,7 +34,22 @@ __device__ void chainBody(const float *__restrict__ src, float *__restrict__ dst
     const int64_t vectors = count / 4;
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
     float4 *d4 = reinterpret_cast<float4 *>(dst);
-    for (int64_t v = i; v < vectors; v += stride) {
+    int64_t v = i;
+    for (; v + 3 * stride < vectors; v += 4 * stride) { // four independent loads in flight
+      float4 x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        x[u] = __ldcs(s4 + v + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        x[u].x = chain<Steps>(x[u].x, spec, scalars);
+        x[u].y = chain<Steps>(x[u].y, spec, scalars);
+        x[u].z = chain<Steps>(x[u].z, spec, scalars);
+        x[u].w = chain<Steps>(x[u].w, spec, scalars);
+        __stcs(d4 + v + u * stride, x[u]);
+      }
+    }
+    for (; v < vectors; v += stride) {
       float4 x = __ldcs(s4 + v);
       x.x = chain<Steps>(x.x, spec, scalars);
       x.y = chain<Steps>(x.y, spec, scalars);
