@@ -361,7 +361,7 @@ def gpu_arm(args, workload, world, rank, local, group):
 
     b, h, a, l, f, v, ctx, steps, seed, eps = workload
     total_steps = args.warmup + args.steps
-    capacity_steps = max(steps, 2 * total_steps + 4 + NAIVE_STEPS + 1)
+    capacity_steps = max(steps, 3 * total_steps + 8 + NAIVE_STEPS)
     shape = S.DecoderShape(batch=b, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
                            steps=capacity_steps)
     arrays, rng = S.make_weights(shape, seed)
@@ -420,6 +420,11 @@ def gpu_arm(args, workload, world, rank, local, group):
         host_tokens[:] = out_tokens
     e2e_s = reduce_max(group, time.perf_counter() - t0)
     e2e = b * world * args.steps / e2e_s
+    # Median step: the same steps timed one at a time (device time of each, CUDA events).
+    barrier(group)
+    inv.synchronize()
+    single = sorted(inv.time_launches(1, mode="graph") for _ in range(args.steps))
+    median_ms = reduce_max(group, statistics.median(single))
     clocks.__exit__(None, None, None)
 
     # Per-kernel device time of one more (profiled, ordinary-mode) step.
@@ -455,6 +460,7 @@ def gpu_arm(args, workload, world, rank, local, group):
             "metric": metric_name(args.workload), "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "median_step_us": median_ms * 1000.0,
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded random weights (reference draw order), uniform prompts",
             "config": workload_config(args, workload, world),
