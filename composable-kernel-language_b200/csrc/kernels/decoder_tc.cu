@@ -114,7 +114,7 @@ bool rmsPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
 // specialization and (last, added at bind time) the weights' tensor map.  SPLITS > 1 splits
 // K over a cluster of that many CTAs per output tile.
 #define CKL_PANEL_KERNEL(fn, EPI, params, assign)                                               \
-  template <int BN, int SPLITS>                                                                \
+  template <int BN, int SPLITS, int MT>                                                        \
   __global__ void __cluster_dims__(1, 1, SPLITS) __launch_bounds__(tc::kThreads)               \
       fn(const float *a, const float *w, CKL_UNPACK params, GemmSpec s,                         \
          const __grid_constant__ tc::WeightMap weights) {                                      \
@@ -122,7 +122,7 @@ bool rmsPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
     Params p;                                                                                  \
     p.a = a, p.w = w, p.s = s;                                                                 \
     CKL_UNPACK assign;                                                                         \
-    tc::body<BN, EPI, SPLITS>(p, weights);                                                     \
+    tc::body<BN, EPI, SPLITS, MT>(p, weights);                                                 \
   }
 #define CKL_UNPACK(...) __VA_ARGS__
 
@@ -145,24 +145,39 @@ CKL_PANEL_KERNEL(panelArgmaxTc, gemm::kArgmax, (float2 *partials),
                  (p.out = nullptr, p.partials = partials))
 
 // Fused gate/up/SwiGLU: out is the panel of silu(a @ wg) * (a @ wu) [M, N].
+template <int MT>
 __global__ void __launch_bounds__(tc::kThreads)
     panelGateUpTc(const float *a, const float *wg, const float *wu, float *out, GemmSpec s,
                   const __grid_constant__ tc::WeightMapPair maps) {
   dependentLaunchEntry();
   Params p;
   p.a = a, p.w = wg, p.w2 = wu, p.out = out, p.s = s;
-  tc::body<128, gemm::kSwiGluPanel, 1>(p, maps.gate, &maps.up);
+  tc::body<128, gemm::kSwiGluPanel, 1, MT>(p, maps.gate, &maps.up);
+}
+
+// Row tiles per CTA of the gate/up kernel (full-width tiles of 64 gate + 64 up columns): two
+// when single-tile CTAs would already fill the SMs.
+int gateUpRowTiles(const GemmSpec &s) {
+  const int64_t tiles = int64_t(ceilDiv(s.M, tc::BM)) * ceilDiv(s.N, tc::BM / 2);
+  return s.M > tc::BM && tiles >= tc::kTargetCtas ? 2 : 1;
 }
 
 bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<GemmSpec>(spec);
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
+  const int mt = gateUpRowTiles(s);
   g->grid[0] = ceilDiv(s.N, tc::BM / 2);
-  g->grid[1] = ceilDiv(s.M, tc::BM);
+  g->grid[1] = ceilDiv(ceilDiv(s.M, tc::BM), mt);
   g->block[0] = tc::kThreads;
-  g->sharedBytes = unsigned(tc::sharedBytes(128));
+  g->sharedBytes = unsigned(tc::sharedBytes(128, mt));
   return g->grid[1] <= 65535;
+}
+
+const void *gateUpSelect(const void *spec) {
+  return gateUpRowTiles(specOf<GemmSpec>(spec)) == 2
+             ? reinterpret_cast<const void *>(&panelGateUpTc<2>)
+             : reinterpret_cast<const void *>(&panelGateUpTc<1>);
 }
 
 // Tensor map of the weights [layers, K, N] for the kernel's column width, built once per bound
@@ -242,12 +257,12 @@ bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t c
 bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
-  const int width = tc::chooseWidth(s);
+  const int width = tc::chooseWidth(s), mt = tc::chooseRowTiles(s);
   g->grid[0] = ceilDiv(s.N, width);
-  g->grid[1] = ceilDiv(s.M, tc::BM);
+  g->grid[1] = ceilDiv(ceilDiv(s.M, tc::BM), mt);
   g->grid[2] = unsigned(tc::chooseSplits(s));
   g->block[0] = tc::kThreads;
-  g->sharedBytes = unsigned(tc::sharedBytes(width));
+  g->sharedBytes = unsigned(tc::sharedBytes(width, mt));
   return g->grid[1] <= 65535;
 }
 
@@ -274,14 +289,21 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
     const GemmSpec &s = specOf<GemmSpec>(spec);                                                \
     switch (tc::chooseWidth(s)) {                                                              \
     case 128:                                                                                  \
+      if (tc::chooseRowTiles(s) == 2)                                                          \
+        switch (tc::chooseSplits(s)) {                                                         \
+        case 8: return reinterpret_cast<const void *>(&fn<128, 8, 2>);                         \
+        case 4: return reinterpret_cast<const void *>(&fn<128, 4, 2>);                         \
+        case 2: return reinterpret_cast<const void *>(&fn<128, 2, 2>);                         \
+        default: return reinterpret_cast<const void *>(&fn<128, 1, 2>);                        \
+        }                                                                                      \
       switch (tc::chooseSplits(s)) {                                                           \
-      case 8: return reinterpret_cast<const void *>(&fn<128, 8>);                              \
-      case 4: return reinterpret_cast<const void *>(&fn<128, 4>);                              \
-      case 2: return reinterpret_cast<const void *>(&fn<128, 2>);                              \
-      default: return reinterpret_cast<const void *>(&fn<128, 1>);                             \
+      case 8: return reinterpret_cast<const void *>(&fn<128, 8, 1>);                           \
+      case 4: return reinterpret_cast<const void *>(&fn<128, 4, 1>);                           \
+      case 2: return reinterpret_cast<const void *>(&fn<128, 2, 1>);                           \
+      default: return reinterpret_cast<const void *>(&fn<128, 1, 1>);                          \
       }                                                                                        \
-    case 64: return reinterpret_cast<const void *>(&fn<64, 1>);                                \
-    default: return reinterpret_cast<const void *>(&fn<32, 1>);                                \
+    case 64: return reinterpret_cast<const void *>(&fn<64, 1, 1>);                             \
+    default: return reinterpret_cast<const void *>(&fn<32, 1, 1>);                             \
     }                                                                                          \
   }
 
@@ -290,28 +312,28 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
 CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPanelKernel),
                     "PPPFS", sizeof(RmsApplySpec), rmsPanelGeometry, nullptr,
                     nullptr, 0, true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&panelGateUpTc),
-                    "PPPPS", sizeof(GemmSpec), gateUpGeometry, nullptr, prepareGateUp,
+CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&panelGateUpTc<1>),
+                    "PPPPS", sizeof(GemmSpec), gateUpGeometry, gateUpSelect, prepareGateUp,
                     sizeof(tc::WeightMapPair), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope", reinterpret_cast<const void *>(&panelLinearRopeTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope", reinterpret_cast<const void *>(&panelLinearRopeTc<32, 1, 1>),
                     "PPPPPS", sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append", reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append", reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32, 1, 1>),
                     "PPPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearRopeAppendTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append", reinterpret_cast<const void *>(&panelLinearAppendTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append", reinterpret_cast<const void *>(&panelLinearAppendTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const void *>(&panelLinearResidualTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const void *>(&panelLinearResidualTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
-CKL_REGISTER_KERNEL("ckl.fused.panel_argmax", reinterpret_cast<const void *>(&panelArgmaxTc<32, 1>),
+CKL_REGISTER_KERNEL("ckl.fused.panel_argmax", reinterpret_cast<const void *>(&panelArgmaxTc<32, 1, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelArgmaxTc),
                     prepareWeights, sizeof(tc::WeightMap), true);
 

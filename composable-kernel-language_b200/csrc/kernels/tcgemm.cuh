@@ -234,11 +234,23 @@ constexpr int64_t kTargetCtas = 148; // one CTA per SM
 // K splits (1, 2, 4 or 8; the CTAs of one tile form a cluster): about one wave of CTAs over
 // the SMs, at least two slices per split, full-width tiles only.  A split whose slice range
 // is empty contributes zeros.
+// Row tiles per CTA: when single-tile CTAs would already fill the SMs, full-width tiles go two
+// per CTA and share every converted weight slice (half the weight conversion and copy traffic
+// per row tile; a wide projection's tiles fit in fewer waves).  Narrower grids keep one row
+// tile per CTA and split K instead.
+inline int chooseRowTiles(const GemmSpec &s) {
+  if (chooseWidth(s) != 128 || s.M <= BM)
+    return 1;
+  const int64_t tiles = ((s.M + BM - 1) / BM) * ((s.N + 127) / 128);
+  return tiles >= kTargetCtas ? 2 : 1;
+}
+
 inline int chooseSplits(const GemmSpec &s) {
   const int width = chooseWidth(s);
   if (width != 128)
     return 1;
-  const int64_t tiles = ((s.M + BM - 1) / BM) * ((s.N + width - 1) / width);
+  const int64_t rowGroups = ((s.M + BM - 1) / BM + chooseRowTiles(s) - 1) / chooseRowTiles(s);
+  const int64_t tiles = rowGroups * ((s.N + width - 1) / width);
   const int64_t slices = panel::slices(s.K);
   int64_t wanted = kTargetCtas / (tiles > 0 ? tiles : 1);
   if (wanted > slices / 2)
@@ -249,8 +261,8 @@ inline int chooseSplits(const GemmSpec &s) {
   return splits;
 }
 
-template <int BN, int S> struct Smem {
-  float a[S][2][BK / 4][BM][4]; // panel blocks (hi, lo) as copied
+template <int BN, int S, int MT = 1> struct Smem {
+  float a[S][MT][2][BK / 4][BM][4]; // panel blocks (MT row tiles x hi, lo) as copied
   float bHi[2][BK / 4][BN][4];  // converted weight slices, K-major
   float bLo[2][BK / 4][BN][4];
   float rawB[S][BK][BN];        // weight box as copied (128-byte aligned)
@@ -260,18 +272,21 @@ template <int BN, int S> struct Smem {
 };
 
 // Deepest ring (at most 6 stages) that fits the shared-memory budget.
-template <int BN, int S = 6> constexpr int stages() {
-  if constexpr (S <= 2 || sizeof(Smem<BN, S>) <= kMaxDynamicSmem)
+template <int BN, int MT = 1, int S = 6> constexpr int stages() {
+  if constexpr (S <= 2 || sizeof(Smem<BN, S, MT>) <= kMaxDynamicSmem)
     return S;
   else
-    return stages<BN, S - 1>();
+    return stages<BN, MT, S - 1>();
 }
 static_assert(sizeof(Smem<128, stages<128>()>) <= kMaxDynamicSmem, "shared memory budget");
+static_assert(sizeof(Smem<128, stages<128, 2>(), 2>) <= kMaxDynamicSmem, "shared memory budget");
 
-// Dynamic shared memory of the kernel at a column width.
-inline std::size_t sharedBytes(int width) {
+// Dynamic shared memory of the kernel at a column width and row tiles per CTA.
+inline std::size_t sharedBytes(int width, int rowTiles = 1) {
   switch (width) {
-  case 128: return sizeof(Smem<128, stages<128>()>);
+  case 128:
+    return rowTiles == 2 ? sizeof(Smem<128, stages<128, 2>(), 2>)
+                         : sizeof(Smem<128, stages<128>()>);
   case 64: return sizeof(Smem<64, stages<64>()>);
   default: return sizeof(Smem<32, stages<32>()>);
   }
@@ -450,26 +465,30 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
   }
 }
 
-// One 128 x BN tile.  p.a is the panel of A [M, K]; p.w the weights [layers, K, N].
-template <int BN, int EPI, int SPLITS>
+// MT x 128 rows by BN columns (MT row tiles sharing every converted weight slice).  p.a is the
+// panel of A [M, K]; p.w the weights [layers, K, N].
+template <int BN, int EPI, int SPLITS, int MT = 1>
 __device__ void body(const gemm::Params &p, const WeightMap &weights,
                      const WeightMap *upWeights = nullptr) {
   static_assert(EPI != gemm::kSwiGluPanel || (SPLITS == 1 && BN == 128), "gate/up tiles");
   static_assert(SPLITS == 1 || BN == 128, "K splits use full-width tiles");
-  static_assert(sizeof(Staging<BN>) <= sizeof(Smem<BN, stages<BN>()>::a), "staging fits the ring");
-  constexpr int S = stages<BN>();
-  using Layout = Smem<BN, S>;
+  static_assert(MT == 1 || BN == 128, "two row tiles use full-width tiles");
+  constexpr int S = stages<BN, MT>();
+  using Layout = Smem<BN, S, MT>;
+  static_assert(sizeof(Staging<BN>) <= sizeof(Layout::a), "staging fits the ring");
   extern __shared__ __align__(1024) unsigned char raw[];
   Layout &sm = *reinterpret_cast<Layout *>(raw);
   const GemmSpec &s = p.s;
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int64_t K = s.K, N = s.N;
-  // Tiles in launch order with the row tile varying fastest: the CTAs that share a weight tile
-  // run together and read it from HBM once.
-  const int64_t rowTiles = gridDim.y;
+  // Tiles in launch order with the row group varying fastest: the CTAs that share a weight
+  // tile run together and read it from HBM once.
+  const int64_t rowGroups = gridDim.y;
   const int64_t tile = int64_t(blockIdx.y) * gridDim.x + blockIdx.x;
-  const int64_t mt = tile % rowTiles, nt = tile / rowTiles;
-  const int64_t m0 = mt * BM, n0 = nt * tileColumns<BN, EPI>();
+  const int64_t group = tile % rowGroups, nt = tile / rowGroups;
+  const int64_t rowTiles = (s.M + BM - 1) / BM;
+  const int tiles = int(rowTiles - group * MT < MT ? rowTiles - group * MT : MT); // >= 1
+  const int64_t n0 = nt * tileColumns<BN, EPI>();
   // This split's K slices [kBegin, kEnd).
   const int64_t allSlices = panel::slices(K);
   const int64_t perSplit = (allSlices + SPLITS - 1) / SPLITS;
@@ -478,7 +497,6 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int64_t slices = kEnd > kBegin ? kEnd - kBegin : 0;
   const bool hasWork = slices > 0;
   const float *W = p.w + s.layer * K * N;
-  const float *blocks = p.a + mt * allSlices * panel::kBlock;
 
   int position = 0;
   if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend) {
@@ -497,7 +515,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const float *W2 = EPI == gemm::kSwiGluPanel ? p.w2 + s.layer * K * N : nullptr;
 
   if (warp == kMmaWarp)
-    tmemAlloc<2 * BN>(&sm.tmemBase);
+    tmemAlloc<2 * BN * MT>(&sm.tmemBase);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbarrierInit(&sm.full[i], 1);
@@ -516,9 +534,11 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   fenceAfterSync();
   const unsigned tmem = sm.tmemBase;
   volatile int *abort = &sm.abort;
+  bool valid = false; // converter warps: every issued MMA completed, nothing aborted
 
   if (warp == kProducerWarp) {
     const unsigned boxBytes = copyRows ? unsigned(BK * BN * 4) : 0u; // full box, OOB zero-filled
+    const unsigned blockBytes = unsigned(2 * panel::kPart * 4);
     int64_t issued = 0;
     if (lane == 0 && copyRows) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&weights.map))
@@ -536,9 +556,11 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       if (!__shfl_sync(0xffffffffu, ok, 0))
         break;
       if (lane == 0) {
-        mbarrierArriveExpectTx(&sm.full[slot], unsigned(2 * panel::kPart * 4) + boxBytes);
-        bulkCopy(&sm.a[slot][0][0][0][0], blocks + (kBegin + kt) * panel::kBlock,
-                 unsigned(2 * panel::kPart * 4), &sm.full[slot]);
+        mbarrierArriveExpectTx(&sm.full[slot], blockBytes * unsigned(tiles) + boxBytes);
+        for (int j = 0; j < tiles; ++j)
+          bulkCopy(&sm.a[slot][j][0][0][0][0],
+                   p.a + ((group * MT + j) * allSlices + kBegin + kt) * panel::kBlock, blockBytes,
+                   &sm.full[slot]);
         if (copyRows) {
           const int k0 = int((kBegin + kt) * BK);
           if constexpr (EPI == gemm::kSwiGluPanel) {
@@ -573,14 +595,19 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
         const int64_t remaining = K - (kBegin + kt) * BK;
         const int steps = int(remaining >= BK ? BK / 8 : (remaining + 7) / 8);
         for (int ks = 0; ks < steps; ++ks) {
-          const unsigned long long aHi = matrixDescriptor(sm.a[slot][0][2 * ks], BM * 16, 128);
-          const unsigned long long aLo = matrixDescriptor(sm.a[slot][1][2 * ks], BM * 16, 128);
           const unsigned long long bHi = matrixDescriptor(sm.bHi[buffer][2 * ks], BN * 16, 128);
           const unsigned long long bLo = matrixDescriptor(sm.bLo[buffer][2 * ks], BN * 16, 128);
           const unsigned first = (kt == 0 && ks == 0) ? 0u : 1u;
-          mma(tmem, aHi, bHi, idesc, first);
-          mma(tmem + BN, aHi, bLo, idesc, first);
-          mma(tmem + BN, aLo, bHi, idesc, 1u);
+          for (int j = 0; j < tiles; ++j) {
+            const unsigned long long aHi =
+                matrixDescriptor(sm.a[slot][j][0][2 * ks], BM * 16, 128);
+            const unsigned long long aLo =
+                matrixDescriptor(sm.a[slot][j][1][2 * ks], BM * 16, 128);
+            const unsigned d = tmem + unsigned(j * 2 * BN);
+            mma(d, aHi, bHi, idesc, first);
+            mma(d + BN, aHi, bLo, idesc, first);
+            mma(d + BN, aLo, bHi, idesc, 1u);
+          }
         }
         commit(&sm.empty[slot]);
         commit(&sm.bEmpty[buffer]);
@@ -658,46 +685,52 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       if (lane == 0)
         mbarrierArrive(&sm.bFull[buffer]);
     }
-    // Epilogue: wait (bounded) for every issued MMA, then stage this warp's TMEM lanes (main +
-    // correction, one row per thread, half of the columns) in shared memory over the idle ring.
+    // Wait (bounded) for every issued MMA.
     const bool done = waitPhase(&sm.accDone, 0, nullptr);
     fenceAfterSync();
-    Staging<BN> &stage = *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0]);
-    const int row = (warp % 4) * 32 + lane;
-    const unsigned rowAddress = tmem + (unsigned((warp % 4) * 32) << 16);
-    const int half = (warp - 2) / 4;
-    const bool valid = epilogueAll(done && !*abort) && hasWork; // uniform over these warps
-#pragma unroll 1
-    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
-      float v[16], correction[16];
-      if (valid) {
-        tmemLoad16(rowAddress + unsigned(c0), v);
-        tmemLoad16(rowAddress + unsigned(BN + c0), correction);
-      }
-#pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4 *>(&stage[row][c0 + j]) =
-            valid ? make_float4(__fadd_rn(v[j], correction[j]), __fadd_rn(v[j + 1], correction[j + 1]),
-                                __fadd_rn(v[j + 2], correction[j + 2]),
-                                __fadd_rn(v[j + 3], correction[j + 3]))
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    valid = epilogueAll(done && !*abort) && hasWork; // uniform over these warps
   }
-  // Every thread of every split CTA of the tile takes part in the same two barriers.
-  if constexpr (SPLITS > 1)
-    clusterSync();
-  else
-    __syncthreads();
-  if (warp >= 2 && __all_sync(0xffffffffu, !*abort))
-    reduceAndStore<BN, EPI, SPLITS>(p, *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0]),
-                                    m0, nt, position);
-  fenceBeforeSync();
-  if constexpr (SPLITS > 1)
-    clusterSync(); // peers read this CTA's staging until here
-  else
-    __syncthreads();
+  // Epilogue, one row tile at a time: stage this warp's TMEM lanes (main + correction, one row
+  // per thread, half of the columns) in shared memory over the idle ring, then reduce the K
+  // splits and store.  Every thread of every split CTA takes part in the same barriers.
+  Staging<BN> &stage = *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0][0]);
+  for (int j = 0; j < MT; ++j) {
+    if (warp >= 2) {
+      const int row = (warp % 4) * 32 + lane;
+      const unsigned rowAddress = tmem + unsigned(j * 2 * BN) + (unsigned((warp % 4) * 32) << 16);
+      const int half = (warp - 2) / 4;
+      const bool use = valid && j < tiles;
+#pragma unroll 1
+      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
+        float v[16], correction[16];
+        if (use) {
+          tmemLoad16(rowAddress + unsigned(c0), v);
+          tmemLoad16(rowAddress + unsigned(BN + c0), correction);
+        }
+#pragma unroll
+        for (int q = 0; q < 16; q += 4)
+          *reinterpret_cast<float4 *>(&stage[row][c0 + q]) =
+              use ? make_float4(__fadd_rn(v[q], correction[q]),
+                                __fadd_rn(v[q + 1], correction[q + 1]),
+                                __fadd_rn(v[q + 2], correction[q + 2]),
+                                __fadd_rn(v[q + 3], correction[q + 3]))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if constexpr (SPLITS > 1)
+      clusterSync();
+    else
+      __syncthreads();
+    if (warp >= 2 && j < tiles && __all_sync(0xffffffffu, !*abort))
+      reduceAndStore<BN, EPI, SPLITS>(p, stage, (group * MT + j) * BM, nt, position);
+    fenceBeforeSync();
+    if constexpr (SPLITS > 1)
+      clusterSync(); // peers read this CTA's staging until here
+    else
+      __syncthreads();
+  }
   if (warp == kMmaWarp)
-    tmemFree<2 * BN>(tmem);
+    tmemFree<2 * BN * MT>(tmem);
 }
 
 } // namespace ckl::kernels::tc
