@@ -30,9 +30,10 @@ constexpr int kStepCtas = 8;      // CTAs per cluster
 constexpr int kStepThreads = 256; // threads per CTA
 constexpr int kStepWarps = kStepThreads / kWarp;
 constexpr int kMaxRows = 16;      // rows (requests) per cluster
-constexpr int kRowBlock = 8;              // rows per projection pass (accumulator registers)
-// Partials of one pass (every thread's rows) plus the segment sums.
-constexpr int kReduceFloats = 4 * (kStepThreads * kRowBlock + kStepThreads);
+constexpr int kRowBlock = 8;              // rows per single projection pass (accumulators)
+constexpr int kFusedRowBlock = 4;         // rows per pass of fused q/k/v or gate/up
+// Partials of one pass (every thread's slices and rows) plus the segment sums.
+constexpr int kReduceFloats = 4 * (kStepThreads * 3 * kFusedRowBlock + kStepThreads);
 constexpr int kMaxCacheRows = 1024;
 constexpr std::size_t kMaxSharedPerCta = 113 * 1024; // two CTAs per SM
 constexpr int kMaxLayers = 32;
@@ -81,41 +82,58 @@ __device__ Slice makeSlice(const float *w, int64_t K, int64_t O, int rank) {
   return s;
 }
 
-// tile[r][4q .. 4q+3] = sum_k in[r][k] * W[k][o0 + 4q ..] for r < rows and the quads of the
-// next slice (tile row stride = slice width).  Rows go kRowBlock at a time, each thread holding
-// a float4 accumulator per row so that every weight load serves all rows of the block.  Thread
-// t owns quad t % nq and the K rows k = t / nq (mod kparts), read straight from L2; the
-// partials reduce through shared memory in two fixed-order levels.  For nq >= 256 a thread owns
-// whole quads.  One out-of-line copy serves every projection.
+// The next COUNT slices of the table (same K and width: q/k/v, or gate/up) applied to the same
+// input: tile[c][r][4q .. 4q+3] = sum_k in[r][k] * W_c[k][o0 + 4q ..] for slice c < COUNT,
+// r < rows and the quads q of the slices (slab of rows * width floats per slice).  Rows go RB
+// at a time, each thread holding a float4 accumulator per (slice, row) so that every weight
+// load serves all rows of the block.  Thread t owns quad t % nq and the K rows
+// k = t / nq (mod kparts), read straight from L2; the partials reduce through shared memory in
+// fixed-order levels.  For nq >= 256 a thread owns whole quads.  One out-of-line copy per
+// COUNT serves every projection.
+template <int COUNT, int RB>
 __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const float *in, int ldIn,
                                      int rows, float *red, float *tile) {
   const int tid = threadIdx.x;
-  const Slice sl = t.slices[cur.slice++];
-  const int nq = sl.width / 4, K = sl.K;
-  const int64_t O4 = sl.O / 4;
-  const float4 *w0 = reinterpret_cast<const float4 *>(sl.w + sl.o0);
-  for (int rb = 0; rb < rows; rb += kRowBlock) {
-    const int rr = rows - rb < kRowBlock ? rows - rb : kRowBlock;
+  const float4 *w0[COUNT];
+  int nq = 0, K = 0;
+  int64_t O4 = 0;
+#pragma unroll
+  for (int c = 0; c < COUNT; ++c) {
+    const Slice sl = t.slices[cur.slice++];
+    w0[c] = reinterpret_cast<const float4 *>(sl.w + sl.o0);
+    nq = sl.width / 4;
+    K = sl.K;
+    O4 = sl.O / 4;
+  }
+  const int slab = rows * nq * 4;
+  for (int rb = 0; rb < rows; rb += RB) {
+    const int rr = rows - rb < RB ? rows - rb : RB;
     const float *x = in + rb * ldIn;
-    float *out = tile + rb * nq * 4;
     if (nq >= kStepThreads) {
       for (int q = tid; q < nq; q += kStepThreads) {
-        float4 acc[kRowBlock];
+        float4 acc[COUNT][RB];
 #pragma unroll
-        for (int r = 0; r < kRowBlock; ++r)
-          acc[r] = f4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
+        for (int c = 0; c < COUNT; ++c)
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            acc[c][r] = f4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
         for (int k = 0; k < K; ++k) {
-          const float4 wk = __ldg(w0 + k * O4 + q);
 #pragma unroll
-          for (int r = 0; r < kRowBlock; ++r)
-            if (r < rr)
-              fma4(acc[r], x[r * ldIn + k], wk);
+          for (int c = 0; c < COUNT; ++c) {
+            const float4 wk = __ldg(w0[c] + k * O4 + q);
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+              if (r < rr)
+                fma4(acc[c][r], x[r * ldIn + k], wk);
+          }
         }
 #pragma unroll
-        for (int r = 0; r < kRowBlock; ++r)
-          if (r < rr)
-            *reinterpret_cast<float4 *>(out + (r * nq + q) * 4) = acc[r];
+        for (int c = 0; c < COUNT; ++c)
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < rr)
+              *reinterpret_cast<float4 *>(tile + c * slab + ((rb + r) * nq + q) * 4) = acc[c][r];
       }
       __syncthreads();
       continue;
@@ -126,49 +144,65 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
       kparts >>= 1;
     const int q = tid % nq, kp = tid / nq;
     const bool busy = kp < kparts;
-    float4 acc[kRowBlock];
+    float4 acc[COUNT][RB];
 #pragma unroll
-    for (int r = 0; r < kRowBlock; ++r)
-      acc[r] = f4(0.f, 0.f, 0.f, 0.f);
+    for (int c = 0; c < COUNT; ++c)
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+        acc[c][r] = f4(0.f, 0.f, 0.f, 0.f);
     if (busy) {
 #pragma unroll 4
       for (int k = kp; k < K; k += kparts) {
-        const float4 wk = __ldg(w0 + k * O4 + q);
 #pragma unroll
-        for (int r = 0; r < kRowBlock; ++r)
-          if (r < rr)
-            fma4(acc[r], x[r * ldIn + k], wk);
+        for (int c = 0; c < COUNT; ++c) {
+          const float4 wk = __ldg(w0[c] + k * O4 + q);
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < rr)
+              fma4(acc[c][r], x[r * ldIn + k], wk);
+        }
       }
     }
-    // Partials of every (K slice, row, quad) to shared memory, then a two-level sum in a fixed
-    // order: segments of K slices per output, then the segments (no warp shuffles: the
-    // shuffle pipe is the scarcer resource here).
-    const int outputs = rr * nq;
+    // Partials of every (K slice, output) to shared memory, then a fixed-order sum: one level
+    // for a few K slices per output, else segments of K slices and then the segments (no warp
+    // shuffles: the shuffle pipe is the scarcer resource here).
+    const int per = rr * nq, outputs = COUNT * per;
     float4 *partial = reinterpret_cast<float4 *>(red);
     if (busy)
 #pragma unroll
-      for (int r = 0; r < kRowBlock; ++r)
-        if (r < rr)
-          partial[kp * outputs + r * nq + q] = acc[r];
+      for (int c = 0; c < COUNT; ++c)
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+          if (r < rr)
+            partial[kp * outputs + c * per + r * nq + q] = acc[c][r];
     __syncthreads();
     int segments = 1; // about sqrt(kparts): both levels sum a few terms each
     while (outputs * segments * 2 <= kStepThreads && segments * segments < kparts)
       segments *= 2;
-    const int span = kparts / segments;
+    const int span = (kparts + segments - 1) / segments; // K slices per segment (last: fewer)
     float4 *level = partial + kparts * outputs;
-    if (tid < outputs * segments) {
-      const int o = tid % outputs, seg = tid / outputs;
-      float4 v = partial[seg * span * outputs + o];
-      for (int j = 1; j < span; ++j)
-        v = add4(v, partial[(seg * span + j) * outputs + o]);
-      level[seg * outputs + o] = v;
+    if (segments > 1) {
+      if (tid < outputs * segments) {
+        const int o = tid % outputs, seg = tid / outputs;
+        const int first = seg * span, last = first + span < kparts ? first + span : kparts;
+        float4 v = f4(0.f, 0.f, 0.f, 0.f);
+        if (first < last) {
+          v = partial[first * outputs + o];
+          for (int j = first + 1; j < last; ++j)
+            v = add4(v, partial[j * outputs + o]);
+        }
+        level[seg * outputs + o] = v;
+      }
+      __syncthreads();
     }
-    __syncthreads();
+    const float4 *terms = segments > 1 ? level : partial;
+    const int count = segments > 1 ? segments : kparts;
     for (int e = tid; e < outputs; e += kStepThreads) {
-      float4 v = level[e];
-      for (int g = 1; g < segments; ++g)
-        v = add4(v, level[g * outputs + e]);
-      *reinterpret_cast<float4 *>(out + e * 4) = v;
+      float4 v = terms[e];
+      for (int g = 1; g < count; ++g)
+        v = add4(v, terms[g * outputs + e]);
+      const int c = e / per, o = e % per;
+      *reinterpret_cast<float4 *>(tile + c * slab + (rb * nq + o) * 4) = v;
     }
     __syncthreads();
   }
@@ -216,9 +250,9 @@ __device__ void rmsRows(const float *x, const float *gain, float *act, int rows,
 // start in different shared-memory banks (and stay 16-byte aligned).
 __host__ __device__ constexpr int64_t rowStride(int64_t columns) { return columns + 4; }
 
-// Widest per-CTA column slice of any projection (the projection output tile's row stride).
+// Columns of one CTA's widest projection output (fused q/k/v, fused gate/up, or the LM head).
 __host__ __device__ inline int64_t tileColumns(const DecodeStepSpec &s) {
-  int64_t widest = s.C > s.F ? s.C : s.F;
+  int64_t widest = 3 * s.C > 2 * s.F ? 3 * s.C : 2 * s.F;
   widest = widest > s.V ? widest : s.V;
   return widest / kStepCtas;
 }
@@ -336,15 +370,15 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
         return reinterpret_cast<float4 *>(cache + (((l * B + b) * A + h) * T + p) * D + d);
       };
       rmsRows(sb.x, norm1 + l * C, sb.act, rows, int(C), ldC, eps);
-      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      // q, k and v in one pass over the normalized rows (tile slabs q | k | v).
+      project<3, kFusedRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      const int slabC = rows * nqC * 4;
       eachQuad(rows, nqC, oC, sb.tile, [&](int r, int col, float4 v) {
         storeAll(cluster, sb.q + r * ldC + col, rope(col, v));
       });
-      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
-      eachQuad(rows, nqC, oC, sb.tile,
+      eachQuad(rows, nqC, oC, sb.tile + slabC,
                [&](int r, int col, float4 v) { *cacheSlot(kc, r, col) = rope(col, v); });
-      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
-      eachQuad(rows, nqC, oC, sb.tile,
+      eachQuad(rows, nqC, oC, sb.tile + 2 * slabC,
                [&](int r, int col, float4 v) { *cacheSlot(vc, r, col) = v; });
       cluster.sync();
 
@@ -402,26 +436,22 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
       cluster.sync();
 
       // o projection + residual.
-      project(table, cur, sb.ctx, ldC, rows, sb.red, sb.tile);
+      project<1, kRowBlock>(table, cur, sb.ctx, ldC, rows, sb.red, sb.tile);
       eachQuad(rows, nqC, oC, sb.tile, residual);
       cluster.sync();
 
       // MLP: gate, then up with the SwiGLU product, then down + residual.
       rmsRows(sb.x, norm2 + l * C, sb.act, rows, int(C), ldC, eps);
-      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
-      eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 v) {
-        *reinterpret_cast<float4 *>(sb.h + r * ldF + col) = v;
-      });
-      project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
-      eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 v) {
-        float *hp = sb.h + r * ldF + col;
-        const float4 gate = *reinterpret_cast<const float4 *>(hp);
+      project<2, kFusedRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+      const int slabF = rows * nqF * 4;
+      eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 gate) {
+        const float4 up = *reinterpret_cast<const float4 *>(sb.tile + slabF + (r * nqF + (col - oF) / 4) * 4);
         auto act = [](float gv, float uv) { return __fmul_rn(gv / (1.0f + expf(-gv)), uv); };
-        storeAll(cluster, hp, f4(act(gate.x, v.x), act(gate.y, v.y), act(gate.z, v.z),
-                                 act(gate.w, v.w)));
+        storeAll(cluster, sb.h + r * ldF + col,
+                 f4(act(gate.x, up.x), act(gate.y, up.y), act(gate.z, up.z), act(gate.w, up.w)));
       });
       cluster.sync();
-      project(table, cur, sb.h, ldF, rows, sb.red, sb.tile);
+      project<1, kRowBlock>(table, cur, sb.h, ldF, rows, sb.red, sb.tile);
       eachQuad(rows, nqC, oC, sb.tile, residual);
       cluster.sync();
     }
@@ -430,7 +460,7 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
     rmsRows(sb.x, finalNorm + s.finalLayer * C, sb.act, rows, int(C), ldC, eps);
     const int64_t Wv = V / kStepCtas;
     const int oV = rank * int(Wv);
-    project(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
+    project<1, kRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
     eachQuad(rows, int(Wv / 4), oV, sb.tile, [&](int r, int col, float4 v) {
       *reinterpret_cast<float4 *>(logits + (r0 + r) * V + col) = v;
     });
@@ -482,13 +512,13 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
 
 bool decodeStepGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<DecodeStepSpec>(spec);
-  // Column quads per CTA: a power of two below 256 (the warp reduction pairs lanes by xor)
-  // or a multiple of 256.
+  // Column quads per CTA: below 256 (threads split K) or a multiple of 256 (whole quads per
+  // thread).
   auto quadsOk = [](int64_t columns) {
     if (columns <= 0 || columns % (kStepCtas * 4))
       return false;
     const int64_t nq = columns / (kStepCtas * 4);
-    return nq % kStepThreads == 0 || (nq < kStepThreads && (nq & (nq - 1)) == 0);
+    return nq < kStepThreads || nq % kStepThreads == 0;
   };
   if (s.B <= 0 || s.L <= 0 || s.L > kMaxLayers || s.A <= 0 || s.D <= 0 || s.D % 4 ||
       s.A * s.D != s.C)

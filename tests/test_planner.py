@@ -167,7 +167,7 @@ def test_tensor_core_decoder_plan_shape():
     (288, 64, 4, 1, 256, 512, 8, True),       # 18 clusters x 16 requests
     (289, 64, 4, 1, 256, 512, 8, False),      # too many requests per cluster
     (3, 48, 3, 1, 80, 129, 6, False),         # columns do not split into 8 x float4
-    (33, 128, 2, 1, 96, 512, 6, False),       # three FFN quads per CTA (not a power of two)
+    (33, 128, 2, 1, 96, 512, 6, True),        # three FFN quads per CTA
     (4, 1024, 16, 4, 4096, 32000, 8, False),  # weights do not stay in L2
 ])
 def test_whole_step_kernel_selection(batch, hidden, heads, layers, ffn, vocab, context, whole):
