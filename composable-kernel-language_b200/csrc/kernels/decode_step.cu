@@ -291,8 +291,8 @@ std::size_t stepSharedBytes(const DecodeStepSpec &s) {
 }
 
 // Two CTAs per SM (at most 128 registers a thread and half of an SM's shared memory each):
-// with one CTA per SM only about 15 eight-CTA clusters fit on the GPU at once, and the last
-// clusters of a larger grid would wait for a second wave.
+// with one CTA per SM only about 15 eight-CTA clusters fit on the GPU at once, with two 33, so
+// grids of up to 32 clusters run in one wave.
 __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads, 2)
     decodeStepKernel(int *tokens, int *position, int *history, const float *emb,
                      const float *norm1, const float *norm2, const float *finalNorm,

@@ -544,9 +544,12 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
 
 
 # Whole-step kernel limits (csrc/kernels/decode_step.cu): weights small enough to stay in L2
-# while every cluster streams them, at most 16 requests per 8-CTA cluster and 18 clusters.
+# while every cluster streams them, at most 16 requests per 8-CTA cluster and 32 clusters (at
+# two CTAs per SM 33 eight-CTA clusters are co-resident on a B200; spreading the requests over
+# all of them shortens every cluster's passes: 256 requests as 32 x 8 take 205 us per step of
+# an 8-layer C = 64 decoder against 309 us as 18 x 15).
 _WHOLE_STEP_WEIGHT_BYTES = 24 << 20
-_WHOLE_STEP_CLUSTERS = 18
+_WHOLE_STEP_CLUSTERS = 32
 _WHOLE_STEP_ROWS = 16
 
 

@@ -116,7 +116,8 @@ def test_batched_shapes_match_oracle(device, batch, hidden, heads, layers, ffn, 
     (7, 128, 4, 3, 512, 1024, 40, 6),      # rows per cluster 1
     (40, 64, 2, 2, 128, 8192, 20, 4),      # 256 vocabulary quads per CTA, D 32
     (200, 128, 1, 1, 256, 256, 12, 3),     # one head of dim 128, ragged last cluster
-    (288, 64, 4, 1, 256, 512, 8, 3),       # 18 clusters x 16 requests (two row blocks)
+    (288, 64, 4, 1, 256, 512, 8, 3),       # 32 clusters x 9 requests, ragged last cluster
+    (512, 64, 4, 1, 256, 512, 8, 3),       # 32 clusters x 16 requests (two row blocks)
 ])
 def test_whole_step_kernel_matches_oracle(device, batch, hidden, heads, layers, ffn, vocab,
                                           context, steps):

@@ -164,8 +164,8 @@ def test_tensor_core_decoder_plan_shape():
     (1, 64, 4, 2, 256, 512, 16, True),
     (64, 256, 8, 2, 1024, 512, 16, True),     # config 3
     (256, 64, 4, 8, 256, 512, 16, True),      # config 4
-    (288, 64, 4, 1, 256, 512, 8, True),       # 18 clusters x 16 requests
-    (289, 64, 4, 1, 256, 512, 8, False),      # too many requests per cluster
+    (512, 64, 4, 1, 256, 512, 8, True),       # 32 clusters x 16 requests
+    (513, 64, 4, 1, 256, 512, 8, False),      # too many requests per cluster
     (3, 48, 3, 1, 80, 129, 6, False),         # columns do not split into 8 x float4
     (33, 128, 2, 1, 96, 512, 6, True),        # three FFN quads per CTA
     (4, 1024, 16, 4, 4096, 32000, 8, False),  # weights do not stay in L2
