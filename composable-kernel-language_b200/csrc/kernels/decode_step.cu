@@ -6,15 +6,20 @@
 // position advance) as one launch of 8-CTA thread-block clusters:
 //   * requests are partitioned across clusters (G rows each); clusters never wait for one
 //     another: the last cluster to finish advances `position` (a last-arriver counter);
-//   * inside a cluster every CTA keeps a full copy of its rows' activations in shared memory;
-//     each projection splits its output columns over the 8 CTAs, and every CTA writes its
-//     columns into all 8 copies through distributed shared memory, followed by one cluster
-//     barrier (barrier.cluster arrive/wait, release/acquire at cluster scope);
+//   * inside a cluster every CTA keeps a full copy of its rows' residual stream in shared
+//     memory; the heads are partitioned over the 8 CTAs (by row group when there are fewer
+//     than 8), and a CTA computes q/k/v of its heads, appends them to the cache, runs their
+//     attention and multiplies the result by its rows of Wo, all in its own shared memory;
+//   * the o projection and the down projection (K split by CTA: its heads' columns, its FFN
+//     columns) leave partial sums [rows][C] in each CTA; after one cluster barrier
+//     (barrier.cluster arrive/wait, release/acquire at cluster scope) every CTA adds all
+//     partials, read through distributed shared memory in rank order, to its own copy, so a
+//     layer needs two cluster barriers; gate/up split their output columns over the CTAs;
 //   * projections read their weights straight from L2 (they stay resident there), each thread
 //     reusing every weight load for up to eight requests held in registers;
 //   * RMSNorm statistics are recomputed by every CTA from its own copy (no exchange);
-//   * attention gives one warp to each (request, head) of the cluster: scores over the cache
-//     rows 0..p, softmax in shared memory, then the weighted value sum, each lane a head dim.
+//   * attention gives each (request, head) of a CTA one or more of its warps, which split the
+//     cache rows: scores, softmax in shared memory, then the weighted value sums.
 // FFMA throughout; per output the K range is split over threads and reduced in a fixed order.
 #include "ckl_b200.h"
 #include "common.cuh"
@@ -72,22 +77,22 @@ struct Cursor {
   int slice = 0;
 };
 
-__device__ Slice makeSlice(const float *w, int64_t K, int64_t O, int rank) {
+__device__ Slice makeSlice(const float *w, int64_t K, int64_t O, int64_t o0, int64_t width) {
   Slice s;
   s.w = w;
   s.K = int(K);
   s.O = int(O);
-  s.width = int(O / kStepCtas);
-  s.o0 = rank * s.width;
+  s.o0 = int(o0);
+  s.width = int(width);
   return s;
 }
 
 // The next COUNT slices of the table (same K and width: q/k/v, or gate/up) applied to the same
 // input: tile[c][r][4q .. 4q+3] = sum_k in[r][k] * W_c[k][o0 + 4q ..] for slice c < COUNT,
-// r < rows and the quads q of the slices (slab of rows * width floats per slice).  Rows go RB
-// at a time, each thread holding a float4 accumulator per (slice, row) so that every weight
-// load serves all rows of the block.  Thread t owns quad t % nq and the K rows
-// k = t / nq (mod kparts), read straight from L2; the partials reduce through shared memory in
+// r < rows and the quads q of the slices (slab of rows * width floats per slice).  Rows are
+// taken in blocks of RB, each thread holding a float4 accumulator per (slice, row of its block)
+// so that every weight load (straight from L2) serves all rows of the block; threads split the
+// quads, the K rows and the row blocks, and the K partials reduce through shared memory in
 // fixed-order levels.  For nq >= 256 a thread owns whole quads.  One out-of-line copy per
 // COUNT serves every projection.
 template <int COUNT, int RB>
@@ -105,11 +110,13 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
     K = sl.K;
     O4 = sl.O / 4;
   }
+  if (rows <= 0) // a CTA without rows in this projection (CTA-uniform)
+    return;
   const int slab = rows * nq * 4;
-  for (int rb = 0; rb < rows; rb += RB) {
-    const int rr = rows - rb < RB ? rows - rb : RB;
-    const float *x = in + rb * ldIn;
-    if (nq >= kStepThreads) {
+  if (nq >= kStepThreads) {
+    for (int rb = 0; rb < rows; rb += RB) {
+      const int rr = rows - rb < RB ? rows - rb : RB;
+      const float *x = in + rb * ldIn;
       for (int q = tid; q < nq; q += kStepThreads) {
         float4 acc[COUNT][RB];
 #pragma unroll
@@ -135,15 +142,28 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
             if (r < rr)
               *reinterpret_cast<float4 *>(tile + c * slab + ((rb + r) * nq + q) * 4) = acc[c][r];
       }
-      __syncthreads();
-      continue;
     }
-    // K split kparts ways, each slice at least four K rows (fewer partials to reduce).
-    int kparts = kStepThreads / nq;
-    while (kparts > 1 && kparts * 4 > K)
-      kparts >>= 1;
-    const int q = tid % nq, kp = tid / nq;
-    const bool busy = kp < kparts;
+    __syncthreads();
+    return;
+  }
+  // Row blocks of RB rows are handled side by side (`together` per pass, as many as keep at
+  // least four K slices per output), and K is split kparts ways with at least four K rows per
+  // slice (fewer partials to reduce).  Thread t owns quad t % nq, K slice (t / nq) % kparts and
+  // row block t / (nq * kparts) of the pass.
+  const int blocks = (rows + RB - 1) / RB;
+  int together = blocks;
+  while (together > 1 && nq * together * 4 > kStepThreads)
+    --together;
+  int kparts = kStepThreads / (nq * together);
+  while (kparts > 1 && kparts * 4 > K)
+    kparts >>= 1;
+  const int q = tid % nq, kp = (tid / nq) % kparts, blk = tid / (nq * kparts);
+  for (int rb = 0; rb < rows; rb += RB * together) {
+    const int passRows = rows - rb < RB * together ? rows - rb : RB * together;
+    const int first = blk * RB;
+    const int rr = passRows - first < RB ? passRows - first : RB;
+    const bool busy = blk < together && rr > 0;
+    const float *x = in + (rb + first) * ldIn;
     float4 acc[COUNT][RB];
 #pragma unroll
     for (int c = 0; c < COUNT; ++c)
@@ -166,7 +186,7 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
     // Partials of every (K slice, output) to shared memory, then a fixed-order sum: one level
     // for a few K slices per output, else segments of K slices and then the segments (no warp
     // shuffles: the shuffle pipe is the scarcer resource here).
-    const int per = rr * nq, outputs = COUNT * per;
+    const int per = passRows * nq, outputs = COUNT * per;
     float4 *partial = reinterpret_cast<float4 *>(red);
     if (busy)
 #pragma unroll
@@ -174,7 +194,7 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
 #pragma unroll
         for (int r = 0; r < RB; ++r)
           if (r < rr)
-            partial[kp * outputs + c * per + r * nq + q] = acc[c][r];
+            partial[kp * outputs + c * per + (first + r) * nq + q] = acc[c][r];
     __syncthreads();
     int segments = 1; // about sqrt(kparts): both levels sum a few terms each
     while (outputs * segments * 2 <= kStepThreads && segments * segments < kparts)
@@ -184,11 +204,11 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
     if (segments > 1) {
       if (tid < outputs * segments) {
         const int o = tid % outputs, seg = tid / outputs;
-        const int first = seg * span, last = first + span < kparts ? first + span : kparts;
+        const int lo = seg * span, hi = lo + span < kparts ? lo + span : kparts;
         float4 v = f4(0.f, 0.f, 0.f, 0.f);
-        if (first < last) {
-          v = partial[first * outputs + o];
-          for (int j = first + 1; j < last; ++j)
+        if (lo < hi) {
+          v = partial[lo * outputs + o];
+          for (int j = lo + 1; j < hi; ++j)
             v = add4(v, partial[j * outputs + o]);
         }
         level[seg * outputs + o] = v;
@@ -215,19 +235,6 @@ __device__ __forceinline__ void eachQuad(int rows, int nq, int o0, const float *
     fn(e / nq, o0 + 4 * (e % nq), *reinterpret_cast<const float4 *>(tile + e * 4));
 }
 
-// Store one value at the same shared-memory offset in every CTA of the cluster.
-__device__ __forceinline__ void storeAll(cg::cluster_group &cluster, float *local, float4 v) {
-#pragma unroll
-  for (int rank = 0; rank < kStepCtas; ++rank)
-    *reinterpret_cast<float4 *>(cluster.map_shared_rank(local, rank)) = v;
-}
-
-__device__ __forceinline__ void storeAll(cg::cluster_group &cluster, float *local, float v) {
-#pragma unroll
-  for (int rank = 0; rank < kStepCtas; ++rank)
-    *cluster.map_shared_rank(local, rank) = v;
-}
-
 // act[g][:] = x[g][:] * rsqrt(mean(x[g]^2) + eps) * gain, one warp per row (row stride ld).
 __device__ void rmsRows(const float *x, const float *gain, float *act, int rows, int C, int ld,
                         float eps) {
@@ -250,18 +257,37 @@ __device__ void rmsRows(const float *x, const float *gain, float *act, int rows,
 // start in different shared-memory banks (and stay 16-byte aligned).
 __host__ __device__ constexpr int64_t rowStride(int64_t columns) { return columns + 4; }
 
-// Columns of one CTA's widest projection output (fused q/k/v, fused gate/up, or the LM head).
+// Heads are partitioned over the cluster's CTAs: with A >= 8 heads CTA r owns the A / 8
+// consecutive heads from r * A / 8 for every row; with fewer, CTA r owns head r % A for the rows
+// of row group r / A (8 / A contiguous groups).  A CTA computes q, k and v of its heads, their
+// attention and their part of the o projection without leaving its shared memory.
+__host__ __device__ inline int64_t headsPerCta(const DecodeStepSpec &s) {
+  return s.A >= kStepCtas ? s.A / kStepCtas : 1;
+}
+__host__ __device__ inline int64_t rowGroups(const DecodeStepSpec &s) {
+  return s.A >= kStepCtas ? 1 : kStepCtas / s.A;
+}
+__host__ __device__ inline int64_t ownColumns(const DecodeStepSpec &s) {
+  return headsPerCta(s) * s.D;
+}
+
+// Columns of one CTA's widest column-split projection output (fused q/k/v of its heads, fused
+// gate/up, or the LM head).
 __host__ __device__ inline int64_t tileColumns(const DecodeStepSpec &s) {
-  int64_t widest = 3 * s.C > 2 * s.F ? 3 * s.C : 2 * s.F;
-  widest = widest > s.V ? widest : s.V;
-  return widest / kStepCtas;
+  int64_t widest = 3 * ownColumns(s);
+  widest = widest > 2 * s.F / kStepCtas ? widest : 2 * s.F / kStepCtas;
+  return widest > s.V / kStepCtas ? widest : s.V / kStepCtas;
 }
 
 constexpr std::size_t kTableBytes = (sizeof(StreamTable) + 15) / 16 * 16;
 
+// x / act: the rows' residual stream and its normalization (full copies in every CTA);
+// q / ctx: queries and attention outputs of the CTA's heads; h: the SwiGLU product of its FFN
+// columns; partO / partD: its partial o and down projections [rows][C], which every CTA of the
+// cluster reads (distributed shared memory) after the cluster barrier that follows them.
 struct StepBuffers {
   StreamTable *table;
-  float *x, *act, *q, *ctx, *h, *red, *probs, *tile, *partValue, *first;
+  float *x, *act, *q, *ctx, *h, *partO, *partD, *red, *probs, *tile, *partValue, *first;
   int *partIndex;
 };
 
@@ -272,9 +298,11 @@ __device__ StepBuffers carve(unsigned char *base, const DecodeStepSpec &s) {
   b.x = reinterpret_cast<float *>(base + kTableBytes);
   b.act = b.x + G * rowStride(C);
   b.q = b.act + G * rowStride(C);
-  b.ctx = b.q + G * rowStride(C);
-  b.h = b.ctx + G * rowStride(C);
-  b.red = b.h + G * rowStride(s.F);
+  b.ctx = b.q + G * rowStride(ownColumns(s));
+  b.h = b.ctx + G * rowStride(ownColumns(s));
+  b.partO = b.h + G * rowStride(s.F / kStepCtas);
+  b.partD = b.partO + G * C;
+  b.red = b.partD + G * C;
   b.probs = b.red + kReduceFloats;
   b.tile = b.probs + kStepWarps * s.T;
   b.partValue = b.tile + G * tileColumns(s);
@@ -284,7 +312,8 @@ __device__ StepBuffers carve(unsigned char *base, const DecodeStepSpec &s) {
 }
 
 std::size_t stepSharedBytes(const DecodeStepSpec &s) {
-  const int64_t floats = 4 * s.G * rowStride(s.C) + s.G * rowStride(s.F) + kReduceFloats +
+  const int64_t floats = 2 * s.G * rowStride(s.C) + 2 * s.G * rowStride(ownColumns(s)) +
+                         s.G * rowStride(s.F / kStepCtas) + 2 * s.G * s.C + kReduceFloats +
                          kStepWarps * s.T +
                          s.G * tileColumns(s) + 3 * kStepCtas * kMaxRows;
   return kTableBytes + std::size_t(floats) * sizeof(float);
@@ -309,7 +338,14 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
   const int64_t B = s.B, C = s.C, A = s.A, D = s.D, F = s.F, V = s.V, T = s.T;
   const int64_t r0 = int64_t(blockIdx.x / kStepCtas) * s.G;
   const int rows = int(s.G < B - r0 ? s.G : B - r0);
-  const int ldC = int(rowStride(C)), ldF = int(rowStride(F));
+  const int64_t own = ownColumns(s), hpc = headsPerCta(s);
+  const int head0 = int(A >= kStepCtas ? rank * hpc : rank % A);
+  const int64_t hc0 = head0 * D; // first column of the CTA's heads
+  const int groupRows = int((rows + rowGroups(s) - 1) / rowGroups(s));
+  const int group = int(A >= kStepCtas ? 0 : rank / A);
+  const int gFirst = group * groupRows < rows ? group * groupRows : rows;
+  const int gCount = rows - gFirst < groupRows ? rows - gFirst : groupRows;
+  const int ldC = int(rowStride(C)), ldO = int(rowStride(own)), ldH = int(rowStride(F / kStepCtas));
   const int p = position[0];
   const bool inside = p >= 0 && p < T;
   // Every CTA of the cluster has read the position before any of them can finish (and so
@@ -318,21 +354,24 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
 
   Cursor cur;
   if (inside) {
-    // The step's weight slices in consumption order: per layer q, k, v, o, gate, up, down;
-    // then the LM head.
+    // The step's weight slices in consumption order: per layer q, k, v (the columns of the
+    // CTA's heads), o (the rows of its heads, all columns), gate, up (its FFN columns), down
+    // (the rows of its FFN columns, all columns); then the LM head (its vocabulary columns).
     const int count = int(s.L) * kProjections + 1;
     for (int i = tid; i < count; i += kStepThreads) {
-      const int64_t l = i / kProjections;
+      const int64_t l = i / kProjections, fr = F / kStepCtas;
       Slice sl;
       switch (i == count - 1 ? -1 : i % kProjections) {
-      case 0: sl = makeSlice(wq + l * C * C, C, C, rank); break;
-      case 1: sl = makeSlice(wk + l * C * C, C, C, rank); break;
-      case 2: sl = makeSlice(wv + l * C * C, C, C, rank); break;
-      case 3: sl = makeSlice(wo + l * C * C, C, C, rank); break;
-      case 4: sl = makeSlice(wg + l * C * F, C, F, rank); break;
-      case 5: sl = makeSlice(wu + l * C * F, C, F, rank); break;
-      case 6: sl = makeSlice(wd + l * F * C, F, C, rank); break;
-      default: sl = makeSlice(lm + s.headLayer * C * V, C, V, rank); break;
+      case 0: sl = makeSlice(wq + l * C * C, C, C, hc0, own); break;
+      case 1: sl = makeSlice(wk + l * C * C, C, C, hc0, own); break;
+      case 2: sl = makeSlice(wv + l * C * C, C, C, hc0, own); break;
+      case 3: sl = makeSlice(wo + l * C * C + hc0 * C, own, C, 0, C); break;
+      case 4: sl = makeSlice(wg + l * C * F, C, F, rank * fr, fr); break;
+      case 5: sl = makeSlice(wu + l * C * F, C, F, rank * fr, fr); break;
+      case 6: sl = makeSlice(wd + l * F * C + rank * fr * C, fr, C, 0, C); break;
+      default:
+        sl = makeSlice(lm + s.headLayer * C * V, C, V, rank * (V / kStepCtas), V / kStepCtas);
+        break;
       }
       table.slices[i] = sl;
     }
@@ -345,8 +384,8 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
     }
     __syncthreads();
 
-    const int nqC = int(C / kStepCtas / 4), nqF = int(F / kStepCtas / 4);
-    const int oC = rank * int(C / kStepCtas), oF = rank * int(F / kStepCtas);
+    const int nqO = int(own / 4), nqF = int(F / kStepCtas / 4);
+    const int oF = rank * int(F / kStepCtas);
     const int64_t R = D / 2;
     const float *cs = sincos + int64_t(p) * R * 2;
     auto rope = [&](int col, float4 v) {
@@ -358,102 +397,187 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
                 __fsub_rn(__fmul_rn(v.z, c1), __fmul_rn(v.w, s1)),
                 __fadd_rn(__fmul_rn(v.z, s1), __fmul_rn(v.w, c1)));
     };
-    auto residual = [&](int r, int col, float4 v) {
-      float *x = sb.x + r * ldC + col;
-      const float4 old = *reinterpret_cast<const float4 *>(x);
-      storeAll(cluster, x, f4(__fadd_rn(old.x, v.x), __fadd_rn(old.y, v.y),
-                              __fadd_rn(old.z, v.z), __fadd_rn(old.w, v.w)));
+    // After the cluster barrier that follows a partial projection: x[r] += the sum of the
+    // partials [row][C] of the CTAs holding row r, in rank order (every CTA computes the same
+    // sums for all rows, so the copies stay identical).  `byHead`: the o projection, whose
+    // partials come from the CTAs of the row's group when heads are split by row group.
+    auto gather = [&](float *part, bool byHead) {
+      const int c4n = int(C / 4);
+      for (int e = tid; e < rows * c4n; e += kStepThreads) {
+        const int r = e / c4n, c = 4 * (e % c4n);
+        int first = 0, ctas = kStepCtas, local = r;
+        if (byHead && A < kStepCtas) {
+          const int gr = r / groupRows;
+          first = gr * int(A);
+          ctas = int(A);
+          local = r - gr * groupRows;
+        }
+        float *at = part + int64_t(local) * C + c;
+        float4 sum = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(at, first));
+        for (int j = 1; j < ctas; ++j)
+          sum = add4(sum, *reinterpret_cast<const float4 *>(cluster.map_shared_rank(at, first + j)));
+        float4 *x = reinterpret_cast<float4 *>(sb.x + r * ldC + c);
+        const float4 old = *x;
+        *x = f4(__fadd_rn(old.x, sum.x), __fadd_rn(old.y, sum.y), __fadd_rn(old.z, sum.z),
+                __fadd_rn(old.w, sum.w));
+      }
+      __syncthreads();
     };
     for (int64_t l = 0; l < s.L; ++l) {
       auto cacheSlot = [&](float *cache, int r, int col) {
         const int64_t b = r0 + r, h = col / D, d = col % D;
         return reinterpret_cast<float4 *>(cache + (((l * B + b) * A + h) * T + p) * D + d);
       };
-      rmsRows(sb.x, norm1 + l * C, sb.act, rows, int(C), ldC, eps);
-      // q, k and v in one pass over the normalized rows (tile slabs q | k | v).
-      project<3, kFusedRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
-      const int slabC = rows * nqC * 4;
-      eachQuad(rows, nqC, oC, sb.tile, [&](int r, int col, float4 v) {
-        storeAll(cluster, sb.q + r * ldC + col, rope(col, v));
+      // Attention block of the CTA's heads over its row group: norm, q/k/v in one pass (tile
+      // slabs q | k | v), RoPE, cache append; no exchange with the other CTAs.
+      rmsRows(sb.x + gFirst * ldC, norm1 + l * C, sb.act + gFirst * ldC, gCount, int(C), ldC, eps);
+      project<3, kFusedRowBlock>(table, cur, sb.act + gFirst * ldC, ldC, gCount, sb.red, sb.tile);
+      const int slabO = gCount * nqO * 4;
+      eachQuad(gCount, nqO, int(hc0), sb.tile, [&](int r, int col, float4 v) {
+        *reinterpret_cast<float4 *>(sb.q + (gFirst + r) * ldO + (col - hc0)) = rope(col, v);
       });
-      eachQuad(rows, nqC, oC, sb.tile + slabC,
-               [&](int r, int col, float4 v) { *cacheSlot(kc, r, col) = rope(col, v); });
-      eachQuad(rows, nqC, oC, sb.tile + 2 * slabC,
-               [&](int r, int col, float4 v) { *cacheSlot(vc, r, col) = v; });
-      cluster.sync();
+      eachQuad(gCount, nqO, int(hc0), sb.tile + slabO, [&](int r, int col, float4 v) {
+        *cacheSlot(kc, gFirst + r, col) = rope(col, v);
+      });
+      eachQuad(gCount, nqO, int(hc0), sb.tile + 2 * slabO,
+               [&](int r, int col, float4 v) { *cacheSlot(vc, gFirst + r, col) = v; });
+      __syncthreads(); // this CTA's cache rows at p and queries are in place
 
-      // Attention: one warp per (row, head) of the cluster.
-      const int64_t n = int64_t(p) + 1;
-      float *probs = sb.probs + warp * T;
-      for (int64_t pair = int64_t(rank) * kStepWarps + warp; pair < rows * A;
-           pair += kStepCtas * kStepWarps) {
-        const int64_t g = pair / A, h = pair % A, b = r0 + g;
-        const float *qv = sb.q + g * ldC + h * D;
-        const int64_t base = ((l * B + b) * A + h) * T * D;
-        float best = -CUDART_INF_F;
-        for (int64_t t = lane; t < n; t += kWarp) {
-          const float4 *krow = reinterpret_cast<const float4 *>(kc + base + t * D);
-          float dot = 0.f;
-          for (int64_t d4 = 0; d4 < D / 4; ++d4) {
-            const float4 kv = __ldcg(krow + d4);
-            dot = fmaf(qv[4 * d4], kv.x, dot);
-            dot = fmaf(qv[4 * d4 + 1], kv.y, dot);
-            dot = fmaf(qv[4 * d4 + 2], kv.z, dot);
-            dot = fmaf(qv[4 * d4 + 3], kv.w, dot);
-          }
-          const float score = dot * scale;
-          probs[t] = score;
-          best = fmaxf(best, score);
-        }
-        best = warpMax(best);
-        float total = 0.f;
-        for (int64_t t = lane; t < n; t += kWarp) {
-          const float e = expf(probs[t] - best);
-          probs[t] = e;
-          total += e;
-        }
-        total = warpSum(total);
-        __syncwarp();
-        for (int64_t d = lane; d < D; d += kWarp) {
-          const float *column = vc + base + d;
-          float acc = 0.f;
-          int64_t t = 0;
-          for (; t + 8 <= n; t += 8) { // eight independent loads in flight per lane
-            float v[8];
+      // Attention: every (row, head) pair of the CTA gets `wp` warps, which split its cache
+      // rows 0..p into contiguous chunks; the chunks' maxima combine before the exponentials,
+      // their sums and value sums after, in warp order (shared memory).
+      {
+        const int64_t n = int64_t(p) + 1;
+        const int pairs = gCount * int(hpc);
+        int wp = 1;
+        while (wp < kStepWarps && pairs * wp * 2 <= kStepWarps)
+          wp *= 2;
+        const int lead = warp - warp % wp, member = warp % wp;
+        const int perRound = kStepWarps / wp;
+        const int64_t chunk = (n + wp - 1) / wp;
+        const int64_t lo = member * chunk, hi = lo + chunk < n ? lo + chunk : n;
+        const int quads = int(D / 4), subs = kWarp / quads;
+        const int dq = lane % quads, sub = lane / quads;
+        float *probs = sb.probs + warp * T;
+        float *stats = sb.red;                  // per warp: chunk maximum, chunk sum
+        float *values = sb.red + 2 * kStepWarps; // per warp: D partial value sums
+        // Uniform trip count over the CTA (its barriers are reached by every warp).
+        for (int base = 0; base < pairs; base += perRound) {
+          const int pair = base + warp / wp;
+          const bool active = pair < pairs;
+          const int g = active ? gFirst + pair / int(hpc) : 0;
+          const int hh = active ? pair % int(hpc) : 0;
+          const int64_t cacheBase = ((l * B + r0 + g) * A + head0 + hh) * T * D;
+          if (active) {
+            // Scores: `quads` lanes per cache row (one float4 each), `subs` rows at a time.
+            const float4 q4 = *reinterpret_cast<const float4 *>(sb.q + g * ldO + hh * D + 4 * dq);
+            float best = -CUDART_INF_F;
+            const float4 *krows = reinterpret_cast<const float4 *>(kc + cacheBase) + dq;
+            for (int64_t t0 = lo + sub; t0 - sub < hi; t0 += 4 * subs) {
+              float4 kv[4]; // four rows' loads in flight per lane
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              v[u] = __ldcg(column + (t + u) * D);
+              for (int u = 0; u < 4; ++u) {
+                const int64_t t = t0 + u * subs;
+                kv[u] = t < hi ? __ldcg(krows + t * quads) : f4(0.f, 0.f, 0.f, 0.f);
+              }
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              acc = fmaf(probs[t + u], v[u], acc);
+              for (int u = 0; u < 4; ++u) {
+                const int64_t t = t0 + u * subs;
+                float dot = 0.f;
+                dot = fmaf(q4.x, kv[u].x, dot);
+                dot = fmaf(q4.y, kv[u].y, dot);
+                dot = fmaf(q4.z, kv[u].z, dot);
+                dot = fmaf(q4.w, kv[u].w, dot);
+                for (int o = 1; o < quads; o <<= 1)
+                  dot += __shfl_xor_sync(0xffffffffu, dot, o);
+                if (t < hi) {
+                  const float score = dot * scale;
+                  if (dq == 0)
+                    probs[t] = score;
+                  best = fmaxf(best, score);
+                }
+              }
+            }
+            best = warpMax(best);
+            if (lane == 0)
+              stats[2 * warp] = best;
           }
-          for (; t < n; ++t)
-            acc = fmaf(probs[t], __ldcg(column + t * D), acc);
-          storeAll(cluster, sb.ctx + g * ldC + h * D + d, acc / total);
+          __syncthreads();
+          if (active) {
+            float top = stats[2 * lead];
+            for (int j = 1; j < wp; ++j)
+              top = fmaxf(top, stats[2 * (lead + j)]);
+            float total = 0.f;
+            for (int64_t t = lo + lane; t < hi; t += kWarp) {
+              const float e = expf(probs[t] - top);
+              probs[t] = e;
+              total += e;
+            }
+            total = warpSum(total);
+            __syncwarp();
+            // Value sums: lane (dq, sub) accumulates quad dq over rows sub, sub + subs, ...
+            float4 acc = f4(0.f, 0.f, 0.f, 0.f);
+            const float4 *vrows = reinterpret_cast<const float4 *>(vc + cacheBase) + dq;
+            for (int64_t t0 = lo + sub; t0 - sub < hi; t0 += 4 * subs) {
+              float4 v[4]; // four rows' loads in flight per lane
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int64_t t = t0 + u * subs;
+                v[u] = t < hi ? __ldcg(vrows + t * quads) : f4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                if (t0 + u * subs < hi)
+                  fma4(acc, probs[t0 + u * subs], v[u]);
+            }
+            for (int o = quads; o < kWarp; o <<= 1) {
+              acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+              acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+              acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+              acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+            }
+            if (sub == 0)
+              *reinterpret_cast<float4 *>(values + warp * D + 4 * dq) = acc;
+            if (lane == 0)
+              stats[2 * warp + 1] = total;
+          }
+          __syncthreads();
+          if (active) {
+            float total = stats[2 * lead + 1];
+            for (int j = 1; j < wp; ++j)
+              total += stats[2 * (lead + j) + 1];
+            for (int64_t d = member * kWarp + lane; d < D; d += wp * kWarp) {
+              float v = values[lead * D + d];
+              for (int j = 1; j < wp; ++j)
+                v += values[(lead + j) * D + d];
+              sb.ctx[g * ldO + hh * D + d] = v / total;
+            }
+          }
+          __syncthreads();
         }
-        __syncwarp();
       }
-      cluster.sync();
 
-      // o projection + residual.
-      project<1, kRowBlock>(table, cur, sb.ctx, ldC, rows, sb.red, sb.tile);
-      eachQuad(rows, nqC, oC, sb.tile, residual);
+      // o projection of the CTA's heads (K = their columns, all C outputs) as a partial sum;
+      // then every CTA adds the partials of all heads to its copy of the residual stream.
+      project<1, kRowBlock>(table, cur, sb.ctx + gFirst * ldO, ldO, gCount, sb.red, sb.partO);
       cluster.sync();
+      gather(sb.partO, true);
 
-      // MLP: gate, then up with the SwiGLU product, then down + residual.
+      // MLP: gate and up of the CTA's FFN columns in one pass with the SwiGLU product, then
+      // the down projection of those columns (K = F / 8, all C outputs) as a partial sum.
       rmsRows(sb.x, norm2 + l * C, sb.act, rows, int(C), ldC, eps);
       project<2, kFusedRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
       const int slabF = rows * nqF * 4;
       eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 gate) {
         const float4 up = *reinterpret_cast<const float4 *>(sb.tile + slabF + (r * nqF + (col - oF) / 4) * 4);
         auto act = [](float gv, float uv) { return __fmul_rn(gv / (1.0f + expf(-gv)), uv); };
-        storeAll(cluster, sb.h + r * ldF + col,
-                 f4(act(gate.x, up.x), act(gate.y, up.y), act(gate.z, up.z), act(gate.w, up.w)));
+        *reinterpret_cast<float4 *>(sb.h + r * ldH + (col - oF)) =
+            f4(act(gate.x, up.x), act(gate.y, up.y), act(gate.z, up.z), act(gate.w, up.w));
       });
+      __syncthreads();
+      project<1, kRowBlock>(table, cur, sb.h, ldH, rows, sb.red, sb.partD);
       cluster.sync();
-      project<1, kRowBlock>(table, cur, sb.h, ldF, rows, sb.red, sb.tile);
-      eachQuad(rows, nqC, oC, sb.tile, residual);
-      cluster.sync();
+      gather(sb.partD, false);
     }
 
     // Head: final norm, logits of this CTA's vocabulary columns and their per-row maximum.
@@ -520,8 +644,10 @@ bool decodeStepGeometry(const void *spec, std::size_t, library::Geometry *g) {
     const int64_t nq = columns / (kStepCtas * 4);
     return nq < kStepThreads || nq % kStepThreads == 0;
   };
-  if (s.B <= 0 || s.L <= 0 || s.L > kMaxLayers || s.A <= 0 || s.D <= 0 || s.D % 4 ||
-      s.A * s.D != s.C)
+  // Head dimension: a power of two up to 128 (one float4 per lane across a cache row); head
+  // count: a power of two (the heads split evenly over the 8 CTAs, or the CTAs over the heads).
+  if (s.B <= 0 || s.L <= 0 || s.L > kMaxLayers || s.A <= 0 || (s.A & (s.A - 1)) || s.D < 4 ||
+      s.D > 128 || (s.D & (s.D - 1)) || s.A * s.D != s.C)
     return false;
   if (!quadsOk(s.C) || !quadsOk(s.F) || !quadsOk(s.V) || s.T <= 0 || s.T > kMaxCacheRows)
     return false;
