@@ -147,7 +147,7 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
     return;
   }
   // Row blocks of RB rows are handled side by side (`together` per pass, as many as keep at
-  // least four K slices per output), and K is split kparts ways with at least four K rows per
+  // least four K slices per output), and K is split kparts ways with at least two K rows per
   // slice (fewer partials to reduce).  Thread t owns quad t % nq, K slice (t / nq) % kparts and
   // row block t / (nq * kparts) of the pass.
   const int blocks = (rows + RB - 1) / RB;
@@ -155,7 +155,7 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
   while (together > 1 && nq * together * 4 > kStepThreads)
     --together;
   int kparts = kStepThreads / (nq * together);
-  while (kparts > 1 && kparts * 4 > K)
+  while (kparts > 1 && kparts * 2 > K)
     kparts >>= 1;
   const int q = tid % nq, kp = (tid / nq) % kparts, blk = tid / (nq * kparts);
   for (int rb = 0; rb < rows; rb += RB * together) {
@@ -319,10 +319,12 @@ std::size_t stepSharedBytes(const DecodeStepSpec &s) {
   return kTableBytes + std::size_t(floats) * sizeof(float);
 }
 
-// Two CTAs per SM (at most 128 registers a thread and half of an SM's shared memory each):
-// with one CTA per SM only about 15 eight-CTA clusters fit on the GPU at once, with two 33, so
-// grids of up to 32 clusters run in one wave.
-__global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads, 2)
+// OCC CTAs per SM.  Two (at most 128 registers a thread and half of an SM's shared memory each)
+// for wide grids: with one CTA per SM only about 15 eight-CTA clusters fit on the GPU at once,
+// with two 33, so grids of up to 32 clusters run in one wave.  One (up to 255 registers, no
+// spills) for grids of a few clusters, which are co-resident either way.
+template <int OCC>
+__global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads, OCC)
     decodeStepKernel(int *tokens, int *position, int *history, const float *emb,
                      const float *norm1, const float *norm2, const float *finalNorm,
                      const float *wq, const float *wk, const float *wv, const float *wo,
@@ -665,11 +667,21 @@ bool decodeStepGeometry(const void *spec, std::size_t, library::Geometry *g) {
   return true;
 }
 
+// Grids of up to this many clusters run the one-CTA-per-SM build (measured at one request,
+// C = 64, two layers: 41 us per step against 45 us for the two-CTA build).
+constexpr int64_t kWideRegisterClusters = 12;
+
+const void *decodeStepSelect(const void *spec) {
+  return specOf<DecodeStepSpec>(spec).clusters <= kWideRegisterClusters
+             ? reinterpret_cast<const void *>(&decodeStepKernel<1>)
+             : reinterpret_cast<const void *>(&decodeStepKernel<2>);
+}
+
 } // namespace
 
-CKL_REGISTER_KERNEL("ckl.fused.decode_step", reinterpret_cast<const void *>(&decodeStepKernel),
+CKL_REGISTER_KERNEL("ckl.fused.decode_step", reinterpret_cast<const void *>(&decodeStepKernel<2>),
                     "PPPPPPPPPPPPPPPPPPPPFFS", sizeof(DecodeStepSpec), decodeStepGeometry,
-                    nullptr, nullptr, 0, false);
+                    decodeStepSelect, nullptr, 0, false);
 
 
 } // namespace ckl::kernels
