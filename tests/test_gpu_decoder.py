@@ -117,6 +117,9 @@ def test_batched_shapes_match_oracle(device, batch, hidden, heads, layers, ffn, 
     (40, 64, 2, 2, 128, 8192, 20, 4),      # 256 vocabulary quads per CTA, D 32
     (200, 128, 1, 1, 256, 256, 12, 3),     # one head of dim 128, ragged last cluster
     (288, 64, 4, 1, 256, 512, 8, 3),       # 32 clusters x 9 requests, ragged last cluster
+    (24, 256, 16, 2, 256, 512, 10, 3),     # two heads per CTA (16 heads)
+    (16, 512, 32, 1, 256, 512, 8, 2),      # four heads per CTA (32 heads)
+    (10, 512, 8, 1, 512, 512, 12, 3),      # one head of dim 64 per CTA, one-CTA-per-SM build
     (512, 64, 4, 1, 256, 512, 8, 3),       # 32 clusters x 16 requests (two row blocks)
 ])
 def test_whole_step_kernel_matches_oracle(device, batch, hidden, heads, layers, ffn, vocab,
