@@ -399,7 +399,8 @@ template <int BN> using Staging = float[BM][BN + 4];
 
 // Output rows [rank * 128 / SPLITS, (rank + 1) * 128 / SPLITS) of the tile: each epilogue warp
 // takes a row at a time, each lane four consecutive columns, summing the K splits' staged
-// partials in rank order (deterministic), and stores them through the fused epilogue.
+// partials in rank order (deterministic), and stores them through the fused epilogue (the
+// gate/up tile, whose output is a panel, goes one row per lane instead).
 template <int BN, int EPI, int SPLITS>
 __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN> &stage,
                                                int64_t m0, int64_t nt, int position) {
@@ -408,6 +409,32 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
   const int warp = threadIdx.x / kWarp - 2, lane = threadIdx.x % kWarp;
   const unsigned rank = blockIdx.z;
   constexpr int kRows = BM / SPLITS;
+  if constexpr (EPI == gemm::kSwiGluPanel) {
+    // One row per lane: the gate and up values of an output quad sit in the same staged row
+    // (columns c and c + 64), and a warp's panel store of one quad then covers 32 consecutive
+    // rows (512 contiguous bytes of the K-major panel) instead of 16 scattered quads of a row.
+    // Warps split the tile into four groups of 32 rows x two halves of the 16 output quads.
+    static_assert(SPLITS == 1 && BN == 4 * kWarp, "gate/up tiles");
+    const int row = (warp % 4) * kWarp + lane;
+    const int64_t m = m0 + row, padded = panel::slices(N) * panel::kSlice;
+    if (m >= M)
+      return;
+    for (int q = (warp / 4) * (BN / 16); q < (warp / 4 + 1) * (BN / 16); ++q) {
+      const int64_t k = n0 + 4 * q; // output column (the panel's K)
+      if (k >= padded)
+        break;
+      const float4 gate = *reinterpret_cast<const float4 *>(&stage[row][4 * q]);
+      const float4 up = *reinterpret_cast<const float4 *>(&stage[row][BN / 2 + 4 * q]);
+      const float *g = &gate.x, *u = &up.x;
+      float4 v;
+      float *out = &v.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        out[j] = k + j < N ? swigluValue(g[j], u[j]) : 0.f;
+      panel::store4(p.out, m, k, N, v);
+    }
+    return;
+  }
   const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
                     (EPI != gemm::kResidual || aligned16(p.residual));
   for (int r = warp; r < kRows; r += kConverterWarps) {
@@ -430,27 +457,9 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
                             __fadd_rn(sum.z, part.z), __fadd_rn(sum.w, part.w));
         }
       }
-      if constexpr (EPI == gemm::kSwiGluPanel) {
-        // Lanes 0-15 hold gate columns, lanes 16-31 the up columns of the same outputs.
-        static_assert(BN == 4 * kWarp, "one quad of columns per lane");
-        const float4 up = make_float4(__shfl_down_sync(0xffffffffu, sum.x, 16),
-                                      __shfl_down_sync(0xffffffffu, sum.y, 16),
-                                      __shfl_down_sync(0xffffffffu, sum.z, 16),
-                                      __shfl_down_sync(0xffffffffu, sum.w, 16));
-        const int64_t k = n0 + c; // output column (the panel's K)
-        const int64_t padded = panel::slices(N) * panel::kSlice;
-        if (lane < 16 && k < padded) {
-          const float *g = &sum.x, *u = &up.x;
-          float4 v;
-          float *out = &v.x;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            out[j] = k + j < N ? swigluValue(g[j], u[j]) : 0.f;
-          panel::store4(p.out, m, k, N, v);
-        }
-      } else if (n0 + c < N) {
-        storeQuad<EPI>(p, m, n0 + c, sum, position, vec4, best, bestIndex);
-      }
+      if constexpr (EPI != gemm::kSwiGluPanel) // handled above
+        if (n0 + c < N)
+          storeQuad<EPI>(p, m, n0 + c, sum, position, vec4, best, bestIndex);
     }
     if constexpr (EPI == gemm::kArgmax) {
 #pragma unroll
