@@ -400,7 +400,7 @@ template <int BN> using Staging = float[BM][BN + 4];
 // Output rows [rank * 128 / SPLITS, (rank + 1) * 128 / SPLITS) of the tile: each epilogue warp
 // takes a row at a time, each lane four consecutive columns, summing the K splits' staged
 // partials in rank order (deterministic), and stores them through the fused epilogue (the
-// gate/up tile, whose output is a panel, goes one row per lane instead).
+// gate/up tile, whose output is a panel, and the unsplit argmax scan go one row per lane).
 template <int BN, int EPI, int SPLITS>
 __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN> &stage,
                                                int64_t m0, int64_t nt, int position) {
@@ -437,6 +437,42 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
   }
   const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
                     (EPI != gemm::kResidual || aligned16(p.residual));
+  if constexpr (EPI == gemm::kArgmax && SPLITS == 1) {
+    // Logits row by row (coalesced stores), then the argmax partial of each row scanned by one
+    // lane over the staged row in column order: the same (largest value, smallest index) as a
+    // shuffle reduction, without five dependent shuffle rounds per row.
+    if (p.out != nullptr) {
+      const int c = 4 * lane;
+      for (int r = warp; r < BM && m0 + r < M; r += kConverterWarps) {
+        if (c >= BN || n0 + c >= N)
+          continue;
+        const int64_t m = m0 + r;
+        const float4 v = *reinterpret_cast<const float4 *>(&stage[r][c]);
+        if (vec4 && n0 + c + 4 <= N) {
+          *reinterpret_cast<float4 *>(p.out + m * N + n0 + c) = v;
+        } else {
+          const float *lanes = &v.x;
+          for (int j = 0; j < 4 && n0 + c + j < N; ++j)
+            p.out[m * N + n0 + c + j] = lanes[j];
+        }
+      }
+    }
+    const int row = warp * kWarp + lane;
+    if (row < BM && m0 + row < M) {
+      float best = -CUDART_INF_F;
+      int bestIndex = 0x7fffffff;
+      for (int c = 0; c < BN && n0 + c < N; c += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(&stage[row][c]);
+        const float *lanes = &v.x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n0 + c + j < N)
+            argmaxMerge(best, bestIndex, lanes[j], int(n0 + c + j));
+      }
+      p.partials[(m0 + row) * s.tiles + nt] = make_float2(best, __int_as_float(bestIndex));
+    }
+    return;
+  }
   for (int r = warp; r < kRows; r += kConverterWarps) {
     const int row = int(rank) * kRows + r;
     const int64_t m = m0 + row;
@@ -461,7 +497,7 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
         if (n0 + c < N)
           storeQuad<EPI>(p, m, n0 + c, sum, position, vec4, best, bestIndex);
     }
-    if constexpr (EPI == gemm::kArgmax) {
+    if constexpr (EPI == gemm::kArgmax && SPLITS > 1) {
 #pragma unroll
       for (int o = kWarp / 2; o > 0; o >>= 1) {
         const float otherBest = __shfl_xor_sync(0xffffffffu, best, o);
