@@ -36,9 +36,13 @@ constexpr int kStepThreads = 256; // threads per CTA
 constexpr int kStepWarps = kStepThreads / kWarp;
 constexpr int kMaxRows = 16;      // rows (requests) per cluster
 constexpr int kRowBlock = 8;              // rows per single projection pass (accumulators)
-constexpr int kFusedRowBlock = 4;         // rows per pass of fused q/k/v or gate/up
-// Partials of one pass (every thread's slices and rows) plus the segment sums.
-constexpr int kReduceFloats = 4 * (kStepThreads * 3 * kFusedRowBlock + kStepThreads);
+constexpr int kFusedRowBlock = 2;         // rows per pass of fused q/k/v or gate/up
+// Partials of one pass plus the segment sums: a pass holds at most 256 x COUNT x RB float4
+// partials (threads x slices x rows of a row block), the larger of the fused three-slice pass
+// and the single-slice pass, and at most 256 float4 segment sums.
+constexpr int kPassPartials =
+    kStepThreads * (3 * kFusedRowBlock > kRowBlock ? 3 * kFusedRowBlock : kRowBlock);
+constexpr int kReduceFloats = 4 * (kPassPartials + kStepThreads);
 constexpr int kMaxCacheRows = 1024;
 constexpr std::size_t kMaxSharedPerCta = 113 * 1024; // two CTAs per SM
 constexpr int kMaxLayers = 32;
@@ -171,7 +175,7 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
       for (int r = 0; r < RB; ++r)
         acc[c][r] = f4(0.f, 0.f, 0.f, 0.f);
     if (busy) {
-#pragma unroll 4
+#pragma unroll 2
       for (int k = kp; k < K; k += kparts) {
 #pragma unroll
         for (int c = 0; c < COUNT; ++c) {
