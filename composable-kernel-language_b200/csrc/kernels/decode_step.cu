@@ -16,7 +16,7 @@
 //     partials, read through distributed shared memory in rank order, to its own copy, so a
 //     layer needs two cluster barriers; gate/up split their output columns over the CTAs;
 //   * projections read their weights straight from L2 (they stay resident there), each thread
-//     reusing every weight load for up to eight requests held in registers;
+//     reusing every weight load for the requests of a row block (two or four) held in registers;
 //   * RMSNorm statistics are recomputed by every CTA from its own copy (no exchange);
 //   * attention gives each (request, head) of a CTA one or more of its warps, which split the
 //     cache rows: scores, softmax in shared memory, then the weighted value sums.
@@ -35,7 +35,7 @@ constexpr int kStepCtas = 8;      // CTAs per cluster
 constexpr int kStepThreads = 256; // threads per CTA
 constexpr int kStepWarps = kStepThreads / kWarp;
 constexpr int kMaxRows = 16;      // rows (requests) per cluster
-constexpr int kRowBlock = 8;              // rows per single projection pass (accumulators)
+constexpr int kRowBlock = 4;              // rows per single projection pass (accumulators)
 constexpr int kFusedRowBlock = 2;         // rows per pass of fused q/k/v or gate/up
 // Partials of one pass plus the segment sums: a pass holds at most 256 x COUNT x RB float4
 // partials (threads x slices x rows of a row block), the larger of the fused three-slice pass
@@ -175,7 +175,8 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
       for (int r = 0; r < RB; ++r)
         acc[c][r] = f4(0.f, 0.f, 0.f, 0.f);
     if (busy) {
-#pragma unroll 2
+      // Loads in flight per thread: four K rows for a single slice, two for the fused passes.
+#pragma unroll(COUNT == 1 ? 4 : 2)
       for (int k = kp; k < K; k += kparts) {
 #pragma unroll
         for (int c = 0; c < COUNT; ++c) {
