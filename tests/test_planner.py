@@ -169,6 +169,8 @@ def test_tensor_core_decoder_plan_shape():
     (3, 48, 3, 1, 80, 129, 6, False),         # columns do not split into 8 x float4
     (33, 128, 2, 1, 96, 512, 6, True),        # three FFN quads per CTA
     (4, 1024, 16, 4, 4096, 32000, 8, False),  # weights do not stay in L2
+    (24, 96, 3, 1, 256, 512, 8, False),       # three heads do not split over 8 CTAs
+    (24, 256, 16, 2, 256, 512, 10, True),     # two heads per CTA
 ])
 def test_whole_step_kernel_selection(batch, hidden, heads, layers, ffn, vocab, context, whole):
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
