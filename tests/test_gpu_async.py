@@ -100,3 +100,32 @@ def test_synchronous_copies_wait_for_submissions(device):
     assert pending.done()
     dst.copy_to_host(out)
     assert np.all(out == 3.0)
+
+
+@pytest.mark.parametrize("nbytes,offset", [(4, 0), (12, 4), (2048, 0), (2051, 1), (65536, 0),
+                                           (65536 + 16, 0), (300000, 8)])
+def test_pinned_async_copies_round_trip(device, nbytes, offset):
+    """Asynchronous copies between page-locked memory and a device buffer, in stream order
+    around a graph launch, for sizes from 4 bytes to 300 KB and host offsets off 16-byte
+    alignment: the bytes arrive unchanged and nothing outside the range is touched."""
+    count = 1 << 17
+    program = _vector_program(count)
+    src = device.empty(ckl.BufferSpec((count,), ckl.f32))
+    dst = device.empty(ckl.BufferSpec((count,), ckl.f32))
+    src.fill_zero()
+    invocation = program.bind(src, dst, 1.0)
+    pinned_in = ckl.PinnedHostBuffer(nbytes + 64)
+    pinned_out = ckl.PinnedHostBuffer(nbytes + 64)
+    data = np.random.default_rng(nbytes).integers(0, 256, nbytes, dtype=np.uint8)
+    np.frombuffer(pinned_in.view(), np.uint8)[offset:offset + nbytes] = data
+    np.frombuffer(pinned_out.view(), np.uint8)[:] = 7
+    invocation.copy_in_async(src, pinned_in.pointer + offset, nbytes)
+    invocation.launch(graph=True)                 # dst = (src + 1) + 1, in stream order
+    invocation.copy_out_async(src, pinned_out.pointer + offset, nbytes)
+    invocation.synchronize()
+    out = np.frombuffer(pinned_out.view(), np.uint8)
+    assert np.array_equal(out[offset:offset + nbytes], data)
+    assert np.all(out[:offset] == 7) and np.all(out[offset + nbytes:] == 7)
+    result = np.empty(count, np.float32)
+    dst.copy_to_host(result)
+    assert np.all(result[(nbytes + 3) // 4:] == 2.0)   # the launch saw src after the copy
