@@ -35,13 +35,13 @@ __device__ void chainBody(const float *__restrict__ src, float *__restrict__ dst
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
     float4 *d4 = reinterpret_cast<float4 *>(dst);
     int64_t v = i;
-    for (; v + 3 * stride < vectors; v += 4 * stride) { // four independent loads in flight
-      float4 x[4];
+    for (; v + 7 * stride < vectors; v += 8 * stride) { // eight independent loads in flight
+      float4 x[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u)
         x[u] = __ldcs(s4 + v + u * stride);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         x[u].x = chain<Steps>(x[u].x, spec, scalars);
         x[u].y = chain<Steps>(x[u].y, spec, scalars);
         x[u].z = chain<Steps>(x[u].z, spec, scalars);
