@@ -145,3 +145,29 @@ def test_overlapping_bindings_take_the_reference_graph(device):
                                        owner=session.owners["vc"])
     invocation = session.program.bind(*aliased, 1e-5, CFG1.head_dim ** -0.5)
     assert invocation.node_count == 21 * CFG1.layers + 6
+
+
+@pytest.mark.parametrize("batch,options", [(2, {}), (2, {"whole_step": False}),
+                                           (20, {"whole_step": False}),
+                                           (2, {"fuse_library": False})],
+                         ids=["whole-step", "fused-layers", "tensor-cores", "unfused"])
+def test_steps_past_the_cache_capacity_write_nothing(device, batch, options):
+    """The last cache row is written like any other; a step at a position at or beyond the
+    capacity (where the reference indexes out of bounds) writes no cache row, no history row
+    and nothing past any buffer, and still advances the position."""
+    config = ref.Config(batch=batch, hidden=64, heads=4, layers=1, ffn=128, vocab=256, context=4,
+                        steps=3)
+    capacity = config.context + config.steps
+    initial, _ = ref.make_inputs(config, 5, eps=1e-5)
+    valid = capacity - int(initial["position"][0])          # steps up to the last cache row
+    expected = ref.expected(initial, config, valid, eps=1e-5)
+    session = open_session(device, config, initial, 1e-5, **options)
+    session.step(valid)
+    verify(session, initial, expected, config)
+    before = {name: session.read(name) for name in ("kc", "vc", "history")}
+    session.step(2)
+    assert int(session.read("position")[0]) == capacity + 2
+    for name in S.MUTABLE + S.WEIGHTS + ("sincos",):
+        assert session.tail_intact(name), f"{name}: tail overwritten"
+    for name, values in before.items():
+        assert np.array_equal(session.read(name), values), f"{name} written past the capacity"
