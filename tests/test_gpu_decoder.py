@@ -171,3 +171,26 @@ def test_steps_past_the_cache_capacity_write_nothing(device, batch, options):
         assert session.tail_intact(name), f"{name}: tail overwritten"
     for name, values in before.items():
         assert np.array_equal(session.read(name), values), f"{name} written past the capacity"
+
+
+@pytest.mark.parametrize("options", [{}, {"whole_step": False}, {"fuse_library": False}],
+                         ids=["whole-step", "fused-layers", "unfused"])
+def test_tokens_outside_the_vocabulary_touch_nothing_past_the_buffers(device, options):
+    """A token outside [0, vocab) (the reference would read past the embedding table) selects
+    no embedding row; the step completes, stays inside every buffer and the other requests'
+    tokens are those of a clean run."""
+    config = ref.Config(batch=3, hidden=64, heads=4, layers=1, ffn=128, vocab=256, context=4,
+                        steps=3)
+    initial, _ = ref.make_inputs(config, 6, eps=1e-5)
+    clean = open_session(device, config, initial, 1e-5, **options)
+    clean.step(1)
+    broken = dict(initial)
+    broken["tokens"] = initial["tokens"].copy()
+    broken["tokens"][0] = -1
+    broken["tokens"][2] = config.vocab
+    session = open_session(device, config, broken, 1e-5, **options)
+    session.step(1)
+    assert int(session.read("position")[0]) == int(initial["position"][0]) + 1
+    for name in S.MUTABLE + S.WEIGHTS + ("sincos",):
+        assert session.tail_intact(name), f"{name}: tail overwritten"
+    assert session.read("tokens")[1] == clean.read("tokens")[1]
