@@ -8,18 +8,25 @@ SwiGLU 4096, vocab 32000, 2048-token prompts in the KV cache, greedy decode).  R
 sharded across GPUs with no collective in the step; each GPU holds 512 requests, so 8 GPUs
 run the full 4096-request configuration (weak scaling; the full configuration's 279 GB KV
 cache does not fit one GPU).  Weights are seeded random (reference draw order, seed 4),
-prompts uniform over the vocabulary; the prompt is prefilled on the GPU by teacher forcing
-through the same decode graph.  Every timed step is one complete decode step (all layers, LM
-head, greedy argmax, KV append) for every request on the GPU.
+prompts uniform over the vocabulary; the prompts are prefilled on the GPU (batched prefill).
+Every timed step is one complete decode step (all layers, LM head, greedy argmax, KV append)
+for every request on the GPU.
 
 Timing: W warm-up steps, then K graph launches bracketed by a barrier and a synchronize on
 both sides, CUDA events on the invocation stream, max over ranks.  The KV cache (34.9 GB per
-GPU) is far larger than L2, so no flush is needed between steps.  ``e2e`` repeats K steps
-through the public API with the step's tokens copied host->device from pinned memory and the
-generated tokens copied back every step.  ``roofline`` reports the attention kernel (the
-dominant, HBM-bound kernel) from per-node CUDA events over one extra profiled step.
-``--impl reference`` times the reference's own CPU decoder (its NumPy algorithm, restated in
-oracle/) on a bounded sample of requests on the host cores.
+GPU) is far larger than L2, so no flush is needed between steps.  Every phase (warm-up, timed,
+end to end, median, profile, parity) restarts at the end of the prompt, so the measured
+positions are the configuration's own (2047 onwards, inside its 2080-row capacity).  ``e2e``
+repeats K steps through the public API with the step's tokens copied host->device from pinned
+memory and the generated tokens copied back every step.  ``roofline`` reports the attention
+kernel (the dominant, HBM-bound kernel) from per-node CUDA events over one extra profiled step.
+``parity`` replays the first steps through the reference's own kernel bodies (generated, naive,
+unfused) on the same state and compares tokens and logits; ``library_faults`` is the kernel
+library's fault word after the run (must be 0).  At one GPU the line also carries
+``small_configs`` (3, 4 and 2: time per step, speed-up over the naive
+graph, parity) and, at every GPU count, ``full_job`` (config 5's 4096 requests in waves of one
+shard per GPU).  ``--impl reference`` times the reference's own CPU decoder (its NumPy
+algorithm, restated in oracle/) on a bounded sample of requests on the host cores.
 """
 from __future__ import annotations
 
@@ -355,15 +362,29 @@ def vector_arm(args, workload, world, rank, local, group):
 
 
 
+def restart(sess, position: int, tokens: np.ndarray) -> None:
+    """Put the session back at the end of its prompt (position, last prompt tokens): every
+    measured phase decodes the same cache positions, inside the configuration's capacity."""
+    sess.write("position", np.array([position], np.int32))
+    sess.write("tokens", tokens)
+
+
+def library_faults() -> int:
+    from ckl import _native
+
+    return _native.library_faults()
+
+
 def gpu_arm(args, workload, world, rank, local, group):
     import ckl
     from ckl.workloads import session as S
 
     b, h, a, l, f, v, ctx, steps, seed, eps = workload
-    total_steps = args.warmup + args.steps
-    capacity_steps = max(steps, 3 * total_steps + 8 + NAIVE_STEPS)
+    # The configuration's own capacity (context + its step count); every phase restarts at
+    # the end of the prompt, so the cache only grows when one phase has more steps than that.
+    phase_steps = max(args.steps, args.warmup, PARITY_STEPS, NAIVE_STEPS + 1)
     shape = S.DecoderShape(batch=b, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
-                           steps=capacity_steps)
+                           steps=max(steps, phase_steps))
     arrays, rng = S.make_weights(shape, seed)
     from ckl.workloads.sharding import shard_prompts
 
@@ -389,11 +410,13 @@ def gpu_arm(args, workload, world, rank, local, group):
         sess.write("position", np.array([ctx - 1], np.int32))
     prefill_s = time.perf_counter() - t_prefill
     setup_s = time.perf_counter() - t_setup
+    p0, last_tokens = ctx - 1, prompts[-1].copy()
     inv = sess.invocation
     nodes = inv.node_count
     clocks = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
         inv.run(mode="graph")
+    restart(sess, p0, last_tokens)
     barrier(group)
     inv.synchronize()
     elapsed_ms = inv.time_launches(args.steps, mode="graph")
@@ -404,11 +427,12 @@ def gpu_arm(args, workload, world, rank, local, group):
 
     # End to end through the public API: per step, tokens host->device from pinned memory,
     # the step, generated tokens device->host, wait for them.
+    restart(sess, p0, last_tokens)
     pinned_in = ckl.cuda.PinnedHostBuffer(4 * b)
     pinned_out = ckl.cuda.PinnedHostBuffer(4 * b)
     tokens_buf = sess.buffers["tokens"]
     host_tokens = np.frombuffer(pinned_in.view(), dtype=np.int32)
-    host_tokens[:] = sess.read("tokens")
+    host_tokens[:] = last_tokens
     out_tokens = np.frombuffer(pinned_out.view(), dtype=np.int32)
     barrier(group)
     t0 = time.perf_counter()
@@ -421,14 +445,17 @@ def gpu_arm(args, workload, world, rank, local, group):
     e2e_s = reduce_max(group, time.perf_counter() - t0)
     e2e = b * world * args.steps / e2e_s
     # Median step: the same steps timed one at a time (device time of each, CUDA events).
+    restart(sess, p0, last_tokens)
     barrier(group)
     inv.synchronize()
     single = sorted(inv.time_launches(1, mode="graph") for _ in range(args.steps))
     median_ms = reduce_max(group, statistics.median(single))
     clocks.__exit__(None, None, None)
 
-    # Per-kernel device time of one more (profiled, ordinary-mode) step.
-    position = int(sess.read("position")[0])
+    # Per-kernel device time of one more (profiled, ordinary-mode) step at the first measured
+    # position (attention over `ctx` cache rows).
+    restart(sess, p0, last_tokens)
+    position = p0
     per_node = inv.profile_nodes(1)
     names = inv.node_names
     attention_kernel = "ckl.fused.attention"
@@ -442,6 +469,8 @@ def gpu_arm(args, workload, world, rank, local, group):
         achieved = algorithmic / (launch_ms / 1000.0) / 1e9
         roofline = {"bound": "hbm", "kernel": attention_kernel, "achieved": achieved,
                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                    "frac_of": "measured copy bandwidth (read + write stream); a read-only "
+                               "stream such as attention's K/V rows can exceed it",
                     "traffic": algorithmic * ATTENTION_TRAFFIC_RATIO,
                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
                                       "32-request shard at position 2049, scaled by algorithmic "
@@ -453,7 +482,10 @@ def gpu_arm(args, workload, world, rank, local, group):
     for n, t in zip(names, per_node):
         share[n] = share.get(n, 0.0) + t
     total = sum(per_node)
-    naive = None if args.no_naive else naive_graph(sess, elapsed_ms / args.steps, group)
+    naive, parity = reference_path(sess, elapsed_ms / args.steps, group, p0, last_tokens)
+    faults = library_faults()
+    if faults:
+        raise RuntimeError(f"kernel library fault word {faults:#x} after the measured steps")
     line = None
     if rank == 0:
         line = {
@@ -471,7 +503,12 @@ def gpu_arm(args, workload, world, rank, local, group):
             "graph_nodes_per_step": nodes,
             "kernel_share": {k: round(t / total, 4) for k, t in sorted(share.items(),
                                                                        key=lambda kv: -kv[1])},
+            "parity_check": parity["passed"],
+            "parity": parity,
+            "library_faults": faults,
             "naive_graph": naive,
+            "measured_positions": [p0, p0 + phase_steps - 1],
+            "cache_capacity": shape.capacity,
             "prefill": args.prefill,
             "projections": args.projections,
             "whole_step": args.whole_step,
@@ -479,18 +516,28 @@ def gpu_arm(args, workload, world, rank, local, group):
             "prefill_s": round(prefill_s, 3),
             "clocks": clocks.summary(),
         }
+    if args.workload == "cfg5" and not args.no_full_job:
+        job = full_job(args, sess, workload, world, rank, group)
+        if line is not None:
+            line["full_job"] = job
     return line
 
 
 NAIVE_STEPS = 3
+PARITY_STEPS = 4
+FULL_JOB_REQUESTS = 4096  # BASELINE config 5's whole job
+FULL_JOB_STEPS = 8
 
 
-def naive_graph(sess, ms_per_step, group):
-    """The reference's own code path on this GPU: every kernel generated from its
-    ``workloads.py`` body (naive FP32 code, no library, no fusion), the unfused 21L+6-node DAG
-    with the reference's may-alias edges, replayed as an inferred CUDA graph on the session's
-    buffers after the timed region.  It stands in for the reference's MLIR-compiled graph,
-    which needs an LLVM/MLIR toolchain absent here."""
+def reference_path(sess, ms_per_step, group, p0, tokens):
+    """The reference's own code path on this GPU, timed and used as the parity check.
+
+    Every kernel is generated from its ``workloads.py`` body (naive FP32 code, no library, no
+    fusion), the unfused 21L+6-node DAG with the reference's may-alias edges replayed as an
+    inferred CUDA graph on the session's buffers.  It stands in for the reference's
+    MLIR-compiled graph, which needs an LLVM/MLIR toolchain absent here.  Parity: from the same
+    state (end of the prompt), `PARITY_STEPS` steps of the measured program and of this one
+    must give the same greedy tokens and logits within 1e-4 relative / 1e-5 absolute."""
     import ckl
     from ckl.workloads import decoder
 
@@ -499,15 +546,147 @@ def naive_graph(sess, ms_per_step, group):
                                    fuse_library=False, library=False)
     compile_s = time.perf_counter() - t0
     arguments = [sess.buffers[name] for name in decoder.ARGUMENTS[:-2]]
-    inv = program.bind(*arguments, float(sess.epsilon), float(sess.attention_scale))
-    inv.run(mode="graph")
-    inv.synchronize()
+    naive = program.bind(*arguments, float(sess.epsilon), float(sess.attention_scale))
+    runs = {}
+    for label, invocation in (("measured", sess.invocation), ("reference", naive)):
+        restart(sess, p0, tokens)
+        for _ in range(PARITY_STEPS):
+            invocation.run(mode="graph")
+        runs[label] = (sess.read("history")[p0:p0 + PARITY_STEPS], sess.read("logits"))
+    (ours, our_logits), (theirs, their_logits) = runs["measured"], runs["reference"]
+    scale = np.maximum(np.abs(their_logits), 1e-30)
+    excess = np.abs(our_logits - their_logits) - (1e-5 + 1e-4 * np.abs(their_logits))
+    parity = {"passed": bool(np.array_equal(ours, theirs) and np.all(excess <= 0)),
+              "steps": PARITY_STEPS, "positions": [p0, p0 + PARITY_STEPS - 1],
+              "tokens_equal": bool(np.array_equal(ours, theirs)),
+              "logits_max_abs_diff": float(np.max(np.abs(our_logits - their_logits))),
+              "logits_max_rel_diff": float(np.max(np.abs(our_logits - their_logits) / scale)),
+              "against": "the reference's kernel bodies compiled naively (generated, unfused, "
+                         "reference DAG) on the same GPU and state",
+              "tolerance": "tokens exact; logits 1e-4 relative + 1e-5 absolute (last step)"}
+    restart(sess, p0, tokens)
+    naive.run(mode="graph")
+    naive.synchronize()
     barrier(group)
-    naive_ms = reduce_max(group, inv.time_launches(NAIVE_STEPS, mode="graph")) / NAIVE_STEPS
-    return {"ms_per_step": naive_ms, "steps": NAIVE_STEPS, "graph_nodes_per_step": inv.node_count,
-            "speedup": naive_ms / ms_per_step, "compile_s": round(compile_s, 2),
-            "what": "reference kernel bodies compiled naively (ckl codegen + NVRTC, sm_100a), "
-                    "reference DAG, inferred graph, same buffers and GPU"}
+    naive_ms = reduce_max(group, naive.time_launches(NAIVE_STEPS, mode="graph")) / NAIVE_STEPS
+    return ({"ms_per_step": naive_ms, "steps": NAIVE_STEPS,
+             "graph_nodes_per_step": naive.node_count, "speedup": naive_ms / ms_per_step,
+             "compile_s": round(compile_s, 2),
+             "what": "reference kernel bodies compiled naively (ckl codegen + NVRTC, sm_100a), "
+                     "reference DAG, inferred graph, same buffers and GPU"}, parity)
+
+
+def full_job(args, sess, workload, world, rank, group):
+    """BASELINE config 5's whole job (4096 requests) at this run's GPU count, in waves of the
+    per-GPU shard: each wave prefills its requests' prompts (batched) and decodes
+    `FULL_JOB_STEPS` steps; device time of the decode steps is max over ranks per wave."""
+    b, h, a, l, f, v, ctx, steps, seed, eps = workload
+    waves = max(1, FULL_JOB_REQUESTS // (b * world))
+    rng = np.random.default_rng([seed, 4096])
+    inv = sess.invocation
+    decode_ms, prefill_s = 0.0, 0.0
+    for wave in range(waves):
+        prompts_all = rng.integers(0, v, (ctx, b * world), dtype=np.int32)
+        prompts = np.ascontiguousarray(prompts_all[:, rank * b:(rank + 1) * b])
+        sess.write("history", np.full(sess.shapes["history"][0], -1, np.int32))
+        barrier(group)
+        t0 = time.perf_counter()
+        sess.prefill(prompts, batched=True)
+        inv.synchronize()
+        prefill_s += reduce_max(group, time.perf_counter() - t0)
+        barrier(group)
+        decode_ms += reduce_max(group, inv.time_launches(FULL_JOB_STEPS, mode="graph"))
+    requests = waves * b * world
+    tokens = requests * FULL_JOB_STEPS
+    return {"requests": requests, "waves": waves, "requests_per_gpu_per_wave": b,
+            "decode_steps_per_wave": FULL_JOB_STEPS,
+            "decode_tokens_per_s": tokens / (decode_ms / 1000.0),
+            "decode_s": decode_ms / 1000.0, "prefill_s": prefill_s,
+            "job_tokens_per_s": tokens / (decode_ms / 1000.0 + prefill_s),
+            "what": "strong scaling of the fixed 4096-request job: waves of one shard per GPU, "
+                    "batched prefill of each wave's 2048-token prompts, then decode steps; "
+                    "prompts seeded per wave"}
+
+
+SMALL_ROUNDS, SMALL_STEPS, SMALL_WARMUP = 5, 16, 20
+
+
+def small_decoder(name, local):
+    """One latency-bound BASELINE decoder config on this GPU: CUDA-event time per step (median
+    of `SMALL_ROUNDS` rounds of `SMALL_STEPS` graph launches from the end of the prompt), the
+    reference's naive code path on the same state and its parity check."""
+    import ckl
+    from ckl.workloads import session as S
+
+    b, h, a, l, f, v, ctx, steps, seed, eps = WORKLOADS[name]
+    shape = S.DecoderShape(batch=b, hidden=h, heads=a, layers=l, ffn=f, vocab=v, context=ctx,
+                           steps=max(steps, SMALL_STEPS, SMALL_WARMUP))
+    arrays, rng = S.make_weights(shape, seed)
+    prompts = S.make_prompts(shape, rng)
+    arrays.update(S.initial_state(shape))
+    arrays["tokens"] = prompts[0].copy()
+    sess = S.DecoderSession(ckl.Device(local), arrays, epsilon=eps,
+                            attention_scale=(h // a) ** -0.5, tails=False)
+    sess.prefill(prompts, batched=True)
+    p0, last = ctx - 1, prompts[-1].copy()
+    inv = sess.invocation
+    for _ in range(SMALL_WARMUP):
+        inv.run(mode="graph")
+    rounds = []
+    for _ in range(SMALL_ROUNDS):
+        restart(sess, p0, last)
+        inv.synchronize()
+        rounds.append(inv.time_launches(SMALL_STEPS, mode="graph") / SMALL_STEPS)
+    ms = statistics.median(rounds)
+    naive, parity = reference_path(sess, ms, None, p0, last)
+    return {"ms_per_step": ms, "us_per_step": 1000.0 * ms, "tokens_per_s": b / (ms / 1000.0),
+            "graph_nodes_per_step": inv.node_count, "naive_ms_per_step": naive["ms_per_step"],
+            "speedup_vs_naive_graph": naive["speedup"], "parity_check": parity["passed"],
+            "parity": parity, "requests": b, "positions": [p0, p0 + SMALL_STEPS - 1],
+            "timing": f"median of {SMALL_ROUNDS} rounds of {SMALL_STEPS} graph launches, CUDA "
+                      f"events, after {SMALL_WARMUP} warm-up steps"}
+
+
+def small_vector(local, steps: int):
+    """BASELINE config 2 on this GPU: the fused pipeline against the reference's own two
+    generated launches through the temporary (same buffers), bitwise parity of the results."""
+    import ckl
+    from ckl.workloads import vector_pipeline
+
+    n, seed, bias = WORKLOADS["vector"][0], WORKLOADS["vector"][8], WORKLOADS["vector"][9]
+    device = ckl.Device(local)
+    spec = ckl.BufferSpec((n,), ckl.f32)
+    src, dst = device.empty(spec), device.empty(spec)
+    src.copy_from_host(np.random.default_rng(seed).uniform(-1.0, 1.0, n).astype(np.float32))
+    lowered = vector_pipeline.lower(n)
+    target = ckl.NVIDIATarget("sm_100a")
+    fused = lowered.compile(target=target, fuse_pointwise=True).bind(src, dst, float(bias))
+    naive = lowered.compile(target=target, fuse_pointwise=False, library=False).bind(
+        src, dst, float(bias))
+    results, times = {}, {}
+    for label, inv in (("fused", fused), ("naive", naive)):
+        for _ in range(3):
+            inv.run(mode="graph")
+        times[label] = inv.time_launches(steps, mode="graph") / steps
+        out = np.empty(n, np.float32)
+        dst.copy_to_host(out)
+        results[label] = out
+    same = results["fused"].tobytes() == results["naive"].tobytes()
+    return {"ms_per_step": times["fused"], "elements_per_s": n / (times["fused"] / 1000.0),
+            "achieved_gbs": 8 * n / (times["fused"] / 1000.0) / 1e9,
+            "naive_ms_per_step": times["naive"], "speedup_vs_naive_graph":
+                times["naive"] / times["fused"], "parity_check": bool(same),
+            "parity": {"passed": bool(same), "against": "the reference program's two generated "
+                       "launches through its temporary, same GPU and buffers",
+                       "tolerance": "bitwise"}, "elements": n}
+
+
+def small_configs(args, local):
+    out = {}
+    for name in ("cfg1", "cfg3", "cfg4"):
+        out[name] = small_decoder(name, local)
+    out["vector"] = small_vector(local, max(args.steps, 3))
+    return out
 
 
 def main():
@@ -523,9 +702,10 @@ def main():
     parser.add_argument("--whole-step", choices=("on", "off"), default="on",
                         help="small decoders: the whole decode step as one kernel (on) or the "
                              "per-layer fused graph (off)")
-    parser.add_argument("--no-naive", action="store_true",
-                        help="skip timing the reference's naive code path (all kernels generated "
-                             "from their bodies) on the same GPU")
+    parser.add_argument("--no-full-job", action="store_true",
+                        help="cfg5: skip the 4096-request full job (waves of one shard per GPU)")
+    parser.add_argument("--no-small-configs", action="store_true",
+                        help="cfg5 at one GPU: skip the cfg1/cfg3/cfg4/vector lines")
     parser.add_argument("--projections", choices=("tensor", "ffma"), default="tensor",
                         help="batched projections on tcgen05 tensor cores (3xTF32) or FFMA")
     parser.add_argument("--prefill", choices=("batched", "graph", "synthetic"), default="batched",
@@ -548,6 +728,8 @@ def main():
     arm = vector_arm if args.workload == "vector" else gpu_arm
     line = arm(args, workload, world, rank, local, group)
     if rank == 0:
+        if world == 1 and args.workload == "cfg5" and not args.no_small_configs:
+            line["small_configs"] = small_configs(args, local)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, workload)
         print(json.dumps(line), flush=True)

@@ -314,28 +314,28 @@ CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPa
                     nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&panelGateUpTc<1>),
                     "PPPPS", sizeof(GemmSpec), gateUpGeometry, gateUpSelect, prepareGateUp,
-                    sizeof(tc::WeightMapPair), true);
+                    sizeof(tc::WeightMapPair), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope", reinterpret_cast<const void *>(&panelLinearRopeTc<32, 1, 1>),
                     "PPPPPS", sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append", reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32, 1, 1>),
                     "PPPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearRopeAppendTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append", reinterpret_cast<const void *>(&panelLinearAppendTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const void *>(&panelLinearResidualTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_argmax", reinterpret_cast<const void *>(&panelArgmaxTc<32, 1, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelArgmaxTc),
-                    prepareWeights, sizeof(tc::WeightMap), true);
+                    prepareWeights, sizeof(tc::WeightMap), true, true);
 
 } // namespace ckl::kernels
 
@@ -355,4 +355,39 @@ extern "C" int ckl_library_faults(uint32_t *out, int reset) {
   if (out)
     *out = value;
   return CKL_OK;
+}
+
+namespace {
+int setSymbolOnDevice(int device, const void *symbol, const void *value, std::size_t bytes) {
+  int previous = 0;
+  cudaError_t status = cudaGetDevice(&previous);
+  if (status == cudaSuccess)
+    status = cudaSetDevice(device);
+  if (status == cudaSuccess)
+    status = cudaMemcpyToSymbol(symbol, value, bytes);
+  const cudaError_t restored = cudaSetDevice(previous);
+  if (status == cudaSuccess)
+    status = restored;
+  if (status != cudaSuccess) {
+    cudaGetLastError();
+    return CKL_RUNTIME_ERROR;
+  }
+  return CKL_OK;
+}
+} // namespace
+
+// Limit of the tensor-core kernels' pipeline waits on `device` for launches made after the
+// call (the default is 2 s); the waits that drain a CTA's own copies keep their fixed limit.
+extern "C" int ckl_set_wait_limit(int device, uint64_t nanoseconds) {
+  const unsigned long long value = nanoseconds;
+  return setSymbolOnDevice(device, &ckl::kernels::tc::g_waitLimitNs, &value, sizeof(value));
+}
+
+// Test hook: while enabled, every tensor-core kernel CTA launched on `device` first waits on an
+// mbarrier that nothing signals; the wait expires after the wait limit, records fault bit 0 and
+// takes the abort path (no work done, tensor memory freed, no copy left in flight).
+extern "C" int ckl_inject_unsignalled_wait(int device, int enable) {
+  const int value = enable ? 1 : 0;
+  return setSymbolOnDevice(device, &ckl::kernels::tc::g_injectUnsignalledWait, &value,
+                           sizeof(value));
 }

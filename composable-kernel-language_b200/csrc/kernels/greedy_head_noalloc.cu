@@ -18,7 +18,9 @@
 //     events between streams);
 //   * the first call on each device resolves the array's device address with
 //     cudaGetSymbolAddress (this may load the module); make that first call before any
-//     stream capture on that device.
+//     stream capture on that device.  The address is cached per device ordinal for the
+//     life of the process, so calls after a cudaDeviceReset or under a context other than the
+//     device's primary context are not supported.
 #include "ckl_b200.h"
 #include "../errors.hpp"
 #include "common.cuh"

@@ -52,7 +52,11 @@ constexpr int kMmaWarp = 1;
 constexpr int kConverterWarps = 8; // warps 2..9; also the epilogue (two warps per TMEM lane quarter)
 constexpr int kConverterThreads = kConverterWarps * kWarp;
 constexpr int kThreads = (2 + kConverterWarps) * kWarp;
+// Default limit of a pipeline wait; ckl_set_wait_limit changes it per device (tests).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull; // 2 s
+// Limit of the waits that drain a CTA's own copies and MMAs before it frees its tensor memory
+// and exits; fixed, so that no setting can let a CTA leave with an operation in flight.
+constexpr unsigned long long kDrainLimitNs = 2000000000ull; // 2 s
 constexpr std::size_t kMaxDynamicSmem = 227 * 1024;
 
 // TMA tensor map of a weight buffer [layers, K, N] with a box of BN x 32 x 1 (N innermost),
@@ -80,6 +84,11 @@ __device__ __forceinline__ float swigluValue(float g, float u) {
 // Fault word of the library (bit 0: a tensor-core wait expired).  One translation unit
 // instantiates these kernels and reports the word (ckl_library_faults).
 static __device__ unsigned g_libraryFaults = 0;
+// Limit of the pipeline waits (those that an abort can end) on this device, in nanoseconds.
+static __device__ unsigned long long g_waitLimitNs = kWaitLimitNs;
+// Nonzero: the MMA warp first waits on an mbarrier that nothing signals, so its bounded wait
+// expires and the CTA takes the abort path (ckl_inject_unsignalled_wait; tests only).
+static __device__ int g_injectUnsignalledWait = 0;
 
 __device__ __forceinline__ unsigned smemAddress(const void *p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -135,18 +144,20 @@ __device__ __forceinline__ unsigned long long globalTimer() {
 }
 
 // Bounded wait for an mbarrier phase.  Gives up when `abort` is raised by another thread, or
-// raises it (and the fault bit) when the time limit expires.
+// raises it (and the fault bit) when the time limit expires.  Pipeline waits (with an abort
+// flag) use the device's settable limit, drain waits (abort == nullptr) the fixed one.
 __device__ __forceinline__ bool waitPhase(unsigned long long *bar, unsigned phase,
                                           volatile int *abort) {
   if (mbarrierTryWait(bar, phase))
     return true;
   const unsigned long long start = globalTimer();
+  const unsigned long long limit = abort != nullptr ? g_waitLimitNs : kDrainLimitNs;
   while (true) {
     if (mbarrierTryWait(bar, phase))
       return true;
     if (abort != nullptr && *abort)
       return false;
-    if (globalTimer() - start > kWaitLimitNs) {
+    if (globalTimer() - start > limit) {
       atomicOr(&g_libraryFaults, 1u);
       if (abort != nullptr)
         *abort = 1;
@@ -267,6 +278,7 @@ template <int BN, int S, int MT = 1> struct Smem {
   float bLo[2][BK / 4][BN][4];
   float rawB[S][BK][BN];        // weight box as copied (128-byte aligned)
   unsigned long long full[S], empty[S], bFull[2], bEmpty[2], accDone;
+  unsigned long long unsignalled; // never arrived on (injected expiring wait)
   unsigned tmemBase;
   int abort;
 };
@@ -571,6 +583,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       mbarrierInit(&sm.bEmpty[i], 1);
     }
     mbarrierInit(&sm.accDone, 1);
+    mbarrierInit(&sm.unsignalled, 1);
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -631,7 +644,10 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr unsigned idesc = instructionDescriptor<BN>();
-      for (int64_t kt = 0; kt < slices; ++kt) {
+      // Injected fault: a wait on a barrier nothing signals expires and aborts the CTA.
+      const bool injected =
+          g_injectUnsignalledWait != 0 && !waitPhase(&sm.unsignalled, 0, abort);
+      for (int64_t kt = 0; kt < slices && !injected; ++kt) {
         const int slot = int(kt % S), buffer = int(kt & 1);
         if (!waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort) ||
             !waitPhase(&sm.bFull[buffer], unsigned((kt / 2) & 1), abort))

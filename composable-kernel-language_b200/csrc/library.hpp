@@ -41,6 +41,9 @@ struct Kernel {
   // The kernel calls dependentLaunchEntry() first: it may be launched with a programmatic
   // dependency on its predecessors (scheduled while they finish).
   bool dependentLaunch = false;
+  // The kernel waits on mbarriers with bounded waits that record a library fault when they
+  // expire (ckl_library_faults): the runtime checks the fault word after synchronizing.
+  bool boundedWaits = false;
 };
 
 // All entries, defined by the kernel translation units (registered at static init time).

@@ -161,6 +161,7 @@ struct GraphExec {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   std::vector<cudaGraphNode_t> nodes;
+  std::vector<KernelLaunch> launches; // explicit graphs: the launch behind each node
   bool captured = false;
   ~GraphExec() {
     cudaSetDevice(device->ordinal);
@@ -262,6 +263,7 @@ std::shared_ptr<GraphExec> instantiate(const Plan &plan, const std::shared_ptr<D
     }
   }
   check(cudaGraphInstantiate(&g->exec, g->graph, 0), "cudaGraphInstantiate");
+  g->launches = plan.nodes;
   return g;
 }
 
@@ -465,6 +467,7 @@ struct InvocationState {
   std::map<std::pair<int, uint64_t>, std::shared_ptr<GraphExec>> graphs;
   std::mutex runMutex;
   std::string error;
+  bool boundedWaits = false; // some node waits with bounded waits (library fault word)
   ~InvocationState() {
     graphs.clear();
     if (stream) {
@@ -545,6 +548,26 @@ void submit(InvocationState &f, int mode, uint64_t batch) {
   } else {
     for (uint64_t i = 0; i < batch; ++i)
       launchOrdinary(f.plan, f.stream);
+  }
+}
+
+// After an invocation's work has completed: a kernel with bounded waits that gave one up did
+// not do its work, so the submission's results are invalid.  The fault word stays set (for
+// every later check on the device) until the caller clears it with ckl_library_faults(&w, 1).
+void checkLibraryFaults(const InvocationState &f) {
+  if (!f.boundedWaits)
+    return;
+  uint32_t word = 0;
+  if (ckl_library_faults(&word, 0) != CKL_OK)
+    throw CudaError("reading the kernel library's fault word failed");
+  if (word) {
+    char text[256];
+    std::snprintf(text, sizeof text,
+                  "kernel library fault word 0x%x on device %d: a tensor-core kernel gave up a "
+                  "bounded wait (bit 0) or found a misaligned operand (bit 1) and skipped its "
+                  "work; the results are invalid (clear with ckl_library_faults(&word, 1))",
+                  word, f.device->ordinal);
+    throw std::runtime_error(text);
   }
 }
 
@@ -825,6 +848,8 @@ int ckl_bind(ckl_program *program, ckl_device *device, uint32_t count, const ckl
     p->entry(entryArguments);
     if (!state->error.empty())
       throw std::runtime_error(state->error);
+    for (const KernelLaunch &k : state->plan.nodes)
+      state->boundedWaits |= k.function.entry != nullptr && k.function.entry->boundedWaits;
     *out = new ckl_invocation{state};
   });
 }
@@ -841,6 +866,7 @@ int ckl_run(ckl_invocation *invocation, int mode, uint64_t batch) {
     f.device->current();
     submit(f, mode, batch);
     check(cudaStreamSynchronize(f.stream), "cudaStreamSynchronize");
+    checkLibraryFaults(f);
   });
 }
 
@@ -864,6 +890,7 @@ int ckl_synchronize(ckl_invocation *invocation) {
     auto &f = *invocation->state;
     f.device->current();
     check(cudaStreamSynchronize(f.stream), "cudaStreamSynchronize");
+    checkLibraryFaults(f);
   });
 }
 
@@ -937,6 +964,7 @@ int ckl_completion_query(const ckl_completion *completion, int *done) {
     }
     check(status, "cudaEventQuery");
     *done = 1;
+    checkLibraryFaults(*completion->state);
   });
 }
 
@@ -949,6 +977,7 @@ int ckl_completion_wait(const ckl_completion *completion, uint64_t timeout_us, i
     if (timeout_us == UINT64_MAX) {
       check(cudaEventSynchronize(completion->event), "cudaEventSynchronize");
       *done = 1;
+      checkLibraryFaults(*completion->state);
       return;
     }
     const auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(timeout_us);
@@ -956,6 +985,7 @@ int ckl_completion_wait(const ckl_completion *completion, uint64_t timeout_us, i
       const cudaError_t status = cudaEventQuery(completion->event);
       if (status == cudaSuccess) {
         *done = 1;
+        checkLibraryFaults(*completion->state);
         return;
       }
       if (status != cudaErrorNotReady)
@@ -1005,6 +1035,7 @@ int ckl_benchmark(ckl_invocation *invocation, int mode, uint64_t iterations, uin
     auto wallStop = Clock::now();
     float elapsed = 0;
     check(cudaEventElapsedTime(&elapsed, start, stop), "cudaEventElapsedTime");
+    checkLibraryFaults(f);
     out[0] = elapsed * 1000.0 / double(iterations) / double(batch);
     out[1] = std::chrono::duration<double, std::micro>(wallStop - wall).count() /
              double(iterations) / double(batch);
@@ -1045,6 +1076,7 @@ int ckl_time_launches(ckl_invocation *invocation, int mode, uint64_t batch, uint
     cudaEventDestroy(start);
     cudaEventDestroy(stop);
     check(status, "event timing");
+    checkLibraryFaults(f);
     *out_ms = ms;
   });
 }
@@ -1089,6 +1121,100 @@ int ckl_profile_nodes(ckl_invocation *invocation, uint64_t iterations, double *o
       throw;
     }
     destroy();
+    checkLibraryFaults(f);
+  });
+}
+
+int ckl_node_argument_sizes(const ckl_invocation *invocation, uint64_t node, uint64_t *sizes,
+                            uint32_t capacity, uint32_t *count) {
+  return guarded([&] {
+    if (!invocation || !count || (capacity && !sizes))
+      throw std::invalid_argument("invalid node argument query");
+    const auto &nodes = invocation->state->plan.nodes;
+    if (node >= nodes.size())
+      throw std::out_of_range("node index out of range");
+    const KernelLaunch &k = nodes[node];
+    const std::size_t slots =
+        k.arguments.size() - (k.function.entry && k.function.entry->prepare ? 1 : 0);
+    *count = uint32_t(slots);
+    for (std::size_t i = 0; i < slots && i < capacity; ++i)
+      sizes[i] = k.arguments[i].size();
+  });
+}
+
+int ckl_update_kernel(ckl_invocation *invocation, int mode, uint64_t batch, uint64_t node,
+                      uint32_t count, const void *const *arguments, const uint64_t *argument_bytes,
+                      const uint32_t *grid, const uint32_t *block, int64_t shared) {
+  return guarded([&] {
+    if (!invocation)
+      throw std::invalid_argument("null invocation");
+    auto &f = *invocation->state;
+    std::lock_guard<std::mutex> lock(f.runMutex);
+    validateExecution(f, mode, batch);
+    if (mode == 2)
+      throw std::invalid_argument("captured graph node indices cannot be updated");
+    if (mode != 1)
+      throw std::invalid_argument("only an explicit graph (mode 1) has updatable kernel nodes");
+    f.device->current();
+    GraphExec &g = executionGraph(f, mode, batch);
+    if (node >= g.nodes.size() || node >= g.launches.size())
+      throw std::out_of_range("graph kernel update references an unknown node");
+    KernelLaunch updated = g.launches[node];
+    const ckl::library::Kernel *entry = updated.function.entry;
+    const std::size_t slots = updated.arguments.size() - (entry && entry->prepare ? 1 : 0);
+    if (count != slots || (count && (!arguments || !argument_bytes)))
+      throw std::invalid_argument("graph kernel update: argument count does not match the node");
+    for (uint32_t i = 0; i < count; ++i) {
+      if (!arguments[i])
+        continue; // keep this slot
+      if (argument_bytes[i] != updated.arguments[i].size())
+        throw std::invalid_argument("graph kernel update: argument " + std::to_string(i) +
+                                    " has " + std::to_string(argument_bytes[i]) +
+                                    " bytes, the node's slot " +
+                                    std::to_string(updated.arguments[i].size()));
+      std::memcpy(updated.arguments[i].data(), arguments[i], argument_bytes[i]);
+    }
+    if (grid)
+      updated.grid = dim3(grid[0], grid[1], grid[2]);
+    if (block)
+      updated.block = dim3(block[0], block[1], block[2]);
+    if (shared >= 0)
+      updated.shared = unsigned(shared);
+    const dim3 &gd = updated.grid, &bd = updated.block;
+    if (!gd.x || !gd.y || !gd.z || !bd.x || !bd.y || !bd.z ||
+        uint64_t(bd.x) * bd.y * bd.z > 1024 || gd.y > 65535 || gd.z > 65535 || gd.x >= (1u << 31))
+      throw std::invalid_argument("graph kernel update: launch exceeds CUDA grid or block limits");
+    if (updated.shared > g.launches[node].shared)
+      throw std::invalid_argument("graph kernel update: more dynamic shared memory than the node "
+                                  "was built with");
+    if (entry && entry->select) {
+      const void *spec = entry->specBytes ? updated.arguments[slots - 1].data() : nullptr;
+      if (entry->select(spec) != updated.function.address)
+        throw std::invalid_argument(std::string("graph kernel update: the new specialization of ") +
+                                    entry->name + " needs another compiled configuration; bind "
+                                    "again instead");
+    }
+    if (entry && entry->prepare) {
+      // The extra parameter (for example a TMA tensor map of a weight buffer) follows the new
+      // arguments.
+      const void *spec = entry->specBytes ? updated.arguments[slots - 1].data() : nullptr;
+      std::vector<const void *> pointers;
+      for (std::size_t i = 0; i < slots; ++i)
+        pointers.push_back(updated.arguments[i].data());
+      if (!entry->prepare(spec, pointers.data(), pointers.size(), updated.arguments.back().data()))
+        throw std::invalid_argument(std::string("graph kernel update: arguments not supported by ") +
+                                    entry->name);
+    }
+    auto pointers = updated.pointers();
+    cudaKernelNodeParams p{};
+    p.func = const_cast<void *>(updated.function.address);
+    p.gridDim = updated.grid;
+    p.blockDim = updated.block;
+    p.sharedMemBytes = updated.shared;
+    p.kernelParams = pointers.data();
+    check(cudaGraphExecKernelNodeSetParams(g.exec, g.nodes[node], &p),
+          "cudaGraphExecKernelNodeSetParams");
+    g.launches[node] = std::move(updated);
   });
 }
 

@@ -72,6 +72,11 @@ _PROTOTYPES = {
                                 C.POINTER(C.c_double)]),
     "ckl_node_count": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
     "ckl_node_name": (C.c_int, [C.c_void_p, C.c_uint64, C.c_char_p, C.c_size_t]),
+    "ckl_node_argument_sizes": (C.c_int, [C.c_void_p, C.c_uint64, C.POINTER(C.c_uint64),
+                                          C.c_uint32, C.POINTER(C.c_uint32)]),
+    "ckl_update_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_uint64, C.c_uint32,
+                                    C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
+                                    C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.c_int64]),
     "ckl_launch": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64]),
     "ckl_synchronize": (C.c_int, [C.c_void_p]),
     "ckl_copy_in_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]),
@@ -95,6 +100,8 @@ _PROTOTYPES = {
                                        C.POINTER(C.c_uint32)]),
     "ckl_library_signature": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t]),
     "ckl_library_faults": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
+    "ckl_set_wait_limit": (C.c_int, [C.c_int, C.c_uint64]),
+    "ckl_inject_unsignalled_wait": (C.c_int, [C.c_int, C.c_int]),
     "ckl_library_count": (C.c_uint32, []),
     "ckl_library_name": (C.c_char_p, [C.c_uint32]),
     "ckl_cuda_compile": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(C.c_void_p),
@@ -167,6 +174,13 @@ def compile_cuda(source: str, name: str = "ckl_generated.cu") -> bytes:
         return C.string_at(binary, size.value)
     finally:
         lib.ckl_binary_free(binary)
+
+
+def library_faults(reset: bool = False) -> int:
+    """The kernel library's fault word on the current device (``ckl_library_faults``)."""
+    value = C.c_uint32()
+    check(load().ckl_library_faults(C.byref(value), int(reset)), "ckl_library_faults")
+    return value.value
 
 
 def message() -> str:

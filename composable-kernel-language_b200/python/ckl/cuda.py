@@ -373,6 +373,68 @@ class Invocation(_ContextManager):
             names.append(buffer.value.decode())
         return names
 
+    def node_argument_sizes(self, node: int) -> list:
+        """Byte sizes of plan node `node`'s argument slots (what :meth:`update_kernel` takes)."""
+        sizes, count = (C.c_uint64 * 64)(), C.c_uint32()
+        _abi.check(self._lib.ckl_node_argument_sizes(self._native_resource.value, node, sizes, 64,
+                                                     C.byref(count)), "node arguments")
+        if count.value > 64:
+            sizes = (C.c_uint64 * count.value)()
+            _abi.check(self._lib.ckl_node_argument_sizes(self._native_resource.value, node, sizes,
+                                                         count.value, C.byref(count)),
+                       "node arguments")
+        return [int(sizes[i]) for i in range(count.value)]
+
+    def update_kernel(self, node: int, arguments, *, mode="graph", batch_size=1, grid=None,
+                      block=None, shared_memory=None) -> None:
+        """Replace one kernel node's launch parameters in this invocation's explicit graph for
+        `batch_size` repetitions, without re-instantiating it (the reference's
+        ``NvidiaGraphExecutable::updateKernel``, ``NvidiaRuntime.cpp:466-496``).
+
+        `arguments` has one entry per argument slot of the node (:meth:`node_argument_sizes`):
+        ``None`` keeps the slot, a :class:`DeviceBuffer` of this device gives its address, and
+        ``bytes`` or a numpy scalar give the slot's new bytes.  Graph node ``r * node_count + i``
+        is repetition r's node i.  Only ``mode="graph"`` has updatable nodes (a captured graph
+        is rejected, as in the reference); the update applies to that graph only."""
+        import numpy as np
+
+        if type(node) is not int or node < 0:
+            raise ValueError("node must be a nonnegative int")
+        if mode not in _MODES:
+            raise ValueError("mode must be ordinary, graph, or capture")
+        arguments = list(arguments)
+        pointers = (C.c_void_p * max(1, len(arguments)))()
+        sizes = (C.c_uint64 * max(1, len(arguments)))()
+        keep = []
+        for i, value in enumerate(arguments):
+            if value is None:
+                continue
+            if isinstance(value, DeviceBuffer):
+                if value.device is not self.device and \
+                        getattr(value.device, "ordinal", None) != getattr(self.device, "ordinal", None):
+                    raise ValueError("updated buffer belongs to another device")
+                keep.append(value)
+                value = C.c_uint64(value.address)
+                raw = bytes(value)
+            elif isinstance(value, (bytes, bytearray)):
+                raw = bytes(value)
+            elif isinstance(value, np.generic):
+                raw = value.tobytes()
+            else:
+                raise TypeError("kernel arguments are None, a DeviceBuffer, bytes or a numpy scalar")
+            holder = C.create_string_buffer(raw, len(raw))
+            keep.append(holder)
+            pointers[i] = C.cast(holder, C.c_void_p)
+            sizes[i] = len(raw)
+        shape = lambda v: None if v is None else (C.c_uint32 * 3)(*(list(v) + [1, 1])[:3])
+        shared = -1 if shared_memory is None else int(shared_memory)
+        _abi.check(self._lib.ckl_update_kernel(self._native_resource.value, _MODES[mode],
+                                               batch_size, node, len(arguments), pointers, sizes,
+                                               shape(grid), shape(block), shared), "update_kernel")
+        # Buffers now referenced by the graph stay alive with the invocation.
+        self._updated = getattr(self, "_updated", []) + [k for k in keep
+                                                         if isinstance(k, DeviceBuffer)]
+
     def benchmark(self, *, iterations=200, graph=False, mode=None, batch_size=1) -> dict:
         """Time ``iterations`` submissions of ``batch_size`` programs; report per program."""
         if type(iterations) is not int or not 0 < iterations < (1 << 64):

@@ -116,6 +116,28 @@ int ckl_node_count(const ckl_invocation *invocation, uint64_t *out);
 /* Kernel nodes of one program execution with their reduced predecessors, for inspection:
  * names[i] receives at most `capacity` bytes. */
 int ckl_node_name(const ckl_invocation *invocation, uint64_t node, char *name, size_t capacity);
+/* Byte sizes of plan node `node`'s argument slots, in order (*count receives the number of
+ * slots; at most `capacity` sizes are written).  No reference counterpart: it tells a caller
+ * of ckl_update_kernel what each slot holds (8 for a pointer or i64/f64, 4 for i32/f32, the
+ * specialization struct's size for a library kernel's last slot). */
+int ckl_node_argument_sizes(const ckl_invocation *invocation, uint64_t node, uint64_t *sizes,
+                            uint32_t capacity, uint32_t *count);
+/* Replaces kernel node `node`'s launch parameters in the invocation's instantiated explicit
+ * graph for `batch` repetitions (built on first use), without re-instantiating it
+ * (cudaGraphExecKernelNodeSetParams).  Graph node r * node_count + i is repetition r's plan
+ * node i.  `arguments[i]` points at `argument_bytes[i]` new bytes for slot i (the slot's own
+ * size), or is NULL to keep the slot; `count` must be the node's slot count.  `grid` and
+ * `block` (three values each) replace the launch shape when non-NULL, `shared` (>= 0, at most
+ * the node's original amount) the dynamic shared memory.  The kernel stays the same: a new
+ * specialization that needs another compiled configuration is rejected.  Library kernels that
+ * derive a bind-time parameter from their arguments (the tensor-core kernels' TMA weight maps)
+ * derive it again.  The update applies to that graph only; ordinary launches and other
+ * graphs keep the bound plan.  Mode 2 (a captured graph, whose node indices are not stable)
+ * and mode 0 are rejected.  Replaces: NvidiaGraphExecutable::updateKernel,
+ * lib/Runtime/NvidiaRuntime.cpp:466-496. */
+int ckl_update_kernel(ckl_invocation *invocation, int mode, uint64_t batch, uint64_t node,
+                      uint32_t count, const void *const *arguments, const uint64_t *argument_bytes,
+                      const uint32_t *grid, const uint32_t *block, int64_t shared);
 
 /* Asynchronous submission on the invocation's stream (no reference counterpart; the
  * reference's only mode is synchronous).  Pair with ckl_synchronize. */
@@ -190,9 +212,23 @@ int ckl_library_geometry(const char *name, const void *spec, uint64_t spec_bytes
                          uint32_t grid[3], uint32_t block[3], uint32_t *shared_bytes);
 int ckl_library_signature(const char *name, char *signature, size_t capacity);
 /* Fault word of the kernel library on the current device: bit 0 is set when a tensor-core
- * kernel gave up a bounded wait (it then skipped its work instead of hanging).  `reset`
- * clears the word after reading it.  No reference counterpart. */
+ * kernel gave up a bounded wait (it then skipped its work instead of hanging), bit 1 when it
+ * found a misaligned operand.  `reset` clears the word after reading it.  While the word is
+ * nonzero, every synchronizing call (ckl_run, ckl_synchronize, ckl_benchmark,
+ * ckl_time_launches, ckl_profile_nodes, a completed ckl_completion_query/_wait) of an
+ * invocation that contains such a kernel returns CKL_RUNTIME_ERROR.  No reference
+ * counterpart (the reference's kernels never wait on the device). */
 int ckl_library_faults(uint32_t *out, int reset);
+/* Limit, in nanoseconds, of the tensor-core kernels' pipeline waits on device `device` for
+ * launches made after the call (default 2000000000, two seconds).  The waits with which an
+ * aborting CTA drains its own copies and MMAs keep a fixed two-second limit.  No reference
+ * counterpart; used by tests to make a wait expire quickly. */
+int ckl_set_wait_limit(int device, uint64_t nanoseconds);
+/* Test hook (no reference counterpart): while `enable` is nonzero, every tensor-core kernel
+ * CTA launched on `device` first waits on an mbarrier that nothing signals.  The wait expires
+ * after the wait limit, sets fault bit 0 and takes the abort path, so the submission's
+ * synchronizing call reports the fault and the context stays usable. */
+int ckl_inject_unsignalled_wait(int device, int enable);
 uint32_t ckl_library_count(void);
 const char *ckl_library_name(uint32_t index);
 
@@ -206,7 +242,9 @@ const char *ckl_library_name(uint32_t index);
  * batch * ceil(vocab / tile width) may not exceed 524288 partials (rejected with
  * CKL_INVALID_ARGUMENT).  All calls on a device share that array: calls that overlap on the
  * GPU race.  The first call on a device resolves the array's address (cudaGetSymbolAddress);
- * make it before any stream capture on that device. */
+ * make it before any stream capture on that device.  The address is kept per device ordinal
+ * for the life of the process: calls after a cudaDeviceReset, or under a context other than
+ * the device's primary context, are not supported. */
 int ckl_greedy_head_noalloc(const float *x, const float *gain, const float *lm, float eps,
                             int64_t batch, int64_t hidden, int64_t vocab, int64_t capacity,
                             float *logits, int32_t *tokens, int32_t *history, int32_t *position,
