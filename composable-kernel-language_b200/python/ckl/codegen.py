@@ -34,14 +34,14 @@ import struct
 from dataclasses import dataclass
 
 from .frontend.checker import BoundSignature, constant
-from .frontend.source import Definition, Intrinsic, Namespace, UnsupportedBinding
-from .types import BufferSpec, Dimension, ScalarType, bool_, f32, f64, i32, i64, index
+from .frontend.source import Definition
+from .frontend.walker import SPELLINGS, BodyWalker, is_static
+from .types import BufferSpec, ScalarType, bool_, f32, f64, i32, i64, index
 
 CTYPE = {f32: "float", f64: "double", i32: "int", i64: "long long", index: "long long",
          bool_: "bool"}
 _COORDINATES = {"thread_id": "threadIdx", "block_id": "blockIdx", "block_dim": "blockDim",
                 "grid_dim": "gridDim"}
-_AXES = "xyz"
 SYMBOL_PREFIX = "ckl_gen_"
 
 
@@ -82,387 +82,287 @@ def _literal(value, dtype: ScalarType) -> str:
     return f"((long long)0x{value & 0xFFFFFFFFFFFFFFFF:016x}ull)"
 
 
-def _static(value) -> bool:
-    return type(value) in (int, float, bool)
+_FLOATS, _INTEGERS = (f32, f64), (i32, i64)
 
 
-class _Emitter:
+def _conversion(source: ScalarType, target: ScalarType, code: str):
+    """C expression converting `code` from `source` to `target` as the reference's ``arith``
+    casts do (extf/truncf, extsi/trunci, fptosi/sitofp, index_cast), or None if there is no
+    direct conversion."""
+    integral = _INTEGERS + (index,)
+    if source in _FLOATS and target in _FLOATS:
+        return f"(double)({code})" if target == f64 else f"__double2float_rn({code})"
+    if source in integral and target in integral:
+        return f"(long long)({code})" if target in (i64, index) else f"(int)(unsigned)({code})"
+    if (source in _FLOATS and target in _INTEGERS) or (source in _INTEGERS and target in _FLOATS):
+        return f"({CTYPE[target]})({code})"
+    return None
+
+
+class _Emitter(BodyWalker):
+    """Walks a kernel body emitting CUDA C++: typed device values become ``const`` locals,
+    runtime branches and loops become C control flow, static values fold."""
+
     def __init__(self, definition: Definition, signature: BoundSignature):
-        self.definition = definition
-        self.signature = signature
-        self.dimensions = dict(signature.dimensions)
+        super().__init__(definition, signature.dimensions)
         self.lines: list[str] = []
         self.depth = 1
         self.counter = 0
-        self.env: dict[str, object] = {}
-        self.local_names = {p.name for p in signature.parameters} | {
-            n.id for n in ast.walk(definition.tree)
-            if isinstance(n, ast.Name) and isinstance(n.ctx, ast.Store)}
+        # Outer names of the innermost runtime branch (their reassignment is rejected).
+        self.branch_outer = None
         self.parameters = []
         for parameter in signature.parameters:
             if parameter.is_constant:
                 self.env[parameter.name] = parameter.value
                 continue
             code = f"p_{parameter.name}"
-            if isinstance(parameter.dtype, BufferSpec):
-                self.env[parameter.name] = _Buffer(code, parameter.dtype)
-                self.parameters.append((code, parameter.dtype))
-            else:
-                self.env[parameter.name] = _Value(code, parameter.dtype)
-                self.parameters.append((code, parameter.dtype))
+            kind = _Buffer if isinstance(parameter.dtype, BufferSpec) else _Value
+            self.env[parameter.name] = kind(code, parameter.dtype)
+            self.parameters.append((code, parameter.dtype))
 
-    # -- helpers ---------------------------------------------------------------------------
-    def fail(self, node, message):
-        raise self.definition.error(node, message)
-
+    # ---- emission helpers ------------------------------------------------------------------
     def line(self, text: str):
         self.lines.append("  " * self.depth + text)
 
-    def temporary(self, expression: str, dtype: ScalarType) -> _Value:
-        self.counter += 1
-        name = f"t{self.counter}"
-        self.line(f"const {CTYPE[dtype]} {name} = {expression};")
-        return _Value(name, dtype)
-
-    def variable(self, prefix: str) -> str:
+    def fresh(self, prefix: str) -> str:
         self.counter += 1
         return f"{prefix}{self.counter}"
 
+    def temporary(self, expression: str, dtype: ScalarType) -> _Value:
+        name = self.fresh("t")
+        self.line(f"const {CTYPE[dtype]} {name} = {expression};")
+        return _Value(name, dtype)
+
     def typed(self, value, dtype: ScalarType, node) -> _Value:
+        """`value` as a device value of `dtype`: typed values must match, static ones convert."""
         if isinstance(value, _Value):
             if value.dtype != dtype:
                 self.fail(node, f"expected {dtype.name}, got {value.dtype.mlir}; use ckl.cast "
                                 "explicitly")
             return value
-        if not _static(value):
+        if not is_static(value):
             self.fail(node, f"expected a {dtype.name} scalar")
         return _Value(_literal(constant(value, dtype, self.definition, node), dtype), dtype)
 
-    # -- expressions -----------------------------------------------------------------------
-    def expression(self, node):
-        if isinstance(node, ast.Constant) and type(node.value) in (int, float, bool):
-            if type(node.value) is float and not math.isfinite(node.value):
-                self.fail(node, "non-finite source constants are unsupported")
-            return node.value
-        if isinstance(node, ast.Name):
-            if node.id in self.env:
-                return self.env[node.id]
-            if node.id in self.local_names:
-                self.fail(node, f"local '{node.id}' is not defined on this path")
-            if node.id not in self.definition.bindings:
-                self.fail(node, f"unknown name '{node.id}'")
-            captured = self.definition.bindings[node.id]
-            if isinstance(captured, UnsupportedBinding):
-                self.fail(node, f"unsupported captured binding '{node.id}'")
-            if isinstance(captured, Dimension):
-                if captured.name not in self.dimensions:
-                    self.fail(node, f"unbound dimension '{captured.name}'")
-                return self.dimensions[captured.name]
-            return captured
-        if isinstance(node, ast.Tuple):
-            return tuple(self.expression(item) for item in node.elts)
-        if isinstance(node, ast.Attribute):
-            base = self.expression(node.value)
-            if isinstance(base, Namespace) and node.attr in base.values:
-                return base.values[node.attr]
-            if isinstance(base, _Buffer):
-                if node.attr == "shape":
-                    return base.spec.shape
-                if node.attr == "dtype":
-                    return base.spec.dtype
-            self.fail(node, f"unsupported attribute '{node.attr}'")
-        if isinstance(node, ast.Subscript):
-            base = self.expression(node.value)
-            if isinstance(base, _Buffer):
-                offset = self.offset(base, node)
-                return self.temporary(f"{base.code}[{offset}]", base.spec.dtype)
-            if type(base) is tuple:
-                position = self.expression(node.slice)
-                if type(position) is not int or not 0 <= position < len(base):
-                    self.fail(node, "tuple/shape axes require an in-range nonnegative "
-                                    "compile-time integer")
-                return base[position]
-            self.fail(node, "unsupported subscript; slices and negative indexing are not "
-                            "supported")
-        if isinstance(node, ast.BinOp):
-            return self.binary(node.left, node.right, node.op, node, comparison=False)
-        if isinstance(node, ast.UnaryOp) and isinstance(node.op, (ast.USub, ast.UAdd)):
-            value = self.expression(node.operand)
-            if type(value) in (int, float):
-                return -value if isinstance(node.op, ast.USub) else value
-            if not isinstance(value, _Value) or value.dtype == bool_:
-                self.fail(node, "unary arithmetic requires a numeric scalar")
-            if isinstance(node.op, ast.UAdd):
-                return value
-            if value.dtype in (f32, f64):
-                return self.temporary(f"-{value.code}", value.dtype)
-            return self.arith(_literal(0, value.dtype), value.code, "-", value.dtype)
-        if isinstance(node, ast.Compare):
-            if len(node.ops) != 1:
-                self.fail(node, "chained comparisons are not supported")
-            return self.binary(node.left, node.comparators[0], node.ops[0], node, comparison=True)
-        if isinstance(node, ast.Call):
-            return self.call(node)
-        self.fail(node, f"unsupported expression: {type(node).__name__}")
-
-    def offset(self, buffer: _Buffer, node: ast.Subscript) -> str:
-        items = node.slice.elts if isinstance(node.slice, ast.Tuple) else [node.slice]
-        shape = buffer.spec.shape
-        if len(items) != len(shape):
-            self.fail(node, "requires one index per buffer dimension")
-        linear = None
-        for axis, item in enumerate(items):
-            value = self.expression(item)
-            if type(value) is int and not 0 <= value < shape[axis]:
-                self.fail(item, f"constant index is out of bounds for dimension {axis}")
-            code = self.typed(value, index, item).code
-            linear = code if linear is None else f"({linear}) * {shape[axis]}LL + {code}"
-        return linear
+    def nested(self, body) -> None:
+        self.depth += 1
+        self.walk(body)
+        self.depth -= 1
 
     def arith(self, left: str, right: str, symbol: str, dtype: ScalarType) -> _Value:
-        if dtype in (f32, f64):
-            suffix = "f" if dtype == f32 else "d"
-            name = {"+": "add", "-": "sub", "*": "mul", "/": "div"}[symbol]
-            return self.temporary(f"__{suffix}{name}_rn({left}, {right})", dtype)
-        if dtype == i32:
-            return self.temporary(f"(int)((unsigned)({left}) {symbol} (unsigned)({right}))", dtype)
-        return self.temporary(
-            f"(long long)((unsigned long long)({left}) {symbol} (unsigned long long)({right}))",
-            dtype)
+        if dtype in _FLOATS:
+            operation = {"+": "add", "-": "sub", "*": "mul", "/": "div"}[symbol]
+            return self.temporary(f"__{'f' if dtype == f32 else 'd'}{operation}_rn({left}, {right})",
+                                  dtype)
+        unsigned = "unsigned" if dtype == i32 else "unsigned long long"
+        return self.temporary(f"({CTYPE[dtype]})(({unsigned})({left}) {symbol} "
+                              f"({unsigned})({right}))", dtype)
 
-    def binary(self, left_node, right_node, op, node, *, comparison: bool):
-        left, right = self.expression(left_node), self.expression(right_node)
-        symbols = {ast.Add: "+", ast.Sub: "-", ast.Mult: "*", ast.Div: "/", ast.Lt: "<",
-                   ast.LtE: "<=", ast.Gt: ">", ast.GtE: ">=", ast.Eq: "==", ast.NotEq: "!="}
-        if type(op) not in symbols:
-            self.fail(node, f"unsupported numeric operator: {type(op).__name__}")
-        symbol = symbols[type(op)]
-        if not isinstance(left, _Value) and not isinstance(right, _Value):
-            allowed = (int, float, bool) if comparison else (int, float)
-            if type(left) not in allowed or type(right) not in allowed:
-                self.fail(node, "numeric expressions require scalar operands")
-            try:
-                result = {"+": lambda a, b: a + b, "-": lambda a, b: a - b,
-                          "*": lambda a, b: a * b, "/": lambda a, b: a / b,
-                          "<": lambda a, b: a < b, "<=": lambda a, b: a <= b,
-                          ">": lambda a, b: a > b, ">=": lambda a, b: a >= b,
-                          "==": lambda a, b: a == b, "!=": lambda a, b: a != b}[symbol](left, right)
-            except (ZeroDivisionError, OverflowError) as error:
-                self.fail(node, f"invalid constant expression: {error}")
-            if type(result) is float and not math.isfinite(result):
-                self.fail(node, "non-finite constant expression")
-            return result
-        dynamic = left if isinstance(left, _Value) else right
-        dtype = dynamic.dtype
-        if dtype == bool_ and symbol not in ("==", "!="):
+    def linear_index(self, buffer: _Buffer, node: ast.Subscript) -> str:
+        indices = node.slice.elts if isinstance(node.slice, ast.Tuple) else [node.slice]
+        extents = buffer.spec.shape
+        if len(indices) != len(extents):
+            self.fail(node, "requires one index per buffer dimension")
+        code = None
+        for axis, (item, extent) in enumerate(zip(indices, extents)):
+            value = self.evaluate(item)
+            if type(value) is int and not 0 <= value < extent:
+                self.fail(item, f"constant index is out of bounds for dimension {axis}")
+            term = self.typed(value, index, item).code
+            code = term if code is None else f"({code}) * {extent}LL + {term}"
+        return code
+
+    # ---- walker hooks ----------------------------------------------------------------------
+    def is_dynamic(self, value) -> bool:
+        return isinstance(value, _Value)
+
+    def buffer_spec(self, value):
+        return value.spec if isinstance(value, _Buffer) else None
+
+    def read_element(self, buffer, node):
+        return self.temporary(f"{buffer.code}[{self.linear_index(buffer, node)}]",
+                              buffer.spec.dtype)
+
+    def dynamic_binary(self, left, right, op, node, comparison):
+        anchor = left if isinstance(left, _Value) else right
+        if not isinstance(anchor, _Value):
+            self.fail(node, "numeric expressions require scalar operands")
+        symbol = SPELLINGS[type(op)]
+        if anchor.dtype == bool_ and symbol not in ("==", "!="):
             self.fail(node, "numeric expressions require compatible scalar types")
-        left, right = self.typed(left, dtype, node), self.typed(right, dtype, node)
+        a, b = self.typed(left, anchor.dtype, node), self.typed(right, anchor.dtype, node)
         if comparison:
-            return self.temporary(f"{left.code} {symbol} {right.code}", bool_)
-        if symbol == "/" and dtype not in (f32, f64):
+            return self.temporary(f"{a.code} {symbol} {b.code}", bool_)
+        if symbol == "/" and anchor.dtype not in _FLOATS:
             self.fail(node, "division requires floating operands")
-        return self.arith(left.code, right.code, symbol, dtype)
+        return self.arith(a.code, b.code, symbol, anchor.dtype)
 
-    def call(self, node: ast.Call):
-        callee = self.expression(node.func)
-        if isinstance(callee, Definition):
-            self.fail(node, "kernel definitions are not ordinary calls; use ckl.launch")
-        if not isinstance(callee, Intrinsic):
-            self.fail(node, "calling arbitrary Python functions is unsupported")
-        if any(isinstance(a, ast.Starred) for a in node.args) or any(k.arg is None
-                                                                     for k in node.keywords):
-            self.fail(node, "argument expansion is unsupported")
-        name = callee.name
-        if name == "launch":
-            self.fail(node, "kernels cannot launch other kernels")
-        args = [self.expression(a) for a in node.args]
-        keywords = {k.arg: self.expression(k.value) for k in node.keywords}
-        if name in ("global_id",) + tuple(_COORDINATES):
-            if len(args) != 1 or keywords or type(args[0]) is not int or not 0 <= args[0] <= 2:
-                self.fail(node, "device coordinates require one constant axis 0, 1, or 2")
-            axis = _AXES[args[0]]
-            if name == "global_id":
-                return self.temporary(f"(long long)blockIdx.{axis} * (long long)blockDim.{axis} "
-                                      f"+ (long long)threadIdx.{axis}", index)
-            return self.temporary(f"(long long){_COORDINATES[name]}.{axis}", index)
-        if name == "cdiv":
-            if len(args) != 2 or keywords or any(type(v) is not int for v in args) \
-                    or args[0] < 0 or args[1] <= 0:
-                self.fail(node, "cdiv requires a nonnegative constant extent and positive constant "
-                                "divisor")
-            return (args[0] + args[1] - 1) // args[1]
-        if name in ("empty", "empty_like"):
-            self.fail(node, "program temporaries cannot be allocated inside kernels")
-        if name == "subview":
-            self.fail(node, "subview is currently supported only in programs")
-        if name == "cast":
-            if len(args) != 2 or keywords or not isinstance(args[1], ScalarType):
-                self.fail(node, "use cast(value, scalar_type)")
-            return self.cast(args[0], args[1], node)
-        if name in ("exp", "rsqrt"):
-            if len(args) != 1 or keywords or not isinstance(args[0], _Value) \
-                    or args[0].dtype not in (f32, f64):
-                self.fail(node, f"{name} requires one typed floating-point scalar")
-            suffix = "f" if args[0].dtype == f32 else ""
-            return self.temporary(f"{name}{suffix}({args[0].code})", args[0].dtype)
-        if name == "select":
-            if len(args) != 3 or keywords:
-                self.fail(node, "use select(predicate, true_value, false_value)")
-            condition = self.typed(args[0], bool_, node)
-            dynamic = next((v for v in args[1:] if isinstance(v, _Value)), None)
-            if dynamic is None:
-                self.fail(node, "select requires a typed scalar alternative")
-            lhs, rhs = [self.typed(v, dynamic.dtype, node) for v in args[1:]]
-            return self.temporary(f"{condition.code} ? {lhs.code} : {rhs.code}", lhs.dtype)
-        self.fail(node, f"unsupported intrinsic: {name}")
-
-    def cast(self, value, dtype: ScalarType, node):
-        if not isinstance(value, _Value):
-            if dtype in (i32, i64, index) and type(value) is float and math.isfinite(value):
-                value = int(value)
-            return constant(value, dtype, self.definition, node)
-        source = value.dtype
-        if source == dtype:
+    def dynamic_unary(self, value, op, node):
+        if not isinstance(value, _Value) or value.dtype == bool_:
+            self.fail(node, "unary arithmetic requires a numeric scalar")
+        if isinstance(op, ast.UAdd):
             return value
-        if bool_ in (source, dtype):
-            self.fail(node, "boolean/buffer casts are unsupported")
-        floats, integers = (f32, f64), (i32, i64)
-        if source in floats and dtype in floats:
-            expression = f"(double)({value.code})" if dtype == f64 \
-                else f"__double2float_rn({value.code})"
-        elif source in integers and dtype in integers:
-            expression = f"(long long)({value.code})" if dtype == i64 \
-                else f"(int)(unsigned)({value.code})"
-        elif source in floats and dtype in integers:
-            expression = f"({CTYPE[dtype]})({value.code})"
-        elif source in integers and dtype in floats:
-            expression = f"({CTYPE[dtype]})({value.code})"
-        elif index in (source, dtype) and (source in integers or dtype in integers):
-            expression = f"(long long)({value.code})" if dtype == index or dtype == i64 \
-                else f"(int)(unsigned)({value.code})"
-        else:
-            self.fail(node, "cast through an integer type to convert between index and float")
-        return self.temporary(expression, dtype)
+        if value.dtype in _FLOATS:
+            return self.temporary(f"-{value.code}", value.dtype)
+        return self.arith(_literal(0, value.dtype), value.code, "-", value.dtype)
 
-    # -- statements ------------------------------------------------------------------------
-    def statements(self, nodes, *, top=False, branch_outer=None):
-        for position, node in enumerate(nodes):
-            if isinstance(node, ast.Return):
-                if not top or position != len(nodes) - 1 or node.value is not None:
-                    self.fail(node, "only a final bare return is supported; buffers carry outputs")
-            elif isinstance(node, ast.Assign):
-                if len(node.targets) != 1:
-                    self.fail(node, "chained assignment is unsupported")
-                target = node.targets[0]
-                value = self.expression(node.value)
-                if isinstance(target, ast.Name):
-                    if branch_outer is not None and target.id in branch_outer:
-                        self.fail(target, "runtime branch results are deferred; write buffers or "
-                                          "use branch-local variables")
-                    old = self.env.get(target.id)
-                    if isinstance(old, _Value):
-                        value = self.typed(value, old.dtype, node.value)
-                    self.env[target.id] = value
-                elif isinstance(target, ast.Subscript):
-                    buffer = self.expression(target.value)
-                    if not isinstance(buffer, _Buffer):
-                        self.fail(target, "expected a typed buffer")
-                    offset = self.offset(buffer, target)
-                    stored = self.typed(value, buffer.spec.dtype, node.value)
-                    self.line(f"{buffer.code}[{offset}] = {stored.code};")
-                else:
-                    self.fail(target, "assignment requires a local name or indexed buffer element")
-            elif isinstance(node, ast.If):
-                predicate = self.expression(node.test)
-                if type(predicate) is bool:
-                    self.statements(node.body if predicate else node.orelse,
-                                    branch_outer=branch_outer)
-                    continue
-                if not isinstance(predicate, _Value) or predicate.dtype != bool_:
-                    self.fail(node.test, "if requires a boolean predicate; program control flow "
-                                         "must be compile-time")
-                outer = dict(self.env)
-                self.line(f"if ({predicate.code}) {{")
-                self.depth += 1
-                self.statements(node.body, branch_outer=set(outer))
-                self.depth -= 1
-                self.env = dict(outer)
-                if node.orelse:
-                    self.line("} else {")
-                    self.depth += 1
-                    self.statements(node.orelse, branch_outer=set(outer))
-                    self.depth -= 1
-                self.line("}")
-                self.env = outer
-            elif isinstance(node, ast.For):
-                self.loop(node, branch_outer)
-            elif isinstance(node, ast.Expr):
-                if isinstance(node.value, ast.Constant) and isinstance(node.value.value, str) \
-                        and position == 0 and top:
-                    continue
-                if not isinstance(node.value, ast.Call) or self.expression(node.value) is not None:
-                    self.fail(node, "expression statements must be kernel launches")
-            elif isinstance(node, ast.Pass):
-                continue
-            else:
-                self.fail(node, f"unsupported statement: {type(node).__name__}")
+    def assign_local(self, target, value, node):
+        if self.branch_outer is not None and target.id in self.branch_outer:
+            self.fail(target, "runtime branch results are deferred; write buffers or use "
+                              "branch-local variables")
+        previous = self.env.get(target.id)
+        if isinstance(previous, _Value):  # a typed local keeps its type
+            value = self.typed(value, previous.dtype, node.value)
+        self.env[target.id] = value
 
-    def loop(self, node: ast.For, branch_outer):
-        if node.orelse or not isinstance(node.target, ast.Name) \
-                or not isinstance(node.iter, ast.Call):
-            self.fail(node, "for requires a simple induction variable and range without else")
-        callee = self.expression(node.iter.func)
-        if not isinstance(callee, Intrinsic) or callee.name != "range" or node.iter.keywords:
-            self.fail(node, "for requires range(start, stop, positive_constant_step)")
-        bounds = [self.expression(a) for a in node.iter.args]
-        if not 1 <= len(bounds) <= 3:
-            self.fail(node, "range requires one to three bounds")
-        start, stop, step = (0, bounds[0], 1) if len(bounds) == 1 else (
-            bounds[0], bounds[1], bounds[2] if len(bounds) == 3 else 1)
-        if type(step) is not int or step <= 0:
-            self.fail(node, "range step must be a positive compile-time integer")
-        induction = node.target.id
-        outer = dict(self.env)
-        assignments = {n.id for statement in node.body for n in ast.walk(statement)
-                       if isinstance(n, ast.Name) and isinstance(n.ctx, ast.Store)}
-        if induction in assignments:
+    def assign_element(self, target, value_node, node):
+        value = self.evaluate(value_node)
+        buffer = self.evaluate(target.value)
+        if not isinstance(buffer, _Buffer):
+            self.fail(target, "expected a typed buffer")
+        where = self.linear_index(buffer, target)
+        stored = self.typed(value, buffer.spec.dtype, value_node)
+        self.line(f"{buffer.code}[{where}] = {stored.code};")
+
+    def runtime_branch(self, node, predicate):
+        if not isinstance(predicate, _Value) or predicate.dtype != bool_:
+            self.fail(node.test, "if requires a boolean predicate; program control flow must "
+                                 "be compile-time")
+        saved_env, saved_outer = dict(self.env), self.branch_outer
+        self.branch_outer = set(saved_env)
+        self.line(f"if ({predicate.code}) {{")
+        self.nested(node.body)
+        self.env = dict(saved_env)
+        if node.orelse:
+            self.line("} else {")
+            self.nested(node.orelse)
+        self.line("}")
+        self.env, self.branch_outer = saved_env, saved_outer
+
+    def loop(self, node, induction, start, stop, step):
+        reassigned = {n.id for statement in node.body for n in ast.walk(statement)
+                      if isinstance(n, ast.Name) and isinstance(n.ctx, ast.Store)}
+        if induction in reassigned:
             self.fail(node, "cannot assign to the loop induction variable")
-        names = sorted(assignments & outer.keys())
-        initials = []
-        for name in names:
-            if branch_outer is not None and name in branch_outer:
+        saved = dict(self.env)
+        # Outer names the body reassigns are carried through the loop (scf.for iteration
+        # arguments); static initial values take f32 / i32 / bool.
+        carried_names = sorted(reassigned & saved.keys())
+        initial = []
+        for name in carried_names:
+            if self.branch_outer is not None and name in self.branch_outer:
                 self.fail(node, "runtime branch results are deferred")
-            value = outer[name]
+            value = saved[name]
             if not isinstance(value, _Value):
-                dtype = f32 if type(value) is float else i32 if type(value) is int else bool_
-                value = self.typed(value, dtype, node)
-            initials.append(value)
-        lower, upper = self.typed(start, index, node), self.typed(stop, index, node)
+                value = self.typed(value, {float: f32, int: i32}.get(type(value), bool_), node)
+            initial.append(value)
+        low, high = self.typed(start, index, node), self.typed(stop, index, node)
         carried = []
-        for name, initial in zip(names, initials):
-            variable = self.variable("c")
-            self.line(f"{CTYPE[initial.dtype]} {variable} = {initial.code};")
-            carried.append(_Value(variable, initial.dtype))
-        counter = self.variable("i")
-        self.line(f"for (long long {counter} = {lower.code}; {counter} < {upper.code}; "
+        for value in initial:
+            variable = self.fresh("c")
+            self.line(f"{CTYPE[value.dtype]} {variable} = {value.code};")
+            carried.append(_Value(variable, value.dtype))
+        counter = self.fresh("i")
+        self.line(f"for (long long {counter} = {low.code}; {counter} < {high.code}; "
                   f"{counter} += {step}LL) {{")
         self.depth += 1
         self.env[induction] = _Value(counter, index)
-        for name, value in zip(names, carried):
-            self.env[name] = value
-        self.statements(node.body, branch_outer=branch_outer)
-        yielded = [self.typed(self.env[name], value.dtype, node) for name, value in
-                   zip(names, carried)]
-        staged = [self.temporary(v.code, v.dtype) if v.code != c.code else v
-                  for v, c in zip(yielded, carried)]
-        for value, variable in zip(staged, carried):
-            if value.code != variable.code:
-                self.line(f"{variable.code} = {value.code};")
+        self.env.update(zip(carried_names, carried))
+        self.walk(node.body)
+        results = [self.typed(self.env[name], slot.dtype, node)
+                   for name, slot in zip(carried_names, carried)]
+        # Stage every new value before any carried variable is overwritten.
+        staged = [value if value.code == slot.code else self.temporary(value.code, value.dtype)
+                  for value, slot in zip(results, carried)]
+        for value, slot in zip(staged, carried):
+            if value.code != slot.code:
+                self.line(f"{slot.code} = {value.code};")
         self.depth -= 1
         self.line("}")
-        self.env = outer
-        for name, value in zip(names, carried):
-            self.env[name] = value
+        self.env = saved
+        self.env.update(zip(carried_names, carried))
+
+    # ---- intrinsics ------------------------------------------------------------------------
+    def _coordinate(self, node, name):
+        values, keywords = self.arguments(node)
+        if keywords or len(values) != 1 or type(values[0]) is not int or values[0] not in (0, 1, 2):
+            self.fail(node, "device coordinates require one constant axis 0, 1, or 2")
+        axis = "xyz"[values[0]]
+        if name == "global_id":
+            return self.temporary(f"(long long)blockIdx.{axis} * (long long)blockDim.{axis} + "
+                                  f"(long long)threadIdx.{axis}", index)
+        return self.temporary(f"(long long){_COORDINATES[name]}.{axis}", index)
+
+    def intrinsic_global_id(self, node):
+        return self._coordinate(node, "global_id")
+
+    def intrinsic_thread_id(self, node):
+        return self._coordinate(node, "thread_id")
+
+    def intrinsic_block_id(self, node):
+        return self._coordinate(node, "block_id")
+
+    def intrinsic_block_dim(self, node):
+        return self._coordinate(node, "block_dim")
+
+    def intrinsic_grid_dim(self, node):
+        return self._coordinate(node, "grid_dim")
+
+    def intrinsic_launch(self, node):
+        self.fail(node, "kernels cannot launch other kernels")
+
+    def _program_only(self, node):
+        self.arguments(node)
+        self.fail(node, "program temporaries cannot be allocated inside kernels")
+
+    intrinsic_empty = intrinsic_empty_like = _program_only
+
+    def intrinsic_subview(self, node):
+        self.arguments(node)
+        self.fail(node, "subview is currently supported only in programs")
+
+    def intrinsic_cast(self, node):
+        values, keywords = self.arguments(node)
+        if keywords or len(values) != 2 or not isinstance(values[1], ScalarType):
+            self.fail(node, "use cast(value, scalar_type)")
+        value, target = values
+        if not isinstance(value, _Value):
+            if target in (i32, i64, index) and type(value) is float and math.isfinite(value):
+                value = int(value)
+            return constant(value, target, self.definition, node)
+        if value.dtype == target:
+            return value
+        if bool_ in (value.dtype, target):
+            self.fail(node, "boolean/buffer casts are unsupported")
+        expression = _conversion(value.dtype, target, value.code)
+        if expression is None:
+            self.fail(node, "cast through an integer type to convert between index and float")
+        return self.temporary(expression, target)
+
+    def _unary_math(self, node, name):
+        values, keywords = self.arguments(node)
+        if keywords or len(values) != 1 or not isinstance(values[0], _Value) \
+                or values[0].dtype not in _FLOATS:
+            self.fail(node, f"{name} requires one typed floating-point scalar")
+        suffix = "f" if values[0].dtype == f32 else ""
+        return self.temporary(f"{name}{suffix}({values[0].code})", values[0].dtype)
+
+    def intrinsic_exp(self, node):
+        return self._unary_math(node, "exp")
+
+    def intrinsic_rsqrt(self, node):
+        return self._unary_math(node, "rsqrt")
+
+    def intrinsic_select(self, node):
+        values, keywords = self.arguments(node)
+        if keywords or len(values) != 3:
+            self.fail(node, "use select(predicate, true_value, false_value)")
+        condition = self.typed(values[0], bool_, node)
+        anchor = next((v for v in values[1:] if isinstance(v, _Value)), None)
+        if anchor is None:
+            self.fail(node, "select requires a typed scalar alternative")
+        chosen, other = (self.typed(v, anchor.dtype, node) for v in values[1:])
+        return self.temporary(f"{condition.code} ? {chosen.code} : {other.code}", chosen.dtype)
 
 
 def symbol_for(definition: Definition, identity: str) -> str:
@@ -476,7 +376,7 @@ _GENERATED: dict = {}
 
 def _generate(definition: Definition, signature: BoundSignature, symbol: str) -> GeneratedKernel:
     emitter = _Emitter(definition, signature)
-    emitter.statements(definition.tree.body, top=True)
+    emitter.walk(definition.tree.body, top=True)
     parameters = []
     for code, dtype in emitter.parameters:
         if isinstance(dtype, BufferSpec):

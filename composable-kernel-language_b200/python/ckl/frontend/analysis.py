@@ -25,8 +25,8 @@ from dataclasses import dataclass, field
 
 from ..types import (BufferSpec, BufferType, ConstexprType, Dimension, ScalarType, f32, f64,
                      i32, i64, index)
-from .checker import BoundSignature, annotation_of
-from .source import Definition, Intrinsic, Namespace, UnsupportedBinding
+from .checker import BoundSignature, parameter_type
+from .source import Definition, Intrinsic, ModuleView, Opaque
 
 READ, WRITE, ALLOCATE, FREE = 1, 2, 4, 8
 WHOLE = "whole"
@@ -101,7 +101,7 @@ class _EffectWalker:
             bound = self.definition.bindings.get(node.id)
             if bound is None:
                 self.fail(node, f"unknown name '{node.id}'")
-            if isinstance(bound, UnsupportedBinding):
+            if isinstance(bound, Opaque):
                 self.fail(node, f"unsupported captured binding '{node.id}'")
             if isinstance(bound, Dimension):
                 if bound.name not in self.dims:
@@ -112,7 +112,7 @@ class _EffectWalker:
             return tuple(self.value(item) for item in node.elts)
         if isinstance(node, ast.Attribute):
             base = self.value(node.value)
-            if isinstance(base, Namespace) and node.attr in base.values:
+            if isinstance(base, ModuleView) and node.attr in base.values:
                 return base.values[node.attr]
             if isinstance(base, _BufferParam):
                 if node.attr == "shape":
@@ -281,7 +281,7 @@ _SKIPPED_FIELDS = {"ctx", "type_comment", "lineno", "col_offset", "end_lineno",
 
 
 def _parameter_descriptor(definition: Definition, argument: ast.arg, dims: dict) -> list:
-    annotation = annotation_of(definition, argument)
+    annotation = parameter_type(definition, argument)
     if isinstance(annotation, BufferType):
         shape = []
         for extent in annotation.shape:
@@ -302,7 +302,7 @@ class _Canonicalizer:
         self.buffer_dims: dict[str, list] = {}
         self.dims: dict[str, str] = {}
         for i, argument in enumerate(arguments):
-            annotation = annotation_of(definition, argument)
+            annotation = parameter_type(definition, argument)
             if isinstance(annotation, BufferType):
                 tokens = []
                 for axis, extent in enumerate(annotation.shape):
@@ -323,7 +323,7 @@ class _Canonicalizer:
         bound = self.definition.bindings.get(identifier)
         if isinstance(bound, Dimension):
             return ["dim", self.dims.get(bound.name, "free:" + bound.name)]
-        if isinstance(bound, Namespace):
+        if isinstance(bound, ModuleView):
             return ["ckl"]
         if isinstance(bound, Intrinsic):
             return ["intrinsic", bound.name]
@@ -342,7 +342,7 @@ class _Canonicalizer:
         if isinstance(node, ast.Attribute):
             base = node.value
             if isinstance(base, ast.Name) and isinstance(self.definition.bindings.get(base.id),
-                                                          Namespace) and base.id not in self.params:
+                                                          ModuleView) and base.id not in self.params:
                 bound = self.definition.bindings[base.id].values.get(node.attr)
                 if isinstance(bound, Intrinsic):
                     return ["intrinsic", bound.name]

@@ -1,9 +1,13 @@
-"""Resolve restricted annotations and bind a concrete specialization of a definition.
+"""Parameter types of a definition and the binding of one concrete specialization.
 
-Semantics of the reference checker (``python/ckl/frontend/checker.py:89-142``): every
-parameter is annotated; ``constexpr`` parameters take a compile-time constant and never a
-runtime signature entry; buffers must match dtype and rank and bind every named dimension
-consistently; scalars must match exactly; definitions return nothing.
+Rules (the reference checker's public behaviour, ``python/ckl/frontend/checker.py``): every
+parameter is annotated with a CKL type; a ``constexpr[...]`` parameter takes a compile-time
+constant from ``constants`` and never appears in the runtime signature; a buffer parameter
+takes a :class:`BufferSpec` of the declared element type and rank, whose extents equal the
+declared fixed extents and bind each named :class:`Dimension` to one value across all
+parameters; a scalar parameter takes exactly its declared scalar type; definitions return
+nothing.  Python constants handed to typed slots must fit the type (integers by range, floats
+finite after rounding to the target precision).
 """
 from __future__ import annotations
 
@@ -15,63 +19,112 @@ from dataclasses import dataclass
 
 from ..types import (Buffer, BufferSpec, BufferType, ConstexprType, Dimension, NUMERIC_TYPES,
                      ScalarType, bool_, constexpr, f32, f64, i32, i64, index)
-from .source import Definition, Namespace, UnsupportedBinding
+from .source import Definition, ModuleView, Opaque
+
+_UNFIT = object()
 
 
-def resolve(node: ast.AST, definition: Definition) -> object:
-    """Evaluate an annotation expression against the definition's captured bindings."""
-    if isinstance(node, ast.Constant) and type(node.value) in (str, int, float, bool, type(None)):
-        if isinstance(node.value, str):
-            return resolve(ast.parse(node.value, mode="eval").body, definition)
-        return node.value
-    if isinstance(node, ast.Name):
-        if node.id not in definition.bindings:
-            raise definition.error(node, f"unknown captured name '{node.id}'")
-        value = definition.bindings[node.id]
-        if isinstance(value, UnsupportedBinding):
-            raise definition.error(node, f"unsupported captured binding '{node.id}'")
-        return value
-    if isinstance(node, ast.Attribute):
-        base = resolve(node.value, definition)
-        if isinstance(base, Namespace) and node.attr in base.values:
-            return base.values[node.attr]
-    if isinstance(node, ast.Tuple):
-        return tuple(resolve(item, definition) for item in node.elts)
-    if isinstance(node, ast.Subscript):
-        base = resolve(node.value, definition)
-        arguments = resolve(node.slice, definition)
+class _AnnotationEvaluator(ast.NodeVisitor):
+    """Evaluates an annotation expression against a definition's frozen scope: names, ``ckl.``
+    attributes, tuples, literals, ``Buffer[...]`` and ``constexpr[...]``."""
+
+    def __init__(self, definition: Definition):
+        self.definition = definition
+
+    def generic_visit(self, node):
+        raise self.definition.error(node, "unsupported annotation; use CKL types and shape "
+                                          "declarations")
+
+    def visit_Expression(self, node):
+        return self.visit(node.body)
+
+    def visit_Constant(self, node):
+        if isinstance(node.value, str):  # a quoted annotation: evaluate its text
+            return self.visit(ast.parse(node.value, mode="eval"))
+        if type(node.value) in (int, float, bool) or node.value is None:
+            return node.value
+        return self.generic_visit(node)
+
+    def visit_Name(self, node):
+        scope = self.definition.bindings
+        if node.id not in scope:
+            raise self.definition.error(node, f"unknown captured name '{node.id}'")
+        if isinstance(scope[node.id], Opaque):
+            raise self.definition.error(node, f"unsupported captured binding '{node.id}'")
+        return scope[node.id]
+
+    def visit_Attribute(self, node):
+        owner = self.visit(node.value)
+        if isinstance(owner, ModuleView) and node.attr in owner.values:
+            return owner.values[node.attr]
+        return self.generic_visit(node)
+
+    def visit_Tuple(self, node):
+        return tuple(self.visit(item) for item in node.elts)
+
+    def visit_Subscript(self, node):
+        constructor = self.visit(node.value)
+        if constructor is not Buffer and constructor is not constexpr:
+            return self.generic_visit(node)
+        arguments = self.visit(node.slice)
         try:
-            if base is Buffer:
-                return Buffer[arguments]
-            if base is constexpr:
-                return constexpr[arguments]
+            return constructor[arguments]
         except ValueError as error:
-            raise definition.error(node, str(error)) from error
-    raise definition.error(node, "unsupported annotation; use CKL types and shape declarations")
+            raise self.definition.error(node, str(error)) from error
 
 
-def constant(value: object, dtype: ScalarType, definition: Definition, node: ast.AST) -> object:
-    """Check that a Python constant fits ``dtype``; f32 values are rounded to f32."""
-    if dtype == bool_ and type(value) is bool:
-        return value
-    if dtype in (i32, i64, index) and type(value) is int:
-        bits = 32 if dtype == i32 else 64
-        if -(1 << (bits - 1)) <= value < (1 << (bits - 1)):
-            return value
-    if dtype in (f32, f64) and type(value) in (int, float):
+def resolve(node: ast.AST, definition: Definition):
+    """The value of an annotation expression of `definition`."""
+    return _AnnotationEvaluator(definition).visit(node)
+
+
+def parameter_type(definition: Definition, argument: ast.arg):
+    """The CKL type a parameter is annotated with (string annotations resolved here)."""
+    declared = definition.annotations.get(argument.arg)
+    if declared is not None and not isinstance(declared, str):
+        return declared
+    if argument.annotation is None:
+        raise definition.error(argument, "every CKL parameter requires a type annotation")
+    return resolve(argument.annotation, definition)
+
+
+# ---- constants ---------------------------------------------------------------------------
+def _integer_fitter(bits: int):
+    low, high = -(1 << (bits - 1)), 1 << (bits - 1)
+    return lambda value: value if type(value) is int and low <= value < high else _UNFIT
+
+
+def _float_fitter(single: bool):
+    def fit(value):
+        if type(value) not in (int, float):
+            return _UNFIT
         try:
-            converted = float(value)
-            if dtype == f32:
-                converted = struct.unpack("f", struct.pack("f", converted))[0]
-            if math.isfinite(converted):
-                return converted
+            result = float(value)
+            if single:  # round to the nearest float32
+                result = struct.unpack("<f", struct.pack("<f", result))[0]
         except (OverflowError, struct.error):
-            pass
-    shown = repr(value) if type(value) in (int, float, bool, str, type(None)) \
-        else f"<{type(value).__name__}>"
-    raise definition.error(node, f"constant {shown} does not fit {dtype.name}")
+            return _UNFIT
+        return result if math.isfinite(result) else _UNFIT
+    return fit
 
 
+_FITTERS = {bool_: lambda value: value if type(value) is bool else _UNFIT,
+            i32: _integer_fitter(32), i64: _integer_fitter(64), index: _integer_fitter(64),
+            f32: _float_fitter(True), f64: _float_fitter(False)}
+
+
+def constant(value, dtype: ScalarType, definition: Definition, node: ast.AST):
+    """`value` as a compile-time constant of `dtype` (f32 values rounded to float32)."""
+    fitter = _FITTERS.get(dtype)
+    result = fitter(value) if fitter is not None else _UNFIT
+    if result is _UNFIT:
+        shown = repr(value) if type(value) in (int, float, bool, str) or value is None \
+            else f"<{type(value).__name__}>"
+        raise definition.error(node, f"constant {shown} does not fit {dtype.name}")
+    return result
+
+
+# ---- binding -----------------------------------------------------------------------------
 @dataclass(frozen=True)
 class BoundParameter:
     name: str
@@ -90,63 +143,83 @@ class BoundSignature:
         return tuple(p for p in self.parameters if not p.is_constant)
 
 
-def annotation_of(definition: Definition, argument: ast.arg) -> object:
-    annotation = definition.annotations.get(argument.arg)
-    if annotation is None or isinstance(annotation, str):
-        if argument.annotation is None:
-            raise definition.error(argument, "every CKL parameter requires a type annotation")
-        annotation = resolve(argument.annotation, definition)
-    return annotation
+class _Binder:
+    """Accumulates the bound parameters and dimension extents of one specialization."""
+
+    def __init__(self, definition: Definition, signature: Mapping, constants: Mapping):
+        self.definition, self.signature, self.constants = definition, signature, constants
+        self.parameters: list = []
+        self.extents: dict = {}
+
+    def add(self, argument: ast.arg) -> None:
+        declared = parameter_type(self.definition, argument)
+        name = argument.arg
+        if isinstance(declared, ConstexprType):
+            if name in self.signature or name not in self.constants:
+                raise self.definition.error(argument, "constexpr parameters require a constants "
+                                                      "binding, not a runtime signature")
+            value = constant(self.constants[name], declared.dtype, self.definition, argument)
+            self.parameters.append(BoundParameter(name, declared.dtype, value, True))
+            return
+        if name in self.constants or name not in self.signature:
+            raise self.definition.error(argument,
+                                        f"missing or misplaced runtime signature for '{name}'")
+        given = self.signature[name]
+        if isinstance(declared, BufferType):
+            self._buffer(argument, declared, given)
+        elif declared in NUMERIC_TYPES:
+            if not (isinstance(given, ScalarType) and given == declared):
+                raise self.definition.error(argument, f"scalar type mismatch for '{name}'")
+        else:
+            raise self.definition.error(argument, "runtime parameters require numeric scalars "
+                                                  "or typed buffers")
+        self.parameters.append(BoundParameter(name, given))
+
+    def _buffer(self, argument, declared: BufferType, given) -> None:
+        if not isinstance(given, BufferSpec) or given.dtype != declared.dtype \
+                or len(given.shape) != len(declared.shape):
+            raise self.definition.error(argument,
+                                        f"buffer type/rank mismatch for '{argument.arg}'")
+        for axis_type, extent in zip(declared.shape, given.shape):
+            if not isinstance(axis_type, Dimension):
+                if axis_type != extent:
+                    raise self.definition.error(
+                        argument, f"fixed extent {axis_type} does not match {extent}")
+                continue
+            known = self.extents.setdefault(axis_type.name, extent)
+            if known != extent:
+                raise self.definition.error(
+                    argument, f"dimension {axis_type.name} conflicts: {known} versus {extent}")
+
+    def check_result(self) -> None:
+        returns = self.definition.tree.returns
+        if returns is None:
+            return
+        declared = self.definition.annotations.get("return")
+        if isinstance(declared, str):
+            declared = resolve(returns, self.definition)
+        if declared is not None:
+            raise self.definition.error(returns, "CKL entry points have no return values")
+
+    def result(self) -> BoundSignature:
+        return BoundSignature(tuple(self.parameters), tuple(sorted(self.extents.items())))
 
 
 def bind(definition: Definition, signature: Mapping, constants: Mapping) -> BoundSignature:
-    if not isinstance(signature, Mapping) or not isinstance(constants, Mapping):
+    """Bind `definition` to runtime parameter types (`signature`) and compile-time values
+    (`constants`), both keyed by parameter name."""
+    if not (isinstance(signature, Mapping) and isinstance(constants, Mapping)):
         raise definition.error(definition.tree, "signature and constants must be mappings")
-    args = definition.tree.args
-    if args.posonlyargs or args.vararg or args.kwarg or args.kwonlyargs or args.defaults \
-            or args.kw_defaults:
-        raise definition.error(definition.tree,
-                               "CKL definitions require named positional parameters without defaults")
-    names = {a.arg for a in args.args}
-    extra = (set(signature) | set(constants)) - names
-    if extra:
-        raise definition.error(definition.tree, f"unknown specialization arguments: {sorted(extra)}")
-    parameters, dimensions = [], {}
-    for argument in args.args:
-        annotation = annotation_of(definition, argument)
-        name = argument.arg
-        if isinstance(annotation, ConstexprType):
-            if name not in constants or name in signature:
-                raise definition.error(
-                    argument, "constexpr parameters require a constants binding, not a runtime signature")
-            value = constant(constants[name], annotation.dtype, definition, argument)
-            parameters.append(BoundParameter(name, annotation.dtype, value, True))
-            continue
-        if name not in signature or name in constants:
-            raise definition.error(argument, f"missing or misplaced runtime signature for '{name}'")
-        actual = signature[name]
-        if isinstance(annotation, BufferType):
-            if not isinstance(actual, BufferSpec) or actual.dtype != annotation.dtype \
-                    or len(actual.shape) != len(annotation.shape):
-                raise definition.error(argument, f"buffer type/rank mismatch for '{name}'")
-            for declared, extent in zip(annotation.shape, actual.shape):
-                if isinstance(declared, Dimension):
-                    previous = dimensions.setdefault(declared.name, extent)
-                    if previous != extent:
-                        raise definition.error(
-                            argument, f"dimension {declared.name} conflicts: {previous} versus {extent}")
-                elif declared != extent:
-                    raise definition.error(argument, f"fixed extent {declared} does not match {extent}")
-        elif annotation in NUMERIC_TYPES:
-            if not isinstance(actual, ScalarType) or actual != annotation:
-                raise definition.error(argument, f"scalar type mismatch for '{name}'")
-        else:
-            raise definition.error(argument, "runtime parameters require numeric scalars or typed buffers")
-        parameters.append(BoundParameter(name, actual))
-    if definition.tree.returns is not None:
-        returned = definition.annotations.get("return")
-        if isinstance(returned, str):
-            returned = resolve(definition.tree.returns, definition)
-        if returned is not None:
-            raise definition.error(definition.tree.returns, "CKL entry points have no return values")
-    return BoundSignature(tuple(parameters), tuple(sorted(dimensions.items())))
+    spec = definition.tree.args
+    if any((spec.posonlyargs, spec.vararg, spec.kwarg, spec.kwonlyargs, spec.defaults,
+            spec.kw_defaults)):
+        raise definition.error(definition.tree, "CKL definitions require named positional "
+                                                "parameters without defaults")
+    stray = sorted((set(signature) | set(constants)) - {a.arg for a in spec.args})
+    if stray:
+        raise definition.error(definition.tree, f"unknown specialization arguments: {stray}")
+    binder = _Binder(definition, signature, constants)
+    for argument in spec.args:
+        binder.add(argument)
+    binder.check_result()
+    return binder.result()

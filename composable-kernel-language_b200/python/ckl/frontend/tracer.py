@@ -18,28 +18,27 @@ The result is a :class:`LoweredProgram` whose ``trace`` feeds the B200 compiler
 """
 from __future__ import annotations
 
-import ast
 import hashlib
-import json
 import math
-import operator
 from dataclasses import dataclass, field
 
-from ..types import (BufferSpec, ConstexprType, Dimension, NUMERIC_TYPES, ScalarType, bool_,
-                     f32, f64, i32, i64, index)
-from .checker import BoundSignature, annotation_of, bind, constant
-from .source import Definition, Intrinsic, Namespace, UnsupportedBinding, fingerprint
+from ..types import BufferSpec, ConstexprType, ScalarType, i32, i64, index
+from .checker import BoundSignature, bind, constant, parameter_type
+from .source import Definition, describe
+from .walker import BodyWalker
 
 
 def identity(definition: Definition, signature: BoundSignature) -> str:
     """Specialization identity: definition content plus every bound parameter."""
-    payload = [definition.identity, [
-        [p.name,
-         fingerprint(p.dtype) if isinstance(p.dtype, ScalarType)
-         else [list(p.dtype.shape), p.dtype.dtype.name, p.dtype.layout],
-         p.value, p.is_constant]
-        for p in signature.parameters]]
-    return hashlib.sha256(json.dumps(payload, sort_keys=True).encode()).hexdigest()
+    lines = [f"specialization of {definition.identity}"]
+    for p in signature.parameters:
+        if isinstance(p.dtype, ScalarType):
+            kind = describe(p.dtype)
+        else:
+            kind = f"{p.dtype.dtype.name} buffer {tuple(p.dtype.shape)} {p.dtype.layout}"
+        bound = f"constant {p.value!r}" if p.is_constant else "runtime"
+        lines.append(f"{p.name}: {kind} {bound}")
+    return hashlib.sha256("\n".join(lines).encode()).hexdigest()
 
 
 @dataclass(frozen=True)
@@ -160,328 +159,205 @@ class _BufferValue:
     spec: BufferSpec
 
 
-_STATIC_BINARY = {ast.Add: operator.add, ast.Sub: operator.sub, ast.Mult: operator.mul,
-                  ast.Div: operator.truediv, ast.Lt: operator.lt, ast.LtE: operator.le,
-                  ast.Gt: operator.gt, ast.GtE: operator.ge, ast.Eq: operator.eq,
-                  ast.NotEq: operator.ne}
+_RUNTIME_SCALAR = ("computed runtime host scalars are unsupported; forward the parameter "
+                   "unchanged")
 
 
-class ProgramTracer:
+class ProgramTracer(BodyWalker):
+    """Walks a program body at compile time: loops unroll, branches must be static, buffers
+    are program resources, and every launch becomes a dispatch of a kernel specialization."""
+
     def __init__(self, definition: Definition, signature: BoundSignature):
-        self.definition = definition
+        super().__init__(definition, signature.dimensions)
         self.signature = signature
-        self.dims = dict(signature.dimensions)
-        self.env: dict[str, object] = {}
         self.resources: list[Resource] = []
         self.events: list[Event] = []
         self.temporaries: list[int] = []
         self.specializations: dict[str, Specialization] = {}
-        self.local_names = {p.name for p in signature.parameters} | {
-            n.id for n in ast.walk(definition.tree)
-            if isinstance(n, ast.Name) and isinstance(n.ctx, ast.Store)}
-        position = 0
-        for parameter in signature.parameters:
-            if parameter.is_constant:
-                self.env[parameter.name] = parameter.value
-                continue
+        for position, parameter in enumerate(signature.runtime):
             if isinstance(parameter.dtype, BufferSpec):
                 resource = self._resource("argument", parameter.dtype, argument=position,
                                           name=f"arg{position}")
                 self.env[parameter.name] = _BufferValue(resource, parameter.dtype)
             else:
                 self.env[parameter.name] = _Runtime(position, parameter.dtype)
-            position += 1
+        self.env.update((p.name, p.value) for p in signature.parameters if p.is_constant)
 
     def _resource(self, kind, spec, **fields) -> int:
         rid = len(self.resources)
         self.resources.append(Resource(rid, kind, spec, **fields))
         return rid
 
-    def fail(self, node, message):
-        raise self.definition.error(node, message)
+    # ---- walker hooks ----------------------------------------------------------------------
+    def is_dynamic(self, value) -> bool:
+        return isinstance(value, _Runtime)
 
-    def location(self, node) -> str:
-        line = self.definition.first_line + getattr(node, "lineno", 1) - 1
-        column = self.definition.indentation + getattr(node, "col_offset", 0) + 1
-        return f"{self.definition.filename}:{line}:{column}"
+    def buffer_spec(self, value):
+        return value.spec if isinstance(value, _BufferValue) else None
 
-    # -- expressions ---------------------------------------------------------------------
-    def expression(self, node):
-        if isinstance(node, ast.Constant) and type(node.value) in (int, float, bool):
-            if type(node.value) is float and not math.isfinite(node.value):
-                self.fail(node, "non-finite source constants are unsupported")
-            return node.value
-        if isinstance(node, ast.Name):
-            if node.id in self.env:
-                return self.env[node.id]
-            if node.id in self.local_names:
-                self.fail(node, f"local '{node.id}' is not defined on this path")
-            if node.id not in self.definition.bindings:
-                self.fail(node, f"unknown name '{node.id}'")
-            bound = self.definition.bindings[node.id]
-            if isinstance(bound, UnsupportedBinding):
-                self.fail(node, f"unsupported captured binding '{node.id}'")
-            if isinstance(bound, Dimension):
-                if bound.name not in self.dims:
-                    self.fail(node, f"unbound dimension '{bound.name}'")
-                return self.dims[bound.name]
-            return bound
-        if isinstance(node, ast.Tuple):
-            return tuple(self.expression(item) for item in node.elts)
-        if isinstance(node, ast.Attribute):
-            base = self.expression(node.value)
-            if isinstance(base, Namespace) and node.attr in base.values:
-                return base.values[node.attr]
-            if isinstance(base, _BufferValue):
-                if node.attr == "shape":
-                    return base.spec.shape
-                if node.attr == "dtype":
-                    return base.spec.dtype
-            self.fail(node, f"unsupported attribute '{node.attr}'")
-        if isinstance(node, ast.Subscript):
-            base = self.expression(node.value)
-            if isinstance(base, _BufferValue):
-                self.fail(node, "buffer contents can only be accessed inside a kernel")
-            if type(base) is tuple:
-                position = self.expression(node.slice)
-                if type(position) is not int or not 0 <= position < len(base):
-                    self.fail(node, "tuple/shape axes require an in-range nonnegative "
-                                    "compile-time integer")
-                return base[position]
-            self.fail(node, "unsupported subscript; slices and negative indexing are not supported")
-        if isinstance(node, (ast.BinOp, ast.Compare)):
-            comparison = isinstance(node, ast.Compare)
-            if comparison and len(node.ops) != 1:
-                self.fail(node, "chained comparisons are not supported")
-            left = self.expression(node.left)
-            right = self.expression(node.comparators[0] if comparison else node.right)
-            op = node.ops[0] if comparison else node.op
-            if type(op) not in _STATIC_BINARY:
-                self.fail(node, f"unsupported numeric operator: {type(op).__name__}")
-            allowed = (int, float, bool) if comparison else (int, float)
-            if type(left) not in allowed or type(right) not in allowed:
-                if isinstance(left, _Runtime) or isinstance(right, _Runtime):
-                    self.fail(node, "computed runtime host scalars are unsupported; forward the "
-                                    "parameter unchanged")
-                self.fail(node, "numeric expressions require scalar operands")
-            try:
-                result = _STATIC_BINARY[type(op)](left, right)
-            except (ZeroDivisionError, OverflowError) as error:
-                self.fail(node, f"invalid constant expression: {error}")
-            if type(result) is float and not math.isfinite(result):
-                self.fail(node, "non-finite constant expression")
-            return result
-        if isinstance(node, ast.UnaryOp) and isinstance(node.op, (ast.USub, ast.UAdd)):
-            value = self.expression(node.operand)
-            if type(value) in (int, float):
-                return -value if isinstance(node.op, ast.USub) else value
-            self.fail(node, "computed runtime host scalars are unsupported; forward the "
-                            "parameter unchanged")
-        if isinstance(node, ast.Call):
-            return self.call(node)
-        self.fail(node, f"unsupported expression: {type(node).__name__}")
+    def dynamic_binary(self, left, right, op, node, comparison):
+        if isinstance(left, _Runtime) or isinstance(right, _Runtime):
+            self.fail(node, _RUNTIME_SCALAR)
+        self.fail(node, "numeric expressions require scalar operands")
 
-    def call(self, node: ast.Call):
-        callee = self.expression(node.func)
-        if isinstance(callee, Definition):
-            self.fail(node, "kernel definitions are not ordinary calls; use ckl.launch")
-        if not isinstance(callee, Intrinsic):
-            self.fail(node, "calling arbitrary Python functions is unsupported")
-        if any(isinstance(a, ast.Starred) for a in node.args) or any(k.arg is None for k in node.keywords):
-            self.fail(node, "argument expansion is unsupported")
-        name = callee.name
-        if name == "launch":
-            return self.launch(node)
-        args = [self.expression(a) for a in node.args]
-        keywords = {k.arg: self.expression(k.value) for k in node.keywords}
-        if len(keywords) != len(node.keywords):
-            self.fail(node, "duplicate keyword arguments")
-        if name in ("global_id", "thread_id", "block_id", "block_dim", "grid_dim"):
-            self.fail(node, "device coordinates are only valid in kernels")
-        if name == "cdiv":
-            if len(args) != 2 or keywords or any(type(v) is not int for v in args) \
-                    or args[0] < 0 or args[1] <= 0:
-                self.fail(node, "cdiv requires a nonnegative constant extent and positive "
-                                "constant divisor")
-            return (args[0] + args[1] - 1) // args[1]
-        if name in ("empty", "empty_like"):
-            if name == "empty_like":
-                if len(args) != 1 or keywords or not isinstance(args[0], _BufferValue):
-                    self.fail(node, "empty_like requires one buffer")
-                spec = args[0].spec
-            else:
-                if len(args) != 1 or set(keywords) != {"dtype"}:
-                    self.fail(node, "use empty(shape_tuple, dtype=element_type)")
-                try:
-                    spec = BufferSpec(args[0], keywords["dtype"])
-                except (ValueError, TypeError) as error:
-                    self.fail(node, str(error))
-            rid = self._resource("temporary", spec, name=f"alloc{len(self.temporaries)}")
-            self.temporaries.append(rid)
-            self.events.append(Event("alloc", resource=rid))
-            return _BufferValue(rid, spec)
-        if name == "subview":
-            if len(args) != 1 or set(keywords) != {"offset", "shape"} \
-                    or not isinstance(args[0], _BufferValue):
-                self.fail(node, "use subview(buffer, offset=element_offset, shape=shape_tuple)")
-            source, offset = args[0], keywords["offset"]
-            try:
-                spec = BufferSpec(keywords["shape"], source.spec.dtype)
-            except (TypeError, ValueError) as error:
-                self.fail(node, str(error))
-            if type(offset) is not int or offset < 0 or offset >= (1 << 63) \
-                    or offset + spec.elements > source.spec.elements:
-                self.fail(node, "subview offset/shape must be constant and within the source")
-            parent = self.resources[source.resource]
-            base = parent.root
-            byte_offset = parent.byte_offset + offset * spec.dtype.bytes
-            rid = self._resource("view", spec, base=base, byte_offset=byte_offset,
-                                 name=f"view{len(self.resources)}")
-            return _BufferValue(rid, spec)
-        if name == "cast":
-            if len(args) != 2 or keywords or not isinstance(args[1], ScalarType):
-                self.fail(node, "use cast(value, scalar_type)")
-            value, dtype = args
-            if isinstance(value, _Runtime):
-                self.fail(node, "computed runtime host scalars are unsupported; forward the "
-                                "parameter unchanged")
-            if dtype in (i32, i64, index) and type(value) is float and math.isfinite(value):
-                value = int(value)
-            return constant(value, dtype, self.definition, node)
-        if name in ("exp", "rsqrt", "select"):
-            self.fail(node, "computed runtime host scalars are unsupported; forward the "
-                            "parameter unchanged")
-        self.fail(node, f"unsupported intrinsic: {name}")
+    def dynamic_unary(self, value, op, node):
+        self.fail(node, _RUNTIME_SCALAR)
 
-    def launch(self, node: ast.Call):
-        if not node.args:
-            self.fail(node, "launch requires a kernel definition")
-        definition = self.expression(node.args[0])
-        if not isinstance(definition, Definition) or definition.kind != "kernel":
-            self.fail(node, "launch requires a @ckl.kernel definition")
-        parameters = definition.tree.args.args
-        if len(node.args) - 1 != len(parameters):
-            self.fail(node, "launch argument count does not match kernel signature")
-        keywords = {k.arg: self.expression(k.value) for k in node.keywords}
-        if set(keywords) - {"grid", "block", "shared_memory"} or not {"grid", "block"} <= set(keywords):
-            self.fail(node, "launch requires grid and block; only shared_memory is optional")
-        geometry = []
+    def assign_local(self, target, value, node):
+        if value is None:
+            self.fail(node, "launches do not return source values")
+        self.env[target.id] = value
+
+    def assign_element(self, target, value, node):
+        self.fail(target, "buffer writes are only valid in kernels")
+
+    def loop(self, node, induction, start, stop, step):
+        if type(start) is not int or type(stop) is not int:
+            self.fail(node, "program range bounds must be compile-time integers")
+        values = range(start, stop, step)
+        if len(values) > 1024:
+            self.fail(node, "program unrolling is limited to 1024 iterations")
+
+        def unrolled():
+            for value in values:
+                self.env[induction] = value
+                self.walk(node.body)
+
+        self.with_binding(induction, None, unrolled)
+
+    # ---- intrinsics ------------------------------------------------------------------------
+    def _coordinate(self, node):
+        self.arguments(node)
+        self.fail(node, "device coordinates are only valid in kernels")
+
+    intrinsic_global_id = intrinsic_thread_id = intrinsic_block_id = _coordinate
+    intrinsic_block_dim = intrinsic_grid_dim = _coordinate
+
+    def _host_math(self, node):
+        self.arguments(node)
+        self.fail(node, _RUNTIME_SCALAR)
+
+    intrinsic_exp = intrinsic_rsqrt = intrinsic_select = _host_math
+
+    def _temporary(self, spec) -> _BufferValue:
+        rid = self._resource("temporary", spec, name=f"alloc{len(self.temporaries)}")
+        self.temporaries.append(rid)
+        self.events.append(Event("alloc", resource=rid))
+        return _BufferValue(rid, spec)
+
+    def intrinsic_empty_like(self, node):
+        values, keywords = self.arguments(node)
+        if keywords or len(values) != 1 or not isinstance(values[0], _BufferValue):
+            self.fail(node, "empty_like requires one buffer")
+        return self._temporary(values[0].spec)
+
+    def intrinsic_empty(self, node):
+        values, keywords = self.arguments(node)
+        if len(values) != 1 or set(keywords) != {"dtype"}:
+            self.fail(node, "use empty(shape_tuple, dtype=element_type)")
+        try:
+            spec = BufferSpec(values[0], keywords["dtype"])
+        except (ValueError, TypeError) as error:
+            self.fail(node, str(error))
+        return self._temporary(spec)
+
+    def intrinsic_subview(self, node):
+        values, keywords = self.arguments(node)
+        if len(values) != 1 or not isinstance(values[0], _BufferValue) \
+                or set(keywords) != {"offset", "shape"}:
+            self.fail(node, "use subview(buffer, offset=element_offset, shape=shape_tuple)")
+        source, offset = values[0], keywords["offset"]
+        try:
+            spec = BufferSpec(keywords["shape"], source.spec.dtype)
+        except (TypeError, ValueError) as error:
+            self.fail(node, str(error))
+        if type(offset) is not int or not 0 <= offset < (1 << 63) \
+                or offset + spec.elements > source.spec.elements:
+            self.fail(node, "subview offset/shape must be constant and within the source")
+        parent = self.resources[source.resource]
+        rid = self._resource("view", spec, base=parent.root,
+                             byte_offset=parent.byte_offset + offset * spec.dtype.bytes,
+                             name=f"view{len(self.resources)}")
+        return _BufferValue(rid, spec)
+
+    def intrinsic_cast(self, node):
+        values, keywords = self.arguments(node)
+        if keywords or len(values) != 2 or not isinstance(values[1], ScalarType):
+            self.fail(node, "use cast(value, scalar_type)")
+        value, dtype = values
+        if isinstance(value, _Runtime):
+            self.fail(node, _RUNTIME_SCALAR)
+        if dtype in (i32, i64, index) and type(value) is float and math.isfinite(value):
+            value = int(value)
+        return constant(value, dtype, self.definition, node)
+
+    def _geometry(self, node, keywords):
+        shape = []
         for name in ("grid", "block"):
-            dims = keywords[name]
-            if type(dims) is not tuple or not 1 <= len(dims) <= 3 or any(
-                    type(d) is not int or not 0 < d < (1 << 63) for d in dims):
-                self.fail(node, f"{name} requires a tuple of one to three positive compile-time integers")
-            geometry.append(tuple(dims) + (1,) * (3 - len(dims)))
+            extents = keywords[name]
+            if type(extents) is not tuple or len(extents) not in (1, 2, 3) or not all(
+                    type(e) is int and 0 < e < (1 << 63) for e in extents):
+                self.fail(node, f"{name} requires a tuple of one to three positive compile-time "
+                                "integers")
+            shape.append(extents + (1,) * (3 - len(extents)))
         shared = keywords.get("shared_memory", 0)
         if type(shared) is not int or not 0 <= shared < (1 << 63):
             self.fail(node, "shared_memory requires nonnegative compile-time bytes")
-        signature, constants, operands = {}, {}, []
-        for parameter, argument in zip(parameters, node.args[1:]):
-            annotation = annotation_of(definition, parameter)
-            actual = self.expression(argument)
-            if isinstance(annotation, ConstexprType):
-                if isinstance(actual, (_Runtime, _BufferValue)):
-                    self.fail(argument, "constexpr launch arguments must be compile-time constants")
-                constants[parameter.arg] = actual
-                continue
-            if isinstance(annotation, ScalarType):
-                if isinstance(actual, _Runtime):
-                    if actual.dtype != annotation:
-                        self.fail(argument, f"expected {annotation.name}, got "
-                                            f"{actual.dtype.mlir}; use ckl.cast explicitly")
-                    operands.append(Operand("scalar", annotation, argument=actual.position))
-                elif isinstance(actual, _BufferValue):
-                    self.fail(argument, "kernel arguments must be typed buffers or scalars")
-                else:
-                    value = constant(actual, annotation, self.definition, argument)
-                    operands.append(Operand("constant", annotation, value=value))
-                signature[parameter.arg] = annotation
-                continue
-            if not isinstance(actual, _BufferValue):
+        return shape[0], shape[1], shared
+
+    def _operand(self, parameter, argument, declared, signature, constants):
+        """Classify one launch argument against the kernel parameter it feeds."""
+        given = self.evaluate(argument)
+        if isinstance(declared, ConstexprType):
+            if isinstance(given, (_Runtime, _BufferValue)):
+                self.fail(argument, "constexpr launch arguments must be compile-time constants")
+            constants[parameter.arg] = given
+            return None
+        if isinstance(declared, ScalarType):
+            signature[parameter.arg] = declared
+            if isinstance(given, _BufferValue):
                 self.fail(argument, "kernel arguments must be typed buffers or scalars")
-            signature[parameter.arg] = actual.spec
-            operands.append(Operand("resource", actual.spec, resource=actual.resource))
-        bound = bind(definition, signature, constants)
-        key = identity(definition, bound)
-        if key not in self.specializations:
-            self.specializations[key] = Specialization("kernel_" + key[:24], key, bound, definition)
-        grid, block = geometry
+            if not isinstance(given, _Runtime):
+                return Operand("constant", declared,
+                               value=constant(given, declared, self.definition, argument))
+            if given.dtype != declared:
+                self.fail(argument, f"expected {declared.name}, got {given.dtype.mlir}; use "
+                                    "ckl.cast explicitly")
+            return Operand("scalar", declared, argument=given.position)
+        if not isinstance(given, _BufferValue):
+            self.fail(argument, "kernel arguments must be typed buffers or scalars")
+        signature[parameter.arg] = given.spec
+        return Operand("resource", given.spec, resource=given.resource)
+
+    def intrinsic_launch(self, node):
+        if not node.args:
+            self.fail(node, "launch requires a kernel definition")
+        kernel = self.evaluate(node.args[0])
+        if not isinstance(kernel, Definition) or kernel.kind != "kernel":
+            self.fail(node, "launch requires a @ckl.kernel definition")
+        parameters = kernel.tree.args.args
+        if len(node.args) != len(parameters) + 1:
+            self.fail(node, "launch argument count does not match kernel signature")
+        keywords = {k.arg: self.evaluate(k.value) for k in node.keywords}
+        if not {"grid", "block"} <= set(keywords) <= {"grid", "block", "shared_memory"}:
+            self.fail(node, "launch requires grid and block; only shared_memory is optional")
+        grid, block, shared = self._geometry(node, keywords)
+        signature, constants = {}, {}
+        operands = [self._operand(p, a, parameter_type(kernel, p), signature, constants)
+                    for p, a in zip(parameters, node.args[1:])]
+        bound = bind(kernel, signature, constants)
+        key = identity(kernel, bound)
+        specialization = self.specializations.setdefault(
+            key, Specialization("kernel_" + key[:24], key, bound, kernel))
         self.events.append(Event("dispatch", dispatch=Dispatch(
-            self.specializations[key], operands, grid, block, shared, self.location(node))))
+            specialization, [o for o in operands if o is not None], grid, block, shared,
+            self.location(node))))
         return None
 
-    # -- statements ----------------------------------------------------------------------
-    def statements(self, nodes, top=False):
-        for position, node in enumerate(nodes):
-            if isinstance(node, ast.Return):
-                if not top or position != len(nodes) - 1 or node.value is not None:
-                    self.fail(node, "only a final bare return is supported; buffers carry outputs")
-            elif isinstance(node, ast.Assign):
-                if len(node.targets) != 1:
-                    self.fail(node, "chained assignment is unsupported")
-                target = node.targets[0]
-                if isinstance(target, ast.Subscript):
-                    self.fail(target, "buffer writes are only valid in kernels")
-                if not isinstance(target, ast.Name):
-                    self.fail(target, "assignment requires a local name or indexed buffer element")
-                value = self.expression(node.value)
-                if value is None:
-                    self.fail(node, "launches do not return source values")
-                self.env[target.id] = value
-            elif isinstance(node, ast.If):
-                predicate = self.expression(node.test)
-                if type(predicate) is not bool:
-                    self.fail(node.test, "if requires a boolean predicate; program control flow "
-                                         "must be compile-time")
-                self.statements(node.body if predicate else node.orelse)
-            elif isinstance(node, ast.For):
-                self.for_loop(node)
-            elif isinstance(node, ast.Expr):
-                if isinstance(node.value, ast.Constant) and isinstance(node.value.value, str) \
-                        and position == 0 and top:
-                    continue
-                if not isinstance(node.value, ast.Call) or self.expression(node.value) is not None:
-                    self.fail(node, "expression statements must be kernel launches")
-            elif isinstance(node, ast.Pass):
-                continue
-            else:
-                self.fail(node, f"unsupported statement: {type(node).__name__}")
-
-    def for_loop(self, node: ast.For):
-        if node.orelse or not isinstance(node.target, ast.Name) or not isinstance(node.iter, ast.Call):
-            self.fail(node, "for requires a simple induction variable and range without else")
-        callee = self.expression(node.iter.func)
-        if not isinstance(callee, Intrinsic) or callee.name != "range" or node.iter.keywords:
-            self.fail(node, "for requires range(start, stop, positive_constant_step)")
-        bounds = [self.expression(a) for a in node.iter.args]
-        if not 1 <= len(bounds) <= 3:
-            self.fail(node, "range requires one to three bounds")
-        start, stop, step = (0, bounds[0], 1) if len(bounds) == 1 else \
-            (bounds[0], bounds[1], bounds[2] if len(bounds) == 3 else 1)
-        if type(step) is not int or step <= 0:
-            self.fail(node, "range step must be a positive compile-time integer")
-        if type(start) is not int or type(stop) is not int:
-            self.fail(node, "program range bounds must be compile-time integers")
-        if len(range(start, stop, step)) > 1024:
-            self.fail(node, "program unrolling is limited to 1024 iterations")
-        induction = node.target.id
-        outer = self.env.get(induction, _MISSING)
-        for value in range(start, stop, step):
-            self.env[induction] = value
-            self.statements(node.body)
-        if outer is _MISSING:
-            self.env.pop(induction, None)
-        else:
-            self.env[induction] = outer
-
     def trace(self) -> ProgramTrace:
-        self.statements(self.definition.tree.body, top=True)
-        for rid in reversed(self.temporaries):
-            self.events.append(Event("free", resource=rid))
+        self.walk(self.definition.tree.body, top=True)
+        self.events.extend(Event("free", resource=rid) for rid in reversed(self.temporaries))
         return ProgramTrace(self.definition.name, self.signature, self.resources, self.events)
-
-
-_MISSING = object()
 
 
 def render(trace: ProgramTrace, symbol: str) -> str:

@@ -2,6 +2,7 @@
 from __future__ import annotations
 
 import importlib.util
+import os
 from pathlib import Path
 
 import pytest
@@ -14,7 +15,9 @@ from ckl.frontend import FrontendError
 from ckl.frontend.analysis import canonical_key, summarize
 from ckl.workloads import decoder, vector_pipeline
 
-REFERENCE = Path("/root/reference")
+# A checkout of the reference project, when one is at hand (CKL_REFERENCE_CHECKOUT).
+REFERENCE = Path(os.environ.get("CKL_REFERENCE_CHECKOUT", "")) \
+    if os.environ.get("CKL_REFERENCE_CHECKOUT") else None
 linear = decoder.linear
 fill, copy, update = vector_pipeline.fill, vector_pipeline.copy, vector_pipeline.update
 N = ckl.dim("N")
@@ -29,7 +32,8 @@ def load(path):
     return module
 
 
-@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout only in the build container")
+@pytest.mark.skipif(REFERENCE is None or not REFERENCE.exists(),
+                    reason="set CKL_REFERENCE_CHECKOUT to a checkout of the reference project")
 def test_reference_workloads_import_lower_and_match_the_library():
     ref = load(REFERENCE / "benchmarks" / "decoder" / "workloads.py")
     for name in ("embedding", "rms_stats", "rms_apply", "linear", "rope", "append_kv",
