@@ -458,7 +458,8 @@ def gpu_arm(args, workload, world, rank, local, group):
     position = p0
     per_node = inv.profile_nodes(1)
     names = inv.node_names
-    attention_kernel = "ckl.fused.attention"
+    attention_kernels = ("ckl.fused.attention", "ckl.fused.attention_split")
+    attention_kernel = next((n for n in names if n in attention_kernels), attention_kernels[0])
     attention = [t for n, t in zip(names, per_node) if n == attention_kernel]
     hbm, peak_kind = peaks()
     roofline = None

@@ -267,6 +267,170 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
   dependentLaunchExit();
 }
 
+// Split-K flash decoding, for few (request, head) pairs and long caches: the cache rows
+// 0..p of every pair are divided into s.splits contiguous ranges of equal length, one CTA per
+// (pair, range), so a small batch still puts hundreds of CTAs on the GPU.  Each CTA streams its
+// range exactly like attentionKernel and writes its softmax state (maximum, normaliser,
+// weighted V sum) to `partials`; the last CTA of a pair to finish (an arrival counter per
+// pair, re-armed to zero by that CTA, so nothing ever waits) merges the states of all ranges in
+// range order - a fixed order, so results do not depend on which CTA finished last - and
+// writes the context row.  Ranges past the last cache row contribute empty states.
+template <int D>
+__global__ void __launch_bounds__(kAttentionWarps *kWarp)
+    attentionSplitKernel(const float *q, const float *kc, const float *vc, const int *position,
+                         float *ctx, float *partials, unsigned *arrivals, float scale,
+                         AttentionSpec s) {
+  dependentLaunchWait();
+  constexpr int LPR = D / 4;
+  constexpr int RPW = kWarp / LPR;
+  constexpr int STEP = kAttentionWarps * RPW;
+  constexpr int ROW4 = D / 4;
+  constexpr int SLOT = D + 4; // m, l, two pad words, acc[D]: acc stays 16-byte aligned
+  __shared__ SoftmaxState warpState[kAttentionWarps][LPR];
+  __shared__ int lastArrival;
+
+  const int64_t rows = s.rows > 0 ? s.rows : s.B;
+  const int64_t splits = s.splits;
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  const int group = lane / LPR, sub = lane % LPR;
+  const int64_t C = s.A * D;
+  const int p = position[0];
+  const int64_t end = int64_t(p) + 1;
+  const int64_t n = end < 0 ? 0 : (end < s.T ? end : s.T);
+  const int64_t span = (n + splits - 1) / splits; // rows per range
+
+  for (int64_t item = blockIdx.x; item < rows * s.A * splits; item += gridDim.x) {
+    const int64_t range = item % splits, bh = item / splits;
+    const int64_t h = bh % s.A, b = bh / s.A;
+    const float4 qv = *reinterpret_cast<const float4 *>(q + b * C + h * D + 4 * sub);
+    const int64_t base = (((s.layer * s.B + b) * s.A + h) * s.T) * D + 4 * sub;
+    const float4 *kRows = reinterpret_cast<const float4 *>(kc + base);
+    const float4 *vRows = reinterpret_cast<const float4 *>(vc + base);
+    const int64_t first = range * span;
+    const int64_t last = first + span < n ? first + span : n;
+
+    SoftmaxState st{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int64_t t0 = first + int64_t(warp) * RPW; t0 < last;
+         t0 += int64_t(STEP) * kAttentionUnroll) {
+      float4 kv[kAttentionUnroll], vv[kAttentionUnroll];
+      bool valid[kAttentionUnroll];
+#pragma unroll
+      for (int u = 0; u < kAttentionUnroll; ++u) {
+        const int64_t t = t0 + int64_t(u) * STEP + group;
+        valid[u] = t < last;
+        if (valid[u]) {
+          kv[u] = __ldcs(kRows + t * ROW4);
+          vv[u] = __ldcs(vRows + t * ROW4);
+        } else {
+          kv[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kAttentionUnroll; ++u) {
+        float dot = qv.x * kv[u].x + qv.y * kv[u].y + qv.z * kv[u].z + qv.w * kv[u].w;
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1)
+          dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (valid[u]) {
+          const float score = dot * scale;
+          const float M = fmaxf(st.m, score);
+          const float c = st.m == -CUDART_INF_F ? 0.f : expf(st.m - M);
+          const float e = expf(score - M);
+          st.l = st.l * c + e;
+          st.acc.x = st.acc.x * c + e * vv[u].x;
+          st.acc.y = st.acc.y * c + e * vv[u].y;
+          st.acc.z = st.acc.z * c + e * vv[u].z;
+          st.acc.w = st.acc.w * c + e * vv[u].w;
+          st.m = M;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = LPR; o < kWarp; o <<= 1) {
+      const SoftmaxState other = shuffleState(st, o);
+      mergeState(st, other);
+    }
+    if (group == 0)
+      warpState[warp][sub] = st;
+    __syncthreads();
+    if (warp == 0 && group == 0) {
+      SoftmaxState total = warpState[0][sub];
+#pragma unroll
+      for (int w = 1; w < kAttentionWarps; ++w)
+        mergeState(total, warpState[w][sub]);
+      float *slot = partials + (bh * splits + range) * SLOT;
+      if (sub == 0) {
+        slot[0] = total.m;
+        slot[1] = total.l;
+      }
+      reinterpret_cast<float4 *>(slot + 4)[sub] = total.acc;
+      __threadfence(); // the state is visible device-wide before this CTA's arrival counts
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+      lastArrival = atomicAdd(&arrivals[bh], 1u) == unsigned(splits - 1);
+    __syncthreads();
+    if (lastArrival) {
+      __threadfence();
+      if (warp == 0 && group == 0) {
+        SoftmaxState total{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
+        for (int64_t r = 0; r < splits; ++r) {
+          const float *slot = partials + (bh * splits + r) * SLOT;
+          const SoftmaxState part{__ldcg(slot), __ldcg(slot + 1),
+                                  __ldcg(reinterpret_cast<const float4 *>(slot + 4) + sub)};
+          if (r == 0)
+            total = part;
+          else
+            mergeState(total, part);
+        }
+        float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (total.l > 0.f) {
+          out.x = total.acc.x / total.l;
+          out.y = total.acc.y / total.l;
+          out.z = total.acc.z / total.l;
+          out.w = total.acc.w / total.l;
+        }
+        if (s.panel)
+          panel::store4(ctx, b, h * D + 4 * sub, C, out);
+        else
+          *reinterpret_cast<float4 *>(ctx + b * C + h * D + 4 * sub) = out;
+      }
+      if (threadIdx.x == 0)
+        arrivals[bh] = 0; // every range of this pair has arrived: re-arm for the next launch
+    }
+    __syncthreads(); // warpState and lastArrival are reused by the next item
+  }
+  dependentLaunchExit();
+}
+
+constexpr int64_t kMaxAttentionSplits = 64;
+
+bool attentionSplitGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<AttentionSpec>(spec);
+  if (s.B <= 0 || s.A <= 0 || s.T <= 0 || s.layer < 0 || s.layer >= s.L || s.splits < 2 ||
+      s.splits > kMaxAttentionSplits)
+    return false;
+  if (s.D != 16 && s.D != 32 && s.D != 64 && s.D != 128)
+    return false;
+  const int64_t rows = s.rows > 0 ? s.rows : s.B;
+  if (s.rows < 0 || rows > s.B || s.grid < 0 || rows * s.A * s.splits >= (int64_t(1) << 31))
+    return false;
+  const int64_t items = rows * s.A * s.splits;
+  g->grid[0] = unsigned(s.grid > 0 && s.grid < items ? s.grid : items);
+  g->block[0] = kAttentionWarps * kWarp;
+  return true;
+}
+
+const void *attentionSplitSelect(const void *spec) {
+  switch (specOf<AttentionSpec>(spec).D) {
+  case 16: return reinterpret_cast<const void *>(&attentionSplitKernel<16>);
+  case 32: return reinterpret_cast<const void *>(&attentionSplitKernel<32>);
+  case 64: return reinterpret_cast<const void *>(&attentionSplitKernel<64>);
+  case 128: return reinterpret_cast<const void *>(&attentionSplitKernel<128>);
+  default: return nullptr;
+  }
+}
+
 bool attentionGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<AttentionSpec>(spec);
   if (s.B <= 0 || s.A <= 0 || s.T <= 0 || s.layer < 0 || s.layer >= s.L || s.splits != 1)
@@ -385,6 +549,10 @@ CKL_REGISTER_KERNEL("ckl.fused.norm_linear_argmax",
                     nullptr, 0, true);
 CKL_REGISTER_KERNEL("ckl.fused.attention", reinterpret_cast<const void *>(&attentionKernel<64>),
                     "PPPPPFS", sizeof(AttentionSpec), attentionGeometry, attentionSelect,
+                    nullptr, 0, false);
+CKL_REGISTER_KERNEL("ckl.fused.attention_split",
+                    reinterpret_cast<const void *>(&attentionSplitKernel<64>), "PPPPPPPFS",
+                    sizeof(AttentionSpec), attentionSplitGeometry, attentionSplitSelect,
                     nullptr, 0, false);
 CKL_REGISTER_KERNEL("ckl.fused.greedy_combine",
                     reinterpret_cast<const void *>(&greedyCombineKernel), "PPPPPPS",

@@ -280,6 +280,25 @@ def _fuse_decoder(events, resources: list, tensor_cores: bool = True,
     return True
 
 
+# Split-K attention (csrc/kernels/decoder_fused.cu, attentionSplitKernel): below two
+# (request, head) pairs per SM the cache rows of each pair are divided over several CTAs,
+# aiming at about eight 4-warp CTAs per SM and keeping at least 128 cache rows (at capacity)
+# per range.
+_ATTENTION_UNSPLIT_PAIRS = 2 * 148
+_ATTENTION_TARGET_CTAS = 8 * 148
+_ATTENTION_MIN_SPAN = 128
+_ATTENTION_MAX_SPLITS = 64
+
+
+def attention_splits(B: int, A: int, T: int) -> int:
+    """Cache-row ranges per (request, head) for the decode attention of B requests."""
+    pairs = B * A
+    if pairs >= _ATTENTION_UNSPLIT_PAIRS:
+        return 1
+    wanted = -(-_ATTENTION_TARGET_CTAS // pairs)
+    return max(1, min(wanted, T // _ATTENTION_MIN_SPAN, _ATTENTION_MAX_SPLITS))
+
+
 def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
     def op(node, i):
         return node.source.operands[i]
@@ -387,6 +406,28 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
 
         R = lambda r: Slot("resource", resource=r)
         pos_read = (position, READ, POSITION)
+
+        def attention_node(qr, kc, vc, out, panel):
+            splits = attention_splits(B, A, T)
+            if splits == 1:
+                return node("ckl.fused.attention",
+                            [R(qr), R(kc), R(vc), R(position), R(out), scale],
+                            pack(B, A, T, D, L_, layer, 1, 0, panel, B, 0),
+                            [qr, kc, vc], [pos_read, (out, WRITE, "whole")], "attention")
+            # Split-K: per-range softmax states (a node-local temporary) and one arrival
+            # counter per (request, head), zeroed at allocation and re-armed by the kernel.
+            states = _add_resource(resources, "temporary",
+                                   BufferSpec((B * A * splits * (D + 4),), f32),
+                                   "attention_states")
+            added.append(states)
+            arrivals = _add_resource(resources, "persistent", BufferSpec((B * A,), i32),
+                                     "arrivals")
+            return node("ckl.fused.attention_split",
+                        [R(qr), R(kc), R(vc), R(position), R(out), R(states), R(arrivals), scale],
+                        pack(B, A, T, D, L_, layer, splits, 0, panel, B, 0),
+                        [qr, kc, vc], [pos_read, (out, WRITE, "whole"),
+                                       (states, READ | WRITE, "whole"),
+                                       (arrivals, READ | WRITE, "whole")], "attention")
         eliminated_here = [(inv, (d[0], d[1])), (normed, (d[1], d[2], d[3], d[4])),
                            (q, (d[2], d[5])), (k, (d[3], d[6])), (v, (d[4], d[7])),
                            (kr, (d[6], d[7])), (scores, (d[8], d[9])), (probs, (d[9], d[10])),
@@ -418,11 +459,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
                                   gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
                                   [x_panel, wv], [pos_read, (vc, WRITE, "whole")],
                                   "v projection"))
-            new_nodes.append(node("ckl.fused.attention",
-                                  [R(qr), R(kc), R(vc), R(position), R(context_panel), scale],
-                                  pack(B, A, T, D, L_, layer, 1, 0, 1, B, 0),
-                                  [qr, kc, vc], [pos_read, (context_panel, WRITE, "whole")],
-                                  "attention"))
+            new_nodes.append(attention_node(qr, kc, vc, context_panel, 1))
             new_nodes.append(node("ckl.fused.panel_linear_residual",
                                   [R(context_panel), R(wo), R(x), R(residual)],
                                   gemm_spec(B, Cdim, Cdim, Lw, layer),
@@ -458,11 +495,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
                                   [R(x), R(g1), R(wv), R(position), R(vc), eps1],
                                   gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
                                   [x, g1, wv], [pos_read, (vc, WRITE, "whole")], "v projection"))
-            new_nodes.append(node("ckl.fused.attention",
-                                  [R(qr), R(kc), R(vc), R(position), R(context), scale],
-                                  pack(B, A, T, D, L_, layer, 1, 0, 0, B, 0),
-                                  [qr, kc, vc], [pos_read, (context, WRITE, "whole")],
-                                  "attention"))
+            new_nodes.append(attention_node(qr, kc, vc, context, 0))
             new_nodes.append(node("ckl.fused.linear_residual",
                                   [R(context), R(wo), R(x), R(residual)],
                                   gemm_spec(B, Cdim, Cdim, Lw, layer),

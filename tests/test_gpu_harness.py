@@ -157,7 +157,7 @@ def test_run_case_flow(device, case, fuse_library):
             bound.run(mode=mode, batch_size=group)
         state.verify(references[config.steps], config)
     published = next(c for c in PUBLISHED if c["name"] == case and "deep-dive" in c["source"])
-    history = references[config.steps]["history"][config.context - 1:]
+    history = references[config.steps]["history"][config.context - 1:config.context - 1 + config.steps]
     assert prompts.tolist() == published["prompts"]
     assert history.tolist() == published["generated_tokens"]
 
