@@ -267,6 +267,8 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
   dependentLaunchExit();
 }
 
+constexpr int kMaxAttentionSplits = 32;
+
 // Split-K flash decoding, for few (request, head) pairs and long caches: the cache rows
 // 0..p of every pair are divided into s.splits contiguous ranges of equal length, one CTA per
 // (pair, range), so a small batch still puts hundreds of CTAs on the GPU.  Each CTA streams its
@@ -288,6 +290,8 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
   constexpr int SLOT = D + 4; // m, l, two pad words, acc[D]: acc stays 16-byte aligned
   __shared__ SoftmaxState warpState[kAttentionWarps][LPR];
   __shared__ int lastArrival;
+  // The last arriver's copy of its pair's range states, loaded by all threads at once.
+  __shared__ __align__(16) float gathered[kMaxAttentionSplits * SLOT];
 
   const int64_t rows = s.rows > 0 ? s.rows : s.B;
   const int64_t splits = s.splits;
@@ -372,12 +376,17 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
     __syncthreads();
     if (lastArrival) {
       __threadfence();
+      // Every thread loads a share of the pair's states (L2, not L1: other CTAs wrote them
+      // during this launch), so the merge below waits for one round of loads, not `splits`.
+      const float4 *states = reinterpret_cast<const float4 *>(partials + bh * splits * SLOT);
+      for (int64_t i = threadIdx.x; i < splits * (SLOT / 4); i += blockDim.x)
+        reinterpret_cast<float4 *>(gathered)[i] = __ldcg(states + i);
+      __syncthreads();
       if (warp == 0 && group == 0) {
         SoftmaxState total{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
         for (int64_t r = 0; r < splits; ++r) {
-          const float *slot = partials + (bh * splits + r) * SLOT;
-          const SoftmaxState part{__ldcg(slot), __ldcg(slot + 1),
-                                  __ldcg(reinterpret_cast<const float4 *>(slot + 4) + sub)};
+          const float *slot = gathered + r * SLOT;
+          const SoftmaxState part{slot[0], slot[1], reinterpret_cast<const float4 *>(slot + 4)[sub]};
           if (r == 0)
             total = part;
           else
@@ -402,8 +411,6 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
   }
   dependentLaunchExit();
 }
-
-constexpr int64_t kMaxAttentionSplits = 64;
 
 bool attentionSplitGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<AttentionSpec>(spec);

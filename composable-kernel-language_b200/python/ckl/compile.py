@@ -287,7 +287,7 @@ def _fuse_decoder(events, resources: list, tensor_cores: bool = True,
 _ATTENTION_UNSPLIT_PAIRS = 2 * 148
 _ATTENTION_TARGET_CTAS = 8 * 148
 _ATTENTION_MIN_SPAN = 128
-_ATTENTION_MAX_SPLITS = 64
+_ATTENTION_MAX_SPLITS = 32
 
 
 def attention_splits(B: int, A: int, T: int) -> int:
