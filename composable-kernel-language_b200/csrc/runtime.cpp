@@ -823,9 +823,13 @@ int ckl_bind(ckl_program *program, ckl_device *device, uint32_t count, const ckl
       }
     }
     // Fused plans assume distinct buffers; overlapping bindings (including shifted views)
-    // take the original kernel boundaries (NvidiaProgram.cpp:194-205).
+    // take the original kernel boundaries (NvidiaProgram.cpp:194-205).  They also read and
+    // write caller buffers with 16-byte vector accesses, so a buffer that does not start on a
+    // 16-byte boundary (a view at an odd element offset) takes the original boundaries too.
     if (p->fallback) {
       bool overlap = false;
+      for (uint32_t i = 0; i < count; ++i)
+        overlap |= p->bufferBytes[i] != 0 && addresses[i] % 16 != 0;
       for (uint32_t i = 0; i < count; ++i)
         for (uint32_t j = i + 1; j < count; ++j) {
           if (!p->bufferBytes[i] || !p->bufferBytes[j])

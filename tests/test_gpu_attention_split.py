@@ -10,8 +10,9 @@ Cases:
   4 layers) with 1, 3 and 8 requests at context 2048: the prompt is prefilled on the GPU
   (batched prefill), the state read back, and three decode steps (cache rows 2047..2049:
   2048-2050 rows per head, so the last ranges are ragged) compared with the oracle run from
-  the same state, on the FFMA path (up to 16 requests) - tokens, history and position exact,
-  logits and appended cache rows within 1e-4 relative / 1e-5 absolute;
+  the same state, with tensor-core projections (the default at this hidden size) and, for 3
+  requests, FFMA projections - tokens, history and position exact, logits and appended cache
+  rows within 1e-4 relative / 1e-5 absolute;
 * a short prompt in a long cache (6 rows filled, capacity 2054): most ranges are empty;
 * the same small-batch case on the tensor-core path (tensor cores are used from 17 requests:
   20 requests of 2 heads still split), which writes the context as a split-operand panel.
@@ -51,8 +52,8 @@ def cache_rows(session, name, request):
     return out
 
 
-@pytest.mark.parametrize("batch", [1, 3, 8])
-def test_split_attention_at_context_2048_matches_oracle(device, batch):
+@pytest.mark.parametrize("batch,tensor_cores", [(1, True), (3, True), (8, True), (3, False)])
+def test_split_attention_at_context_2048_matches_oracle(device, batch, tensor_cores):
     steps = 3
     shape = S.DecoderShape(batch=batch, context=2048, steps=32, **CFG5)
     assert attention_splits(batch, shape.heads, shape.capacity) > 1
@@ -64,8 +65,11 @@ def test_split_attention_at_context_2048_matches_oracle(device, batch):
                  kc=(cache, np.float32), vc=(cache, np.float32),
                  logits=np.zeros((batch, shape.vocab), np.float32))
     session = S.DecoderSession(device, {**arrays, **state}, epsilon=EPS,
-                               attention_scale=shape.head_dim ** -0.5, tails=False)
-    assert "ckl.fused.attention_split" in session.invocation.node_names
+                               attention_scale=shape.head_dim ** -0.5, tails=False,
+                               tensor_cores=tensor_cores)
+    names = session.invocation.node_names
+    assert "ckl.fused.attention_split" in names
+    assert ("ckl.fused.panel_linear_rope" in names) == tensor_cores
     session.prefill(prompts, batched=True)
     initial = {name: arrays[name] for name in S.WEIGHTS + ("sincos",)}
     initial.update(tokens=session.read("tokens"), position=session.read("position"),

@@ -147,6 +147,38 @@ def test_overlapping_bindings_take_the_reference_graph(device):
     assert invocation.node_count == 21 * CFG1.layers + 6
 
 
+def test_misaligned_cache_view_takes_the_reference_graph(device):
+    """Fused plans access caller buffers 16 bytes at a time; a cache bound as a view one element
+    into its storage (4-byte aligned) makes the binding take the 21L+6-node graph, which then
+    reproduces the oracle."""
+    initial, _ = ref.make_inputs(CFG1, 0)
+    expected = ref.expected(initial, CFG1, 4)
+    session = open_session(device, CFG1, initial, 1e-5)
+    buffers = [session.buffers[n] for n in decoder.ARGUMENTS[:-2]]
+    shifted = {}
+    for name in ("kc", "vc"):
+        values = initial[name].ravel()
+        owner = device.empty(ckl.BufferSpec((values.size + 4,), ckl.f32))
+        host = np.zeros(values.size + 4, np.float32)
+        host[1:1 + values.size] = values
+        owner.copy_from_host(host)
+        view = device.import_buffer(owner.address + 4, session.buffers[name].spec, owner=owner)
+        shifted[name] = (owner, view)
+        buffers[decoder.ARGUMENTS.index(name)] = view
+    invocation = session.program.bind(*buffers, 1e-5, CFG1.head_dim ** -0.5)
+    assert invocation.node_count == 21 * CFG1.layers + 6
+    for _ in range(4):
+        invocation.run(mode="graph")
+    start, end = int(initial["position"][0]), int(expected["position"][0])
+    for name, (owner, _) in shifted.items():
+        host = np.empty(initial[name].size + 4, np.float32)
+        owner.copy_to_host(host)
+        actual = host[1:1 + initial[name].size].reshape(initial[name].shape)
+        assert np.allclose(actual[:, :, :, start:end], expected[name][:, :, :, start:end],
+                           rtol=RTOL, atol=ATOL), name
+    assert np.array_equal(session.read("history"), expected["history"])
+
+
 @pytest.mark.parametrize("batch,options", [(2, {}), (2, {"whole_step": False}),
                                            (20, {"whole_step": False}),
                                            (2, {"fuse_library": False})],
