@@ -312,19 +312,6 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
     const float4 *vRows = reinterpret_cast<const float4 *>(vc + base);
     const int64_t first = range * span;
     const int64_t last = first + span < n ? first + span : n;
-    const float *kRange = kc + (base - 4 * sub) + first * D;
-    const float *vRange = vc + (base - 4 * sub) + first * D;
-    if (threadIdx.x == 0 && last > first && aligned16(kRange) && aligned16(vRange)) {
-      // The whole range (K rows, then V rows; a multiple of 16 bytes) is requested into L2 up
-      // front: with every CTA of a small batch resident at once, HBM streams the layer's cache
-      // rows without the gaps between this CTA's successive load rounds.
-      const unsigned bytes = unsigned((last - first) * D * sizeof(float));
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kRange), "r"(bytes)
-                   : "memory");
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(vRange), "r"(bytes)
-                   : "memory");
-    }
-
     SoftmaxState st{-CUDART_INF_F, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
     for (int64_t t0 = first + int64_t(warp) * RPW; t0 < last;
          t0 += int64_t(STEP) * kAttentionUnroll) {

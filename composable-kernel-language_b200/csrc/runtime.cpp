@@ -314,6 +314,7 @@ struct ExecResource {
 };
 struct ExecPlan {
   std::vector<unsigned char> binary;
+  uint64_t alignment = 1; // caller buffers must start on this boundary (else: the fallback)
   std::vector<uint64_t> heaps;
   std::vector<ExecResource> resources;
   std::vector<ExecKernel> kernels;
@@ -375,6 +376,10 @@ std::shared_ptr<ExecPlan> parsePlan(const char *text) {
       } else {
         throw std::invalid_argument("unknown plan binary kind: " + kind);
       }
+    } else if (op == "align") {
+      in >> plan->alignment;
+      if (!in.fail() && (plan->alignment == 0 || (plan->alignment & (plan->alignment - 1))))
+        throw std::invalid_argument("plan alignment must be a power of two");
     } else if (op == "heap") {
       uint64_t id, bytes;
       in >> id >> bytes;
@@ -823,13 +828,14 @@ int ckl_bind(ckl_program *program, ckl_device *device, uint32_t count, const ckl
       }
     }
     // Fused plans assume distinct buffers; overlapping bindings (including shifted views)
-    // take the original kernel boundaries (NvidiaProgram.cpp:194-205).  They also read and
-    // write caller buffers with 16-byte vector accesses, so a buffer that does not start on a
-    // 16-byte boundary (a view at an odd element offset) takes the original boundaries too.
+    // take the original kernel boundaries (NvidiaProgram.cpp:194-205).  A plan whose kernels
+    // access caller buffers in wider units (the fused decoder: 16 bytes) states it, and a
+    // buffer that does not start on such a boundary takes the original boundaries too.
     if (p->fallback) {
       bool overlap = false;
+      const uint64_t alignment = p->plan ? p->plan->alignment : 1;
       for (uint32_t i = 0; i < count; ++i)
-        overlap |= p->bufferBytes[i] != 0 && addresses[i] % 16 != 0;
+        overlap |= p->bufferBytes[i] != 0 && addresses[i] % alignment != 0;
       for (uint32_t i = 0; i < count; ++i)
         for (uint32_t j = i + 1; j < count; ++j) {
           if (!p->bufferBytes[i] || !p->bufferBytes[j])

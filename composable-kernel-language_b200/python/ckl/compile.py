@@ -31,6 +31,9 @@ from .types import BufferSpec, f32, f64, i32, i64
 
 READ, WRITE, ALLOCATE, FREE = analysis.READ, analysis.WRITE, analysis.ALLOCATE, analysis.FREE
 ALIGNMENT = 256  # temporary allocation alignment (lib/Analysis/GraphAnalysis.cpp:147)
+# Caller-buffer alignment the fused decoder kernels require; a binding that misses it takes the
+# program's unfused fallback plan.
+_FUSED_ALIGNMENT = 16
 LIBRARY_BINARY = "ckl-b200:library"
 POSITION = (0, 4)  # position[0] of an i32 buffer
 
@@ -587,6 +590,9 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
 # all of them shortens every cluster's passes: 256 requests as 32 x 8 take 205 us per step of
 # an 8-layer C = 64 decoder against 309 us as 18 x 15).
 _WHOLE_STEP_WEIGHT_BYTES = 24 << 20
+# Single-CTA whole step (csrc/kernels/decode_step_small.cu): up to 8 requests of a decoder
+# whose weights (read once per step by one SM, from L2) stay within 1 MB.
+_SMALL_STEP_WEIGHT_BYTES = 1 << 20
 _WHOLE_STEP_CLUSTERS = 32
 _WHOLE_STEP_ROWS = 16
 
@@ -622,13 +628,23 @@ def _whole_step(dispatches, layers, resources):
     weight_bytes = 4 * (layers * (4 * C * C + 3 * C * F) + 2 * V * C)
     if weight_bytes > _WHOLE_STEP_WEIGHT_BYTES or B > _WHOLE_STEP_CLUSTERS * _WHOLE_STEP_ROWS:
         return None
+    name = "ckl.fused.decode_step"
     G = -(-B // min(_WHOLE_STEP_CLUSTERS, B))
     clusters = -(-B // G)
     spec = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
                 head["head"], G, clusters)
-    try:
-        library_geometry("ckl.fused.decode_step", spec)
-    except CompilationError:
+    small = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
+                 head["head"], B, 1)
+    def fits(kernel, packed):
+        try:
+            library_geometry(kernel, packed)
+            return True
+        except CompilationError:
+            return False
+
+    if weight_bytes <= _SMALL_STEP_WEIGHT_BYTES and fits("ckl.fused.decode_step_small", small):
+        name, spec, clusters = "ckl.fused.decode_step_small", small, 1
+    elif not fits(name, spec):
         return None
     counter = _add_resource(resources, "persistent", BufferSpec((1,), i32), "counter")
     position, sincos = first["position"], first["sincos"]
@@ -641,7 +657,7 @@ def _whole_step(dispatches, layers, resources):
                  (head["history"], WRITE, "whole"), (kc, READ | WRITE, "whole"),
                  (vc, READ | WRITE, "whole"), (head["logits"], WRITE, "whole"),
                  (counter, READ | WRITE, "whole")]
-    return Node("ckl.fused.decode_step",
+    return Node(name,
                 [R(r) for r in operands] + [first["scalars"][0], first["scalars"][2]], spec,
                 accesses, f"whole decode step ({layers} layers, {clusters} clusters)")
 
@@ -740,6 +756,9 @@ def _emit(lowered, lib, handle, events, resources, fused, binary=None) -> Plan:
         else:
             text.append(f"arg {position} scalar {parameter.dtype.name}")
     text.append(f"binary hex {binary.hex()}" if binary else "binary library")
+    if any(e.kind == "dispatch" and e.node.name.startswith("ckl.fused.") for e in events):
+        # The fused decoder kernels access caller buffers 16 bytes at a time.
+        text.append(f"align {_FUSED_ALIGNMENT}")
     for h in range(heap_count.value):
         text.append(f"heap {h} {heaps[h]}")
         ir.append(f'  "ckl_exec.heap"() {{id = {h} : i64, bytes = {heaps[h]} : i64, alignment = '
