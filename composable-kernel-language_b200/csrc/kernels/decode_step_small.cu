@@ -1,10 +1,12 @@
-// Whole decode step of a tiny decoder in one CTA.
+// Whole decode step of a small decoder, one CTA per group of up to eight requests.
 //
-// For a handful of requests of a small model (one request, hidden 64, two
-// layers) the cluster kernel of decode_step.cu spends most of a step in its cluster barriers
-// and distributed-shared-memory exchanges, which exist to spread projections over eight SMs.
-// Here the projections are tiny (the largest reads a few hundred KB of L2-resident weights),
-// so one CTA of 1024 threads runs the whole step with nothing but CTA barriers:
+// For decoders whose weights are a few MB at most (one request, hidden 64,
+// two layers; config 4: 256 requests, hidden 64, eight layers) the cluster kernel of
+// decode_step.cu spends most of a step in cluster barriers and distributed-shared-memory
+// exchanges, which exist to spread each projection's weights over eight SMs.  Here every CTA
+// of 1024 threads runs the whole step for its own requests and reads all weights itself (from
+// L2, where they stay), with nothing but CTA barriers; CTAs never wait for one another and the
+// last one to finish advances the position (an arrival counter it re-arms):
 //   * every projection puts one thread on each (output column, K slice) pair: all of its
 //     weight loads are independent and go out at once (one L2 round trip per projection),
 //     each load serving every request of the step (one accumulator per request); the K slices'
@@ -15,8 +17,8 @@
 //     of a warp by shuffles and across the pair's warps through shared memory in warp order;
 //   * the residual stream, normalized rows, queries, attention outputs and the SwiGLU product
 //     stay in shared memory; only cache rows, logits, tokens, history and position are written.
-// Same arguments as the cluster kernel (the arrival counter is unused: one CTA advances the
-// position itself).  Same arithmetic conventions (RMSNorm with rsqrtf, RoPE and SwiGLU rounded
+// Same arguments as the cluster kernel (DecodeStepSpec::G requests per CTA, ::clusters CTAs).
+// Same arithmetic conventions (RMSNorm with rsqrtf, RoPE and SwiGLU rounded
 // as the other decoder kernels, expf softmax, first-index argmax with the NaN-at-zero rule).
 #include "ckl_b200.h"
 #include "common.cuh"
@@ -27,7 +29,7 @@ namespace {
 
 constexpr int kSmallThreads = 1024;
 constexpr int kSmallWarps = kSmallThreads / kWarp;
-constexpr int kSmallRows = 8;          // requests per step
+constexpr int kSmallRows = 8;          // requests per CTA
 constexpr int kSmallMaxHidden = 256;
 constexpr int kSmallMaxFfn = 1024;
 constexpr int kSmallMaxCache = 4096;
@@ -45,17 +47,38 @@ struct SmallLayout {
 };
 __host__ __device__ inline SmallLayout smallLayout(const DecodeStepSpec &s) {
   SmallLayout o;
-  o.act = pad4(s.B * s.C);
-  o.q = o.act + pad4(s.B * s.C);
-  o.ctx = o.q + pad4(s.B * s.C);
-  o.h = o.ctx + pad4(s.B * s.C);
-  o.tile = o.h + pad4(s.B * s.F);
-  o.partial = o.tile + pad4(s.B * smallTileColumns(s));
+  o.act = pad4(s.G * s.C);
+  o.q = o.act + pad4(s.G * s.C);
+  o.ctx = o.q + pad4(s.G * s.C);
+  o.h = o.ctx + pad4(s.G * s.C);
+  o.tile = o.h + pad4(s.G * s.F);
+  o.partial = o.tile + pad4(s.G * smallTileColumns(s));
   o.states = o.partial + int64_t(kSmallThreads) * kSmallRows;
   o.bestValue = o.states + int64_t(kSmallWarps) * kWarp * 8;
   o.bestIndex = o.bestValue + kSmallWarps * kSmallRows;
   o.total = o.bestIndex + kSmallWarps * kSmallRows;
   return o;
+}
+
+// acc[r] += in[r * ldIn + k] * column[k * width] for k in [k0, k1), in k order, with the weight
+// loads issued BATCH at a time before their multiply-adds (independent loads in flight).
+template <int BATCH>
+__device__ __forceinline__ void accumulate(const float *in, int ldIn, int rows,
+                                           const float *column, int width, int k0, int k1,
+                                           float (&acc)[kSmallRows]) {
+  for (int k = k0; k < k1; k += BATCH) {
+    float weight[BATCH];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j)
+      weight[j] = k + j < k1 ? __ldg(column + int64_t(k + j) * width) : 0.f;
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j)
+      if (k + j < k1)
+#pragma unroll
+        for (int r = 0; r < kSmallRows; ++r)
+          if (r < rows)
+            acc[r] = fmaf(in[r * ldIn + k + j], weight[j], acc[r]);
+  }
 }
 
 // out[r * ldOut + n] = sum_k in[r * ldIn + k] * W(n)[k] for n < count * width and r < rows,
@@ -72,14 +95,7 @@ __device__ void smallProject(const float *in, int ldIn, int rows, int K, const f
 #pragma unroll
       for (int r = 0; r < kSmallRows; ++r)
         acc[r] = 0.f;
-#pragma unroll 4
-      for (int k = 0; k < K; ++k) {
-        const float weight = __ldg(column + int64_t(k) * width);
-#pragma unroll
-        for (int r = 0; r < kSmallRows; ++r)
-          if (r < rows)
-            acc[r] = fmaf(in[r * ldIn + k], weight, acc[r]);
-      }
+      accumulate<16>(in, ldIn, rows, column, width, 0, K, acc);
 #pragma unroll
       for (int r = 0; r < kSmallRows; ++r)
         if (r < rows)
@@ -99,14 +115,7 @@ __device__ void smallProject(const float *in, int ldIn, int rows, int K, const f
 #pragma unroll
     for (int r = 0; r < kSmallRows; ++r)
       acc[r] = 0.f;
-#pragma unroll 8
-    for (int k = k0; k < k1; ++k) {
-      const float weight = __ldg(column + int64_t(k) * width);
-#pragma unroll
-      for (int r = 0; r < kSmallRows; ++r)
-        if (r < rows)
-          acc[r] = fmaf(in[r * ldIn + k], weight, acc[r]);
-    }
+    accumulate<8>(in, ldIn, rows, column, width, k0, k1, acc);
 #pragma unroll
     for (int r = 0; r < kSmallRows; ++r)
       partial[(slice * N + n) * kSmallRows + r] = acc[r];
@@ -140,12 +149,12 @@ __device__ void smallNorm(const float *x, const float *gain, float *act, int row
 
 template <int D>
 __device__ void smallAttention(const float *q, const float *kc, const float *vc, float *ctx,
-                               SoftmaxState *states, int B, int A, int64_t T, int64_t layer,
-                               int64_t n, float scale) {
+                               SoftmaxState *states, int rows, int64_t r0, int64_t B, int A,
+                               int64_t T, int64_t layer, int64_t n, float scale) {
   constexpr int LPR = D / 4, RPW = kWarp / LPR;
   const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
   const int group = lane / LPR, sub = lane % LPR;
-  const int C = A * D, pairs = B * A;
+  const int C = A * D, pairs = rows * A;
   int wp = 1; // warps per (request, head)
   while (wp < kSmallWarps && pairs * wp * 2 <= kSmallWarps)
     wp *= 2;
@@ -156,7 +165,7 @@ __device__ void smallAttention(const float *q, const float *kc, const float *vc,
     if (pair < pairs) {
       const int b = pair / A, h = pair % A;
       const float4 qv = *reinterpret_cast<const float4 *>(q + b * C + h * D + 4 * sub);
-      const int64_t rowsBase = (((layer * B + b) * A + h) * T) * D + 4 * sub;
+      const int64_t rowsBase = (((layer * B + r0 + b) * A + h) * T) * D + 4 * sub;
       const float4 *kRows = reinterpret_cast<const float4 *>(kc + rowsBase);
       const float4 *vRows = reinterpret_cast<const float4 *>(vc + rowsBase);
       for (int64_t t0 = int64_t(member) * RPW; t0 < n; t0 += int64_t(wp) * RPW * 2) {
@@ -218,10 +227,11 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
                           const float *wg, const float *wu, const float *wd, const float *lm,
                           const float *sincos, float *kc, float *vc, float *logits,
                           unsigned *counter, float eps, float scale, DecodeStepSpec s) {
-  (void)counter;
   const int tid = threadIdx.x, lane = tid % kWarp, warp = tid / kWarp;
-  const int B = int(s.B), C = int(s.C), A = int(s.A), D = int(s.D), F = int(s.F);
-  const int64_t V = s.V, T = s.T;
+  const int C = int(s.C), A = int(s.A), D = int(s.D), F = int(s.F);
+  const int64_t B = s.B, V = s.V, T = s.T;
+  const int64_t r0 = int64_t(blockIdx.x) * s.G;
+  const int rows = int(s.G < B - r0 ? s.G : B - r0); // this CTA's requests r0 .. r0 + rows
   extern __shared__ float4 smallShared[];
   const SmallLayout at = smallLayout(s);
   float *x = reinterpret_cast<float *>(smallShared);
@@ -233,19 +243,19 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
 
   const int p = position[0];
   if (p >= 0 && p < T) {
-    for (int e = tid; e < B * C; e += kSmallThreads) {
-      const int token = tokens[e / C];
+    for (int e = tid; e < rows * C; e += kSmallThreads) {
+      const int token = tokens[r0 + e / C];
       x[e] = token >= 0 && token < V ? emb[int64_t(token) * C + e % C] : 0.f;
     }
     __syncthreads();
     const float *cs = sincos + int64_t(p) * (D / 2) * 2;
     const int ldQkv = 3 * C;
     for (int64_t l = 0; l < s.L; ++l) {
-      smallNorm(x, norm1 + l * C, act, B, C, eps);
+      smallNorm(x, norm1 + l * C, act, rows, C, eps);
       const float *qkv[3] = {wq + l * C * C, wk + l * C * C, wv + l * C * C};
-      smallProject(act, C, B, C, qkv, 3, C, partial, tile, ldQkv);
+      smallProject(act, C, rows, C, qkv, 3, C, partial, tile, ldQkv);
       // RoPE on q and k, append k and v at position p.
-      for (int e = tid; e < B * C / 2; e += kSmallThreads) {
+      for (int e = tid; e < rows * C / 2; e += kSmallThreads) {
         const int b = e / (C / 2), c = 2 * (e % (C / 2)), hh = c / D, d = c % D;
         const float cosine = cs[(d / 2) * 2], sine = cs[(d / 2) * 2 + 1];
         const float *row = tile + b * ldQkv;
@@ -254,7 +264,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
           outSecond = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
         };
         rotate(row[c], row[c + 1], q[b * C + c], q[b * C + c + 1]);
-        const int64_t slot = (((l * B + b) * A + hh) * T + p) * D + d;
+        const int64_t slot = (((l * B + r0 + b) * A + hh) * T + p) * D + d;
         rotate(row[C + c], row[C + c + 1], kc[slot], kc[slot + 1]);
         vc[slot] = row[2 * C + c];
         vc[slot + 1] = row[2 * C + c + 1];
@@ -262,40 +272,41 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       __syncthreads();
       const int64_t n = int64_t(p) + 1;
       switch (D) {
-      case 16: smallAttention<16>(q, kc, vc, ctx, states, B, A, T, l, n, scale); break;
-      case 32: smallAttention<32>(q, kc, vc, ctx, states, B, A, T, l, n, scale); break;
-      case 64: smallAttention<64>(q, kc, vc, ctx, states, B, A, T, l, n, scale); break;
-      default: smallAttention<128>(q, kc, vc, ctx, states, B, A, T, l, n, scale); break;
+      case 16: smallAttention<16>(q, kc, vc, ctx, states, rows, r0, B, A, T, l, n, scale); break;
+      case 32: smallAttention<32>(q, kc, vc, ctx, states, rows, r0, B, A, T, l, n, scale); break;
+      case 64: smallAttention<64>(q, kc, vc, ctx, states, rows, r0, B, A, T, l, n, scale); break;
+      default: smallAttention<128>(q, kc, vc, ctx, states, rows, r0, B, A, T, l, n, scale); break;
       }
       const float *o[1] = {wo + l * C * C};
-      smallProject(ctx, C, B, C, o, 1, C, partial, tile, C);
-      for (int e = tid; e < B * C; e += kSmallThreads)
+      smallProject(ctx, C, rows, C, o, 1, C, partial, tile, C);
+      for (int e = tid; e < rows * C; e += kSmallThreads)
         x[e] = __fadd_rn(x[e], tile[e]);
       __syncthreads();
-      smallNorm(x, norm2 + l * C, act, B, C, eps);
+      smallNorm(x, norm2 + l * C, act, rows, C, eps);
       const float *gateUp[2] = {wg + l * C * F, wu + l * C * F};
-      smallProject(act, C, B, C, gateUp, 2, F, partial, tile, 2 * F);
-      for (int e = tid; e < B * F; e += kSmallThreads) {
+      smallProject(act, C, rows, C, gateUp, 2, F, partial, tile, 2 * F);
+      for (int e = tid; e < rows * F; e += kSmallThreads) {
         const int b = e / F, f = e % F;
         const float g = tile[b * 2 * F + f], u = tile[b * 2 * F + F + f];
         h[e] = __fmul_rn(g / (1.0f + expf(-g)), u);
       }
       __syncthreads();
       const float *down[1] = {wd + l * F * C};
-      smallProject(h, F, B, F, down, 1, C, partial, tile, C);
-      for (int e = tid; e < B * C; e += kSmallThreads)
+      smallProject(h, F, rows, F, down, 1, C, partial, tile, C);
+      for (int e = tid; e < rows * C; e += kSmallThreads)
         x[e] = __fadd_rn(x[e], tile[e]);
       __syncthreads();
     }
     // Head: final norm, logits straight to global memory, first-index argmax per request.
-    smallNorm(x, finalNorm + s.finalLayer * C, act, B, C, eps);
+    smallNorm(x, finalNorm + s.finalLayer * C, act, rows, C, eps);
     const float *head[1] = {lm + s.headLayer * C * V};
-    smallProject(act, C, B, C, head, 1, int(V), partial, logits, V);
-    for (int b = 0; b < B; ++b) {
+    float *rowLogits = logits + r0 * V;
+    smallProject(act, C, rows, C, head, 1, int(V), partial, rowLogits, V);
+    for (int b = 0; b < rows; ++b) {
       float best = -CUDART_INF_F;
       int index = 0x7fffffff;
       for (int64_t j = tid; j < V; j += kSmallThreads)
-        argmaxMerge(best, index, logits[b * V + j], int(j));
+        argmaxMerge(best, index, rowLogits[b * V + j], int(j));
 #pragma unroll
       for (int o = kWarp / 2; o > 0; o >>= 1)
         argmaxMerge(best, index, __shfl_xor_sync(0xffffffffu, best, o),
@@ -306,26 +317,35 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
       }
     }
     __syncthreads();
-    if (tid < B) {
+    if (tid < rows) {
       float best = -CUDART_INF_F;
       int index = 0x7fffffff;
       for (int w = 0; w < kSmallWarps; ++w)
         argmaxMerge(best, index, bestValue[w * kSmallRows + tid], bestIndex[w * kSmallRows + tid]);
-      const float first = logits[int64_t(tid) * V];
+      const float first = rowLogits[int64_t(tid) * V];
       if (first != first || index == 0x7fffffff)
         index = 0; // a NaN first score wins the reference's strict scan outright
-      tokens[tid] = index;
-      history[int64_t(p) * B + tid] = index;
+      tokens[r0 + tid] = index;
+      history[int64_t(p) * B + r0 + tid] = index;
     }
   }
+  // The last CTA to finish advances the position (every CTA read it before arriving).
   __syncthreads();
-  if (tid == 0)
-    position[0] = p + 1;
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(counter, 1u) == unsigned(s.clusters) - 1) {
+      position[0] = p + 1;
+      atomicExch(counter, 0u);
+      __threadfence();
+    }
+  }
 }
 
 bool decodeStepSmallGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<DecodeStepSpec>(spec);
-  if (s.B <= 0 || s.B > kSmallRows || s.G != s.B || s.clusters != 1 || s.L <= 0 ||
+  if (s.B <= 0 || s.G <= 0 || s.G > kSmallRows || s.clusters <= 0 ||
+      s.clusters * s.G < s.B || (s.clusters - 1) * s.G >= s.B || s.clusters >= (int64_t(1) << 31) ||
+      s.L <= 0 ||
       s.A <= 0 || (s.D != 16 && s.D != 32 && s.D != 64 && s.D != 128) || s.A * s.D != s.C ||
       s.C > kSmallMaxHidden || s.F <= 0 || s.F > kSmallMaxFfn || s.V <= 0 ||
       s.V >= (int64_t(1) << 31) || s.T <= 0 || s.T > kSmallMaxCache)
@@ -335,7 +355,7 @@ bool decodeStepSmallGeometry(const void *spec, std::size_t, library::Geometry *g
   const std::size_t bytes = std::size_t(smallLayout(s).total) * sizeof(float);
   if (bytes > kSmallMaxShared)
     return false;
-  g->grid[0] = 1;
+  g->grid[0] = unsigned(s.clusters);
   g->block[0] = kSmallThreads;
   g->sharedBytes = unsigned(bytes);
   return true;

@@ -590,9 +590,10 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
 # all of them shortens every cluster's passes: 256 requests as 32 x 8 take 205 us per step of
 # an 8-layer C = 64 decoder against 309 us as 18 x 15).
 _WHOLE_STEP_WEIGHT_BYTES = 24 << 20
-# Single-CTA whole step (csrc/kernels/decode_step_small.cu): up to 8 requests of a decoder
-# whose weights (read once per step by one SM, from L2) stay within 1 MB.
-_SMALL_STEP_WEIGHT_BYTES = 1 << 20
+# One-CTA-per-group whole step (csrc/kernels/decode_step_small.cu): every CTA runs the step for
+# up to 8 requests and reads all weights itself (from L2), so the weights must be small.
+_SMALL_STEP_WEIGHT_BYTES = 3 << 20
+_SMALL_STEP_ROWS = 8
 _WHOLE_STEP_CLUSTERS = 32
 _WHOLE_STEP_ROWS = 16
 
@@ -633,8 +634,9 @@ def _whole_step(dispatches, layers, resources):
     clusters = -(-B // G)
     spec = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
                 head["head"], G, clusters)
+    rows = min(_SMALL_STEP_ROWS, B)
     small = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
-                 head["head"], B, 1)
+                 head["head"], rows, -(-B // rows))
     def fits(kernel, packed):
         try:
             library_geometry(kernel, packed)
@@ -643,7 +645,7 @@ def _whole_step(dispatches, layers, resources):
             return False
 
     if weight_bytes <= _SMALL_STEP_WEIGHT_BYTES and fits("ckl.fused.decode_step_small", small):
-        name, spec, clusters = "ckl.fused.decode_step_small", small, 1
+        name, spec, clusters = "ckl.fused.decode_step_small", small, -(-B // rows)
     elif not fits(name, spec):
         return None
     counter = _add_resource(resources, "persistent", BufferSpec((1,), i32), "counter")
