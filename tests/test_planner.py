@@ -161,19 +161,18 @@ def test_tensor_core_decoder_plan_shape():
 
 
 @pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,context,kernel", [
-    (1, 64, 4, 2, 256, 512, 16, "small"),     # config 1: one CTA
-    (3, 48, 3, 1, 80, 129, 6, "small"),       # awkward shapes fit the one-CTA step
-    (8, 64, 2, 2, 128, 1000, 9, "small"),     # eight requests, head dim 32
-    (9, 64, 4, 1, 256, 512, 8, "cluster"),    # nine requests: clusters
-    (1, 128, 4, 3, 512, 1024, 40, "cluster"), # 4 MB of weights: clusters
+    (1, 64, 4, 2, 256, 512, 16, "small"),       # config 1: one CTA
+    (3, 48, 3, 1, 80, 129, 6, "small"),         # awkward shapes fit the per-CTA step
+    (8, 64, 2, 2, 128, 1000, 9, "small"),       # eight requests, head dim 32
+    (9, 64, 4, 1, 256, 512, 8, "small"),        # nine requests: two CTAs
+    (256, 64, 4, 8, 256, 512, 16, "small"),     # config 4: 32 CTAs of 8 requests
+    (513, 64, 4, 1, 256, 512, 8, None),         # more requests than a whole step takes
+    (24, 96, 3, 1, 256, 512, 8, "small"),       # three heads (no split over CTAs needed)
+    (1, 128, 4, 3, 512, 1024, 40, "cluster"),   # 4 MB of weights: clusters
     (64, 256, 8, 2, 1024, 512, 16, "cluster"),  # config 3
-    (256, 64, 4, 8, 256, 512, 16, "cluster"),   # config 4
-    (512, 64, 4, 1, 256, 512, 8, "cluster"),    # 32 clusters x 16 requests
-    (513, 64, 4, 1, 256, 512, 8, None),         # too many requests per cluster
-    (33, 128, 2, 1, 96, 512, 6, "cluster"),     # three FFN quads per CTA
-    (4, 1024, 16, 4, 4096, 32000, 8, None),     # weights do not stay in L2
-    (24, 96, 3, 1, 256, 512, 8, None),          # three heads do not split over 8 CTAs
     (24, 256, 16, 2, 256, 512, 10, "cluster"),  # two heads per CTA
+    (4, 1024, 16, 4, 4096, 32000, 8, None),     # weights do not stay in L2
+    (40, 64, 4, 1, 256, 1000, 8, "small"),      # 5 CTAs, vocabulary not a multiple of 32
 ])
 def test_whole_step_kernel_selection(batch, hidden, heads, layers, ffn, vocab, context, kernel):
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
