@@ -590,10 +590,6 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
 # all of them shortens every cluster's passes: 256 requests as 32 x 8 take 205 us per step of
 # an 8-layer C = 64 decoder against 309 us as 18 x 15).
 _WHOLE_STEP_WEIGHT_BYTES = 24 << 20
-# One-CTA-per-group whole step (csrc/kernels/decode_step_small.cu): every CTA runs the step for
-# up to 8 requests and reads all weights itself (from L2), so the weights must be small.
-_SMALL_STEP_WEIGHT_BYTES = 3 << 20
-_SMALL_STEP_ROWS = 8
 _WHOLE_STEP_CLUSTERS = 32
 _WHOLE_STEP_ROWS = 16
 
@@ -629,24 +625,13 @@ def _whole_step(dispatches, layers, resources):
     weight_bytes = 4 * (layers * (4 * C * C + 3 * C * F) + 2 * V * C)
     if weight_bytes > _WHOLE_STEP_WEIGHT_BYTES or B > _WHOLE_STEP_CLUSTERS * _WHOLE_STEP_ROWS:
         return None
-    name = "ckl.fused.decode_step"
     G = -(-B // min(_WHOLE_STEP_CLUSTERS, B))
     clusters = -(-B // G)
     spec = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
                 head["head"], G, clusters)
-    rows = min(_SMALL_STEP_ROWS, B)
-    small = pack(B, C, A, D, F, V, layers, T, shape(wq)[0], shape(g1)[0], head["final"],
-                 head["head"], rows, -(-B // rows))
-    def fits(kernel, packed):
-        try:
-            library_geometry(kernel, packed)
-            return True
-        except CompilationError:
-            return False
-
-    if weight_bytes <= _SMALL_STEP_WEIGHT_BYTES and fits("ckl.fused.decode_step_small", small):
-        name, spec, clusters = "ckl.fused.decode_step_small", small, -(-B // rows)
-    elif not fits(name, spec):
+    try:
+        library_geometry("ckl.fused.decode_step", spec)
+    except CompilationError:
         return None
     counter = _add_resource(resources, "persistent", BufferSpec((1,), i32), "counter")
     position, sincos = first["position"], first["sincos"]
@@ -659,7 +644,7 @@ def _whole_step(dispatches, layers, resources):
                  (head["history"], WRITE, "whole"), (kc, READ | WRITE, "whole"),
                  (vc, READ | WRITE, "whole"), (head["logits"], WRITE, "whole"),
                  (counter, READ | WRITE, "whole")]
-    return Node(name,
+    return Node("ckl.fused.decode_step",
                 [R(r) for r in operands] + [first["scalars"][0], first["scalars"][2]], spec,
                 accesses, f"whole decode step ({layers} layers, {clusters} clusters)")
 

@@ -115,7 +115,7 @@ def test_fused_decoder_plan_shape():
     config = ref.Config(batch=1, hidden=64, heads=4, layers=2, ffn=256, vocab=512, context=16, steps=16)
     lowered = decoder.decode.lower(signature=decoder_signature(config))
     whole = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
-    assert whole.primary.node_names == ["ckl.fused.decode_step_small"]
+    assert whole.primary.node_names == ["ckl.fused.decode_step"]
     assert whole.fallback.nodes == 21 * 2 + 6
     plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
                          whole_step=False)
@@ -160,30 +160,25 @@ def test_tensor_core_decoder_plan_shape():
     assert not any("panel" in n for n in ffma.primary.node_names)
 
 
-@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,context,kernel", [
-    (1, 64, 4, 2, 256, 512, 16, "small"),       # config 1: one CTA
-    (3, 48, 3, 1, 80, 129, 6, "small"),         # awkward shapes fit the per-CTA step
-    (8, 64, 2, 2, 128, 1000, 9, "small"),       # eight requests, head dim 32
-    (9, 64, 4, 1, 256, 512, 8, "small"),        # nine requests: two CTAs
-    (256, 64, 4, 8, 256, 512, 16, "small"),     # config 4: 32 CTAs of 8 requests
-    (513, 64, 4, 1, 256, 512, 8, None),         # more requests than a whole step takes
-    (24, 96, 3, 1, 256, 512, 8, "small"),       # three heads (no split over CTAs needed)
-    (1, 128, 4, 3, 512, 1024, 40, "cluster"),   # 4 MB of weights: clusters
-    (64, 256, 8, 2, 1024, 512, 16, "cluster"),  # config 3
-    (24, 256, 16, 2, 256, 512, 10, "cluster"),  # two heads per CTA
-    (4, 1024, 16, 4, 4096, 32000, 8, None),     # weights do not stay in L2
-    (40, 64, 4, 1, 256, 1000, 8, "small"),      # 5 CTAs, vocabulary not a multiple of 32
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,context,whole", [
+    (1, 64, 4, 2, 256, 512, 16, True),
+    (64, 256, 8, 2, 1024, 512, 16, True),     # config 3
+    (256, 64, 4, 8, 256, 512, 16, True),      # config 4
+    (512, 64, 4, 1, 256, 512, 8, True),       # 32 clusters x 16 requests
+    (513, 64, 4, 1, 256, 512, 8, False),      # too many requests per cluster
+    (3, 48, 3, 1, 80, 129, 6, False),         # columns do not split into 8 x float4
+    (33, 128, 2, 1, 96, 512, 6, True),        # three FFN quads per CTA
+    (4, 1024, 16, 4, 4096, 32000, 8, False),  # weights do not stay in L2
+    (24, 96, 3, 1, 256, 512, 8, False),       # three heads do not split over 8 CTAs
+    (24, 256, 16, 2, 256, 512, 10, True),     # two heads per CTA
 ])
-def test_whole_step_kernel_selection(batch, hidden, heads, layers, ffn, vocab, context, kernel):
+def test_whole_step_kernel_selection(batch, hidden, heads, layers, ffn, vocab, context, whole):
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
                         vocab=vocab, context=context, steps=4)
     lowered = decoder.decode.lower(signature=decoder_signature(config))
     plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True)
-    names = {"small": ["ckl.fused.decode_step_small"], "cluster": ["ckl.fused.decode_step"]}
-    if kernel is None:
-        assert not any(n.startswith("ckl.fused.decode_step") for n in plans.primary.node_names)
-    else:
-        assert plans.primary.node_names == names[kernel]
+    assert (plans.primary.node_names == ["ckl.fused.decode_step"]) == whole
+    if whole:
         # The whole step replaces every node; nothing but the cross-cluster counter persists.
         assert plans.primary.temporaries == 0 and plans.primary.edges == 0
 
