@@ -822,12 +822,10 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
 // tensor memory holds one row tile per CTA.  The epilogue reads both (one output column per
 // lane), adds them in FP32 and stages the sums as [row][column] like the shared-memory body, so
 // the split-K reduction and every fused epilogue are shared.
-constexpr int kWeightBuffersT = 4;
-
 template <int S, int MT> struct SmemT {
   float a[S][MT][2][BK / 4][BM][4]; // activation panel blocks (MT row tiles x hi, lo): B operand
   float rawB[S][BK][BM];            // weight box as copied (128 output columns)
-  unsigned long long full[S], empty[S], aFull[kWeightBuffersT], aEmpty[kWeightBuffersT], accDone;
+  unsigned long long full[S], empty[S], aFull[2], aEmpty[2], accDone;
   unsigned long long unsignalled; // never arrived on (injected expiring wait)
   unsigned tmemBase;
   int abort;
@@ -848,9 +846,8 @@ inline std::size_t projectionSharedBytes(int width, int rowTiles) {
   return width == 128 && weightsInTmem() ? sharedBytesT() : sharedBytes(width, rowTiles);
 }
 
-// Tensor-memory columns: the main and the correction accumulator (128 columns each), then four
-// buffers of the weight slice's hi (32 columns) and lo (32 columns) halves (converters run up
-// to three slices ahead of the MMAs).
+// Tensor-memory columns: the main and the correction accumulator (128 columns each), then two
+// buffers of the weight slice's hi (32 columns) and lo (32 columns) halves.
 template <int MT> constexpr unsigned tmemColumnsT() { return 512u; }
 template <int MT> constexpr unsigned weightColumnT(int buffer, int part) {
   return unsigned(2 * BM + buffer * 2 * BK + part * BK);
@@ -936,7 +933,7 @@ __device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
       mbarrierInit(&sm.full[i], 1);
       mbarrierInit(&sm.empty[i], 1);
     }
-    for (int i = 0; i < kWeightBuffersT; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbarrierInit(&sm.aFull[i], kConverterWarps);
       mbarrierInit(&sm.aEmpty[i], 1);
     }
@@ -1002,9 +999,9 @@ __device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
       const bool injected =
           g_injectUnsignalledWait != 0 && !waitPhase(&sm.unsignalled, 0, abort);
       for (int64_t kt = 0; kt < slices && !injected; ++kt) {
-        const int slot = int(kt % S), buffer = int(kt % kWeightBuffersT);
+        const int slot = int(kt % S), buffer = int(kt & 1);
         if (!waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort) ||
-            !waitPhase(&sm.aFull[buffer], unsigned((kt / kWeightBuffersT) & 1), abort))
+            !waitPhase(&sm.aFull[buffer], unsigned((kt / 2) & 1), abort))
           break;
         fenceAfterSync();
         const int64_t remaining = K - (kBegin + kt) * BK;
@@ -1037,10 +1034,10 @@ __device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
     const int n = quarter * kWarp + lane;
     const unsigned laneBase = unsigned(quarter * kWarp) << 16;
     for (int64_t kt = 0; kt < slices; ++kt) {
-      const int slot = int(kt % S), buffer = int(kt % kWeightBuffersT);
+      const int slot = int(kt % S), buffer = int(kt & 1);
       bool ok = !copyRows || waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort);
-      if (ok && kt >= kWeightBuffersT)
-        ok = waitPhase(&sm.aEmpty[buffer], unsigned((kt / kWeightBuffersT - 1) & 1), abort);
+      if (ok && kt >= 2)
+        ok = waitPhase(&sm.aEmpty[buffer], unsigned((kt / 2 - 1) & 1), abort);
       if (!__all_sync(0xffffffffu, ok))
         break;
       fenceAfterSync();
