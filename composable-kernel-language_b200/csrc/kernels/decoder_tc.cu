@@ -172,8 +172,6 @@ __global__ void __launch_bounds__(tc::kThreads)
 // Row tiles per CTA of the gate/up kernel (full-width tiles of 64 gate + 64 up columns): two
 // when single-tile CTAs would already fill the SMs.
 int gateUpRowTiles(const GemmSpec &s) {
-  if (tc::weightsInTmem())
-    return 1; // the weights-in-tensor-memory body holds one row tile per CTA
   const int64_t tiles = int64_t(ceilDiv(s.M, tc::BM)) * ceilDiv(s.N, tc::BM / 2);
   return s.M > tc::BM && tiles >= tc::kTargetCtas ? 2 : 1;
 }
@@ -193,7 +191,8 @@ bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
 const void *gateUpSelect(const void *spec) {
   const bool two = gateUpRowTiles(specOf<GemmSpec>(spec)) == 2;
   if (tc::weightsInTmem())
-    return reinterpret_cast<const void *>(&panelGateUpTcT<1>);
+    return two ? reinterpret_cast<const void *>(&panelGateUpTcT<2>)
+               : reinterpret_cast<const void *>(&panelGateUpTcT<1>);
   return two ? reinterpret_cast<const void *>(&panelGateUpTc<2>)
              : reinterpret_cast<const void *>(&panelGateUpTc<1>);
 }
@@ -308,11 +307,16 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
     switch (tc::chooseWidth(s)) {                                                              \
     case 128:                                                                                  \
       if (tc::weightsInTmem()) {                                                               \
+        const bool two = tc::chooseRowTiles(s) == 2;                                           \
         switch (tc::chooseSplits(s)) {                                                         \
-        case 8: return reinterpret_cast<const void *>(&fn<0, 8, 1>);                           \
-        case 4: return reinterpret_cast<const void *>(&fn<0, 4, 1>);                           \
-        case 2: return reinterpret_cast<const void *>(&fn<0, 2, 1>);                           \
-        default: return reinterpret_cast<const void *>(&fn<0, 1, 1>);                          \
+        case 8: return two ? reinterpret_cast<const void *>(&fn<0, 8, 2>)                      \
+                           : reinterpret_cast<const void *>(&fn<0, 8, 1>);                     \
+        case 4: return two ? reinterpret_cast<const void *>(&fn<0, 4, 2>)                      \
+                           : reinterpret_cast<const void *>(&fn<0, 4, 1>);                     \
+        case 2: return two ? reinterpret_cast<const void *>(&fn<0, 2, 2>)                      \
+                           : reinterpret_cast<const void *>(&fn<0, 2, 1>);                     \
+        default: return two ? reinterpret_cast<const void *>(&fn<0, 1, 2>)                     \
+                            : reinterpret_cast<const void *>(&fn<0, 1, 1>);                    \
         }                                                                                      \
       }                                                                                        \
       if (tc::chooseRowTiles(s) == 2)                                                          \

@@ -251,20 +251,9 @@ constexpr int64_t kTargetCtas = 148; // one CTA per SM
 // per CTA and share every converted weight slice (half the weight conversion and copy traffic
 // per row tile; a wide projection's tiles fit in fewer waves).  Narrower grids keep one row
 // tile per CTA and split K instead.
-// Whether full-width (128-column) projections use the weights-in-tensor-memory body (default;
-// CKL_B200_TC_WEIGHTS_IN_TMEM=0 selects the shared-memory body, for comparisons).  Read once;
-// the geometry (shared-memory bytes) and the kernel selection of a node both follow it.
-inline bool weightsInTmem() {
-  static const bool enabled = [] {
-    const char *value = std::getenv("CKL_B200_TC_WEIGHTS_IN_TMEM");
-    return !(value && value[0] == '0');
-  }();
-  return enabled;
-}
-
 inline int chooseRowTiles(const GemmSpec &s) {
-  if (chooseWidth(s) != 128 || s.M <= BM || weightsInTmem())
-    return 1; // the weights-in-tensor-memory body holds one row tile per CTA
+  if (chooseWidth(s) != 128 || s.M <= BM)
+    return 1;
   const int64_t tiles = ((s.M + BM - 1) / BM) * ((s.N + 127) / 128);
   return tiles >= kTargetCtas ? 2 : 1;
 }
@@ -816,12 +805,9 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
 // shared memory, and the MMAs then read only the activation operand from shared memory.  Per
 // 32-deep slice of a 128 x 128 tile this moves ~96 KB through shared memory instead of ~160-190
 // KB (the previous design's converted weight buffers and its weight-operand reads are gone),
-// which was the bound of the main loop.  hi*hi accumulates into one FP32 accumulator and the
-// corrections hi*lo + lo*hi into a second (one accumulator for all three loses the corrections'
-// low bits in the tensor core's accumulation: logits off by more than 1e-5 at K = 1024), so
-// tensor memory holds one row tile per CTA.  The epilogue reads both (one output column per
-// lane), adds them in FP32 and stages the sums as [row][column] like the shared-memory body, so
-// the split-K reduction and every fused epilogue are shared.
+// which was the bound of the main loop.  hi*hi, hi*lo and lo*hi accumulate into one FP32
+// accumulator per row tile.  The epilogue reads D (one output column per lane) into the same
+// [row][column] staging as before, so the split-K reduction and every fused epilogue are shared.
 template <int S, int MT> struct SmemT {
   float a[S][MT][2][BK / 4][BM][4]; // activation panel blocks (MT row tiles x hi, lo): B operand
   float rawB[S][BK][BM];            // weight box as copied (128 output columns)
@@ -838,19 +824,33 @@ template <int MT, int S = 6> constexpr int stagesT() {
     return stagesT<MT, S - 1>();
 }
 static_assert(sizeof(SmemT<stagesT<1>(), 1>) <= kMaxDynamicSmem, "shared memory budget");
+static_assert(sizeof(SmemT<stagesT<2>(), 2>) <= kMaxDynamicSmem, "shared memory budget");
 
-inline std::size_t sharedBytesT() { return sizeof(SmemT<stagesT<1>(), 1>); }
+inline std::size_t sharedBytesT(int rowTiles) {
+  return rowTiles == 2 ? sizeof(SmemT<stagesT<2>(), 2>) : sizeof(SmemT<stagesT<1>(), 1>);
+}
+
+// Whether full-width (128-column) projections use the weights-in-tensor-memory body (default;
+// CKL_B200_TC_WEIGHTS_IN_TMEM=0 selects the shared-memory body, for comparisons).  Read once;
+// the geometry (shared-memory bytes) and the kernel selection of a node both follow it.
+inline bool weightsInTmem() {
+  static const bool enabled = [] {
+    const char *value = std::getenv("CKL_B200_TC_WEIGHTS_IN_TMEM");
+    return !(value && value[0] == '0');
+  }();
+  return enabled;
+}
 
 // Dynamic shared memory of a projection at a column width and row tiles per CTA.
 inline std::size_t projectionSharedBytes(int width, int rowTiles) {
-  return width == 128 && weightsInTmem() ? sharedBytesT() : sharedBytes(width, rowTiles);
+  return width == 128 && weightsInTmem() ? sharedBytesT(rowTiles) : sharedBytes(width, rowTiles);
 }
 
-// Tensor-memory columns: the main and the correction accumulator (128 columns each), then two
-// buffers of the weight slice's hi (32 columns) and lo (32 columns) halves.
-template <int MT> constexpr unsigned tmemColumnsT() { return 512u; }
+// Tensor-memory columns: MT accumulators of 128 columns, then two buffers of the weight slice's
+// hi (32 columns) and lo (32 columns) halves.
+template <int MT> constexpr unsigned tmemColumnsT() { return MT == 2 ? 512u : 256u; }
 template <int MT> constexpr unsigned weightColumnT(int buffer, int part) {
-  return unsigned(2 * BM + buffer * 2 * BK + part * BK);
+  return unsigned(MT * BM + buffer * 2 * BK + part * BK);
 }
 
 // tf32 MMA with A in tensor memory.
@@ -888,7 +888,6 @@ __device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
                       const WeightMap *upWeights = nullptr) {
   constexpr int BN = 128;
   static_assert(EPI != gemm::kSwiGluPanel || SPLITS == 1, "gate/up tiles");
-  static_assert(MT == 1, "one row tile per CTA (two accumulators fill tensor memory)");
   constexpr int S = stagesT<MT>();
   using Layout = SmemT<S, MT>;
   static_assert(sizeof(Staging<BN>) <= sizeof(Layout::a), "staging fits the ring");
@@ -1015,9 +1014,10 @@ __device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
                 matrixDescriptor(sm.a[slot][j][0][2 * ks], BM * 16, 128);
             const unsigned long long xLo =
                 matrixDescriptor(sm.a[slot][j][1][2 * ks], BM * 16, 128);
-            mmaTmemA(tmem, wHi + unsigned(8 * ks), xHi, idesc, first);
-            mmaTmemA(tmem + unsigned(BM), wHi + unsigned(8 * ks), xLo, idesc, first);
-            mmaTmemA(tmem + unsigned(BM), wLo + unsigned(8 * ks), xHi, idesc, 1u);
+            const unsigned d = tmem + unsigned(j * BM);
+            mmaTmemA(d, wHi + unsigned(8 * ks), xHi, idesc, first);
+            mmaTmemA(d, wHi + unsigned(8 * ks), xLo, idesc, 1u);
+            mmaTmemA(d, wLo + unsigned(8 * ks), xHi, idesc, 1u);
           }
         }
         commit(&sm.empty[slot]);
@@ -1083,18 +1083,16 @@ __device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
     if (warp >= 2) {
       const int quarter = warp % 4, half = (warp - 2) / 4;
       const int n = quarter * kWarp + lane;
-      const unsigned laneAddress = tmem + (unsigned(quarter * kWarp) << 16);
+      const unsigned laneAddress = tmem + unsigned(j * BM) + (unsigned(quarter * kWarp) << 16);
       const bool use = valid && j < tiles;
 #pragma unroll 1
       for (int m0 = half * (BM / 2); m0 < (half + 1) * (BM / 2); m0 += 16) {
-        float v[16], correction[16];
-        if (use) {
+        float v[16];
+        if (use)
           tmemLoad16(laneAddress + unsigned(m0), v);
-          tmemLoad16(laneAddress + unsigned(BM + m0), correction);
-        }
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          stage[m0 + i][n] = use ? __fadd_rn(v[i], correction[i]) : 0.f;
+          stage[m0 + i][n] = use ? v[i] : 0.f;
       }
     }
     if constexpr (SPLITS > 1)
