@@ -122,10 +122,7 @@ bool rmsPanelGeometry(const void *spec, std::size_t, library::Geometry *g) {
     Params p;                                                                                  \
     p.a = a, p.w = w, p.s = s;                                                                 \
     CKL_UNPACK assign;                                                                         \
-    if constexpr (BN == 0)                                                                     \
-      tc::bodyT<EPI, SPLITS, MT>(p, weights); /* width 128, weights in tensor memory */        \
-    else                                                                                       \
-      tc::body<BN, EPI, SPLITS, MT>(p, weights);                                               \
+    tc::body<BN, EPI, SPLITS, MT>(p, weights);                                                 \
   }
 #define CKL_UNPACK(...) __VA_ARGS__
 
@@ -158,17 +155,6 @@ __global__ void __launch_bounds__(tc::kThreads)
   tc::body<128, gemm::kSwiGluPanel, 1, MT>(p, maps.gate, &maps.up);
 }
 
-// The same with the weights in tensor memory.
-template <int MT>
-__global__ void __launch_bounds__(tc::kThreads)
-    panelGateUpTcT(const float *a, const float *wg, const float *wu, float *out, GemmSpec s,
-                   const __grid_constant__ tc::WeightMapPair maps) {
-  dependentLaunchEntry();
-  Params p;
-  p.a = a, p.w = wg, p.w2 = wu, p.out = out, p.s = s;
-  tc::bodyT<gemm::kSwiGluPanel, 1, MT>(p, maps.gate, &maps.up);
-}
-
 // Row tiles per CTA of the gate/up kernel (full-width tiles of 64 gate + 64 up columns): two
 // when single-tile CTAs would already fill the SMs.
 int gateUpRowTiles(const GemmSpec &s) {
@@ -184,16 +170,13 @@ bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
   g->grid[0] = ceilDiv(s.N, tc::BM / 2);
   g->grid[1] = ceilDiv(ceilDiv(s.M, tc::BM), mt);
   g->block[0] = tc::kThreads;
-  g->sharedBytes = unsigned(tc::projectionSharedBytes(128, mt));
+  g->sharedBytes = unsigned(tc::sharedBytes(128, mt));
   return g->grid[1] <= 65535;
 }
 
 const void *gateUpSelect(const void *spec) {
-  const bool two = gateUpRowTiles(specOf<GemmSpec>(spec)) == 2;
-  if (tc::weightsInTmem())
-    return two ? reinterpret_cast<const void *>(&panelGateUpTcT<2>)
-               : reinterpret_cast<const void *>(&panelGateUpTcT<1>);
-  return two ? reinterpret_cast<const void *>(&panelGateUpTc<2>)
+  return gateUpRowTiles(specOf<GemmSpec>(spec)) == 2
+             ? reinterpret_cast<const void *>(&panelGateUpTc<2>)
              : reinterpret_cast<const void *>(&panelGateUpTc<1>);
 }
 
@@ -279,7 +262,7 @@ bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
   g->grid[1] = ceilDiv(ceilDiv(s.M, tc::BM), mt);
   g->grid[2] = unsigned(tc::chooseSplits(s));
   g->block[0] = tc::kThreads;
-  g->sharedBytes = unsigned(tc::projectionSharedBytes(width, mt));
+  g->sharedBytes = unsigned(tc::sharedBytes(width, mt));
   return g->grid[1] <= 65535;
 }
 
@@ -306,19 +289,6 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
     const GemmSpec &s = specOf<GemmSpec>(spec);                                                \
     switch (tc::chooseWidth(s)) {                                                              \
     case 128:                                                                                  \
-      if (tc::weightsInTmem()) {                                                               \
-        const bool two = tc::chooseRowTiles(s) == 2;                                           \
-        switch (tc::chooseSplits(s)) {                                                         \
-        case 8: return two ? reinterpret_cast<const void *>(&fn<0, 8, 2>)                      \
-                           : reinterpret_cast<const void *>(&fn<0, 8, 1>);                     \
-        case 4: return two ? reinterpret_cast<const void *>(&fn<0, 4, 2>)                      \
-                           : reinterpret_cast<const void *>(&fn<0, 4, 1>);                     \
-        case 2: return two ? reinterpret_cast<const void *>(&fn<0, 2, 2>)                      \
-                           : reinterpret_cast<const void *>(&fn<0, 2, 1>);                     \
-        default: return two ? reinterpret_cast<const void *>(&fn<0, 1, 2>)                     \
-                            : reinterpret_cast<const void *>(&fn<0, 1, 1>);                    \
-        }                                                                                      \
-      }                                                                                        \
       if (tc::chooseRowTiles(s) == 2)                                                          \
         switch (tc::chooseSplits(s)) {                                                         \
         case 8: return reinterpret_cast<const void *>(&fn<128, 8, 2>);                         \

@@ -39,8 +39,6 @@
 
 #include <cuda.h>
 
-#include <cstdlib>
-
 #include "common.cuh"
 #include "gemm.cuh"
 #include "panel.cuh"
@@ -794,321 +792,6 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   }
   if (warp == kMmaWarp)
     tmemFree<2 * BN * MT>(tmem);
-}
-
-// ---- weights as the A operand, in tensor memory ---------------------------------------------
-// The same projections with the roles of the operands swapped: the MMA computes the transposed
-// tile D[n][m] (M = 128 output columns in the tensor-memory lanes, N = 128 activation rows per
-// row tile), with the weight slice as A in *tensor memory* and the activation panel as B in
-// shared memory.  The converter warps still split each landed FP32 weight box into TF32 hi/lo,
-// but write the halves straight from registers into tensor memory (tcgen05.st) instead of into
-// shared memory, and the MMAs then read only the activation operand from shared memory.  Per
-// 32-deep slice of a 128 x 128 tile this moves ~96 KB through shared memory instead of ~160-190
-// KB (the previous design's converted weight buffers and its weight-operand reads are gone),
-// which was the bound of the main loop.  hi*hi, hi*lo and lo*hi accumulate into one FP32
-// accumulator per row tile.  The epilogue reads D (one output column per lane) into the same
-// [row][column] staging as before, so the split-K reduction and every fused epilogue are shared.
-template <int S, int MT> struct SmemT {
-  float a[S][MT][2][BK / 4][BM][4]; // activation panel blocks (MT row tiles x hi, lo): B operand
-  float rawB[S][BK][BM];            // weight box as copied (128 output columns)
-  unsigned long long full[S], empty[S], aFull[2], aEmpty[2], accDone;
-  unsigned long long unsignalled; // never arrived on (injected expiring wait)
-  unsigned tmemBase;
-  int abort;
-};
-
-template <int MT, int S = 6> constexpr int stagesT() {
-  if constexpr (S <= 2 || sizeof(SmemT<S, MT>) <= kMaxDynamicSmem)
-    return S;
-  else
-    return stagesT<MT, S - 1>();
-}
-static_assert(sizeof(SmemT<stagesT<1>(), 1>) <= kMaxDynamicSmem, "shared memory budget");
-static_assert(sizeof(SmemT<stagesT<2>(), 2>) <= kMaxDynamicSmem, "shared memory budget");
-
-inline std::size_t sharedBytesT(int rowTiles) {
-  return rowTiles == 2 ? sizeof(SmemT<stagesT<2>(), 2>) : sizeof(SmemT<stagesT<1>(), 1>);
-}
-
-// Whether full-width (128-column) projections use the weights-in-tensor-memory body (default;
-// CKL_B200_TC_WEIGHTS_IN_TMEM=0 selects the shared-memory body, for comparisons).  Read once;
-// the geometry (shared-memory bytes) and the kernel selection of a node both follow it.
-inline bool weightsInTmem() {
-  static const bool enabled = [] {
-    const char *value = std::getenv("CKL_B200_TC_WEIGHTS_IN_TMEM");
-    return !(value && value[0] == '0');
-  }();
-  return enabled;
-}
-
-// Dynamic shared memory of a projection at a column width and row tiles per CTA.
-inline std::size_t projectionSharedBytes(int width, int rowTiles) {
-  return width == 128 && weightsInTmem() ? sharedBytesT(rowTiles) : sharedBytes(width, rowTiles);
-}
-
-// Tensor-memory columns: MT accumulators of 128 columns, then two buffers of the weight slice's
-// hi (32 columns) and lo (32 columns) halves.
-template <int MT> constexpr unsigned tmemColumnsT() { return MT == 2 ? 512u : 256u; }
-template <int MT> constexpr unsigned weightColumnT(int buffer, int part) {
-  return unsigned(MT * BM + buffer * 2 * BK + part * BK);
-}
-
-// tf32 MMA with A in tensor memory.
-__device__ __forceinline__ void mmaTmemA(unsigned tmemD, unsigned tmemA, unsigned long long b,
-                                         unsigned idesc, unsigned accumulate) {
-  asm volatile("{\n\t.reg .pred p;\n\t"
-               "setp.ne.b32 p, %4, 0;\n\t"
-               "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
-               ::"r"(tmemD), "r"(tmemA), "l"(b), "r"(idesc), "r"(accumulate)
-               : "memory");
-}
-
-// 16 consecutive tensor-memory columns of this thread's lane, from registers.
-__device__ __forceinline__ void tmemStore16(unsigned address, const float (&v)[16]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-               "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
-               ::"r"(address), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
-               "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])),
-               "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-               "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-               "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])),
-               "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-               "r"(__float_as_uint(v[15]))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmemStoreWait() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
-// MT x 128 rows by 128 columns, weights in tensor memory (see above).  Same arguments,
-// pipeline roles, bounded waits and abort path as body().
-template <int EPI, int SPLITS, int MT = 1>
-__device__ void bodyT(const gemm::Params &p, const WeightMap &weights,
-                      const WeightMap *upWeights = nullptr) {
-  constexpr int BN = 128;
-  static_assert(EPI != gemm::kSwiGluPanel || SPLITS == 1, "gate/up tiles");
-  constexpr int S = stagesT<MT>();
-  using Layout = SmemT<S, MT>;
-  static_assert(sizeof(Staging<BN>) <= sizeof(Layout::a), "staging fits the ring");
-  extern __shared__ __align__(1024) unsigned char raw[];
-  Layout &sm = *reinterpret_cast<Layout *>(raw);
-  const GemmSpec &s = p.s;
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  const int64_t K = s.K, N = s.N;
-  const int64_t rowGroups = gridDim.y;
-  const int64_t tile = int64_t(blockIdx.y) * gridDim.x + blockIdx.x;
-  const int64_t group = tile % rowGroups, nt = tile / rowGroups;
-  const int64_t rowTiles = (s.M + BM - 1) / BM;
-  const int tiles = int(rowTiles - group * MT < MT ? rowTiles - group * MT : MT); // >= 1
-  const int64_t n0 = nt * tileColumns<BN, EPI>();
-  const int64_t allSlices = panel::slices(K);
-  const int64_t perSplit = (allSlices + SPLITS - 1) / SPLITS;
-  const int64_t kBegin = perSplit * blockIdx.z;
-  const int64_t kEnd = kBegin + perSplit < allSlices ? kBegin + perSplit : allSlices;
-  const int64_t slices = kEnd > kBegin ? kEnd - kBegin : 0;
-  const bool hasWork = slices > 0;
-  const float *W = p.w + s.layer * K * N;
-
-  int position = 0;
-  if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend) {
-    position = p.position[0];
-    if (position < 0 || position >= s.T)
-      return; // outside cache capacity: the step writes nothing
-  }
-  if (!aligned16(p.a) || smemAddress(raw) % 128 != 0) {
-    if (threadIdx.x == 0)
-      atomicOr(&g_libraryFaults, 2u);
-    return;
-  }
-  const bool copyRows =
-      weights.valid != 0 && (EPI != gemm::kSwiGluPanel || upWeights->valid != 0);
-  const float *W2 = EPI == gemm::kSwiGluPanel ? p.w2 + s.layer * K * N : nullptr;
-
-  if (warp == kMmaWarp)
-    tmemAlloc<tmemColumnsT<MT>()>(&sm.tmemBase);
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbarrierInit(&sm.full[i], 1);
-      mbarrierInit(&sm.empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbarrierInit(&sm.aFull[i], kConverterWarps);
-      mbarrierInit(&sm.aEmpty[i], 1);
-    }
-    mbarrierInit(&sm.accDone, 1);
-    mbarrierInit(&sm.unsignalled, 1);
-    sm.abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  fenceBeforeSync();
-  __syncthreads();
-  fenceAfterSync();
-  const unsigned tmem = sm.tmemBase;
-  volatile int *abort = &sm.abort;
-  bool valid = false;
-
-  if (warp == kProducerWarp) {
-    const unsigned boxBytes = copyRows ? unsigned(BK * BN * 4) : 0u;
-    const unsigned blockBytes = unsigned(2 * panel::kPart * 4);
-    int64_t issued = 0;
-    if (lane == 0 && copyRows) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&weights.map))
-                   : "memory");
-      if constexpr (EPI == gemm::kSwiGluPanel)
-        asm volatile("prefetch.tensormap [%0];"
-                     ::"l"(reinterpret_cast<unsigned long long>(&upWeights->map))
-                     : "memory");
-    }
-    for (int64_t kt = 0; kt < slices; ++kt) {
-      const int slot = int(kt % S);
-      bool ok = true;
-      if (lane == 0 && kt >= S)
-        ok = waitPhase(&sm.empty[slot], unsigned((kt / S - 1) & 1), abort);
-      if (!__shfl_sync(0xffffffffu, ok, 0))
-        break;
-      if (lane == 0) {
-        mbarrierArriveExpectTx(&sm.full[slot], blockBytes * unsigned(tiles) + boxBytes);
-        for (int j = 0; j < tiles; ++j)
-          bulkCopy(&sm.a[slot][j][0][0][0][0],
-                   p.a + ((group * MT + j) * allSlices + kBegin + kt) * panel::kBlock, blockBytes,
-                   &sm.full[slot]);
-        if (copyRows) {
-          const int k0 = int((kBegin + kt) * BK);
-          if constexpr (EPI == gemm::kSwiGluPanel) {
-            tensorCopy(&sm.rawB[slot][0][0], &weights.map, int(n0), k0, int(s.layer),
-                       &sm.full[slot]);
-            tensorCopy(&sm.rawB[slot][0][0] + BK * (BN / 2), &upWeights->map, int(n0), k0,
-                       int(s.layer), &sm.full[slot]);
-          } else {
-            tensorCopy(&sm.rawB[slot][0][0], &weights.map, int(n0), k0, int(s.layer),
-                       &sm.full[slot]);
-          }
-        }
-      }
-      issued = kt + 1;
-    }
-    if (lane == 0)
-      for (int64_t kt = issued > S ? issued - S : 0; kt < issued; ++kt)
-        waitPhase(&sm.full[kt % S], unsigned((kt / S) & 1), nullptr);
-    __syncwarp();
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      constexpr unsigned idesc = instructionDescriptor<BN>(); // M = 128, N = 128, tf32, K-major
-      const bool injected =
-          g_injectUnsignalledWait != 0 && !waitPhase(&sm.unsignalled, 0, abort);
-      for (int64_t kt = 0; kt < slices && !injected; ++kt) {
-        const int slot = int(kt % S), buffer = int(kt & 1);
-        if (!waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort) ||
-            !waitPhase(&sm.aFull[buffer], unsigned((kt / 2) & 1), abort))
-          break;
-        fenceAfterSync();
-        const int64_t remaining = K - (kBegin + kt) * BK;
-        const int steps = int(remaining >= BK ? BK / 8 : (remaining + 7) / 8);
-        const unsigned wHi = tmem + weightColumnT<MT>(buffer, 0);
-        const unsigned wLo = tmem + weightColumnT<MT>(buffer, 1);
-        for (int ks = 0; ks < steps; ++ks) {
-          const unsigned first = (kt == 0 && ks == 0) ? 0u : 1u;
-          for (int j = 0; j < tiles; ++j) {
-            const unsigned long long xHi =
-                matrixDescriptor(sm.a[slot][j][0][2 * ks], BM * 16, 128);
-            const unsigned long long xLo =
-                matrixDescriptor(sm.a[slot][j][1][2 * ks], BM * 16, 128);
-            const unsigned d = tmem + unsigned(j * BM);
-            mmaTmemA(d, wHi + unsigned(8 * ks), xHi, idesc, first);
-            mmaTmemA(d, wHi + unsigned(8 * ks), xLo, idesc, 1u);
-            mmaTmemA(d, wLo + unsigned(8 * ks), xHi, idesc, 1u);
-          }
-        }
-        commit(&sm.empty[slot]);
-        commit(&sm.aEmpty[buffer]);
-      }
-      commit(&sm.accDone);
-    }
-    __syncwarp();
-  } else {
-    // Converter warp: its lanes hold output columns n = 32 q + lane, q = warp % 4 (a warp
-    // reaches the tensor-memory lanes of its own quarter only); half (warp - 2) / 4 of the
-    // slice's 32 k.
-    const int quarter = warp % 4, half = (warp - 2) / 4;
-    const int n = quarter * kWarp + lane;
-    const unsigned laneBase = unsigned(quarter * kWarp) << 16;
-    for (int64_t kt = 0; kt < slices; ++kt) {
-      const int slot = int(kt % S), buffer = int(kt & 1);
-      bool ok = !copyRows || waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort);
-      if (ok && kt >= 2)
-        ok = waitPhase(&sm.aEmpty[buffer], unsigned((kt / 2 - 1) & 1), abort);
-      if (!__all_sync(0xffffffffu, ok))
-        break;
-      fenceAfterSync();
-      const int64_t k0 = (kBegin + kt) * BK;
-      float hi[16], lo[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int kk = half * 16 + i;
-        const int64_t k = k0 + kk;
-        float value = 0.f;
-        if (k < K) {
-          if constexpr (EPI == gemm::kSwiGluPanel) {
-            const int box = n / (BN / 2), col = n % (BN / 2);
-            if (copyRows)
-              value = (&sm.rawB[slot][0][0])[(box * BK + kk) * (BN / 2) + col];
-            else if (n0 + col < N)
-              value = (box ? W2 : W)[k * N + n0 + col];
-          } else {
-            if (copyRows)
-              value = sm.rawB[slot][kk][n];
-            else if (n0 + n < N)
-              value = W[k * N + n0 + n];
-          }
-        }
-        panel::split(value, hi[i], lo[i]);
-      }
-      tmemStore16(tmem + laneBase + weightColumnT<MT>(buffer, 0) + unsigned(16 * half), hi);
-      tmemStore16(tmem + laneBase + weightColumnT<MT>(buffer, 1) + unsigned(16 * half), lo);
-      tmemStoreWait();
-      fenceBeforeSync();
-      __syncwarp();
-      if (lane == 0)
-        mbarrierArrive(&sm.aFull[buffer]);
-    }
-    const bool done = waitPhase(&sm.accDone, 0, nullptr);
-    fenceAfterSync();
-    valid = epilogueAll(done && !*abort) && hasWork;
-  }
-  // Epilogue, one row tile at a time: each converter warp reads its 32 output columns (lanes)
-  // for half of the tile's 128 rows (accumulator columns) and stages them as [row][column].
-  Staging<BN> &stage = *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0][0]);
-  for (int j = 0; j < MT; ++j) {
-    if (warp >= 2) {
-      const int quarter = warp % 4, half = (warp - 2) / 4;
-      const int n = quarter * kWarp + lane;
-      const unsigned laneAddress = tmem + unsigned(j * BM) + (unsigned(quarter * kWarp) << 16);
-      const bool use = valid && j < tiles;
-#pragma unroll 1
-      for (int m0 = half * (BM / 2); m0 < (half + 1) * (BM / 2); m0 += 16) {
-        float v[16];
-        if (use)
-          tmemLoad16(laneAddress + unsigned(m0), v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          stage[m0 + i][n] = use ? v[i] : 0.f;
-      }
-    }
-    if constexpr (SPLITS > 1)
-      clusterSync();
-    else
-      __syncthreads();
-    if (warp >= 2 && j < tiles && __all_sync(0xffffffffu, !*abort))
-      reduceAndStore<BN, EPI, SPLITS>(p, stage, (group * MT + j) * BM, nt, position);
-    fenceBeforeSync();
-    if constexpr (SPLITS > 1)
-      clusterSync();
-    else
-      __syncthreads();
-  }
-  if (warp == kMmaWarp)
-    tmemFree<tmemColumnsT<MT>()>(tmem);
 }
 
 } // namespace ckl::kernels::tc
