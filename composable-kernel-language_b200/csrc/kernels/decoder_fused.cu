@@ -169,7 +169,12 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
 // One CTA per (request, head): WARPS warps stream the K and V rows 0..p of the cache with
 // 16-byte loads, D/4 lanes per row; each lane group keeps an online softmax state
 // (running max, normaliser, weighted V) and the states merge across groups and warps.
-constexpr int kAttentionWarps = 4;
+// Eight warps of four-row-deep loads: at the cfg5 shard (8192 request-heads, 2048 rows of 256
+// bytes) 7.40 TB/s against 7.18-7.19 with four warps per CTA and the same unroll (two, three or
+// eight rows deep, 6, 12 or 16 warps, and 1-D bulk copies through shared memory all measured no
+// faster).  The split kernel, which runs few CTAs, keeps four warps.
+constexpr int kAttentionWarps = 8;
+constexpr int kSplitWarps = 4;
 constexpr int kAttentionUnroll = 4;
 
 // Attention is registered without dependent launch: started early behind its q/k/v
@@ -278,17 +283,17 @@ constexpr int kMaxAttentionSplits = 32;
 // range order - a fixed order, so results do not depend on which CTA finished last - and
 // writes the context row.  Ranges past the last cache row contribute empty states.
 template <int D>
-__global__ void __launch_bounds__(kAttentionWarps *kWarp)
+__global__ void __launch_bounds__(kSplitWarps *kWarp)
     attentionSplitKernel(const float *q, const float *kc, const float *vc, const int *position,
                          float *ctx, float *partials, unsigned *arrivals, float scale,
                          AttentionSpec s) {
   dependentLaunchWait();
   constexpr int LPR = D / 4;
   constexpr int RPW = kWarp / LPR;
-  constexpr int STEP = kAttentionWarps * RPW;
+  constexpr int STEP = kSplitWarps * RPW;
   constexpr int ROW4 = D / 4;
   constexpr int SLOT = D + 4; // m, l, two pad words, acc[D]: acc stays 16-byte aligned
-  __shared__ SoftmaxState warpState[kAttentionWarps][LPR];
+  __shared__ SoftmaxState warpState[kSplitWarps][LPR];
   __shared__ int lastArrival;
   // The last arriver's copy of its pair's range states, loaded by all threads at once.
   __shared__ __align__(16) float gathered[kMaxAttentionSplits * SLOT];
@@ -359,7 +364,7 @@ __global__ void __launch_bounds__(kAttentionWarps *kWarp)
     if (warp == 0 && group == 0) {
       SoftmaxState total = warpState[0][sub];
 #pragma unroll
-      for (int w = 1; w < kAttentionWarps; ++w)
+      for (int w = 1; w < kSplitWarps; ++w)
         mergeState(total, warpState[w][sub]);
       float *slot = partials + (bh * splits + range) * SLOT;
       if (sub == 0) {
@@ -423,7 +428,7 @@ bool attentionSplitGeometry(const void *spec, std::size_t, library::Geometry *g)
     return false;
   const int64_t items = rows * s.A * s.splits;
   g->grid[0] = unsigned(s.grid > 0 && s.grid < items ? s.grid : items);
-  g->block[0] = kAttentionWarps * kWarp;
+  g->block[0] = kSplitWarps * kWarp;
   return true;
 }
 
