@@ -530,7 +530,7 @@ FULL_JOB_REQUESTS = 4096  # BASELINE config 5's whole job
 FULL_JOB_STEPS = 8
 
 
-def reference_path(sess, ms_per_step, group, p0, tokens):
+def reference_path(sess, ms_per_step, group, p0, tokens, rounds=1, steps=NAIVE_STEPS):
     """The reference's own code path on this GPU, timed and used as the parity check.
 
     Every kernel is generated from its ``workloads.py`` body (naive FP32 code, no library, no
@@ -538,7 +538,9 @@ def reference_path(sess, ms_per_step, group, p0, tokens):
     inferred CUDA graph on the session's buffers.  It stands in for the reference's
     MLIR-compiled graph, which needs an LLVM/MLIR toolchain absent here.  Parity: from the same
     state (end of the prompt), `PARITY_STEPS` steps of the measured program and of this one
-    must give the same greedy tokens and logits within 1e-4 relative / 1e-5 absolute."""
+    must give the same greedy tokens and logits within 1e-4 relative / 1e-5 absolute.  Its
+    time per step is the median over `rounds` rounds of `steps` graph launches from the end of
+    the prompt (the small configurations use the protocol of their own measurement)."""
     import ckl
     from ckl.workloads import decoder
 
@@ -568,9 +570,14 @@ def reference_path(sess, ms_per_step, group, p0, tokens):
     restart(sess, p0, tokens)
     naive.run(mode="graph")
     naive.synchronize()
-    barrier(group)
-    naive_ms = reduce_max(group, naive.time_launches(NAIVE_STEPS, mode="graph")) / NAIVE_STEPS
-    return ({"ms_per_step": naive_ms, "steps": NAIVE_STEPS,
+    timings = []
+    for _ in range(rounds):
+        restart(sess, p0, tokens)
+        naive.synchronize()
+        barrier(group)
+        timings.append(reduce_max(group, naive.time_launches(steps, mode="graph")) / steps)
+    naive_ms = statistics.median(timings)
+    return ({"ms_per_step": naive_ms, "steps": steps, "rounds": rounds,
              "graph_nodes_per_step": naive.node_count, "speedup": naive_ms / ms_per_step,
              "compile_s": round(compile_s, 2),
              "what": "reference kernel bodies compiled naively (ckl codegen + NVRTC, sm_100a), "
@@ -639,7 +646,8 @@ def small_decoder(name, local):
         inv.synchronize()
         rounds.append(inv.time_launches(SMALL_STEPS, mode="graph") / SMALL_STEPS)
     ms = statistics.median(rounds)
-    naive, parity = reference_path(sess, ms, None, p0, last)
+    naive, parity = reference_path(sess, ms, None, p0, last, rounds=SMALL_ROUNDS,
+                                   steps=SMALL_STEPS)
     return {"ms_per_step": ms, "us_per_step": 1000.0 * ms, "tokens_per_s": b / (ms / 1000.0),
             "graph_nodes_per_step": inv.node_count, "naive_ms_per_step": naive["ms_per_step"],
             "speedup_vs_naive_graph": naive["speedup"], "parity_check": parity["passed"],
