@@ -58,10 +58,10 @@ PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
 # DRAM bytes per algorithmic byte of one attention launch, from an ncu capture of the same
-# kernel on the 32-request cfg5 shard at position 2049 (read 537.02 MB + write 3.85 MB for
-# 537.4 MB of K/V rows).  The traffic grows with the rows read, so the ratio scales it to the
-# bench workload.
-ATTENTION_TRAFFIC_RATIO = (537.02e6 + 3.85e6) / 537.4e6
+# kernel on the 32-request cfg5 shard at position 2047 (read 537.03 MB + write 4.03 MB for
+# 537.13 MB of K/V rows, q and context).  The traffic grows with the rows read, so the ratio
+# scales it to the bench workload.
+ATTENTION_TRAFFIC_RATIO = (537.028608e6 + 4.029952e6) / 537.133056e6
 
 
 def peaks():
@@ -474,7 +474,7 @@ def gpu_arm(args, workload, world, rank, local, group):
                                "stream such as attention's K/V rows can exceed it",
                     "traffic": algorithmic * ATTENTION_TRAFFIC_RATIO,
                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
-                                      "32-request shard at position 2049, scaled by algorithmic "
+                                      "32-request shard at position 2047, scaled by algorithmic "
                                       "bytes",
                     "algorithmic_bytes_per_launch": algorithmic,
                     "launch_ms": launch_ms, "launches_profiled": len(attention),
