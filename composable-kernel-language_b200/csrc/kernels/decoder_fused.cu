@@ -34,10 +34,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.w = w, p.out = dst, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kPlain, gemm::kStore>(p);
-  else
-    gemm::body<Cfg, gemm::kPlain, gemm::kStore>(p);
+  gemm::dispatch<Cfg, gemm::kPlain, gemm::kStore>(p);
 }
 
 template <class Cfg>
@@ -47,10 +44,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.out = dst, p.eps = eps, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kRms, gemm::kStore>(p);
-  else
-    gemm::body<Cfg, gemm::kRms, gemm::kStore>(p);
+  gemm::dispatch<Cfg, gemm::kRms, gemm::kStore>(p);
 }
 
 template <class Cfg>
@@ -61,10 +55,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = dst;
   p.eps = eps, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kRms, gemm::kRope>(p);
-  else
-    gemm::body<Cfg, gemm::kRms, gemm::kRope>(p);
+  gemm::dispatch<Cfg, gemm::kRms, gemm::kRope>(p);
 }
 
 template <class Cfg>
@@ -76,10 +67,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.table = table, p.position = position, p.out = cache;
   p.eps = eps, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
-  else
-    gemm::body<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
+  gemm::dispatch<Cfg, gemm::kRms, gemm::kRopeAppend>(p);
 }
 
 template <class Cfg>
@@ -89,10 +77,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.position = position, p.out = cache, p.eps = eps, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kRms, gemm::kAppend>(p);
-  else
-    gemm::body<Cfg, gemm::kRms, gemm::kAppend>(p);
+  gemm::dispatch<Cfg, gemm::kRms, gemm::kAppend>(p);
 }
 
 template <class Cfg>
@@ -102,10 +87,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.w = w, p.residual = residual, p.out = dst, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kPlain, gemm::kResidual>(p);
-  else
-    gemm::body<Cfg, gemm::kPlain, gemm::kResidual>(p);
+  gemm::dispatch<Cfg, gemm::kPlain, gemm::kResidual>(p);
 }
 
 template <class Cfg>
@@ -115,10 +97,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = gate, p.a2 = up, p.w = w, p.residual = residual, p.out = dst, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
-  else
-    gemm::body<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
+  gemm::dispatch<Cfg, gemm::kSwiGlu, gemm::kResidual>(p);
 }
 
 template <class Cfg>
@@ -128,10 +107,7 @@ __global__ void __launch_bounds__(Cfg::kThreads)
   dependentLaunchEntry();
   Params p;
   p.a = x, p.gain = gain, p.w = w, p.out = logits, p.partials = partials, p.eps = eps, p.s = s;
-  if constexpr (gemm::IsRows<Cfg>::value)
-    gemm::rowsBody<Cfg, gemm::kRms, gemm::kArgmax>(p);
-  else
-    gemm::body<Cfg, gemm::kRms, gemm::kArgmax>(p);
+  gemm::dispatch<Cfg, gemm::kRms, gemm::kArgmax>(p);
 }
 
 bool gemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
@@ -161,6 +137,10 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
     case 6: return reinterpret_cast<const void *>(&fn<gemm::Rows1>);                           \
     case 7: return reinterpret_cast<const void *>(&fn<gemm::Rows4>);                           \
     case 8: return reinterpret_cast<const void *>(&fn<gemm::Rows16>);                          \
+    case 9: return reinterpret_cast<const void *>(&fn<gemm::Streamed1>);                       \
+    case 10: return reinterpret_cast<const void *>(&fn<gemm::Streamed4>);                      \
+    case 11: return reinterpret_cast<const void *>(&fn<gemm::Streamed1Wide>);                  \
+    case 12: return reinterpret_cast<const void *>(&fn<gemm::Streamed4Wide>);                  \
     default: return nullptr;                                                                   \
     }                                                                                          \
   }

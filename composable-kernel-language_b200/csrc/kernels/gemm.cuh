@@ -54,12 +54,22 @@ using Small = Config<16, 64, 16, 2, 4>;    // 128 threads, M <= 16
 using Medium = Config<64, 64, 16, 4, 4>;   // 256 threads
 using Large = Config<128, 128, 8, 8, 8>;   // 256 threads, M >= 256 and wide N
 
+// The streamed few-row kernel (below) takes 1 to 4 rows of a projection with 1 MB or more of
+// weights whose K rows of A fit its shared-memory staging.
+inline bool streamedFits(const GemmSpec &s) {
+  return s.M <= 4 && s.N % 4 == 0 && s.K % 4 == 0 && s.K <= 4096 &&
+         s.K * s.N >= (int64_t(1) << 18);
+}
+
 // Tile configuration for a specialization: 0 small, 1 medium, 2 large, 6/7/8 the few-row
-// kernel for 1 / 4 / 16 rows.  `config` 1-3 forces a tile; 0 (automatic) and 5 (FFMA only)
-// choose by shape.
+// kernel for 1 / 4 / 16 rows, 9/10 the streamed few-row kernel for 1 / 4 rows with 16-column
+// CTAs and 11/12 with 64-column CTAs (outputs of 16384 columns or more).  `config` 1-3 forces
+// a tile; 0 (automatic) and 5 (FFMA only) choose by shape.
 inline int chooseConfig(const GemmSpec &s) {
   if (s.config > 0 && s.config <= 3)
     return int(s.config - 1);
+  if (streamedFits(s))
+    return (s.N >= 16384 ? 11 : 9) + (s.M <= 1 ? 0 : 1);
   if (s.M <= 1)
     return 6;
   if (s.M <= 4)
@@ -91,6 +101,21 @@ inline bool geometry(const GemmSpec &s, library::Geometry *g) {
     g->grid[1] = 1;
     g->block[0] = 256;
     break;
+  case 9:
+  case 10:
+  case 11:
+  case 12: {
+    const bool wide = chooseConfig(s) >= 11;
+    g->grid[0] = ceilDiv(s.N, wide ? 64 : 16);
+    g->grid[1] = 1;
+    g->block[0] = 256;
+    // A [K][rows], gains [K], the k-slots' sums [slots][rows][columns], the tile and the row
+    // scales.
+    const int64_t rows = chooseConfig(s) % 2 == 1 ? 1 : 4, cols = wide ? 64 : 16;
+    g->sharedBytes =
+        unsigned((s.K * rows + s.K + (256 / (cols / 4)) * rows * cols + rows * cols + 4) * 4);
+    break;
+  }
   default: return false;
   }
   return g->grid[1] <= 65535;
@@ -469,6 +494,266 @@ template <class Cfg, int PRO, int EPI> __device__ void rowsBody(const Params &p)
       }
     }
   }
+}
+
+// ---- few-row projections streaming large weights (1 to 4 requests) ----------------------
+// The kernel above gives a 1024-wide output 32 CTAs whose threads each keep eight 4-byte loads
+// in flight, ~8 KB per CTA: far less than HBM needs to stream the weights of the decoder's
+// larger projections (4-131 MB).  Here a CTA owns QUADS float4 columns and its 256 threads are
+// QUADS quads x SLOTS k-slots: thread (q, j) reads the 16-byte quad q of k rows j, j + SLOTS,
+// ..., kDepth loads in flight and the next kDepth issued before the current ones are used (a
+// 1024-wide output runs on 64 CTAs of 16 columns, the LM head on 500 of 64).  The rows of A
+// (all of K, at most four rows) go through the prologue into shared memory once, k-major and
+// read as broadcasts, while the first loads are in flight.  Each thread keeps one float4
+// accumulator per row over its k rows in increasing order; the k-slots' sums are added in slot
+// order (deterministic) and the fused epilogue runs per (row, quad).
+template <int ROWS, int QUADS> struct Streamed {
+  static constexpr int kRows = ROWS, kQuads = QUADS, kThreads = 256;
+  static constexpr int kSlots = kThreads / QUADS, kCols = 4 * QUADS, kDepth = 8;
+};
+using Streamed1 = Streamed<1, 4>;
+using Streamed4 = Streamed<4, 4>;
+using Streamed1Wide = Streamed<1, 16>;
+using Streamed4Wide = Streamed<4, 16>;
+
+template <class Cfg> struct IsStreamed : std::false_type {};
+template <int R, int Q> struct IsStreamed<Streamed<R, Q>> : std::true_type {};
+
+// Dynamic shared memory (geometry, config 9-12): A [K][ROWS], the gains [K], the k-slots'
+// sums [SLOTS][ROWS][COLS], the reduced tile [ROWS][COLS] and the row scales.
+template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params &p) {
+  constexpr int R = Cfg::kRows, Q = Cfg::kQuads, SLOTS = Cfg::kSlots, DEPTH = Cfg::kDepth;
+  constexpr int COLS = Cfg::kCols, kThreads = Cfg::kThreads;
+  extern __shared__ __align__(16) float dynamicShared[];
+  const GemmSpec &s = p.s;
+  const int64_t M = s.M, K = s.K, N = s.N;
+  float *As = dynamicShared;                 // [K][R]
+  float *gainS = As + K * R;                 // [K] (RMSNorm)
+  float *partial = gainS + K;                // [SLOTS][R][COLS]
+  float *tile = partial + SLOTS * R * COLS;  // [R][COLS]
+  float *rowInv = tile + R * COLS;           // [R]
+  const int tid = threadIdx.x, q = tid % Q, slot = tid / Q;
+  const int64_t n0 = int64_t(blockIdx.x) * COLS, n = n0 + 4 * q;
+  const bool live = n < N; // N % 4 == 0 (geometry): a quad is inside or outside as a whole
+  const float *W = p.w + s.layer * K * N + n;
+  const bool vec = aligned16(p.w) && N % 4 == 0; // CTA-uniform
+
+  int position = 0;
+  if constexpr (EPI == kRope || EPI == kRopeAppend || EPI == kAppend) {
+    position = p.position[0];
+    if (position < 0 || position >= s.T)
+      return; // outside cache capacity: the step writes nothing
+  }
+  auto load = [&](int64_t k) {
+    if (!live || k >= K)
+      return make_float4(0.f, 0.f, 0.f, 0.f);
+    const float *row = W + k * N;
+    return vec ? __ldg(reinterpret_cast<const float4 *>(row))
+               : make_float4(__ldg(row), __ldg(row + 1), __ldg(row + 2), __ldg(row + 3));
+  };
+  float4 w[DEPTH];
+#pragma unroll
+  for (int d = 0; d < DEPTH; ++d)
+    w[d] = load(slot + int64_t(d) * SLOTS);
+
+  // Rows of A into As [K][R] (k-major): every thread's float4s of the rows are loaded eight at
+  // a time with all loads in flight (SwiGLU: silu(gate) * up as stored); for RMSNorm the raw
+  // rows and the layer's gains are staged first, the rows' sums of squares reduced over the CTA
+  // (fixed order) and the rows then scaled in place, x * inv * gain rounded as the reference.
+  const int64_t K4 = K / 4; // K % 4 == 0 (streamedFits)
+  const bool avec = aligned16(p.a) && (PRO != kSwiGlu || aligned16(p.a2)) &&
+                    (PRO != kRms || aligned16(p.gain));
+  auto load4 = [&](const float *at) {
+    return avec ? *reinterpret_cast<const float4 *>(at)
+                : make_float4(at[0], at[1], at[2], at[3]);
+  };
+  float sumSquares[R];
+#pragma unroll
+  for (int m = 0; m < R; ++m)
+    sumSquares[m] = 0.f;
+  for (int64_t f0 = tid; f0 < R * K4; f0 += 8 * kThreads) {
+    float4 a[8], b[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t f = f0 + int64_t(u) * kThreads, m = f / K4, k = 4 * (f % K4);
+      a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (f < R * K4 && m < M) {
+        a[u] = load4(p.a + m * K + k);
+        if constexpr (PRO == kSwiGlu)
+          b[u] = load4(p.a2 + m * K + k);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t f = f0 + int64_t(u) * kThreads, m = f / K4, k = 4 * (f % K4);
+      if (f >= R * K4)
+        continue;
+      float4 v = a[u];
+      if constexpr (PRO == kSwiGlu) {
+        v = make_float4(__fmul_rn(a[u].x / (1.0f + expf(-a[u].x)), b[u].x),
+                        __fmul_rn(a[u].y / (1.0f + expf(-a[u].y)), b[u].y),
+                        __fmul_rn(a[u].z / (1.0f + expf(-a[u].z)), b[u].z),
+                        __fmul_rn(a[u].w / (1.0f + expf(-a[u].w)), b[u].w));
+      }
+      if constexpr (PRO == kRms) {
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          if (r == m)
+            sumSquares[r] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      As[(k + 0) * R + m] = v.x;
+      As[(k + 1) * R + m] = v.y;
+      As[(k + 2) * R + m] = v.z;
+      As[(k + 3) * R + m] = v.w;
+    }
+  }
+  if constexpr (PRO == kRms) {
+    // The layer's gains beside A.
+    for (int64_t k4 = tid; k4 < K4; k4 += kThreads)
+      *reinterpret_cast<float4 *>(gainS + 4 * k4) = load4(p.gain + s.layer * K + 4 * k4);
+    // Row sums: warp shuffles, then the eight warps in order.
+    const int warp = tid / kWarp, lane = tid % kWarp;
+    float *warpSums = tile; // [8][R], free until the epilogue (R * COLS >= 8 * R)
+#pragma unroll
+    for (int m = 0; m < R; ++m) {
+      const float total = warpSum(sumSquares[m]);
+      if (lane == 0)
+        warpSums[warp * R + m] = total;
+    }
+    __syncthreads();
+    if (tid < R) {
+      float total = warpSums[tid];
+      for (int w = 1; w < kThreads / kWarp; ++w)
+        total += warpSums[w * R + tid];
+      rowInv[tid] = rsqrtf(total / float(K) + p.eps);
+    }
+    __syncthreads();
+    for (int64_t e = tid; e < K * R; e += kThreads) {
+      const int m = int(e % R);
+      As[e] = m < M ? __fmul_rn(__fmul_rn(As[e], rowInv[m]), gainS[e / R]) : 0.f;
+    }
+  }
+  __syncthreads();
+
+  float4 acc[R];
+#pragma unroll
+  for (int m = 0; m < R; ++m)
+    acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t base = slot; base < K; base += int64_t(DEPTH) * SLOTS) {
+    float4 next[DEPTH];
+#pragma unroll
+    for (int d = 0; d < DEPTH; ++d)
+      next[d] = load(base + int64_t(DEPTH + d) * SLOTS);
+#pragma unroll
+    for (int d = 0; d < DEPTH; ++d) {
+      const int64_t k = base + int64_t(d) * SLOTS;
+      if (k < K) {
+#pragma unroll
+        for (int m = 0; m < R; ++m) {
+          const float a = As[k * R + m];
+          acc[m].x = fmaf(a, w[d].x, acc[m].x);
+          acc[m].y = fmaf(a, w[d].y, acc[m].y);
+          acc[m].z = fmaf(a, w[d].z, acc[m].z);
+          acc[m].w = fmaf(a, w[d].w, acc[m].w);
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < DEPTH; ++d)
+      w[d] = next[d];
+  }
+#pragma unroll
+  for (int m = 0; m < R; ++m)
+    *reinterpret_cast<float4 *>(&partial[(slot * R + m) * COLS + 4 * q]) = acc[m];
+  __syncthreads();
+  // Sum of the k-slots of every (row, column), in slot order.
+  for (int o = tid; o < R * COLS; o += kThreads) {
+    float v = partial[o];
+#pragma unroll 16
+    for (int j = 1; j < SLOTS; ++j)
+      v = __fadd_rn(v, partial[j * R * COLS + o]);
+    tile[o] = v;
+  }
+  __syncthreads();
+
+  if constexpr (EPI == kArgmax) {
+    // One warp per row: the row's logits over the CTA's columns, then its argmax partial.
+    const int warp = tid / kWarp, lane = tid % kWarp;
+    for (int m = warp; m < R && m < M; m += kThreads / kWarp) {
+      float best = -CUDART_INF_F;
+      int bestIndex = 0x7fffffff;
+      for (int c = lane; c < COLS; c += kWarp) {
+        const int64_t col = n0 + c;
+        if (col < N) {
+          const float v = tile[m * COLS + c];
+          p.out[m * N + col] = v;
+          argmaxMerge(best, bestIndex, v, int(col));
+        }
+      }
+#pragma unroll
+      for (int o = kWarp / 2; o > 0; o >>= 1)
+        argmaxMerge(best, bestIndex, __shfl_xor_sync(0xffffffffu, best, o),
+                    __shfl_xor_sync(0xffffffffu, bestIndex, o));
+      if (lane == 0)
+        p.partials[m * s.tiles + blockIdx.x] = make_float2(best, __int_as_float(bestIndex));
+    }
+    return;
+  }
+  // One thread per (row, quad) of the tile.
+  if (tid >= R * Q)
+    return;
+  const int m = tid / Q, qq = tid % Q;
+  const int64_t c = n0 + 4 * qq;
+  if (m >= M || c >= N)
+    return;
+  float4 v = *reinterpret_cast<const float4 *>(&tile[m * COLS + 4 * qq]);
+  if constexpr (EPI == kStore || EPI == kResidual) {
+    float *lanes = &v.x;
+    if constexpr (EPI == kResidual) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        lanes[j] = __fadd_rn(p.residual[m * N + c + j], lanes[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      p.out[m * N + c + j] = lanes[j];
+  } else {
+    // Pairs (c, c + 1) and (c + 2, c + 3): c is a multiple of 4 and D is even, so a pair never
+    // straddles two heads.
+    const float *lanes = &v.x;
+    const int64_t D = s.D, R2 = s.D / 2;
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      const int64_t col = c + j, h = col / D, d = col % D;
+      float first = lanes[j], second = lanes[j + 1];
+      if constexpr (EPI == kRope || EPI == kRopeAppend) {
+        const float *cs = p.table + (int64_t(position) * R2 + d / 2) * 2;
+        const float cosine = cs[0], sine = cs[1];
+        const float x = __fsub_rn(__fmul_rn(first, cosine), __fmul_rn(second, sine));
+        const float y = __fadd_rn(__fmul_rn(first, sine), __fmul_rn(second, cosine));
+        first = x;
+        second = y;
+      }
+      if constexpr (EPI == kRope) {
+        p.out[m * N + col] = first;
+        p.out[m * N + col + 1] = second;
+      } else {
+        float *at = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
+        at[0] = first;
+        at[1] = second;
+      }
+    }
+  }
+}
+
+// The projection body of a tile configuration.
+template <class Cfg, int PRO, int EPI> __device__ __forceinline__ void dispatch(const Params &p) {
+  if constexpr (IsRows<Cfg>::value)
+    rowsBody<Cfg, PRO, EPI>(p);
+  else if constexpr (IsStreamed<Cfg>::value)
+    streamedBody<Cfg, PRO, EPI>(p);
+  else
+    body<Cfg, PRO, EPI>(p);
 }
 
 } // namespace ckl::kernels::gemm
