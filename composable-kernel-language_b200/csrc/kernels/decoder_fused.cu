@@ -141,6 +141,11 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
     case 10: return reinterpret_cast<const void *>(&fn<gemm::Streamed4>);                      \
     case 11: return reinterpret_cast<const void *>(&fn<gemm::Streamed1Wide>);                  \
     case 12: return reinterpret_cast<const void *>(&fn<gemm::Streamed4Wide>);                  \
+    case 13: return reinterpret_cast<const void *>(&fn<gemm::Streamed8>);                      \
+    case 14: return reinterpret_cast<const void *>(&fn<gemm::Streamed8Wide>);                  \
+    case 15: return reinterpret_cast<const void *>(&fn<gemm::Streamed1Deep>);                  \
+    case 16: return reinterpret_cast<const void *>(&fn<gemm::Streamed4Deep>);                  \
+    case 17: return reinterpret_cast<const void *>(&fn<gemm::Streamed8Deep>);                  \
     default: return nullptr;                                                                   \
     }                                                                                          \
   }

@@ -54,22 +54,40 @@ using Small = Config<16, 64, 16, 2, 4>;    // 128 threads, M <= 16
 using Medium = Config<64, 64, 16, 4, 4>;   // 256 threads
 using Large = Config<128, 128, 8, 8, 8>;   // 256 threads, M >= 256 and wide N
 
-// The streamed few-row kernel (below) takes 1 to 4 rows of a projection with 1 MB or more of
+// The streamed few-row kernel (below) takes 1 to 8 rows of a projection with 1 MB or more of
 // weights whose K rows of A fit its shared-memory staging.
 inline bool streamedFits(const GemmSpec &s) {
-  return s.M <= 4 && s.N % 4 == 0 && s.K % 4 == 0 && s.K <= 4096 &&
+  return s.M <= 8 && s.N % 4 == 0 && s.K % 4 == 0 && s.K <= 4096 &&
          s.K * s.N >= (int64_t(1) << 18);
 }
 
+// Rows, CTA columns and threads of a streamed configuration (9-17).
+inline int streamedRows(int config) {
+  switch (config) {
+  case 9: case 11: case 15: return 1;
+  case 10: case 12: case 16: return 4;
+  default: return 8;
+  }
+}
+inline bool streamedWide(int config) { return config == 11 || config == 12 || config == 14; }
+inline int streamedThreads(int config) { return config >= 15 ? 512 : 256; }
+
 // Tile configuration for a specialization: 0 small, 1 medium, 2 large, 6/7/8 the few-row
-// kernel for 1 / 4 / 16 rows, 9/10 the streamed few-row kernel for 1 / 4 rows with 16-column
-// CTAs and 11/12 with 64-column CTAs (outputs of 16384 columns or more).  `config` 1-3 forces
-// a tile; 0 (automatic) and 5 (FFMA only) choose by shape.
+// kernel for 1 / 4 / 16 rows, 9/10/13 the streamed few-row kernel for 1 / 4 / 8 rows with
+// 16-column CTAs, 11/12/14 with 64-column CTAs (outputs of 16384 columns or more) and 15/16/17
+// with 16-column CTAs of 512 threads (K of 2048 or more).
+// `config` 1-3 forces a tile; 0 (automatic) and 5 (FFMA only) choose by shape.
 inline int chooseConfig(const GemmSpec &s) {
   if (s.config > 0 && s.config <= 3)
     return int(s.config - 1);
-  if (streamedFits(s))
-    return (s.N >= 16384 ? 11 : 9) + (s.M <= 1 ? 0 : 1);
+  if (streamedFits(s)) {
+    const int rows = s.M <= 1 ? 0 : s.M <= 4 ? 1 : 2;
+    if (s.N >= 16384)
+      return rows == 2 ? 14 : 11 + rows;
+    if (s.K >= 2048)
+      return 15 + rows;
+    return rows == 2 ? 13 : 9 + rows;
+  }
   if (s.M <= 1)
     return 6;
   if (s.M <= 4)
@@ -104,16 +122,24 @@ inline bool geometry(const GemmSpec &s, library::Geometry *g) {
   case 9:
   case 10:
   case 11:
-  case 12: {
-    const bool wide = chooseConfig(s) >= 11;
+  case 12:
+  case 13:
+  case 14:
+  case 15:
+  case 16:
+  case 17: {
+    const int config = chooseConfig(s);
+    const bool wide = streamedWide(config);
+    const int threads = streamedThreads(config);
     g->grid[0] = ceilDiv(s.N, wide ? 64 : 16);
     g->grid[1] = 1;
-    g->block[0] = 256;
-    // A [K][rows], gains [K], the k-slots' sums [slots][rows][columns], the tile and the row
-    // scales.
-    const int64_t rows = chooseConfig(s) % 2 == 1 ? 1 : 4, cols = wide ? 64 : 16;
+    g->block[0] = unsigned(threads);
+    // A [K][rows], gains [K], the k-slots' sums [slots][rows x columns + 4], the tile and the
+    // row scales.
+    const int64_t rows = streamedRows(config), cols = wide ? 64 : 16;
     g->sharedBytes =
-        unsigned((s.K * rows + s.K + (256 / (cols / 4)) * rows * cols + rows * cols + 4) * 4);
+        unsigned((s.K * rows + s.K + (threads / (cols / 4)) * (rows * cols + 4) + rows * cols + 4) *
+                 4);
     break;
   }
   default: return false;
@@ -496,31 +522,38 @@ template <class Cfg, int PRO, int EPI> __device__ void rowsBody(const Params &p)
   }
 }
 
-// ---- few-row projections streaming large weights (1 to 4 requests) ----------------------
+// ---- few-row projections streaming large weights (1 to 8 requests) ----------------------
 // The kernel above gives a 1024-wide output 32 CTAs whose threads each keep eight 4-byte loads
 // in flight, ~8 KB per CTA: far less than HBM needs to stream the weights of the decoder's
 // larger projections (4-131 MB).  Here a CTA owns QUADS float4 columns and its 256 threads are
 // QUADS quads x SLOTS k-slots: thread (q, j) reads the 16-byte quad q of k rows j, j + SLOTS,
 // ..., kDepth loads in flight and the next kDepth issued before the current ones are used (a
 // 1024-wide output runs on 64 CTAs of 16 columns, the LM head on 500 of 64).  The rows of A
-// (all of K, at most four rows) go through the prologue into shared memory once, k-major and
+// (all of K, at most eight rows) go through the prologue into shared memory once, k-major and
 // read as broadcasts, while the first loads are in flight.  Each thread keeps one float4
 // accumulator per row over its k rows in increasing order; the k-slots' sums are added in slot
 // order (deterministic) and the fused epilogue runs per (row, quad).
-template <int ROWS, int QUADS> struct Streamed {
-  static constexpr int kRows = ROWS, kQuads = QUADS, kThreads = 256;
+template <int ROWS, int QUADS, int THREADS = 256> struct Streamed {
+  static constexpr int kRows = ROWS, kQuads = QUADS, kThreads = THREADS;
   static constexpr int kSlots = kThreads / QUADS, kCols = 4 * QUADS, kDepth = 8;
 };
 using Streamed1 = Streamed<1, 4>;
 using Streamed4 = Streamed<4, 4>;
 using Streamed1Wide = Streamed<1, 16>;
 using Streamed4Wide = Streamed<4, 16>;
+using Streamed8 = Streamed<8, 4>;
+using Streamed8Wide = Streamed<8, 16>;
+// 512 threads for deep K (2048 rows or more): twice the loads in flight per CTA, for grids
+// of fewer CTAs than SMs or CTAs that fill an SM's shared memory alone.
+using Streamed1Deep = Streamed<1, 4, 512>;
+using Streamed4Deep = Streamed<4, 4, 512>;
+using Streamed8Deep = Streamed<8, 4, 512>;
 
 template <class Cfg> struct IsStreamed : std::false_type {};
-template <int R, int Q> struct IsStreamed<Streamed<R, Q>> : std::true_type {};
+template <int R, int Q, int T> struct IsStreamed<Streamed<R, Q, T>> : std::true_type {};
 
-// Dynamic shared memory (geometry, config 9-12): A [K][ROWS], the gains [K], the k-slots'
-// sums [SLOTS][ROWS][COLS], the reduced tile [ROWS][COLS] and the row scales.
+// Dynamic shared memory (geometry, config 9-17): A [K][ROWS], the gains [K], the k-slots'
+// sums [SLOTS][ROWS x COLS + 4], the reduced tile [ROWS][COLS] and the row scales.
 template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params &p) {
   constexpr int R = Cfg::kRows, Q = Cfg::kQuads, SLOTS = Cfg::kSlots, DEPTH = Cfg::kDepth;
   constexpr int COLS = Cfg::kCols, kThreads = Cfg::kThreads;
@@ -529,8 +562,11 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
   const int64_t M = s.M, K = s.K, N = s.N;
   float *As = dynamicShared;                 // [K][R]
   float *gainS = As + K * R;                 // [K] (RMSNorm)
-  float *partial = gainS + K;                // [SLOTS][R][COLS]
-  float *tile = partial + SLOTS * R * COLS;  // [R][COLS]
+  // k-slot j's sums at partial + j * SP: [R][COLS] plus 4 floats, so that the slots of a warp
+  // start in different banks.
+  constexpr int SP = R * COLS + 4;
+  float *partial = gainS + K;                // [SLOTS][SP]
+  float *tile = partial + SLOTS * SP;        // [R][COLS]
   float *rowInv = tile + R * COLS;           // [R]
   const int tid = threadIdx.x, q = tid % Q, slot = tid / Q;
   const int64_t n0 = int64_t(blockIdx.x) * COLS, n = n0 + 4 * q;
@@ -567,15 +603,16 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     return avec ? *reinterpret_cast<const float4 *>(at)
                 : make_float4(at[0], at[1], at[2], at[3]);
   };
-  float sumSquares[R];
-#pragma unroll
-  for (int m = 0; m < R; ++m)
-    sumSquares[m] = 0.f;
+  // Float4 f of the staging is row f % R, columns 4 (f / R) .. + 3: the lanes of a warp write
+  // consecutive rows of the same k (few bank conflicts), and as kThreads % R == 0 every float4
+  // of a thread is in row tid % R.
+  static_assert(kThreads % R == 0, "rows per thread");
+  float sumSquares = 0.f;
   for (int64_t f0 = tid; f0 < R * K4; f0 += 8 * kThreads) {
     float4 a[8], b[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int64_t f = f0 + int64_t(u) * kThreads, m = f / K4, k = 4 * (f % K4);
+      const int64_t f = f0 + int64_t(u) * kThreads, m = f % R, k = 4 * (f / R);
       a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (f < R * K4 && m < M) {
         a[u] = load4(p.a + m * K + k);
@@ -585,7 +622,7 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int64_t f = f0 + int64_t(u) * kThreads, m = f / K4, k = 4 * (f % K4);
+      const int64_t f = f0 + int64_t(u) * kThreads, m = f % R, k = 4 * (f / R);
       if (f >= R * K4)
         continue;
       float4 v = a[u];
@@ -595,12 +632,8 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
                         __fmul_rn(a[u].z / (1.0f + expf(-a[u].z)), b[u].z),
                         __fmul_rn(a[u].w / (1.0f + expf(-a[u].w)), b[u].w));
       }
-      if constexpr (PRO == kRms) {
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-          if (r == m)
-            sumSquares[r] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      }
+      if constexpr (PRO == kRms)
+        sumSquares += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
       As[(k + 0) * R + m] = v.x;
       As[(k + 1) * R + m] = v.y;
       As[(k + 2) * R + m] = v.z;
@@ -611,15 +644,14 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     // The layer's gains beside A.
     for (int64_t k4 = tid; k4 < K4; k4 += kThreads)
       *reinterpret_cast<float4 *>(gainS + 4 * k4) = load4(p.gain + s.layer * K + 4 * k4);
-    // Row sums: warp shuffles, then the eight warps in order.
+    // Row sums: the lanes of one row (lane % R) by shuffles, then the warps in order.
     const int warp = tid / kWarp, lane = tid % kWarp;
-    float *warpSums = tile; // [8][R], free until the epilogue (R * COLS >= 8 * R)
+    float *warpSums = tile; // [warps][R], free until the epilogue (COLS >= warps)
 #pragma unroll
-    for (int m = 0; m < R; ++m) {
-      const float total = warpSum(sumSquares[m]);
-      if (lane == 0)
-        warpSums[warp * R + m] = total;
-    }
+    for (int o = kWarp / 2; o >= R; o >>= 1)
+      sumSquares += __shfl_xor_sync(0xffffffffu, sumSquares, o);
+    if (lane < R)
+      warpSums[warp * R + lane] = sumSquares;
     __syncthreads();
     if (tid < R) {
       float total = warpSums[tid];
@@ -648,13 +680,24 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     for (int d = 0; d < DEPTH; ++d) {
       const int64_t k = base + int64_t(d) * SLOTS;
       if (k < K) {
+        float a[R]; // this k row of every row of A (16-byte reads when R % 4 == 0)
+        if constexpr (R % 4 == 0) {
+#pragma unroll
+          for (int m = 0; m < R; m += 4) {
+            const float4 four = *reinterpret_cast<const float4 *>(&As[k * R + m]);
+            a[m] = four.x, a[m + 1] = four.y, a[m + 2] = four.z, a[m + 3] = four.w;
+          }
+        } else {
+#pragma unroll
+          for (int m = 0; m < R; ++m)
+            a[m] = As[k * R + m];
+        }
 #pragma unroll
         for (int m = 0; m < R; ++m) {
-          const float a = As[k * R + m];
-          acc[m].x = fmaf(a, w[d].x, acc[m].x);
-          acc[m].y = fmaf(a, w[d].y, acc[m].y);
-          acc[m].z = fmaf(a, w[d].z, acc[m].z);
-          acc[m].w = fmaf(a, w[d].w, acc[m].w);
+          acc[m].x = fmaf(a[m], w[d].x, acc[m].x);
+          acc[m].y = fmaf(a[m], w[d].y, acc[m].y);
+          acc[m].z = fmaf(a[m], w[d].z, acc[m].z);
+          acc[m].w = fmaf(a[m], w[d].w, acc[m].w);
         }
       }
     }
@@ -664,14 +707,14 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
   }
 #pragma unroll
   for (int m = 0; m < R; ++m)
-    *reinterpret_cast<float4 *>(&partial[(slot * R + m) * COLS + 4 * q]) = acc[m];
+    *reinterpret_cast<float4 *>(&partial[slot * SP + m * COLS + 4 * q]) = acc[m];
   __syncthreads();
   // Sum of the k-slots of every (row, column), in slot order.
   for (int o = tid; o < R * COLS; o += kThreads) {
     float v = partial[o];
 #pragma unroll 16
     for (int j = 1; j < SLOTS; ++j)
-      v = __fadd_rn(v, partial[j * R * COLS + o]);
+      v = __fadd_rn(v, partial[j * SP + o]);
     tile[o] = v;
   }
   __syncthreads();

@@ -221,13 +221,13 @@ _ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
 # Batches of 17 or more requests run the projections on tcgen05 tensor cores (GemmSpec config
 # 0; partial 128-row tiles with split-K still beat FFMA tiles from 17 rows); up to 16 the
 # few-row FFMA kernel is faster for small decoders, whose projections are latency-bound.  From
-# a hidden size of 512 the weights stream from HBM (1 MB and more per projection): up to four
-# requests the streamed few-row FFMA kernel (gemm.cuh, configs 9-12) reads them at HBM speed,
-# from five to sixteen the tensor-core kernels, which spread a projection over many more CTAs
+# a hidden size of 512 the weights stream from HBM (1 MB and more per projection): up to eight
+# requests the streamed few-row FFMA kernel (gemm.cuh, configs 9-17) reads them at HBM speed,
+# from nine to sixteen the tensor-core kernels, which spread a projection over many more CTAs
 # than the 16-row few-row kernel, are faster.  Config 5 keeps every projection on FFMA.
 _TENSOR_CORE_ROWS = 17
 _TENSOR_CORE_HIDDEN = 512
-_STREAMED_ROWS = 4
+STREAMED_ROWS = 8
 
 
 def _panel_floats(M: int, K: int) -> int:
@@ -343,7 +343,7 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
 
     tensor_cores = config == 0 and (shape(x)[0] >= _TENSOR_CORE_ROWS or
                                     (shape(x)[1] >= _TENSOR_CORE_HIDDEN and
-                                     shape(x)[0] > _STREAMED_ROWS))
+                                     shape(x)[0] > STREAMED_ROWS))
     eliminated: dict[int, list] = {}
     position = sincos = kc = vc = None
     for layer_index in range(layers):

@@ -11,7 +11,7 @@ Cases:
   (batched prefill), the state read back, and three decode steps (cache rows 2047..2049:
   2048-2050 rows per head, so the last ranges are ragged) compared with the oracle run from
   the same state, with the default projections at this hidden size (the streamed few-row FFMA
-  kernel up to four requests, tensor cores from five) and, for 3 requests, FFMA projections
+  kernel up to eight requests, tensor cores from nine) and, for 3 requests, FFMA projections
   forced - tokens, history and position exact, logits and appended cache rows within 1e-4
   relative / 1e-5 absolute;
 * a short prompt in a long cache (6 rows filled, capacity 2054): most ranges are empty;
@@ -24,7 +24,7 @@ import numpy as np
 import pytest
 
 import ckl
-from ckl.compile import attention_splits
+from ckl.compile import STREAMED_ROWS, attention_splits
 from ckl.workloads import session as S
 from oracle import decoder as ref
 from test_gpu_decoder import verify
@@ -70,8 +70,8 @@ def test_split_attention_at_context_2048_matches_oracle(device, batch, tensor_co
                                tensor_cores=tensor_cores)
     names = session.invocation.node_names
     assert "ckl.fused.attention_split" in names
-    # Up to four requests the streamed few-row kernel takes the projections at this size.
-    assert ("ckl.fused.panel_linear_rope" in names) == (tensor_cores and batch > 4)
+    # Up to STREAMED_ROWS requests the streamed few-row kernel takes the projections here.
+    assert ("ckl.fused.panel_linear_rope" in names) == (tensor_cores and batch > STREAMED_ROWS)
     session.prefill(prompts, batched=True)
     initial = {name: arrays[name] for name in S.WEIGHTS + ("sincos",)}
     initial.update(tokens=session.read("tokens"), position=session.read("position"),

@@ -1,15 +1,16 @@
-"""Streamed few-row projections (one to four requests, weights of 1 MB or more) against the oracle.
+"""Streamed few-row projections (one to eight requests, weights of 1 MB or more) vs the oracle.
 
-Up to four requests, a projection whose weights are 1 MB or more runs the streamed few-row FFMA
-kernel (``gemm.cuh``, configs 9-12: 16-column CTAs, 64-column CTAs from 16384 outputs), with
+Up to eight requests, a projection whose weights are 1 MB or more runs the streamed few-row FFMA
+kernel (``gemm.cuh``, configs 9-17: 16-column CTAs, 64 columns from 16384 outputs), with
 its RMSNorm or SwiGLU prologue staged in shared memory and the fused store / residual / RoPE /
 KV-append / logits + argmax epilogues.  The reference computes every projection as a plain
 FP32 dot product per output (``benchmarks/decoder/workloads.py:61-69``).
 
-Cases: hidden 512 (every projection streamed, LM head of 1000 columns: a partial last CTA),
-one to three requests (the four-row build with unused rows); hidden 256 (q/k/v/o below the
-threshold on the 32-column kernel, gate/up and the 4096-deep SwiGLU down projection streamed,
-a 20000-column LM head on 64-column CTAs with a partial last CTA).  Tokens, history and
+Cases: hidden 512 (every projection streamed, LM head of 1000 columns: a partial last CTA)
+with one to three requests (the four-row build, unused rows) and five and eight (the eight-row
+build); hidden 256 with two and seven requests (q/k/v/o below the threshold on the 32-column
+kernel, gate/up and the 4096-deep SwiGLU down projection streamed, a 20000-column LM head on
+64-column CTAs with a partial last CTA).  Tokens, history and
 position exact; logits and appended cache rows within 1e-4 relative / 1e-5 absolute.
 """
 from __future__ import annotations
@@ -34,7 +35,10 @@ def device():
     (1, 512, 8, 1408, 1000, 2),
     (2, 512, 8, 1408, 1000, 2),
     (3, 512, 8, 1408, 1000, 2),
+    (5, 512, 8, 1408, 1000, 2),
+    (8, 512, 8, 1408, 1000, 2),
     (2, 256, 4, 4096, 20000, 1),
+    (7, 256, 4, 4096, 20000, 1),
 ])
 def test_streamed_projections_match_oracle(device, batch, hidden, heads, ffn, vocab, layers):
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
