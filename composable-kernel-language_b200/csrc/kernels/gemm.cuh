@@ -54,10 +54,11 @@ using Small = Config<16, 64, 16, 2, 4>;    // 128 threads, M <= 16
 using Medium = Config<64, 64, 16, 4, 4>;   // 256 threads
 using Large = Config<128, 128, 8, 8, 8>;   // 256 threads, M >= 256 and wide N
 
-// The streamed few-row kernel (below) takes 1 to 8 rows of a projection with 1 MB or more of
-// weights whose K rows of A fit its shared-memory staging.
+// The streamed few-row kernel (below) takes 1 to 16 rows (more than 8 as groups of 8 rows,
+// grid.y) of a projection with 1 MB or more of weights whose K rows of A fit its
+// shared-memory staging.
 inline bool streamedFits(const GemmSpec &s) {
-  return s.M <= 8 && s.N % 4 == 0 && s.K % 4 == 0 && s.K <= 4096 &&
+  return s.M <= 16 && s.N % 4 == 0 && s.K % 4 == 0 && s.K <= 4096 &&
          s.K * s.N >= (int64_t(1) << 18);
 }
 
@@ -132,7 +133,7 @@ inline bool geometry(const GemmSpec &s, library::Geometry *g) {
     const bool wide = streamedWide(config);
     const int threads = streamedThreads(config);
     g->grid[0] = ceilDiv(s.N, wide ? 64 : 16);
-    g->grid[1] = 1;
+    g->grid[1] = ceilDiv(s.M, streamedRows(config));
     g->block[0] = unsigned(threads);
     // A [K][rows], gains [K], the k-slots' sums [slots][rows x columns + 4], the tile and the
     // row scales.
@@ -522,14 +523,15 @@ template <class Cfg, int PRO, int EPI> __device__ void rowsBody(const Params &p)
   }
 }
 
-// ---- few-row projections streaming large weights (1 to 8 requests) ----------------------
+// ---- few-row projections streaming large weights (1 to 16 requests) ---------------------
 // The kernel above gives a 1024-wide output 32 CTAs whose threads each keep eight 4-byte loads
 // in flight, ~8 KB per CTA: far less than HBM needs to stream the weights of the decoder's
 // larger projections (4-131 MB).  Here a CTA owns QUADS float4 columns and its 256 threads are
 // QUADS quads x SLOTS k-slots: thread (q, j) reads the 16-byte quad q of k rows j, j + SLOTS,
 // ..., kDepth loads in flight and the next kDepth issued before the current ones are used (a
 // 1024-wide output runs on 64 CTAs of 16 columns, the LM head on 500 of 64).  The rows of A
-// (all of K, at most eight rows) go through the prologue into shared memory once, k-major and
+// (all of K, at most eight rows: larger batches run as groups of eight rows, one per
+// blockIdx.y, which stream the same weights together) go through the prologue into shared memory once, k-major and
 // read as broadcasts, while the first loads are in flight.  Each thread keeps one float4
 // accumulator per row over its k rows in increasing order; the k-slots' sums are added in slot
 // order (deterministic) and the fused epilogue runs per (row, quad).
@@ -560,6 +562,9 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
   extern __shared__ __align__(16) float dynamicShared[];
   const GemmSpec &s = p.s;
   const int64_t M = s.M, K = s.K, N = s.N;
+  // Row group of this CTA (blockIdx.y): rows m0 .. m0 + rows - 1 of A and of the outputs.
+  const int64_t m0 = int64_t(blockIdx.y) * R;
+  const int64_t rows = M - m0 < R ? M - m0 : R;
   float *As = dynamicShared;                 // [K][R]
   float *gainS = As + K * R;                 // [K] (RMSNorm)
   // k-slot j's sums at partial + j * SP: [R][COLS] plus 4 floats, so that the slots of a warp
@@ -614,10 +619,10 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     for (int u = 0; u < 8; ++u) {
       const int64_t f = f0 + int64_t(u) * kThreads, m = f % R, k = 4 * (f / R);
       a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (f < R * K4 && m < M) {
-        a[u] = load4(p.a + m * K + k);
+      if (f < R * K4 && m < rows) {
+        a[u] = load4(p.a + (m0 + m) * K + k);
         if constexpr (PRO == kSwiGlu)
-          b[u] = load4(p.a2 + m * K + k);
+          b[u] = load4(p.a2 + (m0 + m) * K + k);
       }
     }
 #pragma unroll
@@ -662,7 +667,7 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     __syncthreads();
     for (int64_t e = tid; e < K * R; e += kThreads) {
       const int m = int(e % R);
-      As[e] = m < M ? __fmul_rn(__fmul_rn(As[e], rowInv[m]), gainS[e / R]) : 0.f;
+      As[e] = m < rows ? __fmul_rn(__fmul_rn(As[e], rowInv[m]), gainS[e / R]) : 0.f;
     }
   }
   __syncthreads();
@@ -722,14 +727,14 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
   if constexpr (EPI == kArgmax) {
     // One warp per row: the row's logits over the CTA's columns, then its argmax partial.
     const int warp = tid / kWarp, lane = tid % kWarp;
-    for (int m = warp; m < R && m < M; m += kThreads / kWarp) {
+    for (int m = warp; m < R && m < rows; m += kThreads / kWarp) {
       float best = -CUDART_INF_F;
       int bestIndex = 0x7fffffff;
       for (int c = lane; c < COLS; c += kWarp) {
         const int64_t col = n0 + c;
         if (col < N) {
           const float v = tile[m * COLS + c];
-          p.out[m * N + col] = v;
+          p.out[(m0 + m) * N + col] = v;
           argmaxMerge(best, bestIndex, v, int(col));
         }
       }
@@ -738,7 +743,8 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
         argmaxMerge(best, bestIndex, __shfl_xor_sync(0xffffffffu, best, o),
                     __shfl_xor_sync(0xffffffffu, bestIndex, o));
       if (lane == 0)
-        p.partials[m * s.tiles + blockIdx.x] = make_float2(best, __int_as_float(bestIndex));
+        p.partials[(m0 + m) * s.tiles + blockIdx.x] =
+            make_float2(best, __int_as_float(bestIndex));
     }
     return;
   }
@@ -747,7 +753,7 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     return;
   const int m = tid / Q, qq = tid % Q;
   const int64_t c = n0 + 4 * qq;
-  if (m >= M || c >= N)
+  if (m >= rows || c >= N)
     return;
   float4 v = *reinterpret_cast<const float4 *>(&tile[m * COLS + 4 * qq]);
   if constexpr (EPI == kStore || EPI == kResidual) {
@@ -755,11 +761,11 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     if constexpr (EPI == kResidual) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        lanes[j] = __fadd_rn(p.residual[m * N + c + j], lanes[j]);
+        lanes[j] = __fadd_rn(p.residual[(m0 + m) * N + c + j], lanes[j]);
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      p.out[m * N + c + j] = lanes[j];
+      p.out[(m0 + m) * N + c + j] = lanes[j];
   } else {
     // Pairs (c, c + 1) and (c + 2, c + 3): c is a multiple of 4 and D is even, so a pair never
     // straddles two heads.
@@ -778,10 +784,10 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
         second = y;
       }
       if constexpr (EPI == kRope) {
-        p.out[m * N + col] = first;
-        p.out[m * N + col + 1] = second;
+        p.out[(m0 + m) * N + col] = first;
+        p.out[(m0 + m) * N + col + 1] = second;
       } else {
-        float *at = p.out + (((s.layer * M + m) * s.A + h) * s.T + position) * D + d;
+        float *at = p.out + (((s.layer * M + m0 + m) * s.A + h) * s.T + position) * D + d;
         at[0] = first;
         at[1] = second;
       }

@@ -221,13 +221,14 @@ _ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
 # Batches of 17 or more requests run the projections on tcgen05 tensor cores (GemmSpec config
 # 0; partial 128-row tiles with split-K still beat FFMA tiles from 17 rows); up to 16 the
 # few-row FFMA kernel is faster for small decoders, whose projections are latency-bound.  From
-# a hidden size of 512 the weights stream from HBM (1 MB and more per projection): up to eight
-# requests the streamed few-row FFMA kernel (gemm.cuh, configs 9-17) reads them at HBM speed,
-# from nine to sixteen the tensor-core kernels, which spread a projection over many more CTAs
-# than the 16-row few-row kernel, are faster.  Config 5 keeps every projection on FFMA.
+# a hidden size of 512 the weights stream from HBM (1 MB and more per projection), and up to 16
+# requests the streamed few-row FFMA kernel (gemm.cuh, configs 9-17; groups of eight rows
+# above eight) reads them at HBM speed: at hidden 1024 it took the step from 0.56 / 0.61 / 0.69
+# / 0.78 ms on the tensor cores to 0.24 / 0.30 / 0.49 / 0.74 ms at 1 / 4 / 8 / 16 requests.
+# Config 5 keeps every projection on FFMA.
 _TENSOR_CORE_ROWS = 17
 _TENSOR_CORE_HIDDEN = 512
-STREAMED_ROWS = 8
+STREAMED_ROWS = 16
 
 
 def _panel_floats(M: int, K: int) -> int:

@@ -7,11 +7,11 @@ the reference computes the same attention serially per (request, head)
 
 Cases:
 * BASELINE config 5 dimensions (hidden 1024, 16 heads of 64, SwiGLU 4096, vocabulary 32000,
-  4 layers) with 1, 3 and 8 requests at context 2048: the prompt is prefilled on the GPU
+  4 layers) with 1, 3, 8 and 17 requests at context 2048 (17: tensor-core projections): the prompt is prefilled on the GPU
   (batched prefill), the state read back, and three decode steps (cache rows 2047..2049:
   2048-2050 rows per head, so the last ranges are ragged) compared with the oracle run from
   the same state, with the default projections at this hidden size (the streamed few-row FFMA
-  kernel up to eight requests, tensor cores from nine) and, for 3 requests, FFMA projections
+  kernel up to sixteen requests) and, for 3 requests, FFMA projections
   forced - tokens, history and position exact, logits and appended cache rows within 1e-4
   relative / 1e-5 absolute;
 * a short prompt in a long cache (6 rows filled, capacity 2054): most ranges are empty;
@@ -53,7 +53,8 @@ def cache_rows(session, name, request):
     return out
 
 
-@pytest.mark.parametrize("batch,tensor_cores", [(1, True), (3, True), (8, True), (3, False)])
+@pytest.mark.parametrize("batch,tensor_cores",
+                         [(1, True), (3, True), (8, True), (17, True), (3, False)])
 def test_split_attention_at_context_2048_matches_oracle(device, batch, tensor_cores):
     steps = 3
     shape = S.DecoderShape(batch=batch, context=2048, steps=32, **CFG5)

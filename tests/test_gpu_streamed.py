@@ -8,7 +8,8 @@ FP32 dot product per output (``benchmarks/decoder/workloads.py:61-69``).
 
 Cases: hidden 512 (every projection streamed, LM head of 1000 columns: a partial last CTA)
 with one to three requests (the four-row build, unused rows) and five and eight (the eight-row
-build); hidden 256 with two and seven requests (q/k/v/o below the threshold on the 32-column
+build), and eleven and sixteen with FFMA projections forced (two row groups of the eight-row
+build on every column block); hidden 256 with two and seven requests (q/k/v/o below the threshold on the 32-column
 kernel, gate/up and the 4096-deep SwiGLU down projection streamed, a 20000-column LM head on
 64-column CTAs with a partial last CTA).  Tokens, history and
 position exact; logits and appended cache rows within 1e-4 relative / 1e-5 absolute.
@@ -31,22 +32,26 @@ def device():
     return ckl.Device()
 
 
-@pytest.mark.parametrize("batch,hidden,heads,ffn,vocab,layers", [
-    (1, 512, 8, 1408, 1000, 2),
-    (2, 512, 8, 1408, 1000, 2),
-    (3, 512, 8, 1408, 1000, 2),
-    (5, 512, 8, 1408, 1000, 2),
-    (8, 512, 8, 1408, 1000, 2),
-    (2, 256, 4, 4096, 20000, 1),
-    (7, 256, 4, 4096, 20000, 1),
+@pytest.mark.parametrize("batch,hidden,heads,ffn,vocab,layers,tensor_cores", [
+    (1, 512, 8, 1408, 1000, 2, True),
+    (2, 512, 8, 1408, 1000, 2, True),
+    (3, 512, 8, 1408, 1000, 2, True),
+    (5, 512, 8, 1408, 1000, 2, True),
+    (8, 512, 8, 1408, 1000, 2, True),
+    (11, 512, 8, 1408, 1000, 2, False),
+    (16, 512, 8, 1408, 1000, 2, False),
+    (2, 256, 4, 4096, 20000, 1, True),
+    (7, 256, 4, 4096, 20000, 1, True),
 ])
-def test_streamed_projections_match_oracle(device, batch, hidden, heads, ffn, vocab, layers):
+def test_streamed_projections_match_oracle(device, batch, hidden, heads, ffn, vocab, layers,
+                                           tensor_cores):
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
                         vocab=vocab, context=20, steps=3)
     initial, _ = ref.make_inputs(config, 23, eps=EPS)
     expected = ref.expected(initial, config, config.steps, eps=EPS)
     session = S.DecoderSession(device, initial, epsilon=EPS,
-                               attention_scale=config.head_dim ** -0.5, whole_step=False)
+                               attention_scale=config.head_dim ** -0.5, whole_step=False,
+                               tensor_cores=tensor_cores)
     names = session.invocation.node_names
     assert "ckl.fused.norm_linear_argmax" in names and "ckl.fused.panel_gate_up" not in names
     session.step(config.steps)
