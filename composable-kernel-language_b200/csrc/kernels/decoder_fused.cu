@@ -146,6 +146,7 @@ bool appendGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
     case 15: return reinterpret_cast<const void *>(&fn<gemm::Streamed1Deep>);                  \
     case 16: return reinterpret_cast<const void *>(&fn<gemm::Streamed4Deep>);                  \
     case 17: return reinterpret_cast<const void *>(&fn<gemm::Streamed8Deep>);                  \
+    case 18: return reinterpret_cast<const void *>(&fn<gemm::Streamed8Deep16>);                \
     default: return nullptr;                                                                   \
     }                                                                                          \
   }

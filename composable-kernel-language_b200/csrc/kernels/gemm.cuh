@@ -62,7 +62,7 @@ inline bool streamedFits(const GemmSpec &s) {
          s.K * s.N >= (int64_t(1) << 18);
 }
 
-// Rows, CTA columns and threads of a streamed configuration (9-17).
+// Rows, CTA columns and threads of a streamed configuration (9-18).
 inline int streamedRows(int config) {
   switch (config) {
   case 9: case 11: case 15: return 1;
@@ -72,11 +72,16 @@ inline int streamedRows(int config) {
 }
 inline bool streamedWide(int config) { return config == 11 || config == 12 || config == 14; }
 inline int streamedThreads(int config) { return config >= 15 ? 512 : 256; }
+inline int streamedColumns(int config) {
+  return streamedWide(config) ? 64 : config >= 15 && config <= 17 ? 8 : 16;
+}
 
 // Tile configuration for a specialization: 0 small, 1 medium, 2 large, 6/7/8 the few-row
 // kernel for 1 / 4 / 16 rows, 9/10/13 the streamed few-row kernel for 1 / 4 / 8 rows with
-// 16-column CTAs, 11/12/14 with 64-column CTAs (outputs of 16384 columns or more) and 15/16/17
-// with 16-column CTAs of 512 threads (K of 2048 or more).
+// 16-column CTAs, 11/12/14 with 64-column CTAs (outputs of 16384 columns or more), 15/16/17
+// with 8-column CTAs of 512 threads (K of 2048 or more: twice the CTAs of a narrow output) and
+// 18 with 16-column CTAs of 512 threads (K of 2048 or more, 9 to 16 rows: two row groups of
+// 8-column CTAs, each filling an SM's shared memory, would run in two waves).
 // `config` 1-3 forces a tile; 0 (automatic) and 5 (FFMA only) choose by shape.
 inline int chooseConfig(const GemmSpec &s) {
   if (s.config > 0 && s.config <= 3)
@@ -86,7 +91,7 @@ inline int chooseConfig(const GemmSpec &s) {
     if (s.N >= 16384)
       return rows == 2 ? 14 : 11 + rows;
     if (s.K >= 2048)
-      return 15 + rows;
+      return s.M > 8 ? 18 : 15 + rows;
     return rows == 2 ? 13 : 9 + rows;
   }
   if (s.M <= 1)
@@ -128,16 +133,16 @@ inline bool geometry(const GemmSpec &s, library::Geometry *g) {
   case 14:
   case 15:
   case 16:
-  case 17: {
+  case 17:
+  case 18: {
     const int config = chooseConfig(s);
-    const bool wide = streamedWide(config);
     const int threads = streamedThreads(config);
-    g->grid[0] = ceilDiv(s.N, wide ? 64 : 16);
+    g->grid[0] = ceilDiv(s.N, streamedColumns(config));
     g->grid[1] = ceilDiv(s.M, streamedRows(config));
     g->block[0] = unsigned(threads);
     // A [K][rows], gains [K], the k-slots' sums [slots][rows x columns + 4], the tile and the
     // row scales.
-    const int64_t rows = streamedRows(config), cols = wide ? 64 : 16;
+    const int64_t rows = streamedRows(config), cols = streamedColumns(config);
     g->sharedBytes =
         unsigned((s.K * rows + s.K + (threads / (cols / 4)) * (rows * cols + 4) + rows * cols + 4) *
                  4);
@@ -546,15 +551,17 @@ using Streamed4Wide = Streamed<4, 16>;
 using Streamed8 = Streamed<8, 4>;
 using Streamed8Wide = Streamed<8, 16>;
 // 512 threads for deep K (2048 rows or more): twice the loads in flight per CTA, for grids
-// of fewer CTAs than SMs or CTAs that fill an SM's shared memory alone.
-using Streamed1Deep = Streamed<1, 4, 512>;
-using Streamed4Deep = Streamed<4, 4, 512>;
-using Streamed8Deep = Streamed<8, 4, 512>;
+// of fewer CTAs than SMs or CTAs that fill an SM's shared memory alone; 8 columns per CTA up
+// to eight rows (a 1024-wide output on 128 CTAs), 16 for two row groups.
+using Streamed1Deep = Streamed<1, 2, 512>;
+using Streamed4Deep = Streamed<4, 2, 512>;
+using Streamed8Deep = Streamed<8, 2, 512>;
+using Streamed8Deep16 = Streamed<8, 4, 512>;
 
 template <class Cfg> struct IsStreamed : std::false_type {};
 template <int R, int Q, int T> struct IsStreamed<Streamed<R, Q, T>> : std::true_type {};
 
-// Dynamic shared memory (geometry, config 9-17): A [K][ROWS], the gains [K], the k-slots'
+// Dynamic shared memory (geometry, config 9-18): A [K][ROWS], the gains [K], the k-slots'
 // sums [SLOTS][ROWS x COLS + 4], the reduced tile [ROWS][COLS] and the row scales.
 template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params &p) {
   constexpr int R = Cfg::kRows, Q = Cfg::kQuads, SLOTS = Cfg::kSlots, DEPTH = Cfg::kDepth;
@@ -651,7 +658,7 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
       *reinterpret_cast<float4 *>(gainS + 4 * k4) = load4(p.gain + s.layer * K + 4 * k4);
     // Row sums: the lanes of one row (lane % R) by shuffles, then the warps in order.
     const int warp = tid / kWarp, lane = tid % kWarp;
-    float *warpSums = tile; // [warps][R], free until the epilogue (COLS >= warps)
+    float *warpSums = partial; // [warps][R], free until the k-slots' sums
 #pragma unroll
     for (int o = kWarp / 2; o >= R; o >>= 1)
       sumSquares += __shfl_xor_sync(0xffffffffu, sumSquares, o);

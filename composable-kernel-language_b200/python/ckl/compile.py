@@ -222,7 +222,7 @@ _ATTENTION_HEAD_DIMS = (16, 32, 64, 128)
 # 0; partial 128-row tiles with split-K still beat FFMA tiles from 17 rows); up to 16 the
 # few-row FFMA kernel is faster for small decoders, whose projections are latency-bound.  From
 # a hidden size of 512 the weights stream from HBM (1 MB and more per projection), and up to 16
-# requests the streamed few-row FFMA kernel (gemm.cuh, configs 9-17; groups of eight rows
+# requests the streamed few-row FFMA kernel (gemm.cuh, configs 9-18; groups of eight rows
 # above eight) reads them at HBM speed: at hidden 1024 it took the step from 0.56 / 0.61 / 0.69
 # / 0.78 ms on the tensor cores to 0.24 / 0.30 / 0.49 / 0.74 ms at 1 / 4 / 8 / 16 requests.
 # Config 5 keeps every projection on FFMA.

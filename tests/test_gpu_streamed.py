@@ -1,7 +1,7 @@
 """Streamed few-row projections (one to eight requests, weights of 1 MB or more) vs the oracle.
 
 Up to eight requests, a projection whose weights are 1 MB or more runs the streamed few-row FFMA
-kernel (``gemm.cuh``, configs 9-17: 16-column CTAs, 64 columns from 16384 outputs), with
+kernel (``gemm.cuh``, configs 9-18: 8 to 64 columns per CTA by shape), with
 its RMSNorm or SwiGLU prologue staged in shared memory and the fused store / residual / RoPE /
 KV-append / logits + argmax epilogues.  The reference computes every projection as a plain
 FP32 dot product per output (``benchmarks/decoder/workloads.py:61-69``).
