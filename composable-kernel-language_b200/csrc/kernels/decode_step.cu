@@ -174,7 +174,41 @@ __device__ __noinline__ void project(const StreamTable &t, Cursor &cur, const fl
 #pragma unroll
       for (int r = 0; r < RB; ++r)
         acc[c][r] = f4(0.f, 0.f, 0.f, 0.f);
-    if (busy) {
+    // Long K ranges per thread (a CTA's slice of 64 KB or more, e.g. gate/up at hidden 256)
+    // issue their weight loads in batches of BATCH K rows before any FMA of the batch: eight
+    // loads in flight for single and fused pairs of slices instead of four.  The K rows still
+    // accumulate in increasing order, so the sums are those of the short form.
+    constexpr int BATCH = COUNT == 1 ? 8 : COUNT == 2 ? 4 : 2;
+    const bool deep = (K + kparts - 1) / kparts >= 4 * BATCH; // CTA-uniform
+    if (busy && deep) {
+      int k = kp;
+      for (; k + (BATCH - 1) * kparts < K; k += BATCH * kparts) {
+        float4 wv[BATCH][COUNT];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u)
+#pragma unroll
+          for (int c = 0; c < COUNT; ++c)
+            wv[u][c] = __ldg(w0[c] + (k + u * kparts) * O4 + q);
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u)
+#pragma unroll
+          for (int c = 0; c < COUNT; ++c)
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+              if (r < rr)
+                fma4(acc[c][r], x[r * ldIn + k + u * kparts], wv[u][c]);
+      }
+      for (; k < K; k += kparts) {
+#pragma unroll
+        for (int c = 0; c < COUNT; ++c) {
+          const float4 wk = __ldg(w0[c] + k * O4 + q);
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < rr)
+              fma4(acc[c][r], x[r * ldIn + k], wk);
+        }
+      }
+    } else if (busy) {
       // Loads in flight per thread: four K rows for a single slice, two for the fused passes.
 #pragma unroll(COUNT == 1 ? 4 : 2)
       for (int k = kp; k < K; k += kparts) {
