@@ -76,6 +76,35 @@ inline int streamedColumns(int config) {
   return streamedWide(config) ? 64 : config >= 15 && config <= 17 ? 8 : 16;
 }
 
+// Shared-memory floats of the streamed kernel: [the CTA's weight block, K x COLS, when staged],
+// A [K][R], gains [K], the k-slots' sums [SLOTS][R x COLS + 4], the tile [R][COLS], row scales.
+__host__ __device__ inline int64_t streamedFloats(int64_t K, int R, int COLS, int threads,
+                                                  bool staged) {
+  const int64_t slots = threads / (COLS / 4);
+  return (staged ? K * COLS : 0) + K * R + K + slots * (R * COLS + 4) + R * COLS + 4;
+}
+
+// Whether the weight block is staged in shared memory (one round of cp.async for all of it):
+// single-row launches whose layout fits a CTA and whose grid still runs in one wave at the
+// resulting occupancy (two 256-thread CTAs per SM by registers, one of 512).  Measured at cfg5
+// dimensions (same box, alternating builds): one request 0.234 -> 0.225 ms per step, four
+// requests 0.299 -> 0.310 ms with staging, so it is kept for one row only.
+constexpr int64_t kStreamedSms = 148;
+constexpr int64_t kStreamedSharedLimit = 227 * 1024, kStreamedSmShared = 228 * 1024;
+inline bool streamedStaged(const GemmSpec &s, int config, int64_t ctas) {
+  if (streamedRows(config) != 1)
+    return false;
+  const int threads = streamedThreads(config);
+  const int64_t bytes =
+      4 * streamedFloats(s.K, streamedRows(config), streamedColumns(config), threads, true);
+  if (bytes > kStreamedSharedLimit)
+    return false;
+  int64_t perSm = kStreamedSmShared / (bytes + 1024); // 1 KB reserved per CTA
+  const int64_t byRegisters = threads == 512 ? 1 : 2;
+  perSm = perSm < byRegisters ? perSm : byRegisters;
+  return ctas <= kStreamedSms * perSm;
+}
+
 // Tile configuration for a specialization: 0 small, 1 medium, 2 large, 6/7/8 the few-row
 // kernel for 1 / 4 / 16 rows, 9/10/13 the streamed few-row kernel for 1 / 4 / 8 rows with
 // 16-column CTAs, 11/12/14 with 64-column CTAs (outputs of 16384 columns or more), 15/16/17
@@ -140,12 +169,9 @@ inline bool geometry(const GemmSpec &s, library::Geometry *g) {
     g->grid[0] = ceilDiv(s.N, streamedColumns(config));
     g->grid[1] = ceilDiv(s.M, streamedRows(config));
     g->block[0] = unsigned(threads);
-    // A [K][rows], gains [K], the k-slots' sums [slots][rows x columns + 4], the tile and the
-    // row scales.
-    const int64_t rows = streamedRows(config), cols = streamedColumns(config);
-    g->sharedBytes =
-        unsigned((s.K * rows + s.K + (threads / (cols / 4)) * (rows * cols + 4) + rows * cols + 4) *
-                 4);
+    const bool staged = streamedStaged(s, config, int64_t(g->grid[0]) * g->grid[1]);
+    g->sharedBytes = unsigned(4 * streamedFloats(s.K, streamedRows(config),
+                                                 streamedColumns(config), threads, staged));
     break;
   }
   default: return false;
@@ -563,6 +589,21 @@ template <int R, int Q, int T> struct IsStreamed<Streamed<R, Q, T>> : std::true_
 
 // Dynamic shared memory (geometry, config 9-18): A [K][ROWS], the gains [K], the k-slots'
 // sums [SLOTS][ROWS x COLS + 4], the reduced tile [ROWS][COLS] and the row scales.
+// 16-byte asynchronous copy global -> shared, its commit, and the wait for all of this thread's
+// copies (a wait on its own loads, which always complete).
+__device__ __forceinline__ void copyAsync16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void copyAsyncCommit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void copyAsyncWaitAll() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params &p) {
   constexpr int R = Cfg::kRows, Q = Cfg::kQuads, SLOTS = Cfg::kSlots, DEPTH = Cfg::kDepth;
   constexpr int COLS = Cfg::kCols, kThreads = Cfg::kThreads;
@@ -572,7 +613,14 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
   // Row group of this CTA (blockIdx.y): rows m0 .. m0 + rows - 1 of A and of the outputs.
   const int64_t m0 = int64_t(blockIdx.y) * R;
   const int64_t rows = M - m0 < R ? M - m0 : R;
-  float *As = dynamicShared;                 // [K][R]
+  // The weight block [K][COLS] leads the layout when geometry allocated it (streamedStaged);
+  // it is used when the weights also admit 16-byte copies.
+  unsigned dynamicBytes;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dynamicBytes));
+  const bool stagedLayout =
+      int64_t(dynamicBytes) >= 4 * streamedFloats(K, R, COLS, kThreads, true);
+  float *Ws = dynamicShared;                               // [K][COLS] (staged)
+  float *As = dynamicShared + (stagedLayout ? K * COLS : 0); // [K][R]
   float *gainS = As + K * R;                 // [K] (RMSNorm)
   // k-slot j's sums at partial + j * SP: [R][COLS] plus 4 floats, so that the slots of a warp
   // start in different banks.
@@ -599,10 +647,26 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     return vec ? __ldg(reinterpret_cast<const float4 *>(row))
                : make_float4(__ldg(row), __ldg(row + 1), __ldg(row + 2), __ldg(row + 3));
   };
+  const bool staged = stagedLayout && vec; // CTA-uniform
   float4 w[DEPTH];
+  if (staged) {
+    // The CTA's whole weight block in one round: row k's COLS columns, quads of 16 bytes.
+    const float *block = p.w + s.layer * K * N + n0;
+    for (int64_t e = tid; e < K * Q; e += kThreads) {
+      const int64_t k = e / Q;
+      const int qq = int(e % Q);
+      float *dst = Ws + k * COLS + 4 * qq;
+      if (n0 + 4 * qq < N)
+        copyAsync16(dst, block + k * N + 4 * qq);
+      else
+        *reinterpret_cast<float4 *>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    copyAsyncCommit();
+  } else {
 #pragma unroll
-  for (int d = 0; d < DEPTH; ++d)
-    w[d] = load(slot + int64_t(d) * SLOTS);
+    for (int d = 0; d < DEPTH; ++d)
+      w[d] = load(slot + int64_t(d) * SLOTS);
+  }
 
   // Rows of A into As [K][R] (k-major): every thread's float4s of the rows are loaded eight at
   // a time with all loads in flight (SwiGLU: silu(gate) * up as stored); for RMSNorm the raw
@@ -677,13 +741,44 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
       As[e] = m < rows ? __fmul_rn(__fmul_rn(As[e], rowInv[m]), gainS[e / R]) : 0.f;
     }
   }
+  if (staged)
+    copyAsyncWaitAll(); // this thread's copies of the block; the barrier publishes everyone's
   __syncthreads();
 
   float4 acc[R];
 #pragma unroll
   for (int m = 0; m < R; ++m)
     acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int64_t base = slot; base < K; base += int64_t(DEPTH) * SLOTS) {
+  // This k row of every row of A (16-byte reads when R % 4 == 0).
+  auto rowOfA = [&](int64_t k, float (&a)[R]) {
+    if constexpr (R % 4 == 0) {
+#pragma unroll
+      for (int m = 0; m < R; m += 4) {
+        const float4 four = *reinterpret_cast<const float4 *>(&As[k * R + m]);
+        a[m] = four.x, a[m + 1] = four.y, a[m + 2] = four.z, a[m + 3] = four.w;
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < R; ++m)
+        a[m] = As[k * R + m];
+    }
+  };
+  if (staged) {
+#pragma unroll 4
+    for (int64_t k = slot; k < K; k += SLOTS) {
+      const float4 wk = *reinterpret_cast<const float4 *>(&Ws[k * COLS + 4 * q]);
+      float a[R];
+      rowOfA(k, a);
+#pragma unroll
+      for (int m = 0; m < R; ++m) {
+        acc[m].x = fmaf(a[m], wk.x, acc[m].x);
+        acc[m].y = fmaf(a[m], wk.y, acc[m].y);
+        acc[m].z = fmaf(a[m], wk.z, acc[m].z);
+        acc[m].w = fmaf(a[m], wk.w, acc[m].w);
+      }
+    }
+  }
+  for (int64_t base = slot; !staged && base < K; base += int64_t(DEPTH) * SLOTS) {
     float4 next[DEPTH];
 #pragma unroll
     for (int d = 0; d < DEPTH; ++d)
@@ -692,18 +787,8 @@ template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params
     for (int d = 0; d < DEPTH; ++d) {
       const int64_t k = base + int64_t(d) * SLOTS;
       if (k < K) {
-        float a[R]; // this k row of every row of A (16-byte reads when R % 4 == 0)
-        if constexpr (R % 4 == 0) {
-#pragma unroll
-          for (int m = 0; m < R; m += 4) {
-            const float4 four = *reinterpret_cast<const float4 *>(&As[k * R + m]);
-            a[m] = four.x, a[m + 1] = four.y, a[m + 2] = four.z, a[m + 3] = four.w;
-          }
-        } else {
-#pragma unroll
-          for (int m = 0; m < R; ++m)
-            a[m] = As[k * R + m];
-        }
+        float a[R];
+        rowOfA(k, a);
 #pragma unroll
         for (int m = 0; m < R; ++m) {
           acc[m].x = fmaf(a[m], w[d].x, acc[m].x);
