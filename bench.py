@@ -24,7 +24,8 @@ kernel (the dominant, HBM-bound kernel) from per-node CUDA events over one extra
 unfused) on the same state and compares tokens and logits; ``library_faults`` is the kernel
 library's fault word after the run (must be 0).  At one GPU the line also carries
 ``small_configs`` (3, 4 and 2: time per step, speed-up over the naive
-graph, parity) and, at every GPU count, ``full_job`` (config 5's 4096 requests in waves of one
+graph, parity), ``small_batches`` (config 5's model with 1, 4 and 16 requests: latency-oriented
+decode, with the attention's fraction of the copy bandwidth) and, at every GPU count, ``full_job`` (config 5's 4096 requests in waves of one
 shard per GPU).  ``--impl reference`` times the reference's own CPU decoder (its NumPy
 algorithm, restated in oracle/) on a bounded sample of requests on the host cores.
 """
@@ -698,6 +699,64 @@ def small_configs(args, local):
     return out
 
 
+SMALL_BATCHES = (1, 4, 16)
+
+
+def small_batch(local, requests: int):
+    """BASELINE config 5's model with a few requests on this GPU (latency-oriented decode): the
+    KV prefix of 2048 rows is left zero (the per-step work does not depend on its values),
+    every step decodes from position 2047.  Time per step is the median of `SMALL_ROUNDS`
+    rounds of `SMALL_STEPS` graph launches; the attention kernel's fraction of the measured
+    copy bandwidth comes from one per-node profiled step; the reference's naive path is timed
+    on the same state and replayed as the parity check."""
+    import ckl
+    from ckl.workloads import session as S
+
+    _, h, a, l, f, v, ctx, _, seed, eps = WORKLOADS["cfg5"]
+    shape = S.DecoderShape(batch=requests, hidden=h, heads=a, layers=l, ffn=f, vocab=v,
+                           context=ctx, steps=max(SMALL_STEPS, SMALL_WARMUP, PARITY_STEPS) + 8)
+    arrays, rng = S.make_weights(shape, seed)
+    last = rng.integers(0, v, requests, dtype=np.int32)
+    cache = (l, requests, a, shape.capacity, h // a)
+    arrays.update(tokens=last.copy(), position=np.array([ctx - 1], np.int32),
+                  history=np.full((shape.capacity, requests), -1, np.int32),
+                  kc=(cache, np.float32), vc=(cache, np.float32),
+                  logits=np.zeros((requests, v), np.float32))
+    sess = S.DecoderSession(ckl.Device(local), arrays, epsilon=eps,
+                            attention_scale=(h // a) ** -0.5, tails=False)
+    p0 = ctx - 1
+    inv = sess.invocation
+    for _ in range(SMALL_WARMUP):
+        inv.run(mode="graph")
+    rounds = []
+    for _ in range(SMALL_ROUNDS):
+        restart(sess, p0, last)
+        inv.synchronize()
+        rounds.append(inv.time_launches(SMALL_STEPS, mode="graph") / SMALL_STEPS)
+    ms = statistics.median(rounds)
+    restart(sess, p0, last)
+    per_node = inv.profile_nodes(1)
+    names = inv.node_names
+    attention = [t for n, t in zip(names, per_node)
+                 if n in ("ckl.fused.attention", "ckl.fused.attention_split")]
+    hbm, _ = peaks()
+    frac = None
+    if attention:
+        algorithmic = 2 * requests * a * ctx * (h // a) * 4 + 2 * requests * h * 4
+        frac = algorithmic / (statistics.mean(attention) / 1000.0) / 1e9 / hbm
+    naive, parity = reference_path(sess, ms, None, p0, last)
+    projections = ("streamed few-row FFMA" if "ckl.fused.norm_linear" in names else
+                   "tensor cores" if "ckl.fused.panel_gate_up" in names else "FFMA")
+    return {"ms_per_step": ms, "tokens_per_s": requests / (ms / 1000.0),
+            "attention_frac_of_copy": frac, "attention_nodes": len(attention),
+            "projections": projections, "graph_nodes_per_step": inv.node_count,
+            "naive_ms_per_step": naive["ms_per_step"],
+            "speedup_vs_naive_graph": naive["speedup"], "parity_check": parity["passed"],
+            "parity": parity, "positions": [p0, p0 + SMALL_STEPS - 1],
+            "timing": f"median of {SMALL_ROUNDS} rounds of {SMALL_STEPS} graph launches, CUDA "
+                      f"events, after {SMALL_WARMUP} warm-up steps; zero KV prefix"}
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -739,6 +798,8 @@ def main():
     if rank == 0:
         if world == 1 and args.workload == "cfg5" and not args.no_small_configs:
             line["small_configs"] = small_configs(args, local)
+            if not args.requests_per_gpu:
+                line["small_batches"] = {str(r): small_batch(local, r) for r in SMALL_BATCHES}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, workload)
         print(json.dumps(line), flush=True)
