@@ -45,6 +45,22 @@ __device__ __forceinline__ bool aligned16(const void *p) {
 
 inline unsigned ceilDiv(int64_t a, int64_t b) { return unsigned((a + b - 1) / b); }
 
+// 16-byte asynchronous copy global -> shared (both addresses 16-byte aligned), its commit, and
+// the wait for all of this thread's copies (a wait on its own loads, which always complete;
+// a CTA barrier after it publishes every thread's copies).
+__device__ __forceinline__ void copyAsync16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void copyAsyncCommit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void copyAsyncWaitAll() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // Programmatic dependent launch: wait until every kernel this one depends on has completed and
 // its memory is visible, then allow the kernels that depend on this one to be scheduled (they
 // wait in turn).  Both are no-ops for a kernel launched without a programmatic dependency.

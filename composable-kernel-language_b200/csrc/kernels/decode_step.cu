@@ -324,10 +324,14 @@ constexpr std::size_t kTableBytes = (sizeof(StreamTable) + 15) / 16 * 16;
 // q / ctx: queries and attention outputs of the CTA's heads; h: the SwiGLU product of its FFN
 // columns; partO / partD: its partial o and down projections [rows][C], which every CTA of the
 // cluster reads (distributed shared memory) after the cluster barrier that follows them.
+// operands: the RMSNorm gains of every layer and of the head, [norm1: L][norm2: L][final] x C,
+// and the RoPE row of position p (D floats), copied in at the start of the step when they fit
+// (operandsStaged).
 struct StepBuffers {
   StreamTable *table;
   float *x, *act, *q, *ctx, *h, *partO, *partD, *red, *probs, *tile, *partValue, *first;
   int *partIndex;
+  float *operands;
 };
 
 __device__ StepBuffers carve(unsigned char *base, const DecodeStepSpec &s) {
@@ -347,15 +351,32 @@ __device__ StepBuffers carve(unsigned char *base, const DecodeStepSpec &s) {
   b.partValue = b.tile + G * tileColumns(s);
   b.partIndex = reinterpret_cast<int *>(b.partValue + kStepCtas * kMaxRows);
   b.first = reinterpret_cast<float *>(b.partIndex + kStepCtas * kMaxRows);
+  b.operands = b.first + kStepCtas * kMaxRows; // every region above is a multiple of 4 floats
   return b;
 }
 
-std::size_t stepSharedBytes(const DecodeStepSpec &s) {
+__host__ __device__ inline std::size_t baseSharedBytes(const DecodeStepSpec &s) {
   const int64_t floats = 2 * s.G * rowStride(s.C) + 2 * s.G * rowStride(ownColumns(s)) +
                          s.G * rowStride(s.F / kStepCtas) + 2 * s.G * s.C + kReduceFloats +
                          kStepWarps * s.T +
                          s.G * tileColumns(s) + 3 * kStepCtas * kMaxRows;
   return kTableBytes + std::size_t(floats) * sizeof(float);
+}
+
+// The step's gains and RoPE row in shared memory: each phase that uses them (the RMSNorms, the
+// RoPE of q and k) then reads shared memory instead of making an L2 round trip; staged when
+// they are at most 16 KB and fit the per-CTA budget.
+__host__ __device__ inline int64_t operandFloats(const DecodeStepSpec &s) {
+  return (2 * s.L + 1) * s.C + s.D;
+}
+__host__ __device__ inline bool operandsStaged(const DecodeStepSpec &s) {
+  const std::size_t bytes = std::size_t(operandFloats(s)) * sizeof(float);
+  return bytes <= 16 * 1024 && baseSharedBytes(s) + bytes <= kMaxSharedPerCta;
+}
+
+std::size_t stepSharedBytes(const DecodeStepSpec &s) {
+  return baseSharedBytes(s) +
+         (operandsStaged(s) ? std::size_t(operandFloats(s)) * sizeof(float) : 0);
 }
 
 // OCC CTAs per SM.  Two (at most 128 registers a thread and half of an SM's shared memory each)
@@ -418,17 +439,36 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
     }
     __syncthreads();
 
+    // Gains and the RoPE row copied in behind the embedding gather (C, D multiples of 4; the
+    // fused plan's buffers are 16-byte aligned).
+    const bool staged = operandsStaged(s);
+    float *op = sb.operands;
+    if (staged) {
+      const int64_t LC4 = s.L * C / 4;
+      for (int64_t e = tid; e < LC4; e += kStepThreads) {
+        copyAsync16(op + 4 * e, norm1 + 4 * e);
+        copyAsync16(op + s.L * C + 4 * e, norm2 + 4 * e);
+      }
+      for (int64_t e = tid; e < C / 4; e += kStepThreads)
+        copyAsync16(op + 2 * s.L * C + 4 * e, finalNorm + s.finalLayer * C + 4 * e);
+      for (int64_t e = tid; e < D / 4; e += kStepThreads)
+        copyAsync16(op + (2 * s.L + 1) * C + 4 * e, sincos + int64_t(p) * D + 4 * e);
+      copyAsyncCommit();
+    }
+
     for (int64_t e = tid; e < rows * C; e += kStepThreads) {
       const int64_t g = e / C, c = e % C;
       const int token = tokens[r0 + g];
       sb.x[g * ldC + c] = token >= 0 && token < V ? emb[int64_t(token) * C + c] : 0.f;
     }
+    if (staged)
+      copyAsyncWaitAll(); // this thread's copies; the barrier publishes everyone's
     __syncthreads();
 
     const int nqO = int(own / 4), nqF = int(F / kStepCtas / 4);
     const int oF = rank * int(F / kStepCtas);
     const int64_t R = D / 2;
-    const float *cs = sincos + int64_t(p) * R * 2;
+    const float *cs = staged ? op + (2 * s.L + 1) * C : sincos + int64_t(p) * R * 2;
     auto rope = [&](int col, float4 v) {
       const int d = int(col % D);
       const float c0 = cs[(d / 2) * 2], s0 = cs[(d / 2) * 2 + 1];
@@ -471,7 +511,8 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
       };
       // Attention block of the CTA's heads over its row group: norm, q/k/v in one pass (tile
       // slabs q | k | v), RoPE, cache append; no exchange with the other CTAs.
-      rmsRows(sb.x + gFirst * ldC, norm1 + l * C, sb.act + gFirst * ldC, gCount, int(C), ldC, eps);
+      rmsRows(sb.x + gFirst * ldC, staged ? op + l * C : norm1 + l * C, sb.act + gFirst * ldC,
+              gCount, int(C), ldC, eps);
       project<3, kFusedRowBlock>(table, cur, sb.act + gFirst * ldC, ldC, gCount, sb.red, sb.tile);
       const int slabO = gCount * nqO * 4;
       eachQuad(gCount, nqO, int(hc0), sb.tile, [&](int r, int col, float4 v) {
@@ -606,7 +647,7 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
 
       // MLP: gate and up of the CTA's FFN columns in one pass with the SwiGLU product, then
       // the down projection of those columns (K = F / 8, all C outputs) as a partial sum.
-      rmsRows(sb.x, norm2 + l * C, sb.act, rows, int(C), ldC, eps);
+      rmsRows(sb.x, staged ? op + (s.L + l) * C : norm2 + l * C, sb.act, rows, int(C), ldC, eps);
       project<2, kFusedRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);
       const int slabF = rows * nqF * 4;
       eachQuad(rows, nqF, oF, sb.tile, [&](int r, int col, float4 gate) {
@@ -622,7 +663,8 @@ __global__ void __cluster_dims__(kStepCtas, 1, 1) __launch_bounds__(kStepThreads
     }
 
     // Head: final norm, logits of this CTA's vocabulary columns and their per-row maximum.
-    rmsRows(sb.x, finalNorm + s.finalLayer * C, sb.act, rows, int(C), ldC, eps);
+    rmsRows(sb.x, staged ? op + 2 * s.L * C : finalNorm + s.finalLayer * C, sb.act, rows, int(C),
+            ldC, eps);
     const int64_t Wv = V / kStepCtas;
     const int oV = rank * int(Wv);
     project<1, kRowBlock>(table, cur, sb.act, ldC, rows, sb.red, sb.tile);

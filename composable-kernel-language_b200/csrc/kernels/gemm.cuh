@@ -589,21 +589,6 @@ template <int R, int Q, int T> struct IsStreamed<Streamed<R, Q, T>> : std::true_
 
 // Dynamic shared memory (geometry, config 9-18): A [K][ROWS], the gains [K], the k-slots'
 // sums [SLOTS][ROWS x COLS + 4], the reduced tile [ROWS][COLS] and the row scales.
-// 16-byte asynchronous copy global -> shared, its commit, and the wait for all of this thread's
-// copies (a wait on its own loads, which always complete).
-__device__ __forceinline__ void copyAsync16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   static_cast<unsigned>(__cvta_generic_to_shared(dst))),
-               "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void copyAsyncCommit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void copyAsyncWaitAll() {
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
 template <class Cfg, int PRO, int EPI> __device__ void streamedBody(const Params &p) {
   constexpr int R = Cfg::kRows, Q = Cfg::kQuads, SLOTS = Cfg::kSlots, DEPTH = Cfg::kDepth;
   constexpr int COLS = Cfg::kCols, kThreads = Cfg::kThreads;
