@@ -11,6 +11,7 @@
 //   fused epilogues as the FFMA kernels.
 // The normalised and activated values are rounded exactly as in the FFMA kernels
 // (x * rsqrt(mean(x^2) + eps) * gain, silu(g) * u) before the split.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -19,6 +20,7 @@
 #include "gemm.cuh"
 #include "panel.cuh"
 #include "tcgemm.cuh"
+#include "tcpair.cuh"
 
 namespace ckl::kernels {
 namespace {
@@ -155,6 +157,64 @@ __global__ void __launch_bounds__(tc::kThreads)
   tc::body<128, gemm::kSwiGluPanel, 1, MT>(p, maps.gate, &maps.up);
 }
 
+// ---- 2-SM pair kernels (tcpair.cuh) for the wide projections --------------------------------
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
+    panelLinearArgmaxPairTc(const float *a, const float *w, float *logits, float2 *partials,
+                            GemmSpec s, const __grid_constant__ tc::WeightMap weights) {
+  dependentLaunchEntry();
+  Params p;
+  p.a = a, p.w = w, p.out = logits, p.partials = partials, p.s = s;
+  tc::pair::body<gemm::kArgmax>(p, weights);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
+    panelArgmaxPairTc(const float *a, const float *w, float2 *partials, GemmSpec s,
+                      const __grid_constant__ tc::WeightMap weights) {
+  dependentLaunchEntry();
+  Params p;
+  p.a = a, p.w = w, p.out = nullptr, p.partials = partials, p.s = s;
+  tc::pair::body<gemm::kArgmax>(p, weights);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
+    panelGateUpPairTc(const float *a, const float *wg, const float *wu, float *out, GemmSpec s,
+                      const __grid_constant__ tc::WeightMapPair maps) {
+  dependentLaunchEntry();
+  Params p;
+  p.a = a, p.w = wg, p.w2 = wu, p.out = out, p.s = s;
+  tc::pair::body<gemm::kSwiGluPanel>(p, maps.gate, &maps.up);
+}
+
+// Pair kernels run a projection when its output spans at least two row tiles, one tile width
+// of columns, and pair tiles for at least 96 CTAs (about two thirds of the SMs); otherwise the
+// single-CTA kernel with its row-tile sharing and K splits fills the GPU better.
+// CKL_B200_TC_PAIRS (read when a program is compiled and bound): 0 keeps the single-CTA kernel
+// everywhere, 2 takes pairs whenever there are two row tiles (tests of small shapes).
+bool usePairs(const GemmSpec &s, int64_t tileColumns) {
+  const char *mode = std::getenv("CKL_B200_TC_PAIRS");
+  if ((mode && mode[0] == '0') || s.N < tileColumns || s.K <= 0)
+    return false;
+  const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
+  if (rowTiles < 2)
+    return false;
+  if (mode && mode[0] == '2')
+    return true;
+  const int64_t pairTiles = ((rowTiles + 1) / 2) * ((s.N + tileColumns - 1) / tileColumns);
+  return 2 * pairTiles >= 96;
+}
+
+bool argmaxPairs(const GemmSpec &s) { return usePairs(s, tc::pair::BN); }
+bool gateUpPairs(const GemmSpec &s) { return usePairs(s, tc::pair::HB); }
+
+void pairGeometry(const GemmSpec &s, int64_t tileColumns, library::Geometry *g) {
+  const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
+  g->grid[0] = 2 * ceilDiv(s.N, tileColumns);
+  g->grid[1] = unsigned((rowTiles + 1) / 2);
+  g->grid[2] = 1;
+  g->block[0] = tc::kThreads;
+  g->sharedBytes = unsigned(sizeof(tc::pair::Smem));
+}
+
 // Row tiles per CTA of the gate/up kernel (full-width tiles of 64 gate + 64 up columns): two
 // when single-tile CTAs would already fill the SMs.
 int gateUpRowTiles(const GemmSpec &s) {
@@ -166,6 +226,10 @@ bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
   const auto &s = specOf<GemmSpec>(spec);
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
+  if (gateUpPairs(s)) {
+    pairGeometry(s, tc::pair::HB, g);
+    return g->grid[1] <= 65535;
+  }
   const int mt = gateUpRowTiles(s);
   g->grid[0] = ceilDiv(s.N, tc::BM / 2);
   g->grid[1] = ceilDiv(ceilDiv(s.M, tc::BM), mt);
@@ -175,6 +239,8 @@ bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
 }
 
 const void *gateUpSelect(const void *spec) {
+  if (gateUpPairs(specOf<GemmSpec>(spec)))
+    return reinterpret_cast<const void *>(&panelGateUpPairTc);
   return gateUpRowTiles(specOf<GemmSpec>(spec)) == 2
              ? reinterpret_cast<const void *>(&panelGateUpTc<2>)
              : reinterpret_cast<const void *>(&panelGateUpTc<1>);
@@ -241,15 +307,17 @@ bool prepareWeights(const void *spec, const void *const *arguments, std::size_t 
   return true;
 }
 
-// Gate weights in slot 1, up weights in slot 2; boxes of half a tile each.
+// Gate weights in slot 1, up weights in slot 2; boxes of half a tile each (the pair kernel's
+// tile: 128 gate columns in the leader, 128 up columns in its peer).
 bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t count,
                    void *extra) {
   if (spec == nullptr || count < 3)
     return false;
   const GemmSpec &s = specOf<GemmSpec>(spec);
+  const int width = gateUpPairs(s) ? tc::pair::HB : tc::BM / 2;
   tc::WeightMapPair maps;
-  maps.gate = weightMap(pointerSlot(arguments, 1), s, tc::BM / 2);
-  maps.up = weightMap(pointerSlot(arguments, 2), s, tc::BM / 2);
+  maps.gate = weightMap(pointerSlot(arguments, 1), s, width);
+  maps.up = weightMap(pointerSlot(arguments, 2), s, width);
   std::memcpy(extra, &maps, sizeof(maps));
   return true;
 }
@@ -268,6 +336,20 @@ bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
 
 bool panelGemmGeometry(const void *spec, std::size_t, library::Geometry *g) {
   return panelGeometry(specOf<GemmSpec>(spec), g);
+}
+
+// The argmax heads (LM head, prefill heads) take the pair kernel's 256-column tiles when
+// argmaxPairs holds; their partials hold grid.x entries per row (the pair kernel: two per
+// column tile, one of them empty).
+bool panelArgmaxGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  if (argmaxPairs(s)) {
+    if (s.M <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
+      return false;
+    pairGeometry(s, tc::pair::BN, g);
+    return g->grid[1] <= 65535;
+  }
+  return panelGeometry(s, g);
 }
 
 bool panelRopeGeometry(const void *spec, std::size_t, library::Geometry *g) {
@@ -307,6 +389,18 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
     }                                                                                          \
   }
 
+const void *linearArgmaxSelect(const void *spec) {
+  if (argmaxPairs(specOf<GemmSpec>(spec)))
+    return reinterpret_cast<const void *>(&panelLinearArgmaxPairTc);
+  return CKL_PANEL_SELECT(panelLinearArgmaxTc)(spec);
+}
+
+const void *argmaxSelect(const void *spec) {
+  if (argmaxPairs(specOf<GemmSpec>(spec)))
+    return reinterpret_cast<const void *>(&panelArgmaxPairTc);
+  return CKL_PANEL_SELECT(panelArgmaxTc)(spec);
+}
+
 } // namespace
 
 CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPanelKernel),
@@ -331,10 +425,10 @@ CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const vo
                     "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1, 1>),
-                    "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearArgmaxTc),
+                    "PPPPS", sizeof(GemmSpec), panelArgmaxGeometry, linearArgmaxSelect,
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_argmax", reinterpret_cast<const void *>(&panelArgmaxTc<32, 1, 1>),
-                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelArgmaxTc),
+                    "PPPS", sizeof(GemmSpec), panelArgmaxGeometry, argmaxSelect,
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 
 } // namespace ckl::kernels

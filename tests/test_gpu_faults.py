@@ -29,12 +29,16 @@ def device():
     return ckl.Device()
 
 
-@pytest.mark.parametrize("hidden,heads,ffn,vocab", [
-    (64, 2, 96, 300),      # unsplit tiles
-    (512, 8, 1024, 1000),  # q/k/v/o split over 8-CTA clusters (K = 512)
+@pytest.mark.parametrize("batch,hidden,heads,ffn,vocab,pairs", [
+    (32, 64, 2, 96, 300, None),       # unsplit tiles
+    (32, 512, 8, 1024, 1000, None),   # q/k/v/o split over 8-CTA clusters (K = 512)
+    (256, 64, 2, 256, 512, "2"),      # gate/up and LM head on 2-SM CTA pairs
 ])
-def test_expired_wait_fails_the_step_and_the_context_recovers(device, hidden, heads, ffn, vocab):
-    config = ref.Config(batch=32, hidden=hidden, heads=heads, layers=1, ffn=ffn, vocab=vocab,
+def test_expired_wait_fails_the_step_and_the_context_recovers(device, monkeypatch, batch, hidden,
+                                                              heads, ffn, vocab, pairs):
+    if pairs:
+        monkeypatch.setenv("CKL_B200_TC_PAIRS", pairs)
+    config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=1, ffn=ffn, vocab=vocab,
                         context=4, steps=2)
     initial, _ = ref.make_inputs(config, 5, eps=1e-6)
     expected = ref.expected(initial, config, 1, eps=1e-6)

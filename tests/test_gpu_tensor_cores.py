@@ -34,22 +34,51 @@ def faults():
     return value.value
 
 
-@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", [
+CASES = [
     (128, 256, 4, 2, 512, 1024, 3),    # one full row tile, head dim 64
     (300, 128, 2, 1, 96, 1000, 3),     # ragged rows, K = 96, N tails
     (512, 1024, 16, 1, 4096, 4000, 2), # cfg5 layer shapes, 4 row tiles (smaller vocab)
     (128, 1024, 16, 4, 4096, 32000, 2),  # cfg5 depth and vocabulary
     (200, 64, 2, 1, 98, 1001, 2),      # K = 98 (ragged MMA step), N % 4 != 0, head dim 32
     (129, 96, 3, 2, 160, 520, 2),      # one row in the second tile, C = 96, head dim 32
-])
-def test_tensor_core_decoder_matches_oracle(device, batch, hidden, heads, layers, ffn, vocab, steps):
+]
+# The same shapes with the 2-SM pair kernels (gate/up, LM head) taken wherever there are two
+# row tiles: odd row-tile counts (a pair whose second CTA has no rows), ragged K and MMA steps,
+# N % 4 != 0 (weights read without tensor copies), vocabularies that end inside a tile.
+PAIR_CASES = [c for c in CASES if c[0] > 128] + [
+    (256, 64, 2, 1, 256, 512, 2),      # one pair, exact tiles
+    (640, 128, 4, 1, 384, 32000, 2),   # five row tiles, cfg5 vocabulary
+]
+
+
+@pytest.mark.parametrize("pairs", ["heuristic", "forced"])
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", CASES)
+def test_tensor_core_decoder_matches_oracle(device, monkeypatch, pairs, batch, hidden, heads,
+                                            layers, ffn, vocab, steps):
+    if pairs == "forced":
+        if (batch, hidden, heads, layers, ffn, vocab, steps) not in PAIR_CASES:
+            pytest.skip("one row tile: no pair kernel")
+        monkeypatch.setenv("CKL_B200_TC_PAIRS", "2")
+    run_case(device, batch, hidden, heads, layers, ffn, vocab, steps)
+
+
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", PAIR_CASES[-2:])
+def test_pair_kernel_shapes_match_oracle(device, monkeypatch, batch, hidden, heads, layers, ffn,
+                                         vocab, steps):
+    monkeypatch.setenv("CKL_B200_TC_PAIRS", "2")
+    run_case(device, batch, hidden, heads, layers, ffn, vocab, steps)
+
+
+def run_case(device, batch, hidden, heads, layers, ffn, vocab, steps):
     faults()
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
                         vocab=vocab, context=8, steps=steps)
     initial, _ = ref.make_inputs(config, 21, eps=1e-6)
     expected = ref.expected(initial, config, steps, eps=1e-6)
+    # whole_step=False: small decoders would otherwise run as one whole-step kernel.
     session = S.DecoderSession(device, initial, epsilon=1e-6,
-                               attention_scale=config.head_dim ** -0.5)
+                               attention_scale=config.head_dim ** -0.5, whole_step=False)
+    assert "ckl.fused.panel_gate_up" in session.invocation.node_names
     session.step(steps)
     verify(session, initial, expected, config)
     assert faults() == 0
