@@ -185,6 +185,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
   tc::pair::body<gemm::kSwiGluPanel>(p, maps.gate, &maps.up);
 }
 
+// The projections with store / RoPE / KV-append / residual epilogues on CTA pairs, K split
+// over SPLITS pairs of one cluster (2 x 1 x SPLITS).
+#define CKL_PAIR_KERNEL(fn, EPI, params, assign)                                                \
+  template <int SPLITS>                                                                        \
+  __global__ void __cluster_dims__(2, 1, SPLITS) __launch_bounds__(tc::kThreads, 1)            \
+      fn(const float *a, const float *w, CKL_UNPACK params, GemmSpec s,                         \
+         const __grid_constant__ tc::WeightMap weights) {                                      \
+    dependentLaunchEntry();                                                                    \
+    Params p;                                                                                  \
+    p.a = a, p.w = w, p.s = s;                                                                 \
+    CKL_UNPACK assign;                                                                         \
+    tc::pair::body<EPI, SPLITS>(p, weights);                                                   \
+  }
+
+CKL_PAIR_KERNEL(panelLinearPairTc, gemm::kStore, (float *dst), (p.out = dst))
+CKL_PAIR_KERNEL(panelLinearRopePairTc, gemm::kRope,
+                (const float *table, const int *position, float *dst),
+                (p.table = table, p.position = position, p.out = dst))
+CKL_PAIR_KERNEL(panelLinearRopeAppendPairTc, gemm::kRopeAppend,
+                (const float *table, const int *position, float *cache),
+                (p.table = table, p.position = position, p.out = cache))
+CKL_PAIR_KERNEL(panelLinearAppendPairTc, gemm::kAppend, (const int *position, float *cache),
+                (p.position = position, p.out = cache))
+CKL_PAIR_KERNEL(panelLinearResidualPairTc, gemm::kResidual, (const float *residual, float *dst),
+                (p.residual = residual, p.out = dst))
+
 // Pair kernels run a projection when its output spans at least two row tiles, one tile width
 // of columns, and pair tiles for at least 96 CTAs (about two thirds of the SMs); otherwise the
 // single-CTA kernel with its row-tile sharing and K splits fills the GPU better.
@@ -206,11 +232,35 @@ bool usePairs(const GemmSpec &s, int64_t tileColumns) {
 bool argmaxPairs(const GemmSpec &s) { return usePairs(s, tc::pair::BN); }
 bool gateUpPairs(const GemmSpec &s) { return usePairs(s, tc::pair::HB); }
 
-void pairGeometry(const GemmSpec &s, int64_t tileColumns, library::Geometry *g) {
+// CTAs of a pair grid without K splits.
+int64_t pairCtas(const GemmSpec &s, int64_t tileColumns) {
+  const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
+  return 2 * ((rowTiles + 1) / 2) * ((s.N + tileColumns - 1) / tileColumns);
+}
+
+// K splits of the linear family on pairs (1, 2 or 4: clusters of up to 8 CTAs): doubled while
+// the grid stays within one CTA per SM and every split keeps at least two slices.
+int pairSplits(const GemmSpec &s) {
+  const int64_t ctas = pairCtas(s, tc::pair::BN), slices = panel::slices(s.K);
+  int splits = 1;
+  while (splits < 4 && ctas * splits * 2 <= tc::kTargetCtas && slices >= int64_t(splits) * 4)
+    splits *= 2;
+  return splits;
+}
+
+// The linear family takes pairs under the same rule as the wide projections (at least 96 CTAs
+// without K splits: the batched prefill's projections).  Decode-sized q/k/v/o/down (512 rows,
+// 1024 outputs: 16 pair CTAs) measured slower on pairs split over 4-pair clusters (64 CTAs of
+// 8 slices; 27 vs 24.5 us for q, 38.6 vs 36.8 us for o/down) than on the single-CTA kernel's
+// 128 CTAs, so they keep it; forced pairs (CKL_B200_TC_PAIRS=2) still take the K splits.
+bool linearPairs(const GemmSpec &s) { return usePairs(s, tc::pair::BN); }
+
+void pairGeometry(const GemmSpec &s, int64_t tileColumns, library::Geometry *g,
+                  int splits = 1) {
   const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
   g->grid[0] = 2 * ceilDiv(s.N, tileColumns);
   g->grid[1] = unsigned((rowTiles + 1) / 2);
-  g->grid[2] = 1;
+  g->grid[2] = unsigned(splits);
   g->block[0] = tc::kThreads;
   g->sharedBytes = unsigned(sizeof(tc::pair::Smem));
 }
@@ -322,9 +372,13 @@ bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t c
   return true;
 }
 
-bool panelGeometry(const GemmSpec &s, library::Geometry *g) {
+bool panelGeometry(const GemmSpec &s, library::Geometry *g, bool pairsAllowed = true) {
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
+  if (pairsAllowed && linearPairs(s)) {
+    pairGeometry(s, tc::pair::BN, g, pairSplits(s));
+    return g->grid[1] <= 65535;
+  }
   const int width = tc::chooseWidth(s), mt = tc::chooseRowTiles(s);
   g->grid[0] = ceilDiv(s.N, width);
   g->grid[1] = ceilDiv(ceilDiv(s.M, tc::BM), mt);
@@ -349,7 +403,7 @@ bool panelArgmaxGeometry(const void *spec, std::size_t, library::Geometry *g) {
     pairGeometry(s, tc::pair::BN, g);
     return g->grid[1] <= 65535;
   }
-  return panelGeometry(s, g);
+  return panelGeometry(s, g, false);
 }
 
 bool panelRopeGeometry(const void *spec, std::size_t, library::Geometry *g) {
@@ -365,6 +419,18 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
     return false;
   return panelGeometry(s, g);
 }
+
+#define CKL_PANEL_PAIR_SELECT(fn, pairFn)                                                      \
+  [](const void *spec) -> const void * {                                                       \
+    const GemmSpec &s = specOf<GemmSpec>(spec);                                                \
+    if (linearPairs(s))                                                                        \
+      switch (pairSplits(s)) {                                                                 \
+      case 4: return reinterpret_cast<const void *>(&pairFn<4>);                               \
+      case 2: return reinterpret_cast<const void *>(&pairFn<2>);                               \
+      default: return reinterpret_cast<const void *>(&pairFn<1>);                              \
+      }                                                                                        \
+    return CKL_PANEL_SELECT(fn)(spec);                                                         \
+  }
 
 #define CKL_PANEL_SELECT(fn)                                                                   \
   [](const void *spec) -> const void * {                                                       \
@@ -410,19 +476,19 @@ CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&p
                     "PPPPS", sizeof(GemmSpec), gateUpGeometry, gateUpSelect, prepareGateUp,
                     sizeof(tc::WeightMapPair), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1, 1>),
-                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearTc),
+                    "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_PAIR_SELECT(panelLinearTc, panelLinearPairTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope", reinterpret_cast<const void *>(&panelLinearRopeTc<32, 1, 1>),
-                    "PPPPPS", sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_SELECT(panelLinearRopeTc),
+                    "PPPPPS", sizeof(GemmSpec), panelRopeGeometry, CKL_PANEL_PAIR_SELECT(panelLinearRopeTc, panelLinearRopePairTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_rope_append", reinterpret_cast<const void *>(&panelLinearRopeAppendTc<32, 1, 1>),
-                    "PPPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearRopeAppendTc),
+                    "PPPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_PAIR_SELECT(panelLinearRopeAppendTc, panelLinearRopeAppendPairTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_append", reinterpret_cast<const void *>(&panelLinearAppendTc<32, 1, 1>),
-                    "PPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_SELECT(panelLinearAppendTc),
+                    "PPPPS", sizeof(GemmSpec), panelAppendGeometry, CKL_PANEL_PAIR_SELECT(panelLinearAppendTc, panelLinearAppendPairTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const void *>(&panelLinearResidualTc<32, 1, 1>),
-                    "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_SELECT(panelLinearResidualTc),
+                    "PPPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_PAIR_SELECT(panelLinearResidualTc, panelLinearResidualPairTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelArgmaxGeometry, linearArgmaxSelect,

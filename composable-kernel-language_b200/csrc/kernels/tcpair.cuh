@@ -12,8 +12,8 @@
 // through shared memory (12 MMAs x 8 KB, 48 KB of copies, 48 KB of conversion) against ~1550
 // cycles of tensor work: about balanced, instead of ~2.5x over.
 //
-// Pair protocol (cluster of 2 x 1 x 1 CTAs, rank 0 the leader; the pair lies along x, the
-// cluster dimension CTA pairs are formed on):
+// Pair protocol (the pair's two CTAs adjacent along cluster x, the dimension CTA pairs are
+// formed on; the even cluster rank is the leader; K splits of a tile, if any, along cluster z):
 //   * both CTAs' warp 1 allocate all 512 tensor-memory columns with `tcgen05.alloc.cta_group::2`
 //     (hi*hi accumulator in columns 0-255, the hi*lo + lo*hi correction in 256-511);
 //   * each CTA's producer (warp 0) copies its own panel block (its 128 rows, hi + lo) and its
@@ -96,9 +96,9 @@ __device__ __forceinline__ void mmaPair(unsigned tmem, unsigned long long a, uns
 }
 
 // Arrive (once, when the MMAs issued so far complete) on the barrier at the same offset in
-// both CTAs of the pair.
-__device__ __forceinline__ void commitPair(unsigned long long *bar) {
-  const unsigned short mask = 0x3;
+// both CTAs of the pair whose leader has cluster rank `leader`.
+__device__ __forceinline__ void commitPair(unsigned long long *bar, unsigned leader) {
+  const unsigned short mask = static_cast<unsigned short>(0x3u << leader);
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::"
                "cluster.b64 [%0], %1;" ::"r"(smemAddress(bar)),
                "h"(mask)
@@ -148,17 +148,25 @@ __device__ __forceinline__ void tmemWaitLoads() {
 
 // Rows [128 * (2 * group + rank), +128) of A times a 256-column tile of W (gate/up: 128 gate
 // and 128 up columns).  Grid: x = 2 x column tiles (the pair's two CTAs adjacent in x), y = row
-// pairs.  The argmax head writes two partial slots per row and column tile (slots 2 nt and
-// 2 nt + 1, so that the slot count is grid.x): the row's partial and an empty one.
-template <int EPI>
+// pairs, z = SPLITS contiguous ranges of K slices (cluster 2 x 1 x SPLITS: the pairs of one
+// tile's K splits reduce their partial tiles through distributed shared memory, in split
+// order).  The argmax head (SPLITS == 1) writes two partial slots per row and column tile
+// (slots 2 nt and 2 nt + 1, so that the slot count is grid.x): the row's partial and an empty
+// one.
+template <int EPI, int SPLITS = 1>
 __device__ void body(const gemm::Params &p, const WeightMap &weights,
                      const WeightMap *upWeights = nullptr) {
-  static_assert(EPI == gemm::kSwiGluPanel || EPI == gemm::kArgmax, "pair epilogues");
+  static_assert(SPLITS == 1 || (EPI != gemm::kSwiGluPanel && EPI != gemm::kArgmax),
+                "gate/up and the argmax heads are not split");
+  static_assert(2 * SPLITS <= 8, "portable cluster size");
   extern __shared__ __align__(1024) unsigned char raw[];
   Smem &sm = *reinterpret_cast<Smem *>(raw);
   const GemmSpec &s = p.s;
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  const unsigned rank = clusterRank(); // 0: leader
+  const unsigned clusterRankValue = clusterRank();
+  const unsigned rank = clusterRankValue & 1u;     // 0: the pair's leader
+  const unsigned leader = clusterRankValue & ~1u;  // the leader's rank in the cluster
+  const unsigned split = blockIdx.z;               // == the cluster's z index
   const int64_t K = s.K, N = s.N;
   const int64_t rowTiles = (s.M + BM - 1) / BM;
   const int64_t pairs = gridDim.y, columnTiles = gridDim.x / 2;
@@ -173,8 +181,19 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int64_t wn0 = EPI == gemm::kSwiGluPanel ? n0 : n0 + int64_t(rank) * HB;
   const WeightMap &map = upHalf ? *upWeights : weights;
   const float *W = (upHalf ? p.w2 : p.w) + s.layer * K * N;
-  const int64_t slices = panel::slices(K);
+  // This split's K slices [kBegin, kEnd); an empty range contributes zeros.
+  const int64_t allSlices = panel::slices(K);
+  const int64_t perSplit = (allSlices + SPLITS - 1) / SPLITS;
+  const int64_t kBegin = perSplit * split;
+  const int64_t kEnd = kBegin + perSplit < allSlices ? kBegin + perSplit : allSlices;
+  const int64_t slices = kEnd > kBegin ? kEnd - kBegin : 0;
 
+  int position = 0;
+  if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend) {
+    position = p.position[0];
+    if (position < 0 || position >= s.T)
+      return; // outside cache capacity: the step writes nothing (grid-uniform)
+  }
   if (!aligned16(p.a) || smemAddress(raw) % 128 != 0) {
     if (threadIdx.x == 0)
       atomicOr(&g_libraryFaults, 2u); // grid-uniform: every CTA returns here
@@ -200,7 +219,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fenceBeforeSync();
-  clusterSync(); // both CTAs' barriers initialised before any remote arrival
+  clusterSync(); // every CTA's barriers initialised before any remote arrival
   fenceAfterSync();
   const unsigned tmem = sm.tmemBase;
   volatile int *abort = &sm.abort;
@@ -223,11 +242,12 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       if (lane == 0) {
         mbarrierArriveExpectTx(&sm.full[slot], blockBytes + boxBytes);
         if (hasRows)
-          bulkCopy(&sm.a[slot][0][0][0][0], p.a + (rowTile * slices + kt) * panel::kBlock,
-                   blockBytes, &sm.full[slot]);
+          bulkCopy(&sm.a[slot][0][0][0][0],
+                   p.a + (rowTile * allSlices + kBegin + kt) * panel::kBlock, blockBytes,
+                   &sm.full[slot]);
         if (copyRows)
-          tensorCopy(&sm.rawB[slot][0][0], &map.map, int(wn0), int(kt * BK), int(s.layer),
-                     &sm.full[slot]);
+          tensorCopy(&sm.rawB[slot][0][0], &map.map, int(wn0), int((kBegin + kt) * BK),
+                     int(s.layer), &sm.full[slot]);
       }
       issued = kt + 1;
     }
@@ -245,7 +265,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
         if (!waitPhase(&sm.ready[buffer], unsigned((kt / 2) & 1), abort))
           break;
         fenceAfterSync();
-        const int64_t remaining = K - kt * BK;
+        const int64_t remaining = K - (kBegin + kt) * BK;
         const int steps = int(remaining >= BK ? BK / 8 : (remaining + 7) / 8);
         for (int ks = 0; ks < steps; ++ks) {
           const unsigned long long bHi = matrixDescriptor(sm.bHi[buffer][2 * ks], HB * 16, 128);
@@ -257,11 +277,11 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
           mmaPair(tmem + BN, aHi, bLo, first);
           mmaPair(tmem + BN, aLo, bHi, 1u);
         }
-        commitPair(&sm.empty[slot]);
-        commitPair(&sm.bEmpty[buffer]);
+        commitPair(&sm.empty[slot], leader);
+        commitPair(&sm.bEmpty[buffer], leader);
       }
       // Tracks every MMA issued above, on success and on abort alike.
-      commitPair(&sm.accDone);
+      commitPair(&sm.accDone, leader);
     }
     __syncwarp();
   } else {
@@ -273,7 +293,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
         ok = waitPhase(&sm.bEmpty[buffer], unsigned((kt / 2 - 1) & 1), abort);
       if (!converterAll(ok)) // uniform over the converter warps
         break;
-      const int64_t k0 = kt * BK;
+      const int64_t k0 = (kBegin + kt) * BK;
       if (copyRows) {
         // Rows beyond K and columns beyond N arrive zero-filled.
 #pragma unroll
@@ -308,12 +328,12 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       fenceAsyncShared();
       converterSync();
       if (threadIdx.x == 2 * kWarp)
-        arriveRemote(&sm.ready[buffer], 0);
+        arriveRemote(&sm.ready[buffer], leader);
     }
     // Wait (bounded) for every MMA the leader issued.
     const bool done = waitPhase(&sm.accDone, 0, nullptr);
     fenceAfterSync();
-    valid = epilogueAll(done && !*abort) && hasRows; // uniform over these warps
+    valid = epilogueAll(done && !*abort) && slices > 0; // uniform over these warps
   }
 
   // Epilogue: this CTA's 128 rows from its own tensor memory, one row per thread; the two
@@ -322,10 +342,11 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int row = quarter * kWarp + lane;
   const int64_t m = rowTile * BM + row;
   const unsigned rowAddress = tmem + (unsigned(quarter * kWarp) << 16);
+  Staging &stage = *reinterpret_cast<Staging *>(&sm.a[0][0][0][0][0]);
   if constexpr (EPI == gemm::kSwiGluPanel) {
     // Outputs [half * 64, half * 64 + 64) of the tile: gate in columns c, up in HB + c.  A
     // warp's panel store of one output quad covers 32 consecutive rows (512 contiguous bytes).
-    if (warp >= 2 && valid) {
+    if (warp >= 2 && valid && hasRows) {
       const int64_t padded = panel::slices(N) * panel::kSlice;
 #pragma unroll 1
       for (int c0 = half * (HB / 2); c0 < (half + 1) * (HB / 2); c0 += 16) {
@@ -356,12 +377,11 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
         }
       }
     }
-  } else {
+  } else if constexpr (EPI == gemm::kArgmax) {
     // Logits staged row by row, the row's argmax over each column half from registers in
     // column order; then halves merged (the lower half first: first index wins ties) and the
     // staged rows stored coalesced.
-    Staging &stage = *reinterpret_cast<Staging *>(&sm.a[0][0][0][0][0]);
-    if (warp >= 2 && valid) {
+    if (warp >= 2 && valid && hasRows) {
       float best = -CUDART_INF_F;
       int bestIndex = 0x7fffffff;
 #pragma unroll 1
@@ -386,7 +406,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       sm.halves[half][row] = make_float2(best, __int_as_float(bestIndex));
     }
     __syncthreads();
-    if (warp >= 2 && valid) {
+    if (warp >= 2 && valid && hasRows) {
       if (half == 0 && m < s.M) {
         const float2 lower = sm.halves[0][row], upper = sm.halves[1][row];
         float best = lower.x;
@@ -416,9 +436,72 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
         }
       }
     }
+  } else {
+    // Stage the summed accumulators (zeros for an empty or abandoned split), then each split
+    // CTA reduces rows [split * 128 / SPLITS, +128 / SPLITS) of this CTA's 128 rows over the
+    // splits in rank order (deterministic) and stores them through the fused epilogue: one warp
+    // per row, each lane four consecutive columns (512-byte rows).
+    if (warp >= 2) {
+#pragma unroll 1
+      for (int c0 = half * HB; c0 < (half + 1) * HB; c0 += 16) {
+        unsigned main[16], correction[16];
+        if (valid) {
+          tmemLoad16Async(rowAddress + unsigned(c0), main);
+          tmemLoad16Async(rowAddress + unsigned(BN + c0), correction);
+          tmemWaitLoads();
+        }
+#pragma unroll
+        for (int q = 0; q < 16; q += 4)
+          *reinterpret_cast<float4 *>(&stage[row][c0 + q]) =
+              valid ? make_float4(
+                          __fadd_rn(__uint_as_float(main[q]), __uint_as_float(correction[q])),
+                          __fadd_rn(__uint_as_float(main[q + 1]),
+                                    __uint_as_float(correction[q + 1])),
+                          __fadd_rn(__uint_as_float(main[q + 2]),
+                                    __uint_as_float(correction[q + 2])),
+                          __fadd_rn(__uint_as_float(main[q + 3]),
+                                    __uint_as_float(correction[q + 3])))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if constexpr (SPLITS > 1)
+      clusterSync();
+    else
+      __syncthreads();
+    if (warp >= 2 && hasRows && __all_sync(0xffffffffu, !*abort)) {
+      constexpr int kRows = BM / SPLITS;
+      const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
+                        (EPI != gemm::kResidual || aligned16(p.residual));
+      float best = -CUDART_INF_F; // unused by these epilogues
+      int bestIndex = 0x7fffffff;
+      for (int r = int(split) * kRows + (warp - 2); r < int(split + 1) * kRows;
+           r += kConverterWarps) {
+        const int64_t mr = rowTile * BM + r;
+        if (mr >= s.M)
+          break; // rows increase with r
+#pragma unroll
+        for (int c = 4 * lane; c < BN; c += 4 * kWarp) {
+          if (n0 + c >= N)
+            break;
+          float4 sum;
+          if constexpr (SPLITS == 1) {
+            sum = *reinterpret_cast<const float4 *>(&stage[r][c]);
+          } else {
+            sum = loadCluster(&stage[r][c], rank);
+#pragma unroll
+            for (unsigned q = 1; q < SPLITS; ++q) {
+              const float4 part = loadCluster(&stage[r][c], rank + 2 * q);
+              sum = make_float4(__fadd_rn(sum.x, part.x), __fadd_rn(sum.y, part.y),
+                                __fadd_rn(sum.z, part.z), __fadd_rn(sum.w, part.w));
+            }
+          }
+          storeQuad<EPI>(p, mr, n0 + c, sum, position, vec4, best, bestIndex);
+        }
+      }
+    }
   }
   fenceBeforeSync();
-  clusterSync(); // both CTAs done with tensor memory and with each other's barriers
+  clusterSync(); // every CTA done with tensor memory and with the others' shared memory
   fenceAfterSync();
   if (warp == kMmaWarp)
     tmemFreePair(tmem);
