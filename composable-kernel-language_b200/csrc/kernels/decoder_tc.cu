@@ -164,7 +164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
   dependentLaunchEntry();
   Params p;
   p.a = a, p.w = w, p.out = logits, p.partials = partials, p.s = s;
-  tc::pair::body<gemm::kArgmax>(p, weights);
+  tc::pair::body<gemm::kArgmax, 1, tc::pair::kWide>(p, weights);
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
@@ -173,7 +173,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
   dependentLaunchEntry();
   Params p;
   p.a = a, p.w = w, p.out = nullptr, p.partials = partials, p.s = s;
-  tc::pair::body<gemm::kArgmax>(p, weights);
+  tc::pair::body<gemm::kArgmax, 1, tc::pair::kWide>(p, weights);
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
@@ -182,13 +182,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
   dependentLaunchEntry();
   Params p;
   p.a = a, p.w = wg, p.w2 = wu, p.out = out, p.s = s;
-  tc::pair::body<gemm::kSwiGluPanel>(p, maps.gate, &maps.up);
+  tc::pair::body<gemm::kSwiGluPanel, 1, tc::pair::kWide>(p, maps.gate, &maps.up);
 }
 
 // The projections with store / RoPE / KV-append / residual epilogues on CTA pairs, K split
 // over SPLITS pairs of one cluster (2 x 1 x SPLITS).
 #define CKL_PAIR_KERNEL(fn, EPI, params, assign)                                                \
-  template <int SPLITS>                                                                        \
+  template <int SPLITS, int BN>                                                                \
   __global__ void __cluster_dims__(2, 1, SPLITS) __launch_bounds__(tc::kThreads, 1)            \
       fn(const float *a, const float *w, CKL_UNPACK params, GemmSpec s,                         \
          const __grid_constant__ tc::WeightMap weights) {                                      \
@@ -196,7 +196,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::kThreads, 1)
     Params p;                                                                                  \
     p.a = a, p.w = w, p.s = s;                                                                 \
     CKL_UNPACK assign;                                                                         \
-    tc::pair::body<EPI, SPLITS>(p, weights);                                                   \
+    tc::pair::body<EPI, SPLITS, BN>(p, weights);                                               \
   }
 
 CKL_PAIR_KERNEL(panelLinearPairTc, gemm::kStore, (float *dst), (p.out = dst))
@@ -229,8 +229,8 @@ bool usePairs(const GemmSpec &s, int64_t tileColumns) {
   return 2 * pairTiles >= 96;
 }
 
-bool argmaxPairs(const GemmSpec &s) { return usePairs(s, tc::pair::BN); }
-bool gateUpPairs(const GemmSpec &s) { return usePairs(s, tc::pair::HB); }
+bool argmaxPairs(const GemmSpec &s) { return usePairs(s, tc::pair::kWide); }
+bool gateUpPairs(const GemmSpec &s) { return usePairs(s, tc::pair::kWide / 2); }
 
 // CTAs of a pair grid without K splits.
 int64_t pairCtas(const GemmSpec &s, int64_t tileColumns) {
@@ -238,31 +238,46 @@ int64_t pairCtas(const GemmSpec &s, int64_t tileColumns) {
   return 2 * ((rowTiles + 1) / 2) * ((s.N + tileColumns - 1) / tileColumns);
 }
 
-// K splits of the linear family on pairs (1, 2 or 4: clusters of up to 8 CTAs): doubled while
-// the grid stays within one CTA per SM and every split keeps at least two slices.
-int pairSplits(const GemmSpec &s) {
-  const int64_t ctas = pairCtas(s, tc::pair::BN), slices = panel::slices(s.K);
+// K splits on pairs (1, 2 or 4: clusters of up to 8 CTAs): doubled while the grid stays within
+// one CTA per SM and every split keeps at least two slices.
+int pairSplits(const GemmSpec &s, int width) {
+  const int64_t ctas = pairCtas(s, width), slices = panel::slices(s.K);
   int splits = 1;
   while (splits < 4 && ctas * splits * 2 <= tc::kTargetCtas && slices >= int64_t(splits) * 4)
     splits *= 2;
   return splits;
 }
 
-// The linear family takes pairs under the same rule as the wide projections (at least 96 CTAs
-// without K splits: the batched prefill's projections).  Decode-sized q/k/v/o/down (512 rows,
-// 1024 outputs: 16 pair CTAs) measured slower on pairs split over 4-pair clusters (64 CTAs of
-// 8 slices; 27 vs 24.5 us for q, 38.6 vs 36.8 us for o/down) than on the single-CTA kernel's
-// 128 CTAs, so they keep it; forced pairs (CKL_B200_TC_PAIRS=2) still take the K splits.
-bool linearPairs(const GemmSpec &s) { return usePairs(s, tc::pair::BN); }
+// Pair tile width of the linear family (q/k/v/o/down and the prefill projections), 0 for the
+// single-CTA kernel: 256-wide tiles when they give at least 96 CTAs without K splits (the
+// batched prefill).  The 1024-wide decode projections at 512 rows keep the single-CTA
+// kernel's 128 CTAs: on 256-wide pairs split over 4-pair clusters they get 64 CTAs and
+// measured slower (27 vs 24.5 us for q), and on 128-wide pairs (each CTA holding 64 weight
+// columns, 32 pair CTAs x 4 splits = 128 CTAs) slower still (q ~37 us, o/down shares
+// 5.2 -> 7.5 % of the step): with eight 32-deep slices per CTA the pair's start-up, split
+// reduction and cluster barriers outweigh the halved operand traffic.
+// CKL_B200_TC_PAIRS=2 / 3 force 256- / 128-wide pairs wherever there are two row tiles (the
+// tests run every tensor-core shape both ways), =0 disables pairs.
+int linearPairWidth(const GemmSpec &s) {
+  const char *mode = std::getenv("CKL_B200_TC_PAIRS");
+  const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
+  if ((mode && mode[0] == '0') || s.K <= 0 || rowTiles < 2)
+    return 0;
+  if (mode && mode[0] == '2')
+    return s.N >= tc::pair::kWide ? tc::pair::kWide : 0;
+  if (mode && mode[0] == '3')
+    return s.N >= tc::pair::kNarrow ? tc::pair::kNarrow : 0;
+  return usePairs(s, tc::pair::kWide) ? tc::pair::kWide : 0;
+}
 
 void pairGeometry(const GemmSpec &s, int64_t tileColumns, library::Geometry *g,
-                  int splits = 1) {
+                  int splits = 1, int width = tc::pair::kWide) {
   const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
   g->grid[0] = 2 * ceilDiv(s.N, tileColumns);
   g->grid[1] = unsigned((rowTiles + 1) / 2);
   g->grid[2] = unsigned(splits);
   g->block[0] = tc::kThreads;
-  g->sharedBytes = unsigned(sizeof(tc::pair::Smem));
+  g->sharedBytes = unsigned(tc::pair::sharedBytes(width));
 }
 
 // Row tiles per CTA of the gate/up kernel (full-width tiles of 64 gate + 64 up columns): two
@@ -277,7 +292,7 @@ bool gateUpGeometry(const void *spec, std::size_t, library::Geometry *g) {
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
   if (gateUpPairs(s)) {
-    pairGeometry(s, tc::pair::HB, g);
+    pairGeometry(s, tc::pair::kWide / 2, g);
     return g->grid[1] <= 65535;
   }
   const int mt = gateUpRowTiles(s);
@@ -347,8 +362,23 @@ uint64_t pointerSlot(const void *const *arguments, std::size_t index) {
   return address;
 }
 
+// Box width: half a pair tile of the linear family, or the single-CTA kernel's tile width.
 bool prepareWeights(const void *spec, const void *const *arguments, std::size_t count,
                     void *extra) {
+  if (spec == nullptr || count < 2)
+    return false;
+  const GemmSpec &s = specOf<GemmSpec>(spec);
+  const int pairWidth = linearPairWidth(s);
+  const int width = pairWidth ? pairWidth / 2 : tc::chooseWidth(s);
+  const tc::WeightMap map = weightMap(pointerSlot(arguments, 1), s, width);
+  std::memcpy(extra, &map, sizeof(map));
+  return true;
+}
+
+// The argmax heads: their pair tiles (256 wide, N >= 256) and the single-CTA kernel's tiles
+// (128 wide for N > 64) both take boxes of chooseWidth(s) columns.
+bool prepareArgmaxWeights(const void *spec, const void *const *arguments, std::size_t count,
+                          void *extra) {
   if (spec == nullptr || count < 2)
     return false;
   const GemmSpec &s = specOf<GemmSpec>(spec);
@@ -364,7 +394,7 @@ bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t c
   if (spec == nullptr || count < 3)
     return false;
   const GemmSpec &s = specOf<GemmSpec>(spec);
-  const int width = gateUpPairs(s) ? tc::pair::HB : tc::BM / 2;
+  const int width = gateUpPairs(s) ? tc::pair::kWide / 2 : tc::BM / 2;
   tc::WeightMapPair maps;
   maps.gate = weightMap(pointerSlot(arguments, 1), s, width);
   maps.up = weightMap(pointerSlot(arguments, 2), s, width);
@@ -375,8 +405,8 @@ bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t c
 bool panelGeometry(const GemmSpec &s, library::Geometry *g, bool pairsAllowed = true) {
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
-  if (pairsAllowed && linearPairs(s)) {
-    pairGeometry(s, tc::pair::BN, g, pairSplits(s));
+  if (const int width = pairsAllowed ? linearPairWidth(s) : 0) {
+    pairGeometry(s, width, g, pairSplits(s, width), width);
     return g->grid[1] <= 65535;
   }
   const int width = tc::chooseWidth(s), mt = tc::chooseRowTiles(s);
@@ -400,7 +430,7 @@ bool panelArgmaxGeometry(const void *spec, std::size_t, library::Geometry *g) {
   if (argmaxPairs(s)) {
     if (s.M <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
       return false;
-    pairGeometry(s, tc::pair::BN, g);
+    pairGeometry(s, tc::pair::kWide, g);
     return g->grid[1] <= 65535;
   }
   return panelGeometry(s, g, false);
@@ -423,12 +453,16 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
 #define CKL_PANEL_PAIR_SELECT(fn, pairFn)                                                      \
   [](const void *spec) -> const void * {                                                       \
     const GemmSpec &s = specOf<GemmSpec>(spec);                                                \
-    if (linearPairs(s))                                                                        \
-      switch (pairSplits(s)) {                                                                 \
-      case 4: return reinterpret_cast<const void *>(&pairFn<4>);                               \
-      case 2: return reinterpret_cast<const void *>(&pairFn<2>);                               \
-      default: return reinterpret_cast<const void *>(&pairFn<1>);                              \
-      }                                                                                        \
+    if (const int width = linearPairWidth(s)) {                                                \
+      const int splits = pairSplits(s, width);                                                 \
+      if (width == tc::pair::kWide)                                                            \
+        return splits == 4   ? reinterpret_cast<const void *>(&pairFn<4, tc::pair::kWide>)     \
+               : splits == 2 ? reinterpret_cast<const void *>(&pairFn<2, tc::pair::kWide>)     \
+                             : reinterpret_cast<const void *>(&pairFn<1, tc::pair::kWide>);    \
+      return splits == 4   ? reinterpret_cast<const void *>(&pairFn<4, tc::pair::kNarrow>)     \
+             : splits == 2 ? reinterpret_cast<const void *>(&pairFn<2, tc::pair::kNarrow>)     \
+                           : reinterpret_cast<const void *>(&pairFn<1, tc::pair::kNarrow>);    \
+    }                                                                                          \
     return CKL_PANEL_SELECT(fn)(spec);                                                         \
   }
 
@@ -492,10 +526,10 @@ CKL_REGISTER_KERNEL("ckl.fused.panel_linear_residual", reinterpret_cast<const vo
                     prepareWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear_argmax", reinterpret_cast<const void *>(&panelLinearArgmaxTc<32, 1, 1>),
                     "PPPPS", sizeof(GemmSpec), panelArgmaxGeometry, linearArgmaxSelect,
-                    prepareWeights, sizeof(tc::WeightMap), true, true);
+                    prepareArgmaxWeights, sizeof(tc::WeightMap), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_argmax", reinterpret_cast<const void *>(&panelArgmaxTc<32, 1, 1>),
                     "PPPS", sizeof(GemmSpec), panelArgmaxGeometry, argmaxSelect,
-                    prepareWeights, sizeof(tc::WeightMap), true, true);
+                    prepareArgmaxWeights, sizeof(tc::WeightMap), true, true);
 
 } // namespace ckl::kernels
 

@@ -39,35 +39,51 @@
 
 namespace ckl::kernels::tc::pair {
 
-constexpr int BN = 256;     // output columns of a pair tile (the MMA's N)
-constexpr int HB = BN / 2;  // weight columns held by each CTA of the pair
-constexpr int S = 3;        // ring stages
+constexpr int kWide = 256;   // pair tile width of the wide projections (the MMA's N)
+constexpr int kNarrow = 128; // pair tile width of the 1024-wide decode projections
+constexpr int S = 3;         // ring stages
 constexpr int kReadyArrivals = 2; // one per CTA of the pair
 constexpr int kConverterBarrier = 2; // named barrier of the converter warps (0: CTA, 1: epilogue)
 
-struct Smem {
+// Shared memory of a pair CTA for tiles BN columns wide: each CTA holds HB = BN / 2 weight
+// columns; NB conversion buffers (two for 256-wide tiles, four for 128-wide ones, whose MMAs
+// take half as long, so that conversion runs further ahead of them).
+template <int BN_> struct Layout {
+  static constexpr int BN = BN_, HB = BN_ / 2, NB = BN_ == kWide ? 2 : 4;
   float a[S][2][BK / 4][BM][4]; // panel block of this CTA's 128 rows (hi, lo) as copied
   float rawB[S][BK][HB];        // this CTA's half of the weight box as copied
-  float bHi[2][BK / 4][HB][4];  // converted weight half, K-major
-  float bLo[2][BK / 4][HB][4];
-  unsigned long long full[S], empty[S], ready[2], bEmpty[2], accDone;
+  float bHi[NB][BK / 4][HB][4]; // converted weight half, K-major
+  float bLo[NB][BK / 4][HB][4];
+  unsigned long long full[S], empty[S], ready[NB], bEmpty[NB], accDone;
   unsigned long long unsignalled; // never arrived on (injected expiring wait)
   float2 halves[2][BM];           // argmax partials of each row's two column halves
   unsigned tmemBase;
   int abort;
 };
-static_assert(sizeof(Smem) <= kMaxDynamicSmem, "shared memory budget");
-// Logits staged row by row for coalesced stores; aliases the idle ring after the main loop.
-using Staging = float[BM][BN + 4];
-static_assert(sizeof(Staging) <= sizeof(Smem::a) + sizeof(Smem::rawB), "staging fits the ring");
+static_assert(sizeof(Layout<kWide>) <= kMaxDynamicSmem, "shared memory budget");
+static_assert(sizeof(Layout<kNarrow>) <= kMaxDynamicSmem, "shared memory budget");
+// Accumulators staged row by row (logits, split-K partials); aliases the idle ring after the
+// main loop.
+template <int BN> using Staging = float[BM][BN + 4];
+static_assert(sizeof(Staging<kWide>) <= sizeof(Layout<kWide>::a) + sizeof(Layout<kWide>::rawB),
+              "staging fits the ring");
+static_assert(sizeof(Staging<kNarrow>) <= sizeof(Layout<kNarrow>::a), "staging fits the ring");
 
-// Output columns of one pair tile: the gate/up tile holds 128 gate and 128 up columns of the
-// same 128 outputs (gate in the leader's weight half, up in the peer's).
-template <int EPI> constexpr int tileColumns() { return EPI == gemm::kSwiGluPanel ? HB : BN; }
+inline std::size_t sharedBytes(int width) {
+  return width == kWide ? sizeof(Layout<kWide>) : sizeof(Layout<kNarrow>);
+}
 
-// kind::tf32, D f32, both operands K-major, M = 256 (over the pair), N = 256.
-constexpr unsigned kInstruction =
-    (1u << 4) | (2u << 7) | (2u << 10) | (unsigned(BN >> 3) << 17) | (unsigned(256 >> 4) << 24);
+// Output columns of one pair tile: the gate/up tile holds BN / 2 gate and BN / 2 up columns of
+// the same outputs (gate in the leader's weight half, up in the peer's).
+template <int EPI, int BN> constexpr int tileColumns() {
+  return EPI == gemm::kSwiGluPanel ? BN / 2 : BN;
+}
+
+// kind::tf32, D f32, both operands K-major, M = 256 (over the pair), N = BN.
+template <int BN> constexpr unsigned instruction() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (unsigned(BN >> 3) << 17) |
+         (unsigned(256 >> 4) << 24);
+}
 
 __device__ __forceinline__ unsigned clusterRank() {
   unsigned rank;
@@ -75,23 +91,26 @@ __device__ __forceinline__ unsigned clusterRank() {
   return rank;
 }
 
-__device__ __forceinline__ void tmemAllocPair(unsigned *slot) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;"
-               ::"r"(smemAddress(slot))
+// Both CTAs' same warp allocate (and later free) `Columns` tensor-memory columns as a pair.
+template <int Columns> __device__ __forceinline__ void tmemAllocPair(unsigned *slot) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smemAddress(slot)), "n"(Columns)
                : "memory");
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmemFreePair(unsigned base) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(base) : "memory");
+template <int Columns> __device__ __forceinline__ void tmemFreePair(unsigned base) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "n"(Columns)
+               : "memory");
 }
 
+template <int BN>
 __device__ __forceinline__ void mmaPair(unsigned tmem, unsigned long long a, unsigned long long b,
                                         unsigned accumulate) {
   asm volatile("{\n\t.reg .pred p;\n\t"
                "setp.ne.b32 p, %4, 0;\n\t"
                "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-               ::"r"(tmem), "l"(a), "l"(b), "r"(kInstruction), "r"(accumulate)
+               ::"r"(tmem), "l"(a), "l"(b), "n"(instruction<BN>()), "r"(accumulate)
                : "memory");
 }
 
@@ -153,9 +172,11 @@ __device__ __forceinline__ void tmemWaitLoads() {
 // order).  The argmax head (SPLITS == 1) writes two partial slots per row and column tile
 // (slots 2 nt and 2 nt + 1, so that the slot count is grid.x): the row's partial and an empty
 // one.
-template <int EPI, int SPLITS = 1>
+template <int EPI, int SPLITS = 1, int BN = kWide>
 __device__ void body(const gemm::Params &p, const WeightMap &weights,
                      const WeightMap *upWeights = nullptr) {
+  using Smem = Layout<BN>;
+  constexpr int HB = Smem::HB, NB = Smem::NB;
   static_assert(SPLITS == 1 || (EPI != gemm::kSwiGluPanel && EPI != gemm::kArgmax),
                 "gate/up and the argmax heads are not split");
   static_assert(2 * SPLITS <= 8, "portable cluster size");
@@ -176,7 +197,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int64_t group = tile % pairs, nt = tile / pairs;
   const int64_t rowTile = 2 * group + rank;
   const bool hasRows = rowTile < rowTiles;
-  const int64_t n0 = nt * tileColumns<EPI>();
+  const int64_t n0 = nt * tileColumns<EPI, BN>();
   const bool upHalf = EPI == gemm::kSwiGluPanel && rank == 1;
   const int64_t wn0 = EPI == gemm::kSwiGluPanel ? n0 : n0 + int64_t(rank) * HB;
   const WeightMap &map = upHalf ? *upWeights : weights;
@@ -203,13 +224,13 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       weights.valid != 0 && (EPI != gemm::kSwiGluPanel || upWeights->valid != 0);
 
   if (warp == kMmaWarp)
-    tmemAllocPair(&sm.tmemBase);
+    tmemAllocPair<2 * BN>(&sm.tmemBase);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbarrierInit(&sm.full[i], 1);
       mbarrierInit(&sm.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NB; ++i) {
       mbarrierInit(&sm.ready[i], kReadyArrivals);
       mbarrierInit(&sm.bEmpty[i], 1);
     }
@@ -261,8 +282,8 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       const bool injected =
           g_injectUnsignalledWait != 0 && !waitPhase(&sm.unsignalled, 0, abort);
       for (int64_t kt = 0; kt < slices && !injected; ++kt) {
-        const int slot = int(kt % S), buffer = int(kt & 1);
-        if (!waitPhase(&sm.ready[buffer], unsigned((kt / 2) & 1), abort))
+        const int slot = int(kt % S), buffer = int(kt % NB);
+        if (!waitPhase(&sm.ready[buffer], unsigned((kt / NB) & 1), abort))
           break;
         fenceAfterSync();
         const int64_t remaining = K - (kBegin + kt) * BK;
@@ -273,9 +294,9 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
           const unsigned long long aHi = matrixDescriptor(sm.a[slot][0][2 * ks], BM * 16, 128);
           const unsigned long long aLo = matrixDescriptor(sm.a[slot][1][2 * ks], BM * 16, 128);
           const unsigned first = (kt == 0 && ks == 0) ? 0u : 1u;
-          mmaPair(tmem, aHi, bHi, first);
-          mmaPair(tmem + BN, aHi, bLo, first);
-          mmaPair(tmem + BN, aLo, bHi, 1u);
+          mmaPair<BN>(tmem, aHi, bHi, first);
+          mmaPair<BN>(tmem + BN, aHi, bLo, first);
+          mmaPair<BN>(tmem + BN, aLo, bHi, 1u);
         }
         commitPair(&sm.empty[slot], leader);
         commitPair(&sm.bEmpty[buffer], leader);
@@ -287,10 +308,10 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   } else {
     const int t = threadIdx.x - 2 * kWarp;
     for (int64_t kt = 0; kt < slices; ++kt) {
-      const int slot = int(kt % S), buffer = int(kt & 1);
+      const int slot = int(kt % S), buffer = int(kt % NB);
       bool ok = waitPhase(&sm.full[slot], unsigned((kt / S) & 1), abort);
-      if (ok && kt >= 2)
-        ok = waitPhase(&sm.bEmpty[buffer], unsigned((kt / 2 - 1) & 1), abort);
+      if (ok && kt >= NB)
+        ok = waitPhase(&sm.bEmpty[buffer], unsigned((kt / NB - 1) & 1), abort);
       if (!converterAll(ok)) // uniform over the converter warps
         break;
       const int64_t k0 = (kBegin + kt) * BK;
@@ -342,7 +363,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int row = quarter * kWarp + lane;
   const int64_t m = rowTile * BM + row;
   const unsigned rowAddress = tmem + (unsigned(quarter * kWarp) << 16);
-  Staging &stage = *reinterpret_cast<Staging *>(&sm.a[0][0][0][0][0]);
+  Staging<BN> &stage = *reinterpret_cast<Staging<BN> *>(&sm.a[0][0][0][0][0]);
   if constexpr (EPI == gemm::kSwiGluPanel) {
     // Outputs [half * 64, half * 64 + 64) of the tile: gate in columns c, up in HB + c.  A
     // warp's panel store of one output quad covers 32 consecutive rows (512 contiguous bytes).
@@ -504,7 +525,7 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   clusterSync(); // every CTA done with tensor memory and with the others' shared memory
   fenceAfterSync();
   if (warp == kMmaWarp)
-    tmemFreePair(tmem);
+    tmemFreePair<2 * BN>(tmem);
 }
 
 } // namespace ckl::kernels::tc::pair

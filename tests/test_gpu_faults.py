@@ -33,6 +33,7 @@ def device():
     (32, 64, 2, 96, 300, None),       # unsplit tiles
     (32, 512, 8, 1024, 1000, None),   # q/k/v/o split over 8-CTA clusters (K = 512)
     (256, 64, 2, 256, 512, "2"),      # gate/up and LM head on 2-SM CTA pairs
+    (256, 512, 8, 1024, 1000, "3"),   # q/k/v/o/down on 128-wide pairs, K split over 4 pairs
 ])
 def test_expired_wait_fails_the_step_and_the_context_recovers(device, monkeypatch, batch, hidden,
                                                               heads, ffn, vocab, pairs):

@@ -42,30 +42,36 @@ CASES = [
     (200, 64, 2, 1, 98, 1001, 2),      # K = 98 (ragged MMA step), N % 4 != 0, head dim 32
     (129, 96, 3, 2, 160, 520, 2),      # one row in the second tile, C = 96, head dim 32
 ]
-# The same shapes with the 2-SM pair kernels (gate/up, LM head) taken wherever there are two
-# row tiles: odd row-tile counts (a pair whose second CTA has no rows), ragged K and MMA steps,
-# N % 4 != 0 (weights read without tensor copies), vocabularies that end inside a tile.
+# The same shapes with the 2-SM pair kernels taken wherever there are two row tiles: "wide"
+# (CKL_B200_TC_PAIRS=2) puts every projection with 256 or more outputs on 256-wide pair tiles
+# (K split over pairs of a cluster where the grid is small), "narrow" (=3) puts q/k/v/o/down
+# on 128-wide ones.  Covered: odd row-tile counts (a pair whose second CTA has no rows), ragged
+# K and MMA steps, N % 4 != 0 (weights read without tensor copies), outputs and vocabularies
+# that end inside a tile.
 PAIR_CASES = [c for c in CASES if c[0] > 128] + [
     (256, 64, 2, 1, 256, 512, 2),      # one pair, exact tiles
     (640, 128, 4, 1, 384, 32000, 2),   # five row tiles, cfg5 vocabulary
+    (384, 384, 6, 1, 256, 700, 2),     # three 128-wide column tiles, K = 384
 ]
+MODES = {"wide": "2", "narrow": "3"}
 
 
-@pytest.mark.parametrize("pairs", ["heuristic", "forced"])
+@pytest.mark.parametrize("pairs", ["heuristic", "wide", "narrow"])
 @pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", CASES)
 def test_tensor_core_decoder_matches_oracle(device, monkeypatch, pairs, batch, hidden, heads,
                                             layers, ffn, vocab, steps):
-    if pairs == "forced":
+    if pairs in MODES:
         if (batch, hidden, heads, layers, ffn, vocab, steps) not in PAIR_CASES:
             pytest.skip("one row tile: no pair kernel")
-        monkeypatch.setenv("CKL_B200_TC_PAIRS", "2")
+        monkeypatch.setenv("CKL_B200_TC_PAIRS", MODES[pairs])
     run_case(device, batch, hidden, heads, layers, ffn, vocab, steps)
 
 
-@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", PAIR_CASES[-2:])
-def test_pair_kernel_shapes_match_oracle(device, monkeypatch, batch, hidden, heads, layers, ffn,
-                                         vocab, steps):
-    monkeypatch.setenv("CKL_B200_TC_PAIRS", "2")
+@pytest.mark.parametrize("pairs", ["wide", "narrow"])
+@pytest.mark.parametrize("batch,hidden,heads,layers,ffn,vocab,steps", PAIR_CASES[-3:])
+def test_pair_kernel_shapes_match_oracle(device, monkeypatch, pairs, batch, hidden, heads, layers,
+                                         ffn, vocab, steps):
+    monkeypatch.setenv("CKL_B200_TC_PAIRS", MODES[pairs])
     run_case(device, batch, hidden, heads, layers, ffn, vocab, steps)
 
 
