@@ -211,6 +211,21 @@ CKL_PAIR_KERNEL(panelLinearAppendPairTc, gemm::kAppend, (const int *position, fl
 CKL_PAIR_KERNEL(panelLinearResidualPairTc, gemm::kResidual, (const float *residual, float *dst),
                 (p.residual = residual, p.out = dst))
 
+// q, k and v in one launch on pairs: the panel of the normalised rows times wq | wk | wv, each
+// 256-column tile with its projection's epilogue (RoPE into q; RoPE and cache append into kc;
+// cache append into vc).
+template <int SPLITS>
+__global__ void __cluster_dims__(2, 1, SPLITS) __launch_bounds__(tc::kThreads, 1)
+    panelQkvPairTc(const float *a, const float *wq, const float *wk, const float *wv,
+                   const float *table, const int *position, float *q, float *kc, float *vc,
+                   GemmSpec s, const __grid_constant__ tc::WeightMapTriple maps) {
+  dependentLaunchEntry();
+  Params p;
+  p.a = a, p.w = wq, p.w2 = wk, p.w3 = wv, p.table = table, p.position = position;
+  p.out = q, p.out2 = kc, p.out3 = vc, p.s = s;
+  tc::pair::body<gemm::kQkv, SPLITS, tc::pair::kWide>(p, maps.q, &maps.k, &maps.v);
+}
+
 // Pair kernels run a projection when its output spans at least two row tiles, one tile width
 // of columns, and pair tiles for at least 96 CTAs (about two thirds of the SMs); otherwise the
 // single-CTA kernel with its row-tile sharing and K splits fills the GPU better.
@@ -268,6 +283,27 @@ int linearPairWidth(const GemmSpec &s) {
   if (mode && mode[0] == '3')
     return s.N >= tc::pair::kNarrow ? tc::pair::kNarrow : 0;
   return usePairs(s, tc::pair::kWide) ? tc::pair::kWide : 0;
+}
+
+// The fused q/k/v node applies when each projection is a whole number of 256-wide tiles, there
+// are two row tiles, and the 3N-wide pair grid with its K splits gives at least 96 CTAs (the
+// cfg5 shard: 12 column tiles x 2 row pairs x 2 splits); otherwise the planner keeps three
+// nodes.  CKL_B200_TC_PAIRS=0 (or CKL_B200_TC_QKV=0) disables it, CKL_B200_TC_PAIRS=2 / 3 take
+// it whenever the shape allows.
+bool qkvPairs(const GemmSpec &s, GemmSpec *wide = nullptr) {
+  const char *mode = std::getenv("CKL_B200_TC_PAIRS");
+  const char *fused = std::getenv("CKL_B200_TC_QKV");
+  const int64_t rowTiles = (s.M + tc::BM - 1) / tc::BM;
+  if ((mode && mode[0] == '0') || (fused && fused[0] == '0') || s.K <= 0 || s.N <= 0 || s.N % tc::pair::kWide != 0 ||
+      rowTiles < 2)
+    return false;
+  GemmSpec all = s;
+  all.N = 3 * s.N;
+  if (wide)
+    *wide = all;
+  if (mode && (mode[0] == '2' || mode[0] == '3'))
+    return true;
+  return pairCtas(all, tc::pair::kWide) * pairSplits(all, tc::pair::kWide) >= 96;
 }
 
 void pairGeometry(const GemmSpec &s, int64_t tileColumns, library::Geometry *g,
@@ -402,6 +438,42 @@ bool prepareGateUp(const void *spec, const void *const *arguments, std::size_t c
   return true;
 }
 
+// Weights of q, k and v in slots 1-3; 128-column boxes (half of a 256-wide pair tile).
+bool prepareQkv(const void *spec, const void *const *arguments, std::size_t count,
+                void *extra) {
+  if (spec == nullptr || count < 4)
+    return false;
+  const GemmSpec &s = specOf<GemmSpec>(spec);
+  tc::WeightMapTriple maps;
+  maps.q = weightMap(pointerSlot(arguments, 1), s, tc::pair::kWide / 2);
+  maps.k = weightMap(pointerSlot(arguments, 2), s, tc::pair::kWide / 2);
+  maps.v = weightMap(pointerSlot(arguments, 3), s, tc::pair::kWide / 2);
+  std::memcpy(extra, &maps, sizeof(maps));
+  return true;
+}
+
+bool qkvGeometry(const void *spec, std::size_t, library::Geometry *g) {
+  const auto &s = specOf<GemmSpec>(spec);
+  GemmSpec all;
+  if (s.M <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers || s.D <= 0 ||
+      s.D % 2 || s.N != s.A * s.D || s.T <= 0 || !qkvPairs(s, &all))
+    return false;
+  const int splits = pairSplits(all, tc::pair::kWide);
+  pairGeometry(all, tc::pair::kWide, g, splits, tc::pair::kWide);
+  return g->grid[1] <= 65535;
+}
+
+const void *qkvSelect(const void *spec) {
+  GemmSpec all;
+  if (!qkvPairs(specOf<GemmSpec>(spec), &all))
+    return nullptr;
+  switch (pairSplits(all, tc::pair::kWide)) {
+  case 4: return reinterpret_cast<const void *>(&panelQkvPairTc<4>);
+  case 2: return reinterpret_cast<const void *>(&panelQkvPairTc<2>);
+  default: return reinterpret_cast<const void *>(&panelQkvPairTc<1>);
+  }
+}
+
 bool panelGeometry(const GemmSpec &s, library::Geometry *g, bool pairsAllowed = true) {
   if (s.M <= 0 || s.K <= 0 || s.N <= 0 || s.layers <= 0 || s.layer < 0 || s.layer >= s.layers)
     return false;
@@ -509,6 +581,9 @@ CKL_REGISTER_KERNEL("ckl.fused.rms_panel", reinterpret_cast<const void *>(&rmsPa
 CKL_REGISTER_KERNEL("ckl.fused.panel_gate_up", reinterpret_cast<const void *>(&panelGateUpTc<1>),
                     "PPPPS", sizeof(GemmSpec), gateUpGeometry, gateUpSelect, prepareGateUp,
                     sizeof(tc::WeightMapPair), true, true);
+CKL_REGISTER_KERNEL("ckl.fused.panel_qkv", reinterpret_cast<const void *>(&panelQkvPairTc<1>),
+                    "PPPPPPPPPS", sizeof(GemmSpec), qkvGeometry, qkvSelect, prepareQkv,
+                    sizeof(tc::WeightMapTriple), true, true);
 CKL_REGISTER_KERNEL("ckl.fused.panel_linear", reinterpret_cast<const void *>(&panelLinearTc<32, 1, 1>),
                     "PPPS", sizeof(GemmSpec), panelGemmGeometry, CKL_PANEL_PAIR_SELECT(panelLinearTc, panelLinearPairTc),
                     prepareWeights, sizeof(tc::WeightMap), true, true);

@@ -23,7 +23,10 @@ enum Prologue : int { kPlain = 0, kRms = 1, kSwiGlu = 2 };
 // kSwiGluPanel (tensor-core path only): the tile's columns are gate and up projections of the
 // same outputs; the epilogue writes silu(gate) * up as a split operand panel.
 enum Epilogue : int {
-  kStore = 0, kResidual = 1, kRope = 2, kRopeAppend = 3, kAppend = 4, kArgmax = 5, kSwiGluPanel = 6
+  kStore = 0, kResidual = 1, kRope = 2, kRopeAppend = 3, kAppend = 4, kArgmax = 5, kSwiGluPanel = 6,
+  // q, k and v in one launch (tensor-core pair kernel only): column tiles of q take kRope into
+  // out, of k kRopeAppend into out2, of v kAppend into out3.
+  kQkv = 7
 };
 
 struct Params {
@@ -31,11 +34,13 @@ struct Params {
   const float *a2 = nullptr;       // [M, K] up projection (SwiGLU)
   const float *gain = nullptr;     // [layers, K] (RMSNorm)
   const float *w = nullptr;        // [layers, K, N]
-  const float *w2 = nullptr;       // [layers, K, N] up projection (kSwiGluPanel)
+  const float *w2 = nullptr;       // [layers, K, N] up projection (kSwiGluPanel), k (kQkv)
+  const float *w3 = nullptr;       // [layers, K, N] v (kQkv)
   const float *residual = nullptr; // [M, N]
   const float *table = nullptr;    // [T, D/2, 2]
   const int *position = nullptr;   // [1]
   float *out = nullptr;            // [M, N] or cache [layers, M, A, T, D]
+  float *out2 = nullptr, *out3 = nullptr; // k and v caches (kQkv)
   float2 *partials = nullptr;      // [M, tiles] (value, index bits)
   float eps = 0.f;
   GemmSpec s{};

@@ -71,6 +71,11 @@ struct WeightMapPair {
   WeightMap gate, up;
 };
 
+// q, k and v weights of the fused q/k/v projection.
+struct WeightMapTriple {
+  WeightMap q, k, v;
+};
+
 // Output columns of one tile: the gate/up tile holds BN/2 gate and BN/2 up columns of the same
 // BN/2 outputs.
 template <int BN, int EPI> constexpr int tileColumns() {

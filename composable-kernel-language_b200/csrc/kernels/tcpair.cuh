@@ -172,11 +172,16 @@ __device__ __forceinline__ void tmemWaitLoads() {
 // order).  The argmax head (SPLITS == 1) writes two partial slots per row and column tile
 // (slots 2 nt and 2 nt + 1, so that the slot count is grid.x): the row's partial and an empty
 // one.
+//
+// EPI == kQkv: q, k and v (each [K, N] with N a multiple of 256) as one 3N-wide output; each
+// column tile lies in one projection, whose weight map (weights, upWeights, vWeights), RoPE /
+// cache-append epilogue and output it takes.
 template <int EPI, int SPLITS = 1, int BN = kWide>
 __device__ void body(const gemm::Params &p, const WeightMap &weights,
-                     const WeightMap *upWeights = nullptr) {
+                     const WeightMap *upWeights = nullptr, const WeightMap *vWeights = nullptr) {
   using Smem = Layout<BN>;
   constexpr int HB = Smem::HB, NB = Smem::NB;
+  static_assert(EPI != gemm::kQkv || BN == kWide, "q/k/v tiles are 256 wide");
   static_assert(SPLITS == 1 || (EPI != gemm::kSwiGluPanel && EPI != gemm::kArgmax),
                 "gate/up and the argmax heads are not split");
   static_assert(2 * SPLITS <= 8, "portable cluster size");
@@ -197,11 +202,14 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int64_t group = tile % pairs, nt = tile / pairs;
   const int64_t rowTile = 2 * group + rank;
   const bool hasRows = rowTile < rowTiles;
-  const int64_t n0 = nt * tileColumns<EPI, BN>();
-  const bool upHalf = EPI == gemm::kSwiGluPanel && rank == 1;
+  // kQkv: projection (0 q, 1 k, 2 v) of this column tile; n0 is the tile's first column
+  // within that projection.
+  const int projection = EPI == gemm::kQkv ? int((nt * BN) / N) : 0;
+  const int64_t n0 = nt * tileColumns<EPI, BN>() - int64_t(projection) * N;
+  const bool upHalf = (EPI == gemm::kSwiGluPanel && rank == 1) || projection == 1;
   const int64_t wn0 = EPI == gemm::kSwiGluPanel ? n0 : n0 + int64_t(rank) * HB;
-  const WeightMap &map = upHalf ? *upWeights : weights;
-  const float *W = (upHalf ? p.w2 : p.w) + s.layer * K * N;
+  const WeightMap &map = projection == 2 ? *vWeights : upHalf ? *upWeights : weights;
+  const float *W = (projection == 2 ? p.w3 : upHalf ? p.w2 : p.w) + s.layer * K * N;
   // This split's K slices [kBegin, kEnd); an empty range contributes zeros.
   const int64_t allSlices = panel::slices(K);
   const int64_t perSplit = (allSlices + SPLITS - 1) / SPLITS;
@@ -210,7 +218,8 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   const int64_t slices = kEnd > kBegin ? kEnd - kBegin : 0;
 
   int position = 0;
-  if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend) {
+  if constexpr (EPI == gemm::kRope || EPI == gemm::kRopeAppend || EPI == gemm::kAppend ||
+                EPI == gemm::kQkv) {
     position = p.position[0];
     if (position < 0 || position >= s.T)
       return; // outside cache capacity: the step writes nothing (grid-uniform)
@@ -221,7 +230,9 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
     return;
   }
   const bool copyRows =
-      weights.valid != 0 && (EPI != gemm::kSwiGluPanel || upWeights->valid != 0);
+      weights.valid != 0 &&
+      (EPI != gemm::kSwiGluPanel || upWeights->valid != 0) &&
+      (EPI != gemm::kQkv || (upWeights->valid != 0 && vWeights->valid != 0));
 
   if (warp == kMmaWarp)
     tmemAllocPair<2 * BN>(&sm.tmemBase);
@@ -493,6 +504,10 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
       constexpr int kRows = BM / SPLITS;
       const bool vec4 = N % 4 == 0 && aligned16(p.out) &&
                         (EPI != gemm::kResidual || aligned16(p.residual));
+      // kQkv: the projection's own epilogue and output.
+      gemm::Params own = p;
+      if constexpr (EPI == gemm::kQkv)
+        own.out = projection == 0 ? p.out : projection == 1 ? p.out2 : p.out3;
       float best = -CUDART_INF_F; // unused by these epilogues
       int bestIndex = 0x7fffffff;
       for (int r = int(split) * kRows + (warp - 2); r < int(split + 1) * kRows;
@@ -516,7 +531,16 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
                                 __fadd_rn(sum.z, part.z), __fadd_rn(sum.w, part.w));
             }
           }
-          storeQuad<EPI>(p, mr, n0 + c, sum, position, vec4, best, bestIndex);
+          if constexpr (EPI == gemm::kQkv) {
+            if (projection == 0)
+              storeQuad<gemm::kRope>(own, mr, n0 + c, sum, position, vec4, best, bestIndex);
+            else if (projection == 1)
+              storeQuad<gemm::kRopeAppend>(own, mr, n0 + c, sum, position, vec4, best, bestIndex);
+            else
+              storeQuad<gemm::kAppend>(own, mr, n0 + c, sum, position, vec4, best, bestIndex);
+          } else {
+            storeQuad<EPI>(p, mr, n0 + c, sum, position, vec4, best, bestIndex);
+          }
         }
       }
     }

@@ -335,6 +335,9 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
         if any(v != values[0] for v in values):
             raise _NoMatch
 
+    def same_shape(*rids):
+        return all(shape(r) == shape(rids[0]) for r in rids)
+
     def gemm_spec(M, K, N, layers_, layer, A=0, D=0, T=0, tiles=0):
         return pack(M, K, N, layers_, layer, A, D, T, tiles, config, M)
 
@@ -462,21 +465,29 @@ def _decoder_nodes(dispatches, layers, resources, config=0, collect=None):
             new_nodes.append(node("ckl.fused.rms_panel", [R(x), R(g1), R(x_panel), eps1],
                                   pack(B, Cdim, shape(g1)[0], layer), [x, g1],
                                   [(x_panel, WRITE, "whole")], "attention norm"))
-            new_nodes.append(node("ckl.fused.panel_linear_rope",
-                                  [R(x_panel), R(wq), R(sincos), R(position), R(qr)],
-                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                                  [x_panel, wq, sincos], [pos_read, (qr, WRITE, "whole")],
-                                  "q projection"))
-            new_nodes.append(node("ckl.fused.panel_linear_rope_append",
-                                  [R(x_panel), R(wk), R(sincos), R(position), R(kc)],
-                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                                  [x_panel, wk, sincos], [pos_read, (kc, WRITE, "whole")],
-                                  "k projection"))
-            new_nodes.append(node("ckl.fused.panel_linear_append",
-                                  [R(x_panel), R(wv), R(position), R(vc)],
-                                  gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T),
-                                  [x_panel, wv], [pos_read, (vc, WRITE, "whole")],
-                                  "v projection"))
+            qkv_spec = gemm_spec(B, Cdim, Cdim, Lw, layer, A, D, T)
+            if same_shape(wq, wk, wv) and library_accepts("ckl.fused.panel_qkv", qkv_spec):
+                # One launch for q, k and v on tensor-core CTA pairs (each column tile takes
+                # its projection's epilogue).
+                new_nodes.append(node("ckl.fused.panel_qkv",
+                                      [R(x_panel), R(wq), R(wk), R(wv), R(sincos), R(position),
+                                       R(qr), R(kc), R(vc)], qkv_spec,
+                                      [x_panel, wq, wk, wv, sincos],
+                                      [pos_read, (qr, WRITE, "whole"), (kc, WRITE, "whole"),
+                                       (vc, WRITE, "whole")], "q/k/v projections"))
+            else:
+                new_nodes.append(node("ckl.fused.panel_linear_rope",
+                                      [R(x_panel), R(wq), R(sincos), R(position), R(qr)],
+                                      qkv_spec, [x_panel, wq, sincos],
+                                      [pos_read, (qr, WRITE, "whole")], "q projection"))
+                new_nodes.append(node("ckl.fused.panel_linear_rope_append",
+                                      [R(x_panel), R(wk), R(sincos), R(position), R(kc)],
+                                      qkv_spec, [x_panel, wk, sincos],
+                                      [pos_read, (kc, WRITE, "whole")], "k projection"))
+                new_nodes.append(node("ckl.fused.panel_linear_append",
+                                      [R(x_panel), R(wv), R(position), R(vc)],
+                                      qkv_spec, [x_panel, wv],
+                                      [pos_read, (vc, WRITE, "whole")], "v projection"))
             new_nodes.append(attention_node(qr, kc, vc, context_panel, 1))
             new_nodes.append(node("ckl.fused.panel_linear_residual",
                                   [R(context_panel), R(wo), R(x), R(residual)],
@@ -670,6 +681,15 @@ def _add_resource(resources, kind, spec, name) -> int:
 
 
 # ---- native planning -------------------------------------------------------------------
+def library_accepts(name: str, spec: bytes) -> bool:
+    """Whether library kernel ``name`` has a launch geometry for this specialization."""
+    try:
+        library_geometry(name, spec)
+    except CompilationError:
+        return False
+    return True
+
+
 def library_geometry(name: str, spec: bytes):
     lib = _native.load()
     grid, block, shared = (C.c_uint32 * 3)(), (C.c_uint32 * 3)(), C.c_uint32()

@@ -41,6 +41,7 @@ CASES = [
     (128, 1024, 16, 4, 4096, 32000, 2),  # cfg5 depth and vocabulary
     (200, 64, 2, 1, 98, 1001, 2),      # K = 98 (ragged MMA step), N % 4 != 0, head dim 32
     (129, 96, 3, 2, 160, 520, 2),      # one row in the second tile, C = 96, head dim 32
+    (300, 256, 4, 2, 512, 1000, 2),    # C = 256: q/k/v as one launch when pairs are forced
 ]
 # The same shapes with the 2-SM pair kernels taken wherever there are two row tiles: "wide"
 # (CKL_B200_TC_PAIRS=2) puts every projection with 256 or more outputs on 256-wide pair tiles
@@ -76,6 +77,8 @@ def test_pair_kernel_shapes_match_oracle(device, monkeypatch, pairs, batch, hidd
 
 
 def run_case(device, batch, hidden, heads, layers, ffn, vocab, steps):
+    import os
+    forced = os.environ.get("CKL_B200_TC_PAIRS") in ("2", "3")
     faults()
     config = ref.Config(batch=batch, hidden=hidden, heads=heads, layers=layers, ffn=ffn,
                         vocab=vocab, context=8, steps=steps)
@@ -84,7 +87,12 @@ def run_case(device, batch, hidden, heads, layers, ffn, vocab, steps):
     # whole_step=False: small decoders would otherwise run as one whole-step kernel.
     session = S.DecoderSession(device, initial, epsilon=1e-6,
                                attention_scale=config.head_dim ** -0.5, whole_step=False)
-    assert "ckl.fused.panel_gate_up" in session.invocation.node_names
+    names = session.invocation.node_names
+    assert "ckl.fused.panel_gate_up" in names
+    # q, k and v run as one pair launch when each is a whole number of 256-wide tiles and
+    # there are two row tiles (always when pairs are forced; at the cfg5 layer shapes anyway).
+    if hidden % 256 == 0 and batch > 128 and (forced or hidden == 1024):
+        assert "ckl.fused.panel_qkv" in names and "ckl.fused.panel_linear_rope" not in names
     session.step(steps)
     verify(session, initial, expected, config)
     assert faults() == 0

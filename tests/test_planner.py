@@ -133,6 +133,30 @@ def test_fused_decoder_plan_shape():
     assert topology[gate] == topology[up]
 
 
+def test_fused_qkv_node(monkeypatch):
+    """cfg5-shaped layers at 512 rows plan q, k and v as one tensor-core pair launch."""
+    config = ref.Config(batch=512, hidden=1024, heads=16, layers=2, ffn=4096, vocab=1000,
+                        context=8, steps=8)
+    lowered = decoder.decode.lower(signature=decoder_signature(config))
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
+                         whole_step=False)
+    names = plans.primary.node_names
+    layer = ["ckl.fused.rms_panel", "ckl.fused.panel_qkv", "ckl.fused.attention",
+             "ckl.fused.panel_linear_residual", "ckl.fused.rms_panel",
+             "ckl.fused.panel_gate_up", "ckl.fused.panel_linear_residual"]
+    head = ["ckl.fused.rms_panel", "ckl.fused.panel_linear_argmax", "ckl.fused.greedy_combine"]
+    assert names == ["ckl.decoder.embedding"] + layer * 2 + head
+    topology = plans.primary.topology
+    ids = sorted(topology)
+    assert topology[ids[2]] == [ids[1]] and topology[ids[3]] == [ids[2]]  # norm -> qkv -> attn
+    # Pairs switched off: three projection nodes again.
+    monkeypatch.setenv("CKL_B200_TC_PAIRS", "0")
+    plans = plan_program(lowered, fuse_pointwise=True, fuse_library=True, reuse_storage=True,
+                         whole_step=False)
+    assert "ckl.fused.panel_qkv" not in plans.primary.node_names
+    assert plans.primary.nodes == 1 + 9 * 2 + 3
+
+
 def test_tensor_core_decoder_plan_shape():
     """Batches of 128+ requests: split-operand panels feed tensor-core projections."""
     config = ref.Config(batch=256, hidden=128, heads=2, layers=2, ffn=256, vocab=512, context=8,
