@@ -253,12 +253,14 @@ int64_t pairCtas(const GemmSpec &s, int64_t tileColumns) {
   return 2 * ((rowTiles + 1) / 2) * ((s.N + tileColumns - 1) / tileColumns);
 }
 
-// K splits on pairs (1, 2 or 4: clusters of up to 8 CTAs): doubled while the grid stays within
-// one CTA per SM and every split keeps at least two slices.
+// K splits on pairs: doubled while the grid stays within one CTA per SM and every split keeps
+// at least two slices; at most 4 (portable 8-CTA clusters) for 128-wide tiles, 8 (16-CTA
+// clusters) for 256-wide ones.
 int pairSplits(const GemmSpec &s, int width) {
   const int64_t ctas = pairCtas(s, width), slices = panel::slices(s.K);
+  const int most = width == tc::pair::kWide ? 8 : 4;
   int splits = 1;
-  while (splits < 4 && ctas * splits * 2 <= tc::kTargetCtas && slices >= int64_t(splits) * 4)
+  while (splits < most && ctas * splits * 2 <= tc::kTargetCtas && slices >= int64_t(splits) * 4)
     splits *= 2;
   return splits;
 }
@@ -271,6 +273,9 @@ int pairSplits(const GemmSpec &s, int width) {
 // columns, 32 pair CTAs x 4 splits = 128 CTAs) slower still (q ~37 us, o/down shares
 // 5.2 -> 7.5 % of the step): with eight 32-deep slices per CTA the pair's start-up, split
 // reduction and cluster barriers outweigh the halved operand traffic.
+// 256-wide pairs with an eight-way K split on 16-CTA clusters (128 CTAs for the o and down
+// projections at the cfg5 shard) measured slower too: o/down 5.5 -> 6.2 % of the step, 5.60
+// -> 5.66 ms per step in one call; forced pairs still take them where the grid is small.
 // CKL_B200_TC_PAIRS=2 / 3 force 256- / 128-wide pairs wherever there are two row tiles (the
 // tests run every tensor-core shape both ways), =0 disables pairs.
 int linearPairWidth(const GemmSpec &s) {
@@ -468,6 +473,7 @@ const void *qkvSelect(const void *spec) {
   if (!qkvPairs(specOf<GemmSpec>(spec), &all))
     return nullptr;
   switch (pairSplits(all, tc::pair::kWide)) {
+  case 8: return reinterpret_cast<const void *>(&panelQkvPairTc<8>);
   case 4: return reinterpret_cast<const void *>(&panelQkvPairTc<4>);
   case 2: return reinterpret_cast<const void *>(&panelQkvPairTc<2>);
   default: return reinterpret_cast<const void *>(&panelQkvPairTc<1>);
@@ -528,7 +534,8 @@ bool panelAppendGeometry(const void *spec, std::size_t, library::Geometry *g) {
     if (const int width = linearPairWidth(s)) {                                                \
       const int splits = pairSplits(s, width);                                                 \
       if (width == tc::pair::kWide)                                                            \
-        return splits == 4   ? reinterpret_cast<const void *>(&pairFn<4, tc::pair::kWide>)     \
+        return splits == 8   ? reinterpret_cast<const void *>(&pairFn<8, tc::pair::kWide>)     \
+               : splits == 4 ? reinterpret_cast<const void *>(&pairFn<4, tc::pair::kWide>)     \
                : splits == 2 ? reinterpret_cast<const void *>(&pairFn<2, tc::pair::kWide>)     \
                              : reinterpret_cast<const void *>(&pairFn<1, tc::pair::kWide>);    \
       return splits == 4   ? reinterpret_cast<const void *>(&pairFn<4, tc::pair::kNarrow>)     \

@@ -184,7 +184,9 @@ __device__ void body(const gemm::Params &p, const WeightMap &weights,
   static_assert(EPI != gemm::kQkv || BN == kWide, "q/k/v tiles are 256 wide");
   static_assert(SPLITS == 1 || (EPI != gemm::kSwiGluPanel && EPI != gemm::kArgmax),
                 "gate/up and the argmax heads are not split");
-  static_assert(2 * SPLITS <= 8, "portable cluster size");
+  // Clusters of up to 16 CTAs: more than 8 is a non-portable size, allowed per kernel by the
+  // runtime (cudaFuncAttributeNonPortableClusterSizeAllowed) when it selects the kernel.
+  static_assert(2 * SPLITS <= 16 && (BN == kWide || 2 * SPLITS <= 8), "cluster size");
   extern __shared__ __align__(1024) unsigned char raw[];
   Smem &sm = *reinterpret_cast<Smem *>(raw);
   const GemmSpec &s = p.s;

@@ -1411,6 +1411,10 @@ void ckl_commit(void *frame, uint64_t id) {
           check(cudaFuncSetAttribute(chosen, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(f.pending.shared)),
                 "cudaFuncSetAttribute");
+          // Tensor-core pair kernels may be compiled for 16-CTA clusters (a non-portable size
+          // that each kernel must opt into); other kernels are unaffected by the permission.
+          check(cudaFuncSetAttribute(chosen, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                "cudaFuncSetAttribute");
         }
       }
       if (k->prepare) {
