@@ -40,42 +40,59 @@ __device__ __forceinline__ float4 rmsScale(const float4 &a, float inv, const flo
                      __fmul_rn(__fmul_rn(a.z, inv), g.z), __fmul_rn(__fmul_rn(a.w, inv), g.w));
 }
 
+// Rows of up to 1024 columns (the decoder's common case) take the staged path: the CTA's
+// eight normalised rows go to shared memory, then eight consecutive threads store one 8-row x
+// 16-byte core matrix of the panel (128 contiguous bytes) instead of each lane storing 16 bytes
+// 2 KB apart along its own row.  The arithmetic is the same on both paths.
+constexpr int kStagedColumns = 4 * kWarp * kRmsHeld; // 1024
+
 __global__ void __launch_bounds__(kPanelWarps *kWarp)
     rmsPanelKernel(const float *x, const float *gain, float *out, float eps, RmsApplySpec s) {
   dependentLaunchEntry();
+  __shared__ __align__(16) float staged[kPanelWarps][kStagedColumns + 4]; // +4: no bank conflicts
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int64_t m = int64_t(blockIdx.x) * kPanelWarps + warp;
-  if (m >= s.B)
-    return;
   const int64_t K = s.C;
-  const float *row = x + m * K;
   const float *g = gain + s.layer * K;
-  const bool vec = K % 4 == 0 && aligned16(row) && aligned16(g);
+  const bool vec = K % 4 == 0 && aligned16(x) && aligned16(g);
   const int64_t padded = panel::slices(K) * panel::kSlice;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float total = 0.f;
-  if (vec && padded <= 4 * kWarp * kRmsHeld) {
-    const float4 *row4 = reinterpret_cast<const float4 *>(row);
-    float4 held[kRmsHeld];
+  if (vec && padded <= kStagedColumns) { // uniform over the CTA
+    if (m < s.B) {
+      const float4 *row4 = reinterpret_cast<const float4 *>(x + m * K);
+      float4 held[kRmsHeld];
+      float total = 0.f;
 #pragma unroll
-    for (int i = 0; i < kRmsHeld; ++i) {
-      const int64_t q = lane + i * kWarp;
-      held[i] = q < K / 4 ? row4[q] : zero;
-      total += held[i].x * held[i].x + held[i].y * held[i].y + held[i].z * held[i].z +
-               held[i].w * held[i].w;
+      for (int i = 0; i < kRmsHeld; ++i) {
+        const int64_t q = lane + i * kWarp;
+        held[i] = q < K / 4 ? row4[q] : zero;
+        total += held[i].x * held[i].x + held[i].y * held[i].y + held[i].z * held[i].z +
+                 held[i].w * held[i].w;
+      }
+      total = warpSum(total);
+      const float inv = rsqrtf(total / float(K) + eps);
+#pragma unroll
+      for (int i = 0; i < kRmsHeld; ++i) {
+        const int64_t k = 4 * (lane + int64_t(i) * kWarp);
+        if (k < padded)
+          *reinterpret_cast<float4 *>(&staged[warp][k]) =
+              k < K ? rmsScale(held[i], inv, reinterpret_cast<const float4 *>(g)[k / 4]) : zero;
+      }
     }
-    total = warpSum(total);
-    const float inv = rsqrtf(total / float(K) + eps);
-#pragma unroll
-    for (int i = 0; i < kRmsHeld; ++i) {
-      const int64_t k = 4 * (lane + int64_t(i) * kWarp);
-      if (k < padded)
-        panel::store4(out, m, k, K,
-                      k < K ? rmsScale(held[i], inv, reinterpret_cast<const float4 *>(g)[k / 4])
-                            : zero);
+    __syncthreads();
+    const int64_t m0 = int64_t(blockIdx.x) * kPanelWarps;
+    for (int64_t i = threadIdx.x; i < kPanelWarps * (padded / 4); i += kPanelWarps * kWarp) {
+      const int r = int(i % kPanelWarps);
+      const int64_t k = 4 * (i / kPanelWarps);
+      if (m0 + r < s.B)
+        panel::store4(out, m0 + r, k, K, *reinterpret_cast<const float4 *>(&staged[r][k]));
     }
     return;
   }
+  if (m >= s.B)
+    return;
+  const float *row = x + m * K;
+  float total = 0.f;
   if (vec) {
     for (int64_t q = lane; q < K / 4; q += kWarp) {
       const float4 v = reinterpret_cast<const float4 *>(row)[q];
