@@ -28,7 +28,7 @@ import numpy as np
 
 import ckl
 from ..compile import (POSITION, READ, WRITE, CompiledPlans, Event, Node, Slot, _panel_floats,
-                       _plan, library_geometry)
+                       _plan, library_accepts, library_geometry)
 from ..frontend.checker import BoundParameter, BoundSignature
 from ..frontend.tracer import Resource
 from ..library import pack
@@ -100,16 +100,26 @@ def build_plan(specs: dict, positions: int):
              pack(M, C, L, layer), [x, arg["norm1"]], [(x_panel, WRITE, "whole")],
              "attention norm" + tag)
         q = temporary((M, C), "q")
-        node("ckl.fused.panel_linear_rope", [R(x_panel), R(arg["wq"]), R(sincos), R(position), R(q)],
-             _gemm(M, C, C, L, layer, A, D, T, cache=B), [x_panel, arg["wq"], sincos],
-             [pos_read, (q, WRITE, "whole")], "q projection" + tag)
-        node("ckl.fused.panel_linear_rope_append",
-             [R(x_panel), R(arg["wk"]), R(sincos), R(position), R(kc)],
-             _gemm(M, C, C, L, layer, A, D, T, cache=B), [x_panel, arg["wk"], sincos],
-             [pos_read, (kc, WRITE, "whole")], "k projection" + tag)
-        node("ckl.fused.panel_linear_append", [R(x_panel), R(arg["wv"]), R(position), R(vc)],
-             _gemm(M, C, C, L, layer, A, D, T, cache=B), [x_panel, arg["wv"]],
-             [pos_read, (vc, WRITE, "whole")], "v projection" + tag)
+        qkv = _gemm(M, C, C, L, layer, A, D, T, cache=B)
+        if library_accepts("ckl.fused.panel_qkv", qkv):
+            # q, k and v as one tensor-core pair launch (each column tile with its epilogue).
+            node("ckl.fused.panel_qkv",
+                 [R(x_panel), R(arg["wq"]), R(arg["wk"]), R(arg["wv"]), R(sincos), R(position),
+                  R(q), R(kc), R(vc)], qkv, [x_panel, arg["wq"], arg["wk"], arg["wv"], sincos],
+                 [pos_read, (q, WRITE, "whole"), (kc, WRITE, "whole"), (vc, WRITE, "whole")],
+                 "q/k/v projections" + tag)
+        else:
+            node("ckl.fused.panel_linear_rope",
+                 [R(x_panel), R(arg["wq"]), R(sincos), R(position), R(q)], qkv,
+                 [x_panel, arg["wq"], sincos], [pos_read, (q, WRITE, "whole")],
+                 "q projection" + tag)
+            node("ckl.fused.panel_linear_rope_append",
+                 [R(x_panel), R(arg["wk"]), R(sincos), R(position), R(kc)], qkv,
+                 [x_panel, arg["wk"], sincos], [pos_read, (kc, WRITE, "whole")],
+                 "k projection" + tag)
+            node("ckl.fused.panel_linear_append", [R(x_panel), R(arg["wv"]), R(position), R(vc)],
+                 qkv, [x_panel, arg["wv"]], [pos_read, (vc, WRITE, "whole")],
+                 "v projection" + tag)
         context_panel = panel(C, "context_panel")
         node("ckl.prefill.attention", [R(q), R(kc), R(vc), R(position), R(context_panel), scale],
              pack(B, A, T, D, L, layer, positions), [q, kc, vc],
