@@ -28,7 +28,7 @@ namespace {
 using gemm::Params;
 
 // ---- panel producers -----------------------------------------------------------------------
-constexpr int kPanelWarps = 8;
+constexpr int kPanelWarps = 4;
 
 // One warp per row: sum of squares, then the normalised row split into the panel.  Columns
 // between K and the next multiple of 32 are written as zeros.  Rows of up to 1024 columns are
