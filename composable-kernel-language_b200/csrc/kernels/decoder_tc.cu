@@ -9,8 +9,9 @@
 //   panel_gate_up: panel = split(silu(a @ wg) * (a @ wu))  (feeds the down projection)
 //   panel_linear{,_rope,_rope_append,_append,_residual,_argmax}: the projections with the same
 //   fused epilogues as the FFMA kernels.
-// The normalised and activated values are rounded exactly as in the FFMA kernels
-// (x * rsqrt(mean(x^2) + eps) * gain, silu(g) * u) before the split.
+// The normalised values are rounded exactly as in the FFMA kernels (x * rsqrt(mean(x^2) + eps)
+// * gain); silu(g) * u uses the fast division (within 2 ulp of the FFMA kernels' value) before
+// the split.
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
