@@ -1,6 +1,7 @@
 // Tensor-core projections on CTA pairs: 2-SM (cta_group::2) tcgen05 3xTF32 with 256 x 256
-// output tiles, for the wide projections of batched decode and prefill (fused gate/up + SwiGLU
-// and the LM head with its argmax partials).
+// output tiles (256 x 128 in the narrow build), for the wide projections of batched decode and
+// prefill: fused gate/up + SwiGLU, the LM head with its argmax partials, fused q/k/v, and the
+// batched prefill's o / down projections.
 //
 // Why pairs.  The single-CTA kernel (tcgemm.cuh) is bound by shared-memory bandwidth: an
 // M=128, N=128, K=8 tf32 MMA reads 8 KB of operands for 65 cycles of tensor work, about the
@@ -14,8 +15,9 @@
 //
 // Pair protocol (the pair's two CTAs adjacent along cluster x, the dimension CTA pairs are
 // formed on; the even cluster rank is the leader; K splits of a tile, if any, along cluster z):
-//   * both CTAs' warp 1 allocate all 512 tensor-memory columns with `tcgen05.alloc.cta_group::2`
-//     (hi*hi accumulator in columns 0-255, the hi*lo + lo*hi correction in 256-511);
+//   * both CTAs' warp 1 allocate 2 x BN tensor-memory columns with `tcgen05.alloc.cta_group::2`
+//     (hi*hi accumulator in columns 0..BN-1, the hi*lo + lo*hi correction in BN..2BN-1: all 512
+//     columns for 256-wide tiles);
 //   * each CTA's producer (warp 0) copies its own panel block (its 128 rows, hi + lo) and its
 //     half of the weight box into its own ring, completing on its own `full` barrier: no copy
 //     signals the other CTA;
@@ -25,7 +27,7 @@
 //     CTA), which certifies both the panel block and the converted weights of that CTA (a
 //     cluster-scope release per warp and slice measured as the kernel's top stall);
 //   * the leader's MMA thread waits on `ready`, issues per 8-deep
-//     k-step three `tcgen05.mma.cta_group::2.kind::tf32` (M=256, N=256), and commits with
+//     k-step three `tcgen05.mma.cta_group::2.kind::tf32` (M=256, N=BN), and commits with
 //     `.multicast::cluster` to both CTAs' `empty` (ring stage) and `bEmpty` (conversion
 //     buffer) barriers, and finally to both CTAs' `accDone`;
 //   * each CTA's epilogue reads its own tensor memory (its 128 rows, all 256 columns);
