@@ -247,8 +247,10 @@ __global__ void __cluster_dims__(2, 1, SPLITS) __launch_bounds__(tc::kThreads, 1
 // Pair kernels run a projection when its output spans at least two row tiles, one tile width
 // of columns, and pair tiles for at least 96 CTAs (about two thirds of the SMs); otherwise the
 // single-CTA kernel with its row-tile sharing and K splits fills the GPU better.
-// CKL_B200_TC_PAIRS (read when a program is compiled and bound): 0 keeps the single-CTA kernel
-// everywhere, 2 takes pairs whenever there are two row tiles (tests of small shapes).
+// CKL_B200_TC_PAIRS (read when a program is compiled and again when it is bound; keep it
+// unchanged between the two, or the bound kernel may not match the planned grid): 0 keeps the
+// single-CTA kernel everywhere, 2 takes pairs whenever there are two row tiles (tests of small
+// shapes).
 bool usePairs(const GemmSpec &s, int64_t tileColumns) {
   const char *mode = std::getenv("CKL_B200_TC_PAIRS");
   if ((mode && mode[0] == '0') || s.N < tileColumns || s.K <= 0)
