@@ -69,6 +69,18 @@ template <int D> struct PrefillSmem {
   float p[kPrefillKeys][kPrefillQueries + 4]; // probabilities, key-major
 };
 
+// 16-byte asynchronous copy global -> shared that zero-fills the destination instead when
+// `valid` is false (no bytes are read then), and waits for all but the newest `N` groups.
+__device__ __forceinline__ void copyAsync16OrZero(void *dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(valid ? 16u : 0u)
+               : "memory");
+}
+template <int N> __device__ __forceinline__ void copyAsyncWaitAllBut() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <int D>
 __global__ void __launch_bounds__(kPrefillThreads)
     prefillAttentionKernel(const float *q, const float *kc, const float *vc, const int *position,
@@ -120,7 +132,45 @@ __global__ void __launch_bounds__(kPrefillThreads)
       acc[a][j] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 
+  // Keys and values stream through the same shared buffers with cp.async when the cache rows
+  // start on 16-byte boundaries: the next block's keys are requested as soon as every thread
+  // has read this block's keys (they load under the softmax and the value pass), the next
+  // block's values as soon as the value pass is done (they load under the next score pass).
+  // No second buffer (which would halve the CTAs per SM) and no registers hold them.
+  const bool streamed = last >= 0 && aligned16(kc + base) && aligned16(vc + base);
+  auto copyKeys = [&](int64_t from) {
+    for (int e = tid; e < KB * G; e += kPrefillThreads) {
+      const int r = e / G, g = e % G;
+      const int64_t t = from + r;
+      const bool valid = t <= last;
+      copyAsync16OrZero(&sm.k[r][4 * g], kc + base + (valid ? t * D + 4 * g : 0), valid);
+    }
+  };
+  auto copyValues = [&](int64_t from) {
+    for (int e = tid; e < KB * G; e += kPrefillThreads) {
+      const int r = e / G, g = e % G;
+      const int64_t t = from + r;
+      const bool valid = t <= last;
+      copyAsync16OrZero(&sm.v[r][g], vc + base + (valid ? t * D + 4 * g : 0), valid);
+    }
+  };
+  if (streamed) {
+    copyKeys(0);
+    copyValues(0);
+    copyAsyncCommit();
+  }
+
   for (int64_t t0 = 0; t0 <= last; t0 += KB) {
+    const bool more = t0 + KB <= last; // uniform over the CTA
+    if (streamed) {
+      // This block's keys (group committed after the previous score pass, or the first group
+      // with the first values) have landed; the newest group (values) may still be in flight.
+      if (t0 == 0)
+        copyAsyncWaitAllBut<0>();
+      else
+        copyAsyncWaitAllBut<1>();
+      __syncthreads(); // every thread's copies visible (and the queries staged)
+    } else {
     __syncthreads(); // previous block's keys and probabilities consumed (queries staged)
     for (int e = tid; e < KB * G; e += kPrefillThreads) {
       const int r = e / G, g = e % G;
@@ -140,6 +190,7 @@ __global__ void __launch_bounds__(kPrefillThreads)
       sm.v[r][g] = vv;
     }
     __syncthreads();
+    }
     float score[4][KPT];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
@@ -164,6 +215,13 @@ __global__ void __launch_bounds__(kPrefillThreads)
           score[a][u] = fmaf(qv[a].z, kv[u].z, score[a][u]);
           score[a][u] = fmaf(qv[a].w, kv[u].w, score[a][u]);
         }
+    }
+    if (streamed) {
+      __syncthreads(); // every thread has read this block's keys
+      if (more) {
+        copyKeys(t0 + KB);
+        copyAsyncCommit();
+      }
     }
     float correction[4], e[4][KPT];
 #pragma unroll
@@ -197,6 +255,14 @@ __global__ void __launch_bounds__(kPrefillThreads)
       *reinterpret_cast<float4 *>(&sm.p[lane16 + TG * u][4 * quad]) =
           make_float4(e[0][u], e[1][u], e[2][u], e[3][u]);
     __syncwarp(); // a quad's probabilities come from the 16 threads of this half-warp
+    if (streamed) {
+      // This block's values: all but the newest group (the next keys, if requested).
+      if (more)
+        copyAsyncWaitAllBut<1>();
+      else
+        copyAsyncWaitAllBut<0>();
+      __syncthreads();
+    }
 #pragma unroll
     for (int j = 0; j < GPT; ++j) {
       const int g = lane16 + TG * j;
@@ -223,6 +289,13 @@ __global__ void __launch_bounds__(kPrefillThreads)
 #pragma unroll
       for (int a = 0; a < 4; ++a)
         acc[a][j] = r[a];
+    }
+    if (streamed) {
+      __syncthreads(); // every thread has read this block's values and probabilities
+      if (more) {
+        copyValues(t0 + KB);
+        copyAsyncCommit();
+      }
     }
   }
 #pragma unroll
