@@ -500,6 +500,55 @@ __device__ __forceinline__ void reduceAndStore(const gemm::Params &p, Staging<BN
     }
     return;
   }
+  if constexpr ((EPI == gemm::kResidual || EPI == gemm::kStore) && BN == 4 * kWarp &&
+                kRows % kConverterWarps == 0) {
+    if (vec4) {
+      // One quad per lane; a warp's rows in batches of up to four, every load of a batch (the
+      // splits' staged partials through distributed shared memory, the residual from global
+      // memory) issued before any is used: one round trip per batch instead of per row (the
+      // per-row loop spent ~4,300 of a ~24,000-cycle o-projection CTA here).  The sums and the
+      // residual add are the per-row loop's, in the same order.
+      constexpr int kPerWarp = kRows / kConverterWarps;
+      constexpr int kBatch = kPerWarp < 4 ? kPerWarp : 4;
+      const int c = 4 * lane;
+      for (int b0 = 0; b0 < kPerWarp; b0 += kBatch) {
+        float4 part[kBatch][SPLITS], res[kBatch];
+        bool use[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          const int row = int(rank) * kRows + warp + (b0 + i) * kConverterWarps;
+          const int64_t m = m0 + row;
+          use[i] = m < M && n0 + c < N;
+          if constexpr (SPLITS == 1) {
+            part[i][0] = *reinterpret_cast<const float4 *>(&stage[row][c]);
+          } else {
+#pragma unroll
+            for (unsigned q = 0; q < SPLITS; ++q)
+              part[i][q] = loadCluster(&stage[row][c], q);
+          }
+          if constexpr (EPI == gemm::kResidual)
+            if (use[i])
+              res[i] = *reinterpret_cast<const float4 *>(p.residual + m * N + n0 + c);
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (!use[i])
+            continue;
+          const int64_t m = m0 + int(rank) * kRows + warp + (b0 + i) * kConverterWarps;
+          float4 v = part[i][0];
+#pragma unroll
+          for (int q = 1; q < SPLITS; ++q)
+            v = make_float4(__fadd_rn(v.x, part[i][q].x), __fadd_rn(v.y, part[i][q].y),
+                            __fadd_rn(v.z, part[i][q].z), __fadd_rn(v.w, part[i][q].w));
+          if constexpr (EPI == gemm::kResidual)
+            v = make_float4(__fadd_rn(res[i].x, v.x), __fadd_rn(res[i].y, v.y),
+                            __fadd_rn(res[i].z, v.z), __fadd_rn(res[i].w, v.w));
+          *reinterpret_cast<float4 *>(p.out + m * N + n0 + c) = v;
+        }
+      }
+      return;
+    }
+  }
   for (int r = warp; r < kRows; r += kConverterWarps) {
     const int row = int(rank) * kRows + r;
     const int64_t m = m0 + row;
